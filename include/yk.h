@@ -1,0 +1,117 @@
+// Kernel-level C ABI of the B200 engine (libyolob200.so).
+//
+// One launcher per hot-path kernel family.  Every launcher is asynchronous on the given
+// stream, takes plain pointers and view descriptors (no C++ or torch types), validates its
+// arguments on the host and returns 0 on success or a negative YK_E* code (nothing is
+// launched on error).  The engine's executor calls these for every op of a model graph; the
+// parity tests call them one op at a time through ctypes.
+//
+// Tensors are NHWC fp16 "views" over a buffer of shape [batch][H][W][stride]:
+// element (n, y, x, c) lives at ptr[((n*H + y)*W + x)*stride + coff + c].  This is the
+// reference's (buffer, channel offset, C) view (engine/engine.cu:1254-1259) with the batch
+// made explicit.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* yk_stream_t;   // == cudaStream_t
+
+#define YK_OK 0
+#define YK_EINVAL (-1)      // bad shape / alignment / argument
+#define YK_ECUDA (-2)       // CUDA launch error (see yk_last_cuda_error)
+#define YK_ETIMEOUT (-3)    // a kernel's bounded wait gave up (device error word set)
+#define YK_EUNSUP (-4)      // shape outside what the kernels implement
+
+typedef struct {
+  void* ptr;          // fp16 buffer base (NOT offset by coff)
+  int batch, H, W;    // logical shape of the view
+  int stride;         // channels per pixel of the underlying buffer
+  int coff;           // first channel of the view
+  int C;              // channels in the view
+} YkView;
+
+typedef struct {
+  const void* weight;   // fp16 OHWI [Cout][k][k][Cin/groups]
+  const float* bias;    // fp32 [Cout]
+  int k, s, p;          // square kernel, stride, padding
+  int groups;           // 1 (dense) or == Cin == Cout (depthwise)
+  int act;              // 0 identity, 1 SiLU
+  int Cin, Cout;
+  int tile;             // tensor-core N tile (0 = heuristic, else 32/64/128/256)
+  int splitk;           // reserved, 0
+} YkConv;
+
+// Convolution with bias, activation, optional residual (y = act(conv(x)+b) + res) written
+// into y's channel slice.  Dense convs with Cin % 8 == 0 run on the tcgen05 implicit-GEMM
+// kernel; Cin == 3 (first conv) and depthwise convs run on dedicated direct kernels.
+// Replaces the CONV dispatch of runOp (engine/engine.cu:1263-1336).
+int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, yk_stream_t st);
+
+// 5x5 stride-1 pad-2 max pool (SPPF), engine/engine.cu:672-695.
+int yk_maxpool5(const YkView* x, const YkView* y, yk_stream_t st);
+// The SPPF chain y1 = pool5(x), y2 = pool5(y1), y3 = pool5(y2) in one pass over x.
+int yk_maxpool5x3(const YkView* x, const YkView* y1, const YkView* y2, const YkView* y3, yk_stream_t st);
+// Nearest 2x upsample, engine/engine.cu:697-708.
+int yk_upsample2(const YkView* x, const YkView* y, yk_stream_t st);
+// Pixel shuffle r=2 from quadrant channel blocks, engine/engine.cu:713-725.
+int yk_ps2(const YkView* x, const YkView* y, yk_stream_t st);
+// Channel-slice copy, engine/engine.cu:727-732.
+int yk_copyc(const YkView* x, const YkView* y, yk_stream_t st);
+// y = a + b, engine/engine.cu:663-670.
+int yk_add(const YkView* a, const YkView* b, const YkView* y, yk_stream_t st);
+// PSA attention: per image and head, out = softmax(q k^T / sqrt(kd)) v over the H*W tokens;
+// qkv channel layout per head [q kd | k kd | v hd].  Replaces engine/engine.cu:1363-1404.
+int yk_attn(const YkView* qkv, const YkView* y, int heads, int kd, int hd, yk_stream_t st);
+
+// Letterbox one BGR u8 HWC frame (device memory, sh x sw) into batch slot `slot` of the
+// S x S x 3 input view y (RGB, /255, pad 114, bilinear as cv2 INTER_LINEAR's formula).
+// Geometry (scale, top, left) is computed on the host as in engine/engine.cu:1704-1713
+// and returned through the optional out pointers.  Kernel: engine/engine.cu:968-998.
+int yk_letterbox(const uint8_t* bgr, int sh, int sw, const YkView* y, int slot,
+                 float* scale_out, int* top_out, int* left_out, yk_stream_t st);
+
+// Detection head levels for decode / NMS / masks.
+typedef struct {
+  YkView box;     // 64 channels: 4 sides x 16 DFL bins
+  YkView cls;     // >= nc channels (multiple of 8; pad logits ignored)
+  YkView coef;    // segment: nm mask coefficients; ptr == NULL for detect
+  int stride;     // 8, 16, 32
+} YkLevel;
+
+// Device workspace of the post-processing chain, sized by yk_post_workspace_bytes.
+typedef struct {
+  void* ws;          // device scratch
+  size_t ws_bytes;
+  float* outdets;    // device [batch][max_out][6]: x1 y1 x2 y2 score cls (letterbox px)
+  int* outidx;       // device [batch][max_out]: anchor index of each survivor
+  int* outcnt;       // device [batch]: survivors
+  int* rawcnt;       // device [batch]: conf-passing candidates before NMS
+} YkPost;
+
+size_t yk_post_workspace_bytes(int batch, int anchors);
+// Decode (engine/engine.cu:848-906): per anchor best class over nc, score = sigmoid,
+// keep if score >= conf, DFL box.  Candidates keep anchor order (no atomics).
+int yk_decode(const YkLevel* levels, int nlevels, int batch, int nc, float conf,
+              const YkPost* post, yk_stream_t st);
+// NMS (engine/engine.cu:1051-1123, made exact and deterministic): every candidate is
+// considered (no 1024 cap); order = score desc, anchor index asc; same-class IoU > iou
+// suppresses; at most max_out survivors per image.
+int yk_nms(int batch, int anchors, float iou, int max_out, const YkPost* post, yk_stream_t st);
+// Masks for NMS survivors (engine/engine.cu:1129-1158): logit = coef . proto, crop to the
+// box scaled to proto resolution (half-open), mask = logit > 0.  masks: [batch][max_out][Ph][Pw].
+int yk_masks(const YkLevel* levels, int nlevels, const YkView* proto, int in_h, int in_w,
+             int max_out, const YkPost* post, uint8_t* masks, yk_stream_t st);
+
+// Device error word (bounded-wait timeouts) of the current device; cleared by the call.
+int yk_fetch_device_error(void);
+const char* yk_last_cuda_error(void);
+// Number of kernels this library launched since load (all devices) — a host-side counter.
+long long yk_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,82 @@
+// Engine C ABI of the B200 engine (libyolob200.so): a drop-in for the reference's
+// engine/yolo.h (same symbols, same structs, same argument meaning), plus additive
+// extensions marked EXT.  Each entry cites the reference declaration it replaces.
+//
+// Differences from the reference, all in the direction of safety:
+//   * errors never exit(): yolo_create returns NULL (see yolo_last_error), the void calls
+//     record the error for yolo_last_error and do nothing;
+//   * NMS considers every candidate (the reference truncates at 1024) and orders ties by
+//     anchor index, so results are deterministic;
+//   * CUDA graphs are captured lazily per batch size on first use (the reference captures
+//     B = 1..max_batch inside yolo_create); yolo_exec_ms(B) captures and calibrates B on demand.
+#pragma once
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// engine/yolo.h:7-8
+typedef struct { float x1, y1, x2, y2, score; int cls; } YoloDet;
+typedef struct { float x, y, w, h, angle, score; int cls; } YoloObbDet;
+
+// engine/yolo.h:10-11 — load a model directory on the current device; buffers for up to
+// max_batch frames.  NULL on failure.
+void* yolo_create(const char* model_dir, int max_batch);
+// engine/yolo.h:12-16 — 0 detect, 1 obb, 2 classify, 3 segment (only 0 and 3 load here).
+int yolo_task(void* h);
+// engine/yolo.h:17-18 — calibrated GPU latency (ms) of one batch-B graph launch.
+float yolo_exec_ms(void* h, int B);
+// engine/yolo.h:19
+cudaStream_t yolo_stream(void* h);
+// engine/yolo.h:20-23 — letterbox a device BGR u8 HWC frame into batch slot `slot`
+// (async on the engine stream; the frame must stay valid until the stream passes it).
+void yolo_preprocess(void* h, const unsigned char* dev_bgr, int height, int width, int slot);
+// engine/yolo.h:24-25 — run the batch-B graph (net + decode + NMS [+ masks] + D2H) and sync.
+void yolo_run(void* h, int B);
+// engine/yolo.h:26-28
+void yolo_run_async(void* h, int B);
+void yolo_sync(void* h);
+// engine/yolo.h:29-30 — detections of a slot in original-image coordinates; returns count.
+int yolo_get(void* h, int slot, YoloDet* out, int cap);
+// engine/yolo.h:36-38
+void yolo_slot_geom(void* h, int slot, float* scale, int* top, int* left);
+// engine/yolo.h:42-43 — proto resolution (0/0 for detect models).
+void yolo_mask_dim(void* h, int* ph, int* pw);
+// engine/yolo.h:44-49 — binary {0,1} mask (ph*pw bytes) of detection `det`; 0 or -1.
+int yolo_get_mask(void* h, int slot, int det, unsigned char* out);
+
+// ---- EXT (no counterpart in the reference header) ----
+typedef struct {
+  int device;          // CUDA device ordinal (-1 = current)
+  float conf;          // score gate (reference: 0.25)
+  float iou;           // NMS IoU threshold (reference: 0.45)
+  int max_det;         // survivors per image (reference: 300)
+  int autotune;        // 1 = time tensor-core tile variants per conv at create
+  int fuse;            // 1 = fold CONV + ADD into the conv epilogue (reference fuseAdds)
+} YoloOptions;
+void yolo_default_options(YoloOptions* o);
+void* yolo_create_ex(const char* model_dir, int max_batch, const YoloOptions* opts);
+void yolo_destroy(void* h);
+const char* yolo_last_error(void);
+// Number of conf-passing candidates of a slot before NMS (reference h_rawcnt tripwire).
+int yolo_raw_count(void* h, int slot);
+// Run one op of the UNFUSED graph for B images (dump mode, engine/engine.cu:1843-1888);
+// returns 0, 1 if the op has no output view (decode/masks), <0 on error.
+int yolo_run_op(void* h, int op_index, int B);
+int yolo_num_ops(void* h);
+// Device pointer / geometry of a graph tensor view (for dump / resync / tests).
+int yolo_tensor_view(void* h, int tensor, void** ptr, int* H, int* W, int* stride, int* coff, int* C);
+// Copy a graph tensor view of images 0..B-1 to / from contiguous host fp16 [B][H][W][C]
+// (dump mode, resync, tests).  Synchronous; 0 or -1.
+int yolo_read_tensor(void* h, int tensor, int B, void* host);
+int yolo_write_tensor(void* h, int tensor, int B, const void* host);
+// Per-op device timings over `iters` runs of the fused op list (CLI `profile`); fills up to
+// cap entries of ms[] in op order and returns the number of ops.
+int yolo_profile(void* h, int B, int iters, float* ms, int cap);
+// Kind name of fused op i ("CONV", ...) and its tensor-core tile (0 if none).
+const char* yolo_op_desc(void* h, int op_index, int* tile);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,186 @@
+/* ORACLE / TEST INFRASTRUCTURE — CPU restatement of the reference's pre/post-processing.
+ *
+ * Used only by tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg as the
+ * checker; never by the engine.  Plain C, single thread, straight loops in the order the
+ * reference kernels define:
+ *   oref_letterbox  engine/engine.cu:968-998 (k_preprocess) + 1704-1713 (host geometry)
+ *   oref_decode     engine/engine.cu:848-906 (k_decode): first-max class over nc logits,
+ *                   sigmoid score, gate score >= conf, DFL softmax expectation, xyxy*stride
+ *   oref_nms        engine/engine.cu:1051-1123 (k_nms) without its 1024-candidate cap:
+ *                   candidates sorted by score desc (ties: anchor index asc), greedy
+ *                   same-class suppression with IoU = inter/(area_a+area_b-inter) > thr
+ *   oref_masks      engine/engine.cu:1129-1158 (k_mask_assemble): logit = coef . proto
+ *                   (fp32, c = 0..nm-1 in order), half-open crop at proto scale, logit > 0
+ * Arithmetic goes through detmath.h (explicitly rounded binary32 ops, Cody-Waite exp), the
+ * same formulas the CUDA kernels use, so results must match bit for bit.  Build with
+ * -ffp-contract=off (oracle/Makefile).
+ */
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <math.h>
+
+#include "../yolo11.cu_b200/csrc/detmath.h"
+
+/* fp16 NHWC view: element (y, x, c) of image n at base[((n*H + y)*W + x)*stride + c] */
+typedef struct {
+  const uint16_t* base; /* already offset by the view's channel offset */
+  int H, W, stride;
+} OView;
+
+static const uint16_t* opix(const OView* v, int n, int y, int x) {
+  return v->base + (((size_t)n * v->H + y) * v->W + x) * (size_t)v->stride;
+}
+
+void oref_letterbox_geom(int S, int sh, int sw, float* scale, int* nh, int* nw, int* top,
+                         int* left) {
+  float a = (float)S / (float)sh, b = (float)S / (float)sw;
+  float s = a < b ? a : b;
+  *scale = s;
+  *nh = (int)roundf((float)sh * s);
+  *nw = (int)roundf((float)sw * s);
+  *top = (S - *nh) / 2;
+  *left = (S - *nw) / 2;
+}
+
+/* bgr: sh x sw x 3 u8; out: S x S x 3 fp16 bits (RGB, /255, pad 114) */
+void oref_letterbox(const uint8_t* bgr, int sh, int sw, int S, uint16_t* out) {
+  float scale;
+  int nh, nw, top, left;
+  oref_letterbox_geom(S, sh, sw, &scale, &nh, &nw, &top, &left);
+  for (int y = 0; y < S; y++)
+    for (int x = 0; x < S; x++) {
+      float r, g, b;
+      if (y < top || y >= top + nh || x < left || x >= left + nw) {
+        r = g = b = 114.f;
+      } else {
+        float fy = DM_SUB(DM_DIV(DM_ADD((float)(y - top), 0.5f), scale), 0.5f);
+        float fx = DM_SUB(DM_DIV(DM_ADD((float)(x - left), 0.5f), scale), 0.5f);
+        int y0 = (int)floorf(fy), x0 = (int)floorf(fx);
+        float wy = DM_SUB(fy, (float)y0), wx = DM_SUB(fx, (float)x0);
+        int y1 = y0 + 1 < sh - 1 ? y0 + 1 : sh - 1, x1 = x0 + 1 < sw - 1 ? x0 + 1 : sw - 1;
+        if (y0 < 0) y0 = 0;
+        if (x0 < 0) x0 = 0;
+        const uint8_t* p00 = bgr + ((size_t)y0 * sw + x0) * 3;
+        const uint8_t* p01 = bgr + ((size_t)y0 * sw + x1) * 3;
+        const uint8_t* p10 = bgr + ((size_t)y1 * sw + x0) * 3;
+        const uint8_t* p11 = bgr + ((size_t)y1 * sw + x1) * 3;
+        float w00 = DM_MUL(DM_SUB(1.f, wy), DM_SUB(1.f, wx));
+        float w01 = DM_MUL(DM_SUB(1.f, wy), wx);
+        float w10 = DM_MUL(wy, DM_SUB(1.f, wx));
+        float w11 = DM_MUL(wy, wx);
+        float v[3];
+        for (int c = 0; c < 3; c++) {
+          float t = DM_MUL((float)p00[c], w00);
+          t = DM_ADD(t, DM_MUL((float)p01[c], w01));
+          t = DM_ADD(t, DM_MUL((float)p10[c], w10));
+          v[c] = DM_ADD(t, DM_MUL((float)p11[c], w11));
+        }
+        b = v[0]; g = v[1]; r = v[2];
+      }
+      uint16_t* o = out + ((size_t)y * S + x) * 3;
+      o[0] = dm_f2h(DM_DIV(r, 255.f));
+      o[1] = dm_f2h(DM_DIV(g, 255.f));
+      o[2] = dm_f2h(DM_DIV(b, 255.f));
+    }
+}
+
+/* One level of one image.  Writes conf-passing anchors in anchor order as 7-float records
+ * [x1 y1 x2 y2 score cls anchor] (anchor = abase + y*W + x).  Returns the count. */
+int oref_decode_level(const uint16_t* box, int bstride, const uint16_t* cls, int cstride, int H,
+                      int W, int img, int nc, int stride, float conf, int abase, float* out) {
+  OView bv = {box, H, W, bstride}, cv = {cls, H, W, cstride};
+  int n = 0;
+  for (int y = 0; y < H; y++)
+    for (int x = 0; x < W; x++) {
+      const uint16_t* cp = opix(&cv, img, y, x);
+      float best = -INFINITY;
+      int bc = 0;
+      for (int c = 0; c < nc; c++) {
+        float f = dm_h2f(cp[c]);
+        if (f > best) { best = f; bc = c; }
+      }
+      float score = dm_sigmoid(best);
+      if (!(score >= conf)) continue;
+      const uint16_t* bp = opix(&bv, img, y, x);
+      float d[4];
+      for (int s = 0; s < 4; s++) {
+        float l[16];
+        for (int i = 0; i < 16; i++) l[i] = dm_h2f(bp[s * 16 + i]);
+        d[s] = dm_dfl16(l);
+      }
+      float cx = DM_ADD((float)x, 0.5f), cy = DM_ADD((float)y, 0.5f), st = (float)stride;
+      float* o = out + (size_t)n * 7;
+      o[0] = DM_MUL(DM_SUB(cx, d[0]), st);
+      o[1] = DM_MUL(DM_SUB(cy, d[1]), st);
+      o[2] = DM_MUL(DM_ADD(cx, d[2]), st);
+      o[3] = DM_MUL(DM_ADD(cy, d[3]), st);
+      o[4] = score;
+      o[5] = (float)bc;
+      o[6] = (float)(abase + y * W + x);
+      n++;
+    }
+  return n;
+}
+
+static const float* g_sort_recs;
+static int cmp_score_desc(const void* a, const void* b) {
+  const float* ra = g_sort_recs + (size_t)(*(const int*)a) * 7;
+  const float* rb = g_sort_recs + (size_t)(*(const int*)b) * 7;
+  if (ra[4] != rb[4]) return ra[4] > rb[4] ? -1 : 1;
+  return ra[6] < rb[6] ? -1 : (ra[6] > rb[6] ? 1 : 0);
+}
+
+/* recs: n 7-float records from oref_decode_level (any order).  Writes up to max_out
+ * survivors as 7-float records (same layout) in output order; returns the count. */
+int oref_nms(const float* recs, int n, float thr, int max_out, float* out) {
+  int* order = (int*)malloc(sizeof(int) * (n > 0 ? n : 1));
+  unsigned char* dead = (unsigned char*)calloc(n > 0 ? n : 1, 1);
+  for (int i = 0; i < n; i++) order[i] = i;
+  g_sort_recs = recs;
+  qsort(order, n, sizeof(int), cmp_score_desc);
+  int m = 0;
+  for (int i = 0; i < n; i++) {
+    const float* a = recs + (size_t)order[i] * 7;
+    if (dead[order[i]]) continue;
+    if (m < max_out) memcpy(out + (size_t)m * 7, a, 7 * sizeof(float));
+    m++;
+    float aarea = dm_area(a[0], a[1], a[2], a[3]);
+    for (int j = i + 1; j < n; j++) {
+      const float* b = recs + (size_t)order[j] * 7;
+      if (dead[order[j]] || b[5] != a[5]) continue;
+      if (dm_iou_gt(a[0], a[1], a[2], a[3], aarea, b[0], b[1], b[2], b[3], thr)) dead[order[j]] = 1;
+    }
+  }
+  free(order);
+  free(dead);
+  return m < max_out ? m : max_out;
+}
+
+/* coef: nm fp16 coefficients of the survivor's anchor; proto view of image img;
+ * det: x1 y1 x2 y2 in letterbox pixels; out: Ph*Pw bytes. */
+void oref_mask(const uint16_t* coef, int nm, const uint16_t* proto, int pstride, int Ph, int Pw,
+               int img, const float* det, float rx, float ry, uint8_t* out) {
+  OView pv = {proto, Ph, Pw, pstride};
+  float co[256];
+  for (int c = 0; c < nm; c++) co[c] = dm_h2f(coef[c]);
+  float bx1 = DM_MUL(det[0], rx), by1 = DM_MUL(det[1], ry);
+  float bx2 = DM_MUL(det[2], rx), by2 = DM_MUL(det[3], ry);
+  for (int py = 0; py < Ph; py++)
+    for (int px = 0; px < Pw; px++) {
+      uint8_t m = 0;
+      if ((float)px >= bx1 && (float)px < bx2 && (float)py >= by1 && (float)py < by2) {
+        const uint16_t* pp = opix(&pv, img, py, px);
+        float acc = 0.f;
+        for (int c = 0; c < nm; c++) acc = DM_FMA(co[c], dm_h2f(pp[c]), acc);
+        m = acc > 0.f;
+      }
+      out[(size_t)py * Pw + px] = m;
+    }
+}
+
+/* exposed for the math tests */
+float oref_exp(float x) { return dm_exp(x); }
+float oref_sigmoid(float x) { return dm_sigmoid(x); }
+uint16_t oref_f2h(float x) { return dm_f2h(x); }
+float oref_h2f(uint16_t h) { return dm_h2f(h); }

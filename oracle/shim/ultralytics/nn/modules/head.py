@@ -1,0 +1,10 @@
+"""Shim: ultralytics.nn.modules.head names backed by the repository's module zoo."""
+from yolo11_cu_b200_nn import Detect, Segment  # noqa: F401
+
+
+class OBB(Detect):      # never instantiated here; only used in isinstance checks
+    pass
+
+
+class Classify:         # never instantiated here; only used in isinstance checks
+    pass

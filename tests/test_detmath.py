@@ -1,0 +1,37 @@
+"""Host tests of the shared deterministic math (csrc/detmath.h) through the C oracle build."""
+import numpy as np
+
+import graph_ref
+
+
+def test_exp_accuracy():
+    lib = graph_ref.oracle_postproc()
+    xs = np.concatenate([np.linspace(-87, 88, 20001, dtype=np.float32),
+                         np.random.default_rng(0).uniform(-20, 20, 20000).astype(np.float32),
+                         np.float32([0.0, -0.0, 1e-30, -1e-30, 0.5, -0.5])])
+    got = np.array([lib.oref_exp(float(x)) for x in xs], np.float32)
+    want = np.exp(xs.astype(np.float64))
+    ulp = np.spacing(want.astype(np.float32)).astype(np.float64)
+    err = np.abs(got.astype(np.float64) - want) / ulp
+    assert err.max() <= 2.0, err.max()
+    assert lib.oref_exp(-100.0) == 0.0
+    assert np.isinf(lib.oref_exp(100.0))
+
+
+def test_sigmoid_monotone_and_bounds():
+    lib = graph_ref.oracle_postproc()
+    xs = np.linspace(-30, 30, 4001, dtype=np.float32)
+    s = np.array([lib.oref_sigmoid(float(x)) for x in xs])
+    assert np.all(np.diff(s) >= 0) and s.min() >= 0 and s.max() <= 1
+    ref = 1 / (1 + np.exp(-xs.astype(np.float64)))
+    assert np.abs(s - ref).max() < 1e-6
+
+
+def test_f2h_matches_numpy_rne():
+    lib = graph_ref.oracle_postproc()
+    rng = np.random.default_rng(1)
+    xs = np.concatenate([rng.standard_normal(20000).astype(np.float32) * 10 ** rng.uniform(-8, 5, 20000).astype(np.float32),
+                         np.float32([0, -0.0, 65504, 65519.9, 65520, 1e-8, 6e-8, 2.98e-8, 5.96e-8, np.inf, -np.inf])])
+    got = np.array([lib.oref_f2h(float(x)) for x in xs], np.uint16)
+    want = xs.astype(np.float16).view(np.uint16)
+    assert np.array_equal(got, want)

@@ -1,0 +1,206 @@
+"""GPU parity of the yk_* kernels (called through the C ABI) against plain torch fp32.
+
+Tolerance (north_star: per-op deviation <= 1.5 % vs fp32): max|gpu - ref| / max|ref| < 1.5e-2
+with fp16 inputs shared by both sides; the fp16 output rounding alone is ~5e-4.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+TOL = 1.5e-2
+
+
+def rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).abs().max() / (b.abs().max() + 1e-6)).item()
+
+
+def nhwc(t):
+    return t.permute(0, 2, 3, 1)
+
+
+def vw(rt, buf, coff, Cv):
+    B, H, W, Ct = buf.shape
+    return rt.view(buf.data_ptr(), B, H, W, Ct, coff, Cv)
+
+
+def run_conv(lib, rt, x, w, b, k, s, p, act, groups=1, res=None, tile=0, xc=(0, None), yc=(0, 0)):
+    """x: NHWC fp16 buffer (view = channels xc[0]:xc[0]+Cin); output written into a fresh
+    buffer with yc = (coff, extra channels) to exercise channel-slice stores."""
+    B, H, W, _ = x.shape
+    Cout = w.shape[0]
+    Cin = w.shape[1] * groups
+    Ho, Wo = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
+    ybuf = torch.full((B, Ho, Wo, yc[0] + Cout + yc[1]), 7.0, dtype=torch.half, device=x.device)
+    wt = w.permute(0, 2, 3, 1).contiguous().half()            # OHWI
+    bt = b.float().contiguous()
+    prm = rt.YkConv(wt.data_ptr(), bt.data_ptr(), k, s, p, groups, act, Cin, Cout, tile, 0)
+    xv = vw(rt, x, xc[0], Cin)
+    yv = vw(rt, ybuf, yc[0], Cout)
+    rv = vw(rt, res, 0, Cout) if res is not None else None
+    r = lib.yk_conv(C.byref(xv), C.byref(yv), C.byref(rv) if rv is not None else None,
+                    C.byref(prm), torch.cuda.current_stream().cuda_stream)
+    assert r == 0, (r, lib.yk_last_cuda_error())
+    torch.cuda.synchronize()
+    assert lib.yk_fetch_device_error() == 0
+    xin = x[..., xc[0]:xc[0] + Cin].permute(0, 3, 1, 2).float()
+    ref = F.conv2d(xin, wt.permute(0, 3, 1, 2).float(), bt, stride=s, padding=p, groups=groups)
+    if act:
+        ref = F.silu(ref)
+    ref = nhwc(ref)
+    if res is not None:
+        ref = ref + res.float()
+    out = ybuf[..., yc[0]:yc[0] + Cout]
+    if yc[0]:
+        assert torch.all(ybuf[..., :yc[0]] == 7.0)
+    if yc[1]:
+        assert torch.all(ybuf[..., yc[0] + Cout:] == 7.0)
+    return out, ref
+
+
+CONV_CASES = [
+    # B, H, W, Cin, Cout, k, s, p
+    (1, 20, 20, 64, 64, 1, 1, 0),
+    (2, 40, 40, 32, 48, 3, 1, 1),
+    (1, 33, 17, 8, 16, 3, 1, 1),       # thin channels, ragged M
+    (1, 32, 32, 16, 8, 3, 1, 1),       # Cout 8 (padded N tile)
+    (3, 40, 40, 64, 128, 3, 2, 1),     # stride 2
+    (1, 20, 20, 256, 256, 1, 1, 0),
+    (2, 10, 10, 512, 512, 3, 1, 1),    # deep K (4608)
+    (1, 80, 80, 96, 200, 1, 1, 0),     # Cout not a tile multiple
+    (1, 5, 7, 24, 40, 3, 2, 1),
+    (1, 1, 1, 64, 80, 1, 1, 0),        # M = 1 (linear)
+]
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+@pytest.mark.parametrize("tile", [0, 64, 128, 256])
+def test_conv_tc(lib, cuda, case, tile):
+    from yolo11_cu_b200 import runtime as rt
+    B, H, W, Cin, Cout, k, s, p = case
+    g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000)
+    x = torch.randn(B, H, W, Cin + 16, generator=g).half().to(cuda)
+    w = (torch.randn(Cout, Cin, k, k, generator=g) / (Cin * k * k) ** 0.5)
+    b = torch.randn(Cout, generator=g) * 0.1
+    out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), k, s, p, act=1, tile=tile,
+                        xc=(8, None), yc=(8, 8))
+    assert rel(out, ref) < TOL
+
+
+def test_conv_tc_residual_and_inplace(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(2, 24, 24, 64, generator=g).half().to(cuda)
+    w = (torch.randn(64, 64, 3, 3, generator=g) / 24).to(cuda)
+    b = (torch.randn(64, generator=g) * 0.1).to(cuda)
+    res = torch.randn(2, 24, 24, 64, generator=g).half().to(cuda)
+    out, ref = run_conv(lib, rt, x, w, b, 3, 1, 1, act=0, res=res)
+    assert rel(out, ref) < TOL
+
+
+def test_conv_first_layer(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(4)
+    x = torch.rand(2, 64, 64, 3, generator=g).half().to(cuda)
+    w = (torch.randn(16, 3, 3, 3, generator=g) / 5).to(cuda)
+    b = (torch.randn(16, generator=g) * 0.1).to(cuda)
+    out, ref = run_conv(lib, rt, x, w, b, 3, 2, 1, act=1)
+    assert rel(out, ref) < TOL
+
+
+@pytest.mark.parametrize("s", [1, 2])
+def test_dwconv(lib, cuda, s):
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(5)
+    C_ = 64
+    x = torch.randn(2, 20, 20, C_, generator=g).half().to(cuda)
+    w = (torch.randn(C_, 1, 3, 3, generator=g) / 3).to(cuda)
+    b = (torch.randn(C_, generator=g) * 0.1).to(cuda)
+    res = None
+    if s == 1:
+        res = torch.randn(2, 20, 20, C_, generator=g).half().to(cuda)
+    out, ref = run_conv(lib, rt, x, w, b, 3, s, 1, act=1, groups=C_, res=res)
+    assert rel(out, ref) < TOL
+
+
+def _v(rt, t, coff=0, Cv=None):
+    return rt.tview(t, coff, Cv)
+
+
+def test_maxpool_chain(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    x = torch.randn(2, 20, 20, 32, device=cuda).half()
+    ys = [torch.empty_like(x) for _ in range(3)]
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.yk_maxpool5x3(C.byref(_v(rt, x)), *[C.byref(_v(rt, y)) for y in ys], st) == 0
+    y1 = torch.empty_like(x)
+    assert lib.yk_maxpool5(C.byref(_v(rt, x)), C.byref(_v(rt, y1)), st) == 0
+    torch.cuda.synchronize()
+    t = x.permute(0, 3, 1, 2).float()
+    refs = []
+    for _ in range(3):
+        t = F.max_pool2d(t, 5, 1, 2)
+        refs.append(nhwc(t).half())
+    assert torch.equal(y1, refs[0])
+    for y, r in zip(ys, refs):
+        assert torch.equal(y, r)
+
+
+def test_upsample_ps2_copy_add(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    st = torch.cuda.current_stream().cuda_stream
+    x = torch.randn(2, 8, 10, 48, device=cuda).half()
+    up = torch.zeros(2, 16, 20, 64, device=cuda).half()
+    assert lib.yk_upsample2(C.byref(_v(rt, x, 8, 32)), C.byref(_v(rt, up, 16, 32)), st) == 0
+    ps = torch.zeros(2, 16, 20, 8, device=cuda).half()
+    assert lib.yk_ps2(C.byref(_v(rt, x, 8, 32)), C.byref(_v(rt, ps)), st) == 0
+    cp = torch.zeros(2, 8, 10, 24, device=cuda).half()
+    assert lib.yk_copyc(C.byref(_v(rt, x, 0, 24)), C.byref(_v(rt, cp)), st) == 0
+    cps = torch.zeros(2, 8, 10, 5, device=cuda).half()
+    assert lib.yk_copyc(C.byref(_v(rt, x, 3, 5)), C.byref(_v(rt, cps)), st) == 0
+    ad = torch.zeros(2, 8, 10, 16, device=cuda).half()
+    assert lib.yk_add(C.byref(_v(rt, x, 0, 16)), C.byref(_v(rt, x, 16, 16)), C.byref(_v(rt, ad)), st) == 0
+    torch.cuda.synchronize()
+    xs = x[..., 8:40]
+    assert torch.equal(up[..., 16:48], xs.repeat_interleave(2, 1).repeat_interleave(2, 2))
+    assert torch.all(up[..., :16] == 0) and torch.all(up[..., 48:] == 0)
+    ref = torch.zeros_like(ps)
+    for di in range(2):
+        for dj in range(2):
+            q = 2 * di + dj
+            ref[:, di::2, dj::2] = xs[..., q * 8:(q + 1) * 8]
+    assert torch.equal(ps, ref)
+    assert torch.equal(cp, x[..., :24]) and torch.equal(cps, x[..., 3:8])
+    assert torch.equal(ad, (x[..., :16].float() + x[..., 16:32].float()).half())
+
+
+@pytest.mark.parametrize("hw,heads", [((20, 20), 2), ((20, 20), 4), ((32, 32), 6), ((7, 7), 2)])
+def test_attention(lib, cuda, hw, heads):
+    from yolo11_cu_b200 import runtime as rt
+    H, W = hw
+    kd, hd = 32, 64
+    qkv = torch.randn(3, H, W, heads * (2 * kd + hd) + 8, device=cuda).half()
+    y = torch.zeros(3, H, W, heads * hd, device=cuda).half()
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.yk_attn(C.byref(_v(rt, qkv, 8, heads * (2 * kd + hd))), C.byref(_v(rt, y)), heads, kd, hd, st) == 0
+    torch.cuda.synchronize()
+    N = H * W
+    t = qkv[..., 8:].float().reshape(3, N, heads, 2 * kd + hd).permute(0, 2, 3, 1)
+    q, k, v = t.split([kd, kd, hd], dim=2)
+    att = ((q.transpose(-2, -1) @ k) * kd ** -0.5).softmax(-1)
+    ref = (v @ att.transpose(-2, -1)).reshape(3, heads * hd, N).permute(0, 2, 1).reshape(3, H, W, heads * hd)
+    assert rel(y, ref) < TOL
+
+
+def test_bad_arguments_rejected(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    st = torch.cuda.current_stream().cuda_stream
+    x = torch.randn(1, 8, 8, 16, device=cuda).half()
+    y = torch.zeros(1, 8, 8, 16, device=cuda).half()
+    bad = rt.tview(x, 4, 16)       # coff + C > stride
+    assert lib.yk_copyc(C.byref(bad), C.byref(rt.tview(y)), st) != 0
+    assert lib.yk_attn(C.byref(rt.tview(x)), C.byref(rt.tview(y)), 1, 4, 8, st) != 0

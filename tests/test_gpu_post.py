@@ -1,0 +1,138 @@
+"""GPU pre/post-processing vs the C oracle (oracle/postproc_ref.c): bit-exact.
+
+Given identical fp16 head tensors, the engine's decode + NMS must return the same survivors
+(same anchor indices, same order, identical box / score bits) as the oracle's restatement of
+the reference's k_decode / k_nms (engine/engine.cu:848-906, 1051-1123); letterbox and masks
+must match byte for byte.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import graph_ref
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("hw,S", [((1080, 810), 640), ((720, 1280), 640), ((1080, 1920), 1024),
+                                  ((37, 53), 64), ((640, 640), 640)])
+def test_letterbox_bitexact(lib, cuda, pkg, hw, S):
+    from yolo11_cu_b200 import frames, runtime as rt
+    bgr = frames.synthetic_bgr(*hw, seed=3)
+    d = torch.from_numpy(bgr).to(cuda)
+    out = torch.zeros(2, S, S, 3, dtype=torch.half, device=cuda)
+    sc, top, left = C.c_float(), C.c_int(), C.c_int()
+    r = lib.yk_letterbox(C.c_void_p(d.data_ptr()), hw[0], hw[1], C.byref(rt.tview(out)), 1,
+                         C.byref(sc), C.byref(top), C.byref(left),
+                         torch.cuda.current_stream().cuda_stream)
+    assert r == 0
+    torch.cuda.synchronize()
+    ref = graph_ref.letterbox(bgr, S)
+    assert np.array_equal(out[1].cpu().numpy().view(np.uint16), ref.view(np.uint16))
+    assert torch.all(out[0] == 0)
+
+
+def _levels(S, B, g, cls_bias, box_scale=1.0):
+    sizes = [(S // 8, 8), (S // 16, 16), (S // 32, 32)]
+    box = [(torch.randn(B, n, n, 64, generator=g) * box_scale).half() for n, _ in sizes]
+    cls = [(torch.randn(B, n, n, 80, generator=g) + cls_bias).half() for n, _ in sizes]
+    return sizes, box, cls
+
+
+def _run_gpu_post(lib, rt, cuda, sizes, box, cls, B, iou, max_out, coef=None, proto=None, S=None):
+    A = sum(n * n for n, _ in sizes)
+    dev = [(b.to(cuda), c.to(cuda)) for b, c in zip(box, cls)]
+    lv = (rt.YkLevel * 3)()
+    keep = []
+    for i, ((n, st), (b, c)) in enumerate(zip(sizes, dev)):
+        lv[i].box = rt.tview(b)
+        lv[i].cls = rt.tview(c)
+        if coef is not None:
+            cf = coef[i].to(cuda)
+            keep.append(cf)
+            lv[i].coef = rt.tview(cf)
+        lv[i].stride = st
+    wsb = lib.yk_post_workspace_bytes(B, A)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device=cuda)
+    od = torch.zeros(B, max_out, 6, device=cuda)
+    oi = torch.zeros(B, max_out, dtype=torch.int32, device=cuda)
+    oc = torch.zeros(B, dtype=torch.int32, device=cuda)
+    rc = torch.zeros(B, dtype=torch.int32, device=cuda)
+    post = rt.YkPost(ws.data_ptr(), wsb, od.data_ptr(), oi.data_ptr(), oc.data_ptr(), rc.data_ptr())
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.yk_decode(lv, 3, B, 80, 0.25, C.byref(post), st) == 0
+    assert lib.yk_nms(B, A, iou, max_out, C.byref(post), st) == 0
+    masks = None
+    if coef is not None:
+        pr = proto.to(cuda)
+        masks = torch.full((B, max_out, pr.shape[1], pr.shape[2]), 9, dtype=torch.uint8, device=cuda)
+        assert lib.yk_masks(lv, 3, C.byref(rt.tview(pr)), S, S, max_out, C.byref(post),
+                            C.c_void_p(masks.data_ptr()), st) == 0
+    torch.cuda.synchronize()
+    assert lib.yk_fetch_device_error() == 0
+    return od.cpu().numpy(), oi.cpu().numpy(), oc.cpu().numpy(), rc.cpu().numpy(), \
+        (masks.cpu().numpy() if masks is not None else None)
+
+
+def _oracle(sizes, box, cls, img, iou, max_out):
+    lv = [(b[img].numpy(), c[img].numpy(), st) for (n, st), b, c in zip(sizes, box, cls)]
+    recs = graph_ref.decode(lv, 80, 0.25)
+    return recs, graph_ref.nms(recs, iou, max_out)
+
+
+@pytest.mark.parametrize("S,B,cls_bias,iou,max_out", [
+    (640, 2, -4.0, 0.45, 300),     # a few hundred candidates
+    (640, 1, -4.0, 0.7, 300),
+    (320, 3, -20.0, 0.45, 300),    # no candidates
+    (320, 1, 6.0, 0.45, 300),      # every anchor is a candidate
+    (640, 1, 6.0, 0.45, 50),       # max_out truncation
+    (1024, 1, 6.0, 0.45, 300),     # 21504 candidates: global-memory sort path
+])
+def test_decode_nms_bitexact(lib, cuda, S, B, cls_bias, iou, max_out):
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(S + B)
+    sizes, box, cls = _levels(S, B, g, cls_bias)
+    od, oi, oc, rc, _ = _run_gpu_post(lib, rt, cuda, sizes, box, cls, B, iou, max_out)
+    for img in range(B):
+        recs, keep = _oracle(sizes, box, cls, img, iou, max_out)
+        assert rc[img] == len(recs)
+        assert oc[img] == len(keep)
+        n = len(keep)
+        assert np.array_equal(oi[img, :n], keep[:, 6].astype(np.int32))
+        assert np.array_equal(od[img, :n].view(np.uint32), keep[:, :6].view(np.uint32))
+
+
+def test_nms_ties_deterministic(lib, cuda):
+    """Identical logits everywhere: every score ties; order must be by anchor index."""
+    from yolo11_cu_b200 import runtime as rt
+    S, B = 320, 2
+    sizes = [(S // 8, 8), (S // 16, 16), (S // 32, 32)]
+    box = [torch.zeros(B, n, n, 64).half() for n, _ in sizes]
+    cls = [torch.full((B, n, n, 80), 1.0).half() for n, _ in sizes]
+    od, oi, oc, rc, _ = _run_gpu_post(lib, rt, cuda, sizes, box, cls, B, 0.45, 300)
+    recs, keep = _oracle(sizes, box, cls, 0, 0.45, 300)
+    assert oc[0] == oc[1] == len(keep)
+    assert np.array_equal(oi[0, :oc[0]], keep[:, 6].astype(np.int32))
+    assert np.array_equal(oi[0], oi[1])
+
+
+def test_masks_bitexact(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    S, B = 320, 2
+    g = torch.Generator().manual_seed(9)
+    sizes, box, cls = _levels(S, B, g, -3.0)
+    coef = [torch.randn(B, n, n, 32, generator=g).half() for n, _ in sizes]
+    proto = torch.randn(B, S // 4, S // 4, 32, generator=g).half()
+    od, oi, oc, rc, masks = _run_gpu_post(lib, rt, cuda, sizes, box, cls, B, 0.45, 300, coef, proto, S)
+    Ws = [n for n, _ in sizes]
+    bases = np.cumsum([0] + [n * n for n in Ws])
+    for img in range(B):
+        assert oc[img] > 0
+        for d in range(oc[img]):
+            a = oi[img, d]
+            li = int(np.searchsorted(bases, a, side="right") - 1)
+            y, x = divmod(a - bases[li], Ws[li])
+            ref = graph_ref.mask(coef[li][img, y, x].numpy(), proto[img].numpy(), od[img, d], S)
+            assert np.array_equal(masks[img, d], ref), (img, d)

@@ -1,0 +1,337 @@
+// Bandwidth-bound kernels: first conv (Cin = 3), depthwise conv, SPPF max pools, nearest
+// upsample, pixel shuffle, channel-slice copy and add, plus the yk_conv dispatcher.
+// All activation accesses are 16-byte vectors of 8 channels where the view allows it
+// (channel counts, offsets and strides are multiples of 8 in every exported graph).
+#include <atomic>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace yk {
+
+static std::atomic<long long> g_launches{0};
+static thread_local char g_cuda_err[256];
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return YK_OK;
+  snprintf(g_cuda_err, sizeof g_cuda_err, "%s: %s", what, cudaGetErrorString(e));
+  return YK_ECUDA;
+}
+
+int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, cudaStream_t st);
+
+static inline unsigned nblk(long long n, int tb) { return (unsigned)((n + tb - 1) / tb); }
+
+// ---------------- first conv: Cin <= 4, dense, direct FMA ----------------
+// Thread = one output pixel x 8 output channels; the block's 8-channel weight slice and bias
+// live in shared memory.  Replaces k_conv0 (engine/engine.cu:487-532).
+__global__ void conv_small_cin_kernel(DView x, DView y, const __half* __restrict__ w,
+                                      const float* __restrict__ b, int Cin, int k, int s, int p,
+                                      int act, long long npix) {
+  extern __shared__ float wsm[];   // [8][k*k*Cin] then bias[8]
+  const int KK = k * k * Cin;
+  const int co0 = blockIdx.y * 8;
+  for (int i = threadIdx.x; i < 8 * KK; i += blockDim.x) wsm[i] = __half2float(w[(size_t)co0 * KK + i]);
+  if (threadIdx.x < 8) wsm[8 * KK + threadIdx.x] = b[co0 + threadIdx.x];
+  __syncthreads();
+  long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= npix) return;
+  const int HW = y.H * y.W;
+  const int img = (int)(pix / HW), rem = (int)(pix - (long long)img * HW);
+  const int oy = rem / y.W, ox = rem - oy * y.W;
+  float acc[8];
+#pragma unroll
+  for (int c = 0; c < 8; c++) acc[c] = wsm[8 * KK + c];
+  for (int ky = 0; ky < k; ky++) {
+    const int iy = oy * s - p + ky;
+    if (iy < 0 || iy >= x.H) continue;
+    for (int kx = 0; kx < k; kx++) {
+      const int ix = ox * s - p + kx;
+      if (ix < 0 || ix >= x.W) continue;
+      const __half* xp = x.p + x.pix(img, iy, ix);
+      for (int ci = 0; ci < Cin; ci++) {
+        const float v = __half2float(xp[ci]);
+        const int kidx = (ky * k + kx) * Cin + ci;
+#pragma unroll
+        for (int c = 0; c < 8; c++) acc[c] = fmaf(v, wsm[c * KK + kidx], acc[c]);
+      }
+    }
+  }
+  uint4 o;
+  __half2* oh = (__half2*)&o;
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    float a0 = acc[2 * q], a1 = acc[2 * q + 1];
+    if (act == 1) { a0 = silu(a0); a1 = silu(a1); }
+    oh[q] = __floats2half2_rn(a0, a1);
+  }
+  *(uint4*)(y.p + (size_t)pix * y.stride + co0) = o;
+}
+
+// ---------------- depthwise conv ----------------
+// Thread = one output pixel x 8 channels, 16-byte loads; weights OHWI [C][k][k][1].
+// Replaces k_dwconv8 (engine/engine.cu:535-580), including its fused residual.
+__global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restrict__ w,
+                              const float* __restrict__ b, int k, int s, int p, int act,
+                              long long total) {
+  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int cg = y.C >> 3;
+  if (idx >= total) return;
+  const int g = (int)(idx % cg);
+  const long long pix = idx / cg;
+  const int c = g << 3;
+  const int HW = y.H * y.W;
+  const int img = (int)(pix / HW), rem = (int)(pix - (long long)img * HW);
+  const int oy = rem / y.W, ox = rem - oy * y.W;
+  const int KK = k * k;
+  float acc[8];
+  {
+    const float4 b0 = *(const float4*)(b + c), b1 = *(const float4*)(b + c + 4);
+    acc[0] = b0.x; acc[1] = b0.y; acc[2] = b0.z; acc[3] = b0.w;
+    acc[4] = b1.x; acc[5] = b1.y; acc[6] = b1.z; acc[7] = b1.w;
+  }
+  for (int ky = 0; ky < k; ky++) {
+    const int iy = oy * s - p + ky;
+    if (iy < 0 || iy >= x.H) continue;
+    for (int kx = 0; kx < k; kx++) {
+      const int ix = ox * s - p + kx;
+      if (ix < 0 || ix >= x.W) continue;
+      const uint4 xv = *(const uint4*)(x.p + x.pix(img, iy, ix) + c);
+      const __half* xh = (const __half*)&xv;
+      const int t = ky * k + kx;
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+        acc[q] = fmaf(__half2float(xh[q]), __half2float(w[(size_t)(c + q) * KK + t]), acc[q]);
+    }
+  }
+  float rv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (r.p) {
+    const uint4 v = *(const uint4*)(r.p + (size_t)pix * r.stride + c);
+    const __half* h = (const __half*)&v;
+#pragma unroll
+    for (int q = 0; q < 8; q++) rv[q] = __half2float(h[q]);
+  }
+  uint4 o;
+  __half2* oh = (__half2*)&o;
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    float a0 = acc[2 * q], a1 = acc[2 * q + 1];
+    if (act == 1) { a0 = silu(a0); a1 = silu(a1); }
+    oh[q] = __floats2half2_rn(a0 + rv[2 * q], a1 + rv[2 * q + 1]);
+  }
+  *(uint4*)(y.p + (size_t)pix * y.stride + c) = o;
+}
+
+// ---------------- SPPF max pools ----------------
+__device__ __forceinline__ void hmax8(uint4& m, const uint4 v) {
+  __half2* a = (__half2*)&m;
+  const __half2* b = (const __half2*)&v;
+#pragma unroll
+  for (int i = 0; i < 4; i++) a[i] = __hmax2(a[i], b[i]);
+}
+
+// nr outputs: output j (j < nr) is the max over the (5+4j) x (5+4j) window clipped to the
+// image, i.e. j+1 chained 5x5/s1/p2 pools (max pooling composes: pool5(pool5(x)) = pool9(x)
+// with -inf padding).  Replaces k_maxpool5 (engine/engine.cu:672-695).
+__global__ void maxpool_kernel(DView x, DView y1, DView y2, DView y3, int nr, long long total) {
+  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int cg = x.C >> 3;
+  if (idx >= total) return;
+  const int g = (int)(idx % cg);
+  const long long pix = idx / cg;
+  const int c = g << 3;
+  const int HW = x.H * x.W;
+  const int img = (int)(pix / HW), rem = (int)(pix - (long long)img * HW);
+  const int y0 = rem / x.W, x0 = rem - y0 * x.W;
+  const uint4 ninf = make_uint4(0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u);
+  uint4 m1 = ninf, m2 = ninf, m3 = ninf;
+  const int R = 2 + 2 * (nr - 1);
+  for (int dy = -R; dy <= R; dy++) {
+    const int iy = y0 + dy;
+    if (iy < 0 || iy >= x.H) continue;
+    const int ady = dy < 0 ? -dy : dy;
+    for (int dx = -R; dx <= R; dx++) {
+      const int ix = x0 + dx;
+      if (ix < 0 || ix >= x.W) continue;
+      const int adx = dx < 0 ? -dx : dx;
+      const int d = ady > adx ? ady : adx;
+      const uint4 v = *(const uint4*)(x.p + x.pix(img, iy, ix) + c);
+      if (d <= 2) hmax8(m1, v);
+      if (d <= 4) hmax8(m2, v);
+      hmax8(m3, v);
+    }
+  }
+  *(uint4*)(y1.p + (size_t)pix * y1.stride + c) = m1;
+  if (nr > 1) *(uint4*)(y2.p + (size_t)pix * y2.stride + c) = m2;
+  if (nr > 2) *(uint4*)(y3.p + (size_t)pix * y3.stride + c) = m3;
+}
+
+// ---------------- data movement ----------------
+// mode 0: nearest 2x upsample (engine/engine.cu:697-708); mode 1: pixel shuffle r=2 from
+// quadrant blocks (engine/engine.cu:713-725); mode 2: channel-slice copy (727-732).
+// Thread = one output pixel x 8 channels.
+__global__ void move8_kernel(DView x, DView y, int mode, long long total) {
+  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int cg = y.C >> 3;
+  if (idx >= total) return;
+  const int g = (int)(idx % cg);
+  const long long pix = idx / cg;
+  const int c = g << 3;
+  const int HW = y.H * y.W;
+  const int img = (int)(pix / HW), rem = (int)(pix - (long long)img * HW);
+  const int oy = rem / y.W, ox = rem - oy * y.W;
+  const __half* src;
+  if (mode == 0) src = x.p + x.pix(img, oy >> 1, ox >> 1) + c;
+  else if (mode == 1) src = x.p + x.pix(img, oy >> 1, ox >> 1) + (((oy & 1) << 1) | (ox & 1)) * y.C + c;
+  else src = x.p + x.pix(img, oy, ox) + c;
+  *(uint4*)(y.p + (size_t)pix * y.stride + c) = *(const uint4*)src;
+}
+
+__global__ void copy_scalar_kernel(DView x, DView y, long long total) {
+  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int c = (int)(idx % y.C);
+  const long long pix = idx / y.C;
+  y.p[(size_t)pix * y.stride + c] = x.p[(size_t)pix * x.stride + c];
+}
+
+__global__ void add8_kernel(DView a, DView b, DView y, long long total) {
+  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int cg = y.C >> 3;
+  if (idx >= total) return;
+  const int c = (int)(idx % cg) << 3;
+  const long long pix = idx / cg;
+  const uint4 va = *(const uint4*)(a.p + (size_t)pix * a.stride + c);
+  const uint4 vb = *(const uint4*)(b.p + (size_t)pix * b.stride + c);
+  const __half2* ha = (const __half2*)&va;
+  const __half2* hb = (const __half2*)&vb;
+  uint4 o;
+  __half2* ho = (__half2*)&o;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    float2 fa = __half22float2(ha[i]), fb = __half22float2(hb[i]);
+    ho[i] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+  }
+  *(uint4*)(y.p + (size_t)pix * y.stride + c) = o;
+}
+
+static bool same_shape(const YkView* a, const YkView* b) {
+  return a->batch == b->batch && a->H == b->H && a->W == b->W && a->C == b->C;
+}
+
+}  // namespace yk
+
+using namespace yk;
+
+extern "C" {
+
+long long yk_launch_count(void) { return g_launches.load(); }
+const char* yk_last_cuda_error(void) { return g_cuda_err; }
+
+int yk_fetch_device_error(void) {
+  int v = 0, z = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof v) != cudaSuccess) return YK_ECUDA;
+  if (v) cudaMemcpyToSymbol(g_device_error, &z, sizeof z);
+  return v;
+}
+
+int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p,
+            yk_stream_t st_) {
+  cudaStream_t st = (cudaStream_t)st_;
+  if (!p || !view_ok(x) || !view_ok(y) || !p->weight || !p->bias) return YK_EINVAL;
+  if (x->batch != y->batch || x->C != p->Cin || y->C != p->Cout || p->k < 1 || p->s < 1) return YK_EINVAL;
+  const int Ho = (x->H + 2 * p->p - p->k) / p->s + 1, Wo = (x->W + 2 * p->p - p->k) / p->s + 1;
+  if (Ho != y->H || Wo != y->W) return YK_EINVAL;
+  if (res && (!view_vec8(res) || !same_shape(res, y))) return YK_EINVAL;
+  if (!view_vec8(y) || ((uintptr_t)p->bias & 15) || ((uintptr_t)p->weight & 15)) return YK_EINVAL;
+  const long long npix = (long long)y->batch * y->H * y->W;
+  if (p->groups == 1 && p->Cin % 8 == 0) {
+    if (!view_vec8(x)) return YK_EINVAL;
+    return conv_tc(x, y, res, p, st);
+  }
+  if (p->groups == 1 && p->Cin <= 4) {
+    if (res || p->Cout % 8) return YK_EUNSUP;
+    const int KK = p->k * p->k * p->Cin;
+    dim3 grid(nblk(npix, 256), p->Cout / 8);
+    conv_small_cin_kernel<<<grid, 256, (8 * KK + 8) * sizeof(float), st>>>(
+        dview(*x), dview(*y), (const __half*)p->weight, p->bias, p->Cin, p->k, p->s, p->p,
+        p->act, npix);
+    note_launch();
+    return check_launch("conv_small_cin");
+  }
+  if (p->groups == p->Cin && p->Cin == p->Cout && p->Cin % 8 == 0) {
+    if (!view_vec8(x)) return YK_EINVAL;
+    DView r = res ? dview(*res) : DView{nullptr, 0, 0, 0, 0};
+    const long long total = npix * (p->Cout / 8);
+    dwconv_kernel<<<nblk(total, 256), 256, 0, st>>>(dview(*x), dview(*y), r,
+                                                    (const __half*)p->weight, p->bias, p->k,
+                                                    p->s, p->p, p->act, total);
+    note_launch();
+    return check_launch("dwconv");
+  }
+  return YK_EUNSUP;
+}
+
+int yk_maxpool5(const YkView* x, const YkView* y, yk_stream_t st) {
+  if (!view_vec8(x) || !view_vec8(y) || !same_shape(x, y)) return YK_EINVAL;
+  const long long total = (long long)x->batch * x->H * x->W * (x->C / 8);
+  DView Y = dview(*y);
+  maxpool_kernel<<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), Y, Y, Y, 1, total);
+  note_launch();
+  return check_launch("maxpool5");
+}
+
+int yk_maxpool5x3(const YkView* x, const YkView* y1, const YkView* y2, const YkView* y3,
+                  yk_stream_t st) {
+  if (!view_vec8(x) || !view_vec8(y1) || !view_vec8(y2) || !view_vec8(y3) ||
+      !same_shape(x, y1) || !same_shape(x, y2) || !same_shape(x, y3))
+    return YK_EINVAL;
+  const long long total = (long long)x->batch * x->H * x->W * (x->C / 8);
+  maxpool_kernel<<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y1),
+                                                                 dview(*y2), dview(*y3), 3, total);
+  note_launch();
+  return check_launch("maxpool5x3");
+}
+
+static int move8(const YkView* x, const YkView* y, int mode, yk_stream_t st) {
+  const long long total = (long long)y->batch * y->H * y->W * (y->C / 8);
+  move8_kernel<<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), mode, total);
+  note_launch();
+  return check_launch("move8");
+}
+
+int yk_upsample2(const YkView* x, const YkView* y, yk_stream_t st) {
+  if (!view_vec8(x) || !view_vec8(y) || x->batch != y->batch || x->C != y->C ||
+      y->H != 2 * x->H || y->W != 2 * x->W)
+    return YK_EINVAL;
+  return move8(x, y, 0, st);
+}
+
+int yk_ps2(const YkView* x, const YkView* y, yk_stream_t st) {
+  if (!view_vec8(x) || !view_vec8(y) || x->batch != y->batch || x->C != 4 * y->C ||
+      y->H != 2 * x->H || y->W != 2 * x->W)
+    return YK_EINVAL;
+  return move8(x, y, 1, st);
+}
+
+int yk_copyc(const YkView* x, const YkView* y, yk_stream_t st) {
+  if (!view_ok(x) || !view_ok(y) || !same_shape(x, y)) return YK_EINVAL;
+  if (view_vec8(x) && view_vec8(y)) return move8(x, y, 2, st);
+  const long long total = (long long)y->batch * y->H * y->W * y->C;
+  copy_scalar_kernel<<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), total);
+  note_launch();
+  return check_launch("copyc");
+}
+
+int yk_add(const YkView* a, const YkView* b, const YkView* y, yk_stream_t st) {
+  if (!view_vec8(a) || !view_vec8(b) || !view_vec8(y) || !same_shape(a, b) || !same_shape(a, y))
+    return YK_EINVAL;
+  const long long total = (long long)y->batch * y->H * y->W * (y->C / 8);
+  add8_kernel<<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*a), dview(*b), dview(*y), total);
+  note_launch();
+  return check_launch("add");
+}
+
+}  // extern "C"

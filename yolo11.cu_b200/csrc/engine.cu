@@ -1,0 +1,793 @@
+// Engine runtime: model-directory loader, op planner (residual / pool-chain fusion),
+// executor over the yk_* kernel ABI, per-batch CUDA graphs, and the yolo.h C ABI.
+//
+// Reference counterparts: loadGraph (engine/engine.cu:88-248), runOp (1261-1453),
+// forward (1455-1481), fuseAdds (1484-1501), autotune (1504-1533), the yolo_* API
+// (1653-1794).  Differences: every failure is an error return (never exit), device memory
+// is owned per handle and released by yolo_destroy, NMS output is exact (no 1024 cap),
+// and graphs are captured per batch size on first use.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/yk.h"
+#include "../../include/yolo.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+struct Error : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+#define CKE(x)                                                                          \
+  do {                                                                                  \
+    cudaError_t e_ = (x);                                                               \
+    if (e_ != cudaSuccess)                                                              \
+      throw Error(std::string(#x) + ": " + cudaGetErrorString(e_));                     \
+  } while (0)
+#define CKY(x)                                                                          \
+  do {                                                                                  \
+    int r_ = (x);                                                                       \
+    if (r_ != YK_OK)                                                                    \
+      throw Error(std::string(#x) + " failed (" + std::to_string(r_) + ") " +          \
+                  yk_last_cuda_error());                                                \
+  } while (0)
+
+enum Kind { CONV, ADD, MAXPOOL5, UPSAMPLE2, COPYC, ATTN, DECODE, GAP, SOFTMAX, DECODEOBB, PS2,
+            DECODESEG, MASKS, POOLX3 };
+const char* kKindNames[] = {"CONV", "ADD", "MAXPOOL5", "UPSAMPLE2", "COPYC", "ATTN", "DECODE",
+                            "GAP", "SOFTMAX", "DECODEOBB", "PS2", "DECODESEG", "MASKS", "POOLX3"};
+
+struct Buf { int H, W, C; void* p = nullptr; };
+struct Ten { int buf, coff, C; };
+struct Op {
+  Kind kind;
+  int a = -1, b = -1, out = -1;   // tensors (CONV: a in, out; ADD: a, b, out; DECODE*: a box, b cls, out coef)
+  int k = 0, s = 0, p = 0, g = 0, act = 0, Cin = 0, Cout = 0;
+  long woff = 0, boff = 0;
+  int heads = 0, kd = 0, hd = 0, stride = 0;
+  int res = -1;                   // fused residual tensor
+  int y2 = -1, y3 = -1;           // POOLX3 outputs 2 and 3
+  int tile = 0;                   // tensor-core N tile chosen by the planner / autotuner
+};
+
+struct SlotGeom { float scale = 1.f; int top = 0, left = 0; };
+
+std::vector<char> read_file(const std::string& path) {
+  FILE* f = fopen(path.c_str(), "rb");
+  if (!f) throw Error("cannot open " + path);
+  fseek(f, 0, SEEK_END);
+  long n = ftell(f);
+  fseek(f, 0, SEEK_SET);
+  std::vector<char> v(n);
+  size_t rd = n ? fread(v.data(), 1, n, f) : 0;
+  fclose(f);
+  if ((long)rd != n) throw Error("short read " + path);
+  return v;
+}
+
+struct Engine {
+  YoloOptions opt;
+  int device = 0, maxB = 1;
+  std::string task = "detect";
+  int nc = 80, S = 0;
+  std::vector<Buf> bufs;
+  std::vector<Ten> tens;
+  std::vector<Op> raw, ops;       // unfused (dump order) and planned (fused) op lists
+  void* dweights = nullptr;
+  float* dbias = nullptr;
+  size_t nweights = 0, nbias = 0;
+  // head
+  struct Level { int box, cls, coef, stride; };
+  std::vector<Level> levels;
+  int protoTen = -1, A = 0;
+  // post-processing state
+  YkPost post{};
+  uint8_t* dmasks = nullptr;
+  float* h_out = nullptr;
+  int* h_cnt = nullptr;
+  int* h_raw = nullptr;
+  cudaStream_t st = nullptr;
+  std::map<int, cudaGraphExec_t> graphs;
+  std::map<int, float> exec_ms;
+  std::vector<SlotGeom> slots;
+  bool seg() const { return task == "segment"; }
+
+  ~Engine() { release(); }
+
+  void release() {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    graphs.clear();
+    for (auto& b : bufs)
+      if (b.p) cudaFree(b.p), b.p = nullptr;
+    if (dweights) cudaFree(dweights);
+    if (dbias) cudaFree(dbias);
+    if (post.ws) cudaFree(post.ws);
+    if (post.outdets) cudaFree(post.outdets);
+    if (post.outidx) cudaFree(post.outidx);
+    if (post.outcnt) cudaFree(post.outcnt);
+    if (post.rawcnt) cudaFree(post.rawcnt);
+    if (dmasks) cudaFree(dmasks);
+    if (h_out) cudaFreeHost(h_out);
+    if (h_cnt) cudaFreeHost(h_cnt);
+    if (h_raw) cudaFreeHost(h_raw);
+    if (st) cudaStreamDestroy(st);
+    dweights = nullptr; dbias = nullptr; post = YkPost{}; dmasks = nullptr;
+    h_out = nullptr; h_cnt = nullptr; h_raw = nullptr; st = nullptr;
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+
+  YkView view(int t, int B) const {
+    const Ten& tv = tens.at(t);
+    const Buf& b = bufs.at(tv.buf);
+    YkView v;
+    v.ptr = b.p; v.batch = B; v.H = b.H; v.W = b.W; v.stride = b.C; v.coff = tv.coff; v.C = tv.C;
+    return v;
+  }
+
+  void parse(const std::string& dir);
+  void validate(const std::string& dir);
+  void allocate(const std::string& dir);
+  void plan();
+  void autotune();
+  void run_op(const Op& op, int B);
+  void run_post(int B);
+  void forward(int B);
+  cudaGraphExec_t graph_for(int B);
+};
+
+void Engine::parse(const std::string& dir) {
+  FILE* f = fopen((dir + "/model.graph").c_str(), "r");
+  if (!f) throw Error("no model.graph in " + dir);
+  std::unique_ptr<FILE, int (*)(FILE*)> guard(f, fclose);
+  char magic[64], tag[32], taskbuf[32];
+  int ver = 0;
+  if (fscanf(f, "%63s %d", magic, &ver) != 2 || strcmp(magic, "YOLO11GRAPH"))
+    throw Error("bad graph magic");
+  int hsz = 0;
+  if (ver >= 2) {
+    if (fscanf(f, "%31s %31s %d %d", tag, taskbuf, &nc, &hsz) != 4 || strcmp(tag, "TASK"))
+      throw Error("bad TASK header");
+    task = taskbuf;
+  }
+  int nb, nt, no;
+  if (fscanf(f, "%d %d %d", &nb, &nt, &no) != 3 || nb < 1 || nt < 1 || no < 1 || nb > 100000 ||
+      nt > 100000 || no > 100000)
+    throw Error("bad graph counts");
+  bufs.resize(nb);
+  tens.resize(nt);
+  for (auto& b : bufs)
+    if (fscanf(f, "%31s %d %d %d", tag, &b.H, &b.W, &b.C) != 4 || strcmp(tag, "B") || b.H < 1 ||
+        b.W < 1 || b.C < 1)
+      throw Error("bad buffer line");
+  for (auto& t : tens)
+    if (fscanf(f, "%31s %d %d %d", tag, &t.buf, &t.coff, &t.C) != 4 || strcmp(tag, "T") ||
+        t.buf < 0 || t.buf >= nb || t.coff < 0 || t.C < 1 || t.coff + t.C > bufs[t.buf].C)
+      throw Error("bad tensor line");
+  auto rd = [&](int n, int* v) {
+    for (int i = 0; i < n; i++)
+      if (fscanf(f, "%d", &v[i]) != 1) throw Error("truncated op line");
+  };
+  for (int i = 0; i < no; i++) {
+    if (fscanf(f, "%31s", tag) != 1) throw Error("truncated graph");
+    Op op;
+    int v[10];
+    if (!strcmp(tag, "CONV")) {
+      op.kind = CONV;
+      rd(9, v);
+      op.a = v[0]; op.out = v[1]; op.k = v[2]; op.s = v[3]; op.p = v[4]; op.g = v[5];
+      op.act = v[6]; op.Cin = v[7]; op.Cout = v[8];
+      if (fscanf(f, "%ld %ld", &op.woff, &op.boff) != 2) throw Error("truncated CONV");
+    } else if (!strcmp(tag, "ADD")) {
+      op.kind = ADD; rd(3, v); op.a = v[0]; op.b = v[1]; op.out = v[2];
+    } else if (!strcmp(tag, "MAXPOOL5") || !strcmp(tag, "UPSAMPLE2") || !strcmp(tag, "COPYC") ||
+               !strcmp(tag, "PS2") || !strcmp(tag, "GAP") || !strcmp(tag, "SOFTMAX")) {
+      op.kind = !strcmp(tag, "MAXPOOL5") ? MAXPOOL5 : !strcmp(tag, "UPSAMPLE2") ? UPSAMPLE2
+              : !strcmp(tag, "COPYC") ? COPYC : !strcmp(tag, "PS2") ? PS2
+              : !strcmp(tag, "GAP") ? GAP : SOFTMAX;
+      rd(2, v); op.a = v[0]; op.out = v[1];
+    } else if (!strcmp(tag, "ATTN")) {
+      op.kind = ATTN; rd(5, v);
+      op.a = v[0]; op.out = v[1]; op.heads = v[2]; op.kd = v[3]; op.hd = v[4];
+    } else if (!strcmp(tag, "DECODE")) {
+      op.kind = DECODE; rd(3, v); op.a = v[0]; op.b = v[1]; op.stride = v[2];
+    } else if (!strcmp(tag, "DECODESEG") || !strcmp(tag, "DECODEOBB")) {
+      op.kind = !strcmp(tag, "DECODESEG") ? DECODESEG : DECODEOBB;
+      rd(4, v); op.a = v[0]; op.b = v[1]; op.out = v[2]; op.stride = v[3];
+    } else if (!strcmp(tag, "MASKS")) {
+      op.kind = MASKS; rd(1, v); op.a = v[0];
+    } else {
+      throw Error(std::string("bad op ") + tag);
+    }
+    for (int t : {op.a, op.b, op.out})
+      if (t >= nt) throw Error("op references a missing tensor");
+    raw.push_back(op);
+  }
+  const Buf& ib = bufs[tens[0].buf];
+  if (hsz && (hsz != ib.H || hsz != ib.W)) throw Error("imgsz header mismatch");
+  S = ib.H;
+}
+
+void Engine::validate(const std::string& dir) {
+  if (task != "detect" && task != "segment")
+    throw Error("task '" + task + "' is not supported by this engine (detect, segment)");
+  const Ten& t0 = tens[0];
+  if (t0.coff != 0 || t0.C != 3 || bufs[t0.buf].C != 3 || bufs[t0.buf].H != bufs[t0.buf].W)
+    throw Error("tensor 0 must be a standalone S x S x 3 input");
+  A = 0;
+  for (const Op& op : raw) {
+    switch (op.kind) {
+      case CONV: {
+        const Ten &x = tens[op.a], &y = tens[op.out];
+        const Buf &bx = bufs[x.buf], &by = bufs[y.buf];
+        if (x.C != op.Cin || y.C != op.Cout || op.k < 1 || op.s < 1)
+          throw Error("CONV channel mismatch");
+        if ((bx.H + 2 * op.p - op.k) / op.s + 1 != by.H || (bx.W + 2 * op.p - op.k) / op.s + 1 != by.W)
+          throw Error("CONV spatial mismatch");
+        const bool dw = op.g > 1;
+        if (dw && (op.g != op.Cin || op.Cin != op.Cout)) throw Error("unsupported grouped CONV");
+        if (op.woff < 0 || op.boff < 0 || op.woff % 8 || op.boff % 4) throw Error("bad weight offset");
+        break;
+      }
+      case GAP: case SOFTMAX: case DECODEOBB:
+        throw Error(std::string(kKindNames[op.kind]) + " (classify/obb) is not supported");
+      case DECODE: case DECODESEG: {
+        const Ten& c = tens[op.b];
+        if (c.C % 8 || c.C < nc) throw Error("DECODE needs an 8-aligned cls view covering nc");
+        if (tens[op.a].C != 64) throw Error("DECODE box view must have 64 channels");
+        if ((op.kind == DECODESEG) != seg()) throw Error("DECODESEG needs task=segment");
+        levels.push_back({op.a, op.b, op.kind == DECODESEG ? op.out : -1, op.stride});
+        const Buf& bb = bufs[tens[op.a].buf];
+        A += bb.H * bb.W;
+        break;
+      }
+      case MASKS: protoTen = op.a; break;
+      default: break;
+    }
+  }
+  if (levels.empty() || levels.size() > 4) throw Error("graph needs 1..4 DECODE levels");
+  auto fsize = [&](const char* name) -> long {
+    FILE* f = fopen((dir + "/" + name).c_str(), "rb");
+    if (!f) throw Error(std::string("cannot open ") + dir + "/" + name);
+    fseek(f, 0, SEEK_END);
+    long n = ftell(f);
+    fclose(f);
+    return n;
+  };
+  const long nw = fsize("weights.f16") / 2, nbb = fsize("bias.f32") / 4;
+  for (const Op& op : raw)
+    if (op.kind == CONV) {
+      const long wcount = (long)op.Cout * op.k * op.k * (op.Cin / std::max(op.g, 1));
+      if (op.woff + wcount > nw || op.boff + op.Cout > nbb)
+        throw Error("weights.f16 / bias.f32 too small for the graph");
+    }
+  if (seg()) {
+    if (protoTen < 0) throw Error("segment graph without MASKS op");
+    const int nm = tens[protoTen].C;
+    if (nm % 8 || nm > 64) throw Error("unsupported mask coefficient count");
+    for (auto& l : levels)
+      if (tens[l.coef].C != nm) throw Error("coef view width != proto channels");
+  }
+}
+
+void Engine::allocate(const std::string& dir) {
+  CKE(cudaSetDevice(device));
+  CKE(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  for (auto& b : bufs) {
+    const size_t bytes = (size_t)maxB * b.H * b.W * b.C * 2;
+    CKE(cudaMalloc(&b.p, bytes));
+    CKE(cudaMemset(b.p, 0, bytes));
+  }
+  auto wf = read_file(dir + "/weights.f16");
+  auto bf = read_file(dir + "/bias.f32");
+  nweights = wf.size() / 2;
+  nbias = bf.size() / 4;
+  for (const Op& op : raw)
+    if (op.kind == CONV) {
+      const size_t wcount = (size_t)op.Cout * op.k * op.k * (op.Cin / std::max(op.g, 1));
+      if (op.woff + wcount > nweights || op.boff + (size_t)op.Cout > nbias)
+        throw Error("weights.f16 / bias.f32 too small for the graph");
+    }
+  CKE(cudaMalloc(&dweights, std::max<size_t>(wf.size(), 16)));
+  CKE(cudaMemcpy(dweights, wf.data(), wf.size(), cudaMemcpyHostToDevice));
+  CKE(cudaMalloc(&dbias, std::max<size_t>(bf.size(), 16)));
+  CKE(cudaMemcpy(dbias, bf.data(), bf.size(), cudaMemcpyHostToDevice));
+  post.ws_bytes = yk_post_workspace_bytes(maxB, A);
+  CKE(cudaMalloc(&post.ws, post.ws_bytes));
+  CKE(cudaMalloc(&post.outdets, (size_t)maxB * opt.max_det * 6 * sizeof(float)));
+  CKE(cudaMalloc(&post.outidx, (size_t)maxB * opt.max_det * sizeof(int)));
+  CKE(cudaMalloc(&post.outcnt, maxB * sizeof(int)));
+  CKE(cudaMalloc(&post.rawcnt, maxB * sizeof(int)));
+  CKE(cudaMemset(post.outcnt, 0, maxB * sizeof(int)));
+  CKE(cudaMemset(post.rawcnt, 0, maxB * sizeof(int)));
+  if (seg()) {
+    const Buf& pb = bufs[tens[protoTen].buf];
+    CKE(cudaMalloc(&dmasks, (size_t)maxB * opt.max_det * pb.H * pb.W));
+  }
+  CKE(cudaMallocHost(&h_out, (size_t)maxB * opt.max_det * 6 * sizeof(float)));
+  CKE(cudaMallocHost(&h_cnt, maxB * sizeof(int)));
+  CKE(cudaMallocHost(&h_raw, maxB * sizeof(int)));
+  memset(h_cnt, 0, maxB * sizeof(int));
+  memset(h_raw, 0, maxB * sizeof(int));
+  slots.assign(maxB, SlotGeom{});
+}
+
+// Planner: the reference's fuseAdds (a CONV directly followed by an ADD that consumes its
+// output becomes a residual epilogue) plus folding SPPF's three chained MAXPOOL5 ops into
+// one pass.  The unfused list stays available for per-op dumps.
+void Engine::plan() {
+  ops.clear();
+  for (size_t i = 0; i < raw.size(); i++) {
+    Op op = raw[i];
+    if (opt.fuse && op.kind == CONV && i + 1 < raw.size()) {
+      const Op& nx = raw[i + 1];
+      if (nx.kind == ADD && (nx.a == op.out || nx.b == op.out)) {
+        op.res = nx.a == op.out ? nx.b : nx.a;
+        op.out = nx.out;
+        i++;
+      }
+    } else if (opt.fuse && op.kind == MAXPOOL5 && i + 2 < raw.size() &&
+               raw[i + 1].kind == MAXPOOL5 && raw[i + 2].kind == MAXPOOL5 &&
+               raw[i + 1].a == op.out && raw[i + 2].a == raw[i + 1].out) {
+      op.kind = POOLX3;
+      op.y2 = raw[i + 1].out;
+      op.y3 = raw[i + 2].out;
+      i += 2;
+    }
+    if (op.kind == DECODE || op.kind == DECODESEG || op.kind == MASKS) continue;
+    ops.push_back(op);
+  }
+}
+
+void Engine::run_op(const Op& op, int B) {
+  switch (op.kind) {
+    case CONV: {
+      YkConv p;
+      p.weight = (const uint16_t*)dweights + op.woff;
+      p.bias = dbias + op.boff;
+      p.k = op.k; p.s = op.s; p.p = op.p; p.groups = op.g; p.act = op.act;
+      p.Cin = op.Cin; p.Cout = op.Cout; p.tile = op.tile; p.splitk = 0;
+      YkView x = view(op.a, B), y = view(op.out, B);
+      YkView r;
+      if (op.res >= 0) r = view(op.res, B);
+      CKY(yk_conv(&x, &y, op.res >= 0 ? &r : nullptr, &p, (yk_stream_t)st));
+      break;
+    }
+    case ADD: {
+      YkView a = view(op.a, B), b = view(op.b, B), y = view(op.out, B);
+      CKY(yk_add(&a, &b, &y, (yk_stream_t)st));
+      break;
+    }
+    case MAXPOOL5: {
+      YkView x = view(op.a, B), y = view(op.out, B);
+      CKY(yk_maxpool5(&x, &y, (yk_stream_t)st));
+      break;
+    }
+    case POOLX3: {
+      YkView x = view(op.a, B), y1 = view(op.out, B), y2 = view(op.y2, B), y3 = view(op.y3, B);
+      CKY(yk_maxpool5x3(&x, &y1, &y2, &y3, (yk_stream_t)st));
+      break;
+    }
+    case UPSAMPLE2: {
+      YkView x = view(op.a, B), y = view(op.out, B);
+      CKY(yk_upsample2(&x, &y, (yk_stream_t)st));
+      break;
+    }
+    case PS2: {
+      YkView x = view(op.a, B), y = view(op.out, B);
+      CKY(yk_ps2(&x, &y, (yk_stream_t)st));
+      break;
+    }
+    case COPYC: {
+      YkView x = view(op.a, B), y = view(op.out, B);
+      CKY(yk_copyc(&x, &y, (yk_stream_t)st));
+      break;
+    }
+    case ATTN: {
+      YkView q = view(op.a, B), y = view(op.out, B);
+      CKY(yk_attn(&q, &y, op.heads, op.kd, op.hd, (yk_stream_t)st));
+      break;
+    }
+    default:
+      break;   // DECODE / DECODESEG / MASKS run in run_post
+  }
+}
+
+void Engine::run_post(int B) {
+  std::vector<YkLevel> lv(levels.size());
+  for (size_t i = 0; i < levels.size(); i++) {
+    lv[i].box = view(levels[i].box, B);
+    lv[i].cls = view(levels[i].cls, B);
+    if (levels[i].coef >= 0) lv[i].coef = view(levels[i].coef, B);
+    else memset(&lv[i].coef, 0, sizeof(YkView));
+    lv[i].stride = levels[i].stride;
+  }
+  CKY(yk_decode(lv.data(), (int)lv.size(), B, nc, opt.conf, &post, (yk_stream_t)st));
+  CKY(yk_nms(B, A, opt.iou, opt.max_det, &post, (yk_stream_t)st));
+  if (seg()) {
+    YkView pr = view(protoTen, B);
+    CKY(yk_masks(lv.data(), (int)lv.size(), &pr, S, S, opt.max_det, &post, dmasks,
+                 (yk_stream_t)st));
+  }
+  CKE(cudaMemcpyAsync(h_raw, post.rawcnt, B * sizeof(int), cudaMemcpyDeviceToHost, st));
+  CKE(cudaMemcpyAsync(h_cnt, post.outcnt, B * sizeof(int), cudaMemcpyDeviceToHost, st));
+  CKE(cudaMemcpyAsync(h_out, post.outdets, (size_t)B * opt.max_det * 6 * sizeof(float),
+                      cudaMemcpyDeviceToHost, st));
+}
+
+void Engine::forward(int B) {
+  for (const Op& op : ops) run_op(op, B);
+  run_post(B);
+}
+
+// Startup autotune (reference engine/engine.cu:1504-1533): time every tensor-core tile width
+// that fits the layer at the full batch and keep the fastest.
+void Engine::autotune() {
+  cudaEvent_t e0, e1;
+  CKE(cudaEventCreate(&e0));
+  CKE(cudaEventCreate(&e1));
+  for (Op& op : ops) {
+    if (op.kind != CONV || op.g != 1 || op.Cin % 8) continue;
+    int best = 0;
+    float tbest = 1e30f;
+    for (int tile : {64, 128, 256}) {
+      if (tile > 64 && tile / 2 >= op.Cout) continue;
+      op.tile = tile;
+      run_op(op, maxB);
+      CKE(cudaEventRecord(e0, st));
+      for (int r = 0; r < 5; r++) run_op(op, maxB);
+      CKE(cudaEventRecord(e1, st));
+      CKE(cudaEventSynchronize(e1));
+      float ms = 0;
+      CKE(cudaEventElapsedTime(&ms, e0, e1));
+      if (ms < tbest) { tbest = ms; best = tile; }
+    }
+    op.tile = op.Cout <= 32 ? 32 : best;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  // the tuning runs overwrote activations; nothing downstream depends on them
+}
+
+cudaGraphExec_t Engine::graph_for(int B) {
+  auto it = graphs.find(B);
+  if (it != graphs.end()) return it->second;
+  cudaGraph_t g;
+  CKE(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  try {
+    forward(B);
+  } catch (...) {
+    cudaGraph_t dummy;
+    cudaStreamEndCapture(st, &dummy);
+    if (dummy) cudaGraphDestroy(dummy);
+    throw;
+  }
+  CKE(cudaStreamEndCapture(st, &g));
+  cudaGraphExec_t ge;
+  CKE(cudaGraphInstantiate(&ge, g, 0));
+  cudaGraphDestroy(g);
+  graphs[B] = ge;
+  // calibrate (reference: 3 warm + 10 timed launches)
+  cudaEvent_t e0, e1;
+  CKE(cudaEventCreate(&e0));
+  CKE(cudaEventCreate(&e1));
+  for (int i = 0; i < 3; i++) CKE(cudaGraphLaunch(ge, st));
+  CKE(cudaEventRecord(e0, st));
+  for (int i = 0; i < 10; i++) CKE(cudaGraphLaunch(ge, st));
+  CKE(cudaEventRecord(e1, st));
+  CKE(cudaEventSynchronize(e1));
+  float ms = 0;
+  cudaEventElapsedTime(&ms, e0, e1);
+  exec_ms[B] = ms / 10.f;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  return ge;
+}
+
+Engine* as_engine(void* h) { return (Engine*)h; }
+
+struct DeviceScope {   // makes the handle's device current for the duration of a call
+  int prev = -1;
+  explicit DeviceScope(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+template <class F>
+auto guarded(F&& f, decltype(f()) fail) -> decltype(f()) {
+  try {
+    return f();
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return fail;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* yolo_last_error(void) { return g_err.c_str(); }
+
+void yolo_default_options(YoloOptions* o) {
+  o->device = -1;
+  o->conf = 0.25f;
+  o->iou = 0.45f;
+  o->max_det = 300;
+  o->autotune = 1;
+  o->fuse = 1;
+}
+
+void* yolo_create_ex(const char* model_dir, int max_batch, const YoloOptions* opts) {
+  return guarded([&]() -> void* {
+    if (!model_dir || max_batch < 1) throw Error("yolo_create: bad arguments");
+    std::unique_ptr<Engine> e(new Engine());
+    if (opts) e->opt = *opts; else yolo_default_options(&e->opt);
+    if (e->opt.max_det < 1 || e->opt.max_det > 100000) throw Error("bad max_det");
+    e->maxB = max_batch;
+    e->parse(model_dir);      // host-only checks first: bad directories fail without a GPU
+    e->validate(model_dir);
+    int dev = e->opt.device;
+    if (dev < 0) CKE(cudaGetDevice(&dev));
+    e->device = dev;
+    DeviceScope ds(dev);
+    e->allocate(model_dir);
+    e->plan();
+    if (e->opt.autotune) e->autotune();
+    CKE(cudaStreamSynchronize(e->st));
+    int derr = yk_fetch_device_error();
+    if (derr) throw Error("device error word set during create: " + std::to_string(derr));
+    return e.release();
+  }, nullptr);
+}
+
+void* yolo_create(const char* model_dir, int max_batch) {
+  YoloOptions o;
+  yolo_default_options(&o);
+  return yolo_create_ex(model_dir, max_batch, &o);
+}
+
+void yolo_destroy(void* h) { delete as_engine(h); }
+
+int yolo_task(void* h) { return h && as_engine(h)->seg() ? 3 : 0; }
+
+float yolo_exec_ms(void* h, int B) {
+  return guarded([&]() -> float {
+    Engine* e = as_engine(h);
+    if (!e || B < 1 || B > e->maxB) throw Error("yolo_exec_ms: bad batch");
+    DeviceScope ds(e->device);
+    e->graph_for(B);
+    return e->exec_ms[B];
+  }, -1.f);
+}
+
+cudaStream_t yolo_stream(void* h) { return h ? as_engine(h)->st : nullptr; }
+
+void yolo_preprocess(void* h, const unsigned char* dev_bgr, int height, int width, int slot) {
+  guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || slot < 0 || slot >= e->maxB) throw Error("yolo_preprocess: bad slot");
+    DeviceScope ds(e->device);
+    YkView in = e->view(0, e->maxB);
+    SlotGeom& g = e->slots[slot];
+    CKY(yk_letterbox(dev_bgr, height, width, &in, slot, &g.scale, &g.top, &g.left,
+                     (yk_stream_t)e->st));
+    return 0;
+  }, -1);
+}
+
+void yolo_run_async(void* h, int B) {
+  guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || B < 1 || B > e->maxB) throw Error("yolo_run: bad batch");
+    DeviceScope ds(e->device);
+    CKE(cudaGraphLaunch(e->graph_for(B), e->st));
+    return 0;
+  }, -1);
+}
+
+void yolo_sync(void* h) {
+  guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e) throw Error("yolo_sync: null handle");
+    CKE(cudaStreamSynchronize(e->st));
+    int derr = yk_fetch_device_error();
+    if (derr) throw Error("device error word set: " + std::to_string(derr));
+    return 0;
+  }, -1);
+}
+
+void yolo_run(void* h, int B) {
+  yolo_run_async(h, B);
+  yolo_sync(h);
+}
+
+int yolo_get(void* h, int slot, YoloDet* out, int cap) {
+  Engine* e = as_engine(h);
+  if (!e || slot < 0 || slot >= e->maxB || (!out && cap > 0)) return 0;
+  const SlotGeom& g = e->slots[slot];
+  const int n = std::min(e->h_cnt[slot], cap);
+  for (int i = 0; i < n; i++) {
+    const float* d = e->h_out + ((size_t)slot * e->opt.max_det + i) * 6;
+    out[i].x1 = (d[0] - g.left) / g.scale;
+    out[i].y1 = (d[1] - g.top) / g.scale;
+    out[i].x2 = (d[2] - g.left) / g.scale;
+    out[i].y2 = (d[3] - g.top) / g.scale;
+    out[i].score = d[4];
+    out[i].cls = (int)d[5];
+  }
+  return n;
+}
+
+int yolo_raw_count(void* h, int slot) {
+  Engine* e = as_engine(h);
+  if (!e || slot < 0 || slot >= e->maxB) return -1;
+  return e->h_raw[slot];
+}
+
+void yolo_slot_geom(void* h, int slot, float* scale, int* top, int* left) {
+  Engine* e = as_engine(h);
+  if (!e || slot < 0 || slot >= e->maxB) return;
+  const SlotGeom& g = e->slots[slot];
+  if (scale) *scale = g.scale;
+  if (top) *top = g.top;
+  if (left) *left = g.left;
+}
+
+void yolo_mask_dim(void* h, int* ph, int* pw) {
+  Engine* e = as_engine(h);
+  int H = 0, W = 0;
+  if (e && e->seg()) {
+    const Buf& b = e->bufs[e->tens[e->protoTen].buf];
+    H = b.H; W = b.W;
+  }
+  if (ph) *ph = H;
+  if (pw) *pw = W;
+}
+
+int yolo_get_mask(void* h, int slot, int det, unsigned char* out) {
+  return guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || !e->seg() || slot < 0 || slot >= e->maxB || det < 0 || det >= e->h_cnt[slot] || !out)
+      return -1;
+    DeviceScope ds(e->device);
+    const Buf& b = e->bufs[e->tens[e->protoTen].buf];
+    const size_t sz = (size_t)b.H * b.W;
+    CKE(cudaMemcpy(out, e->dmasks + ((size_t)slot * e->opt.max_det + det) * sz, sz,
+                   cudaMemcpyDeviceToHost));
+    return 0;
+  }, -1);
+}
+
+int yolo_num_ops(void* h) { return h ? (int)as_engine(h)->raw.size() : -1; }
+
+int yolo_run_op(void* h, int op_index, int B) {
+  return guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || op_index < 0 || op_index >= (int)e->raw.size() || B < 1 || B > e->maxB)
+      throw Error("yolo_run_op: bad arguments");
+    DeviceScope ds(e->device);
+    const Op& op = e->raw[op_index];
+    if (op.kind == DECODE || op.kind == DECODESEG || op.kind == MASKS) {
+      // the whole post chain runs once, at the last head op of the graph
+      bool last = true;
+      for (size_t j = op_index + 1; j < e->raw.size(); j++)
+        if (e->raw[j].kind == DECODE || e->raw[j].kind == DECODESEG || e->raw[j].kind == MASKS)
+          last = false;
+      if (last) e->run_post(B);
+      CKE(cudaStreamSynchronize(e->st));
+      return 1;
+    }
+    Op o = op;
+    if (o.kind == CONV && o.g == 1 && o.Cin % 8 == 0) {
+      for (const Op& f : e->ops)   // reuse the tuned tile of the matching planned conv
+        if (f.kind == CONV && f.woff == o.woff) o.tile = f.tile;
+    }
+    e->run_op(o, B);
+    CKE(cudaStreamSynchronize(e->st));
+    int derr = yk_fetch_device_error();
+    if (derr) throw Error("device error word set: " + std::to_string(derr));
+    return 0;
+  }, -2);
+}
+
+int yolo_tensor_view(void* h, int tensor, void** ptr, int* H, int* W, int* stride, int* coff,
+                     int* C) {
+  Engine* e = as_engine(h);
+  if (!e || tensor < 0 || tensor >= (int)e->tens.size()) return -1;
+  YkView v = e->view(tensor, e->maxB);
+  if (ptr) *ptr = v.ptr;
+  if (H) *H = v.H;
+  if (W) *W = v.W;
+  if (stride) *stride = v.stride;
+  if (coff) *coff = v.coff;
+  if (C) *C = v.C;
+  return 0;
+}
+
+static int copy_tensor(void* h, int tensor, int B, void* host, bool to_host) {
+  return guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || tensor < 0 || tensor >= (int)e->tens.size() || B < 1 || B > e->maxB || !host)
+      throw Error("yolo_read/write_tensor: bad arguments");
+    DeviceScope ds(e->device);
+    CKE(cudaStreamSynchronize(e->st));
+    YkView v = e->view(tensor, B);
+    char* dev = (char*)v.ptr + (size_t)v.coff * 2;
+    const size_t rows = (size_t)B * v.H * v.W;
+    if (to_host)
+      CKE(cudaMemcpy2D(host, (size_t)v.C * 2, dev, (size_t)v.stride * 2, (size_t)v.C * 2, rows,
+                       cudaMemcpyDeviceToHost));
+    else
+      CKE(cudaMemcpy2D(dev, (size_t)v.stride * 2, host, (size_t)v.C * 2, (size_t)v.C * 2, rows,
+                       cudaMemcpyHostToDevice));
+    return 0;
+  }, -1);
+}
+
+int yolo_read_tensor(void* h, int tensor, int B, void* host) {
+  return copy_tensor(h, tensor, B, host, true);
+}
+int yolo_write_tensor(void* h, int tensor, int B, const void* host) {
+  return copy_tensor(h, tensor, B, (void*)host, false);
+}
+
+const char* yolo_op_desc(void* h, int op_index, int* tile) {
+  Engine* e = as_engine(h);
+  if (!e || op_index < 0 || op_index >= (int)e->ops.size()) return nullptr;
+  if (tile) *tile = e->ops[op_index].tile;
+  return kKindNames[e->ops[op_index].kind];
+}
+
+int yolo_profile(void* h, int B, int iters, float* ms, int cap) {
+  return guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || B < 1 || B > e->maxB || iters < 1) throw Error("yolo_profile: bad arguments");
+    DeviceScope ds(e->device);
+    const int n = (int)e->ops.size();
+    std::vector<cudaEvent_t> ev(n + 2);
+    for (auto& x : ev) CKE(cudaEventCreate(&x));
+    std::vector<double> acc(n + 1, 0.0);
+    for (int w = 0; w < 3; w++) e->forward(B);
+    for (int it = 0; it < iters; it++) {
+      CKE(cudaEventRecord(ev[0], e->st));
+      for (int k = 0; k < n; k++) {
+        e->run_op(e->ops[k], B);
+        CKE(cudaEventRecord(ev[k + 1], e->st));
+      }
+      e->run_post(B);
+      CKE(cudaEventRecord(ev[n + 1], e->st));
+      CKE(cudaEventSynchronize(ev[n + 1]));
+      for (int k = 0; k <= n; k++) {
+        float t = 0;
+        cudaEventElapsedTime(&t, ev[k], ev[k + 1]);
+        acc[k] += t;
+      }
+    }
+    for (auto& x : ev) cudaEventDestroy(x);
+    for (int k = 0; k <= n && k < cap; k++) ms[k] = (float)(acc[k] / iters);
+    return n + 1;   // the last entry is the decode + NMS (+ masks) tail
+  }, -1);
+}
+
+}  // extern "C"

@@ -1,0 +1,7 @@
+// Single translation unit of libyolob200.so: device globals shared by the kernels (the
+// device error word) then need no relocatable device code.
+#include "conv_misc.cu"
+#include "conv_tc.cu"
+#include "attn.cu"
+#include "post.cu"
+#include "engine.cu"
