@@ -226,6 +226,10 @@ def bench_latency_yolo11n(rt, pkg, dev, iters=200):
     return out
 
 
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
 def run_ours(args):
     import ctypes as C
     import numpy as np
@@ -242,6 +246,7 @@ def run_ours(args):
         export.ensure_model_dir(MODEL, MODELS, S, FRAME_HW)
     barrier(world)
     d = export.ensure_model_dir(MODEL, MODELS, S, FRAME_HW)
+    log('bench: engine create')
     lib = rt.load()
     B = PER_GPU
     lo, hi = shard(PER_GPU * world, world, rank)
@@ -251,6 +256,7 @@ def run_ours(args):
     graph_kernels = lib.yk_launch_count() - n0
     launches_per_step = graph_kernels + B          # graph kernels + one letterbox per frame
 
+    log('bench: frames')
     hostf = torch.from_numpy(np.stack([frames.synthetic_bgr(*FRAME_HW, seed=i) for i in range(lo, hi)])).pin_memory()
     dev = f"cuda:{local}"
     dbuf = [torch.empty_like(hostf, device=dev) for _ in range(2)]
@@ -269,6 +275,7 @@ def run_ours(args):
     eng.sync()
     eng._check()
 
+    log('bench: timed value')
     # ---- value: frames resident in HBM, CUDA events on the engine stream ----
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
@@ -284,6 +291,7 @@ def run_ours(args):
     dev_ms_max = max_over_ranks(dev_ms, world)
     eng._check()
 
+    log('bench: e2e')
     # ---- e2e: pinned host frames -> H2D (double-buffered) -> ABI -> D2H results ----
     cs = torch.cuda.Stream(device=dev)
     copied = [torch.cuda.Event() for _ in range(2)]
@@ -322,6 +330,7 @@ def run_ours(args):
     t_e2e_max = max_over_ranks(t_e2e, world)
     eng._check()
 
+    log('bench: roofline')
     # ---- roofline of the dominant kernel (tensor-core implicit-GEMM conv) ----
     ms = (C.c_float * 4096)()
     nprof = lib.yolo_profile(eng.h, B, 10, ms, 4096)
@@ -338,7 +347,9 @@ def run_ours(args):
     achieved = flops / (conv_ms * 1e-3) / 1e12 if conv_ms > 0 else None
     peak = pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
 
+    log('bench: latency')
     lat = bench_latency_yolo11n(rt, pkg, local) if rank == 0 and not args.no_latency else None
+    log('bench: cpu')
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         n, secs, thr = cpu_forward_frames(d, 40, args.cpu_seconds)

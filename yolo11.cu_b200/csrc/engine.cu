@@ -324,6 +324,7 @@ void Engine::allocate(const std::string& dir) {
   memset(h_cnt, 0, maxB * sizeof(int));
   memset(h_raw, 0, maxB * sizeof(int));
   slots.assign(maxB, SlotGeom{});
+  CKE(cudaDeviceSynchronize());   // weights / memsets complete before the non-blocking stream runs
 }
 
 // Planner: the reference's fuseAdds (a CONV directly followed by an ADD that consumes its
@@ -735,12 +736,15 @@ static int copy_tensor(void* h, int tensor, int B, void* host, bool to_host) {
     YkView v = e->view(tensor, B);
     char* dev = (char*)v.ptr + (size_t)v.coff * 2;
     const size_t rows = (size_t)B * v.H * v.W;
+    // on the engine stream (non-blocking w.r.t. the legacy stream), then wait for it: a
+    // plain cudaMemcpy from pageable memory may return before the data reaches the device
     if (to_host)
-      CKE(cudaMemcpy2D(host, (size_t)v.C * 2, dev, (size_t)v.stride * 2, (size_t)v.C * 2, rows,
-                       cudaMemcpyDeviceToHost));
+      CKE(cudaMemcpy2DAsync(host, (size_t)v.C * 2, dev, (size_t)v.stride * 2, (size_t)v.C * 2,
+                            rows, cudaMemcpyDeviceToHost, e->st));
     else
-      CKE(cudaMemcpy2D(dev, (size_t)v.stride * 2, host, (size_t)v.C * 2, (size_t)v.C * 2, rows,
-                       cudaMemcpyHostToDevice));
+      CKE(cudaMemcpy2DAsync(dev, (size_t)v.stride * 2, host, (size_t)v.C * 2, (size_t)v.C * 2,
+                            rows, cudaMemcpyHostToDevice, e->st));
+    CKE(cudaStreamSynchronize(e->st));
     return 0;
   }, -1);
 }

@@ -81,6 +81,7 @@ static int load_input(void* h, const std::string& dir, int batch) {
   }
   for (int b = 0; b < batch; b++)
     CK(cudaMemcpy((char*)p + (size_t)b * in.size(), in.data(), in.size(), cudaMemcpyHostToDevice));
+  CK(cudaDeviceSynchronize());
   return 0;
 }
 
@@ -175,6 +176,7 @@ int main(int argc, char** argv) {
         for (size_t i = 0; i < host.size(); i++) host[i] = __float2half(rf[i]);
         CK(cudaMemcpy2D((char*)p + (size_t)c * 2, (size_t)s * 2, host.data(), C * 2, C * 2,
                         (size_t)H * W, cudaMemcpyHostToDevice));
+        CK(cudaDeviceSynchronize());
       }
     }
     printf("dumped %d ops\n", n);
