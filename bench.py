@@ -111,7 +111,7 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for s in self.samples for n, v in zip(names, s[3:7]) if "Active" in v})
+        reasons = sorted({n for s in self.samples for n, v in zip(names, s[3:7]) if v.strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": float(self.samples[0][2]) if self.samples[0][2].replace(".", "").isdigit() else None,
                 "reasons": reasons, "samples": len(self.samples)}
@@ -218,6 +218,8 @@ def bench_latency_yolo11n(rt, pkg, dev, iters=200):
         if i >= 20:
             lat.append(1000 * (t1 - t0))
     eng._check()
+    torch.cuda.synchronize()
+    del host, dbuf          # blocks used on the engine stream are freed while it still exists
     lat.sort()
     out = {"p50_ms": lat[len(lat) // 2], "p99_ms": lat[int(0.99 * (len(lat) - 1))],
            "graph_exec_ms": eng.exec_ms(1), "iters": iters,
@@ -356,13 +358,16 @@ def run_ours(args):
         cpu = {"value": n / secs, "unit": "frames/s", "cores": thr, "kind": "port",
                "sample": f"{n} frames of the same workload (fp32 torch restatement of the reference "
                          f"interpreter + C decode/NMS), {secs:.1f} s"}
+    torch.cuda.synchronize()
+    h2d_bytes = int(hostf.numel())
+    del hostf, dbuf          # free the blocks used on the engine stream before closing it
     eng.close()
     if rank != 0:
         return 0
     frames_total = PER_GPU * world * args.steps
     value = frames_total / (dev_ms_max / 1000)
     e2e = frames_total / t_e2e_max
-    h2d = int(hostf.numel()) * world
+    h2d = h2d_bytes * world
     d2h = (B * 300 * 6 * 4 + 2 * B * 4) * world
     line = {
         "metric": "frames/s", "value": value, "unit": "frames/s", "n_gpus": world,
