@@ -106,6 +106,21 @@ int yk_nms(int batch, int anchors, float iou, int max_out, const YkPost* post, y
 int yk_masks(const YkLevel* levels, int nlevels, const YkView* proto, int in_h, int in_w,
              int max_out, const YkPost* post, uint8_t* masks, yk_stream_t st);
 
+// Decode + NMS with no allocation at all (no counterpart in the reference).  For callers
+// that cannot call cudaMalloc — code under a fixed device-memory budget, plugins whose host
+// framework owns all allocations, loops that must never enter the allocator — the scratch
+// lives in one static 8 MiB device array inside the library instead of a YkPost workspace.
+// Same arguments and results as yk_decode + yk_nms; outputs as in YkPost ([batch][max_out][6],
+// [batch][max_out], [batch], [batch]).  Limit: batch * per-image scratch <= 8 MiB (about
+// 14 images of 8400 anchors at 640, 5 images at 1024); larger requests return YK_EINVAL with
+// the reason in yk_last_cuda_error.  The first call on each device looks up the array's
+// device address (cudaGetSymbolAddress), so make that first call before any stream capture.
+// All calls on a device share the one array and it keeps the last call's contents: calls
+// whose kernels overlap on the GPU (other streams, other threads) race and corrupt each other.
+int yk_decode_nms_static(const YkLevel* levels, int nlevels, int batch, int nc, float conf,
+                         float iou, int max_out, float* outdets, int* outidx, int* outcnt,
+                         int* rawcnt, yk_stream_t st);
+
 // Device error word (bounded-wait timeouts) of the current device; cleared by the call.
 int yk_fetch_device_error(void);
 const char* yk_last_cuda_error(void);

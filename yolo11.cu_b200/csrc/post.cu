@@ -6,6 +6,7 @@
 // (the reference appends candidates with atomicAdd and truncates NMS input at 1024 in that
 // order, engine/engine.cu:890, 1064).
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "detmath.h"
@@ -466,4 +467,66 @@ int yk_masks(const YkLevel* levels, int nlevels, const YkView* proto, int in_h, 
   return check_launch("masks");
 }
 
+
 }  // extern "C"
+
+// ---------------- decode + NMS without any allocation ----------------
+// Some callers cannot allocate device memory: code running where cudaMalloc is off limits
+// (a host with a fixed memory budget, a plugin whose host framework owns every allocation,
+// a real-time loop that must never hit the allocator).  yk_decode_nms_static gives them the
+// decode + NMS chain with its workspace in this fixed device array instead of a caller
+// buffer.  Every GPU that loads the library holds it until the process exits.
+namespace yk {
+constexpr size_t kStaticPostBytes = (size_t)8 << 20;   // 8 MiB
+static __device__ __align__(256) unsigned char g_static_post_ws[kStaticPostBytes];
+}  // namespace yk
+
+extern "C" int yk_decode_nms_static(const YkLevel* levels, int nlevels, int batch, int nc,
+                                    float conf, float iou, int max_out, float* outdets,
+                                    int* outidx, int* outcnt, int* rawcnt, yk_stream_t st) {
+  using namespace yk;
+  if (!levels || nlevels < 1 || nlevels > 4 || batch < 1) return YK_EINVAL;
+  const int A = anchors_of(levels, nlevels);
+  const size_t need = (size_t)batch * ws_layout(A).per_img;
+  if (need > kStaticPostBytes) {
+    snprintf(g_cuda_err, sizeof g_cuda_err,
+             "yk_decode_nms_static: batch %d x %d anchors needs %zu bytes of scratch, more than "
+             "the %zu-byte static array",
+             batch, A, need, kStaticPostBytes);
+    return YK_EINVAL;
+  }
+  // Host code cannot use g_static_post_ws directly (the name is a host-side stand-in, not a
+  // device address): look up its address once per device, with that device current.
+  static std::mutex mu;
+  static void* addr[128] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return check_launch("static ws");
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_static_post_ws);
+      if (e != cudaSuccess || !p) {
+        snprintf(g_cuda_err, sizeof g_cuda_err, "yk_decode_nms_static: cudaGetSymbolAddress: %s",
+                 cudaGetErrorString(e));
+        return YK_ECUDA;
+      }
+      addr[dev] = p;
+    }
+    ws = addr[dev];
+  }
+  // No part of the scratch has to start at zero: decode writes every anchor's flag and the
+  // NMS kernel writes each key / kept / survivor slot before reading it.
+  YkPost post;
+  post.ws = ws;
+  post.ws_bytes = kStaticPostBytes;
+  post.outdets = outdets;
+  post.outidx = outidx;
+  post.outcnt = outcnt;
+  post.rawcnt = rawcnt;
+  int r = yk_decode(levels, nlevels, batch, nc, conf, &post, st);
+  if (r != YK_OK) return r;
+  return yk_nms(batch, A, iou, max_out, &post, st);
+}
+

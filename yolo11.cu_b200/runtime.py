@@ -63,6 +63,9 @@ _SIGS = {
     "yk_nms": (C.c_int, [C.c_int, C.c_int, C.c_float, C.c_int, _P(YkPost), C.c_void_p]),
     "yk_masks": (C.c_int, [_P(YkLevel), C.c_int, _P(YkView), C.c_int, C.c_int, C.c_int,
                            _P(YkPost), C.c_void_p, C.c_void_p]),
+    "yk_decode_nms_static": (C.c_int, [_P(YkLevel), C.c_int, C.c_int, C.c_int, C.c_float,
+                                       C.c_float, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                       C.c_void_p, C.c_void_p]),
     "yk_fetch_device_error": (C.c_int, []),
     "yk_last_cuda_error": (C.c_char_p, []),
     "yk_launch_count": (C.c_longlong, []),
