@@ -74,6 +74,9 @@ CONV_CASES = [
     (1, 80, 80, 96, 200, 1, 1, 0),     # Cout not a tile multiple
     (1, 5, 7, 24, 40, 3, 2, 1),
     (1, 1, 1, 64, 80, 1, 1, 0),        # M = 1 (linear)
+    (2, 12, 12, 96, 64, 3, 1, 1),      # im2col TMA, Cin not a multiple of 64
+    (3, 13, 9, 64, 64, 3, 2, 1),       # im2col TMA, stride 2, odd sizes, tiles across images
+    (2, 7, 7, 128, 32, 3, 1, 1),
 ]
 
 
@@ -102,13 +105,14 @@ def test_conv_tc_residual_and_inplace(lib, cuda):
     assert rel(out, ref) < TOL
 
 
-def test_conv_first_layer(lib, cuda):
+@pytest.mark.parametrize("cout,k,s", [(16, 3, 2), (64, 3, 2), (96, 3, 2), (16, 3, 1), (16, 1, 1)])
+def test_conv_first_layer(lib, cuda, cout, k, s):
     from yolo11_cu_b200 import runtime as rt
     g = torch.Generator().manual_seed(4)
-    x = torch.rand(2, 64, 64, 3, generator=g).half().to(cuda)
-    w = (torch.randn(16, 3, 3, 3, generator=g) / 5).to(cuda)
-    b = (torch.randn(16, generator=g) * 0.1).to(cuda)
-    out, ref = run_conv(lib, rt, x, w, b, 3, 2, 1, act=1)
+    x = torch.rand(2, 64, 48, 3, generator=g).half().to(cuda)
+    w = (torch.randn(cout, 3, k, k, generator=g) / 5).to(cuda)
+    b = (torch.randn(cout, generator=g) * 0.1).to(cuda)
+    out, ref = run_conv(lib, rt, x, w, b, k, s, k // 2, act=1)
     assert rel(out, ref) < TOL
 
 

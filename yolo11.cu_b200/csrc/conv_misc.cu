@@ -70,14 +70,78 @@ __global__ void conv_small_cin_kernel(DView x, DView y, const __half* __restrict
   *(uint4*)(y.p + (size_t)pix * y.stride + co0) = o;
 }
 
+// First conv specialised for k=3, Cin=3 (every YOLO stem): thread = one output pixel, all
+// Cout channels.  The 27 input taps are loaded once into registers; weights (fp32) and bias
+// sit in shared memory and are read as broadcast float4s; the pixel's Cout outputs are
+// written as contiguous 16-byte chunks.
+template <int K>
+__global__ void __launch_bounds__(128) conv_stem3_kernel(DView x, DView y,
+                                                         const __half* __restrict__ w,
+                                                         const float* __restrict__ b, int Cout,
+                                                         int s, int p, int act, long long npix) {
+  extern __shared__ __align__(16) float wst[];   // [Cout][K*K*3] then bias[Cout]
+  constexpr int KK = K * K * 3;
+  for (int i = threadIdx.x; i < Cout * KK; i += blockDim.x) wst[i] = __half2float(w[i]);
+  for (int i = threadIdx.x; i < Cout; i += blockDim.x) wst[Cout * KK + i] = b[i];
+  __syncthreads();
+  const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= npix) return;
+  const int HW = y.H * y.W;
+  const int img = (int)(pix / HW), rem = (int)(pix - (long long)img * HW);
+  const int oy = rem / y.W, ox = rem - oy * y.W;
+  float in[KK];
+#pragma unroll
+  for (int ky = 0; ky < K; ky++) {
+    const int iy = oy * s - p + ky;
+#pragma unroll
+    for (int kx = 0; kx < K; kx++) {
+      const int ix = ox * s - p + kx;
+      const bool ok = iy >= 0 && iy < x.H && ix >= 0 && ix < x.W;
+      const __half* xp = x.p + x.pix(img, ok ? iy : 0, ok ? ix : 0);
+#pragma unroll
+      for (int ci = 0; ci < 3; ci++) in[(ky * K + kx) * 3 + ci] = ok ? __half2float(xp[ci]) : 0.f;
+    }
+  }
+  __half* yp = y.p + (size_t)pix * y.stride;
+  for (int c0 = 0; c0 < Cout; c0 += 8) {
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) acc[c] = wst[Cout * KK + c0 + c];
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+      const float* wr = wst + (c0 + c) * KK;
+#pragma unroll
+      for (int t = 0; t < KK; t++) acc[c] = fmaf(in[t], wr[t], acc[c]);
+    }
+    uint4 o;
+    __half2* oh = (__half2*)&o;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      float a0 = acc[2 * q], a1 = acc[2 * q + 1];
+      if (act == 1) { a0 = __fdividef(a0, 1.f + __expf(-a0)); a1 = __fdividef(a1, 1.f + __expf(-a1)); }
+      oh[q] = __floats2half2_rn(a0, a1);
+    }
+    *(uint4*)(yp + c0) = o;
+  }
+}
+
 // ---------------- depthwise conv ----------------
-// Thread = one output pixel x 8 channels, 16-byte loads; weights OHWI [C][k][k][1].
-// Replaces k_dwconv8 (engine/engine.cu:535-580), including its fused residual.
+// Thread = one output pixel x 8 channels, 16-byte activation loads.  The block first stages
+// the OHWI [C][k][k][1] weights transposed to [k*k][C] in shared memory, so each tap's 8
+// channel weights are one 16-byte shared load.  Replaces k_dwconv8 (engine/engine.cu:535-580,
+// which repacks the weights on the host at load time), including its fused residual.
 __global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restrict__ w,
                               const float* __restrict__ b, int k, int s, int p, int act,
                               long long total) {
+  extern __shared__ __align__(16) __half wt[];   // [k*k][C]
+  const int C = y.C, KK = k * k;
+  for (int i = threadIdx.x; i < C * KK; i += blockDim.x) {
+    const int c = i / KK, t = i - c * KK;
+    wt[t * C + c] = w[i];
+  }
+  __syncthreads();
   long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int cg = y.C >> 3;
+  const int cg = C >> 3;
   if (idx >= total) return;
   const int g = (int)(idx % cg);
   const long long pix = idx / cg;
@@ -85,7 +149,6 @@ __global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restric
   const int HW = y.H * y.W;
   const int img = (int)(pix / HW), rem = (int)(pix - (long long)img * HW);
   const int oy = rem / y.W, ox = rem - oy * y.W;
-  const int KK = k * k;
   float acc[8];
   {
     const float4 b0 = *(const float4*)(b + c), b1 = *(const float4*)(b + c + 4);
@@ -99,11 +162,15 @@ __global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restric
       const int ix = ox * s - p + kx;
       if (ix < 0 || ix >= x.W) continue;
       const uint4 xv = *(const uint4*)(x.p + x.pix(img, iy, ix) + c);
-      const __half* xh = (const __half*)&xv;
-      const int t = ky * k + kx;
+      const uint4 wv = *(const uint4*)(wt + (ky * k + kx) * C + c);
+      const __half2* xh = (const __half2*)&xv;
+      const __half2* wh = (const __half2*)&wv;
 #pragma unroll
-      for (int q = 0; q < 8; q++)
-        acc[q] = fmaf(__half2float(xh[q]), __half2float(w[(size_t)(c + q) * KK + t]), acc[q]);
+      for (int q = 0; q < 4; q++) {
+        const float2 fx = __half22float2(xh[q]), fw = __half22float2(wh[q]);
+        acc[2 * q] = fmaf(fx.x, fw.x, acc[2 * q]);
+        acc[2 * q + 1] = fmaf(fx.y, fw.y, acc[2 * q + 1]);
+      }
     }
   }
   float rv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -251,6 +318,15 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     if (!view_vec8(x)) return YK_EINVAL;
     return conv_tc(x, y, res, p, st);
   }
+  if (p->groups == 1 && p->Cin == 3 && p->k == 3 && !res && p->Cout % 8 == 0 &&
+      p->Cout <= 256) {
+    const size_t smem = ((size_t)p->Cout * 27 + p->Cout) * sizeof(float);
+    conv_stem3_kernel<3><<<nblk(npix, 128), 128, smem, st>>>(
+        dview(*x), dview(*y), (const __half*)p->weight, p->bias, p->Cout, p->s, p->p, p->act,
+        npix);
+    note_launch();
+    return check_launch("conv_stem3");
+  }
   if (p->groups == 1 && p->Cin <= 4) {
     if (res || p->Cout % 8) return YK_EUNSUP;
     const int KK = p->k * p->k * p->Cin;
@@ -265,7 +341,14 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     if (!view_vec8(x)) return YK_EINVAL;
     DView r = res ? dview(*res) : DView{nullptr, 0, 0, 0, 0};
     const long long total = npix * (p->Cout / 8);
-    dwconv_kernel<<<nblk(total, 256), 256, 0, st>>>(dview(*x), dview(*y), r,
+    const size_t smem = (size_t)p->Cout * p->k * p->k * sizeof(__half);
+    if (smem > 96 * 1024) return YK_EUNSUP;
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(dwconv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      attr = true;
+    }
+    dwconv_kernel<<<nblk(total, 256), 256, smem, st>>>(dview(*x), dview(*y), r,
                                                     (const __half*)p->weight, p->bias, p->k,
                                                     p->s, p->p, p->act, total);
     note_launch();

@@ -7,18 +7,31 @@
 // engine/engine.cu:270-358), so Cin = 8/16 layers waste nothing.  W is the OHWI weight
 // tensor, already [N][K] K-contiguous.
 //
-// CTA = 160 threads, one 128 x BN output tile:
-//   warps 0-3  producers: gather 16-byte chunks of A (im2col with zero padding) and W with
-//              cp.async into a STAGES-deep ring of 128-byte-swizzled K-major tiles
-//              (BK = 64), then signal "full" on an mbarrier once their copies landed;
-//              after the mainloop the same warps are the epilogue (warp w owns TMEM lanes
-//              32w..32w+31 = output rows), reading the fp32 accumulator with tcgen05.ld and
-//              applying bias, SiLU, residual and the fp16 channel-slice store.
-//   warp 4     allocates TMEM (BN columns) and one lane issues tcgen05.mma (M=128, N=BN,
-//              K=16, four per stage) and tcgen05.commit to release each stage and finally
-//              signal the epilogue.
-// Every mbarrier wait is bounded (common.cuh kWaitNs); on timeout the CTA records an error
-// in the device error word, drains its copies, frees TMEM and returns.
+// Persistent, warp-specialised CTA (416 threads, one per SM), 128 x BN output tiles taken
+// round-robin:
+//   warps 0-3  producers, into a STAGES-deep ring of 128-byte-swizzled K-major tiles (BK=64):
+//              W tiles come by TMA (2-D tensor map over [Cout][K], zero fill past the edges,
+//              no cluster sharing); A tiles with Cin >= 64 come by TMA too (2-D for 1x1
+//              stride-1 convs, the TMA im2col mode for k x k / stride s, where one stage is
+//              one 64-channel block of one filter tap); thinner A tiles are gathered in 16-byte
+//              cp.async chunks whose completion arrives on the stage's mbarrier in hardware
+//              (cp.async.mbarrier.arrive.noinc), so producers never stall on their own loads.
+//   warp 12    allocates TMEM (two BN-column fp32 accumulators) and one lane issues
+//              tcgen05.mma (M=128, N=BN, K=16, four per stage), releasing each stage with
+//              tcgen05.commit and handing a finished accumulator to the epilogue.
+//   warps 4-11 epilogue, two groups of four warps taking alternate tiles (warp w reads TMEM
+//              lanes 32(w%4)..): tcgen05.ld of the accumulator, bias (cached in shared
+//              memory), SiLU, residual, fp16 store into the output channel slice; then free the
+//              accumulator.  A ring of 2-4 TMEM accumulators lets the epilogues of earlier
+//              tiles overlap the mainloop of later ones.
+// Every mbarrier wait is bounded (common.cuh kWaitNs): on timeout the CTA records an error
+// in the device error word, raises an abort flag that every role polls, drains its copies,
+// frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 
 namespace yk {
@@ -33,129 +46,196 @@ struct ConvArgs {
   const __half* w;
   const float* bias;
   int Cin, Cout, k, s, p, act;
-  int Ktot, M, nk, ntn;
+  int Ktot, M, nk, ntn, ntiles;
+  int tmaA;          // A tiles: 0 cp.async gather, 1 TMA 2-D (1x1 s1 p0), 2 TMA im2col
+  int ncb;           // im2col mode: 64-channel blocks per filter tap
+  int dbg;           // experiment switches (0 in production)
 };
 
 constexpr int kProducers = 128;
-constexpr int kThreads = 160;
+constexpr int kEpiGroup = 128;      // one epilogue group = 4 warps = all 128 tile rows
+constexpr int kBiasSmem = 2048;     // bias floats cached in shared memory
+constexpr int kThreads = 416;
+constexpr int kMmaWarp = 12;
 
 template <int BN, int STAGES>
 struct TcCfg {
   static constexpr int kABytes = 128 * 128;
   static constexpr int kBBytes = BN * 128;
   static constexpr int kStage = kABytes + kBBytes;
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  static constexpr size_t kSmem = (size_t)STAGES * kStage + 1024 + 256;
+  static constexpr int kAccCols = BN < 32 ? 32 : BN;
+  static constexpr int kNacc = BN >= 256 ? 2 : 4;        // TMEM accumulator ring
+  static constexpr int kTmemCols = kNacc * kAccCols;     // <= 512
+  static constexpr size_t kSmem = (size_t)STAGES * kStage + 1024 + 256 + kBiasSmem * 4;
 };
 
 __device__ __forceinline__ uint32_t sw_off(int r, int c) {
   return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+// im2col-mode TMA load (NHWC, 4-D): 128 output pixels starting at input coordinate (w, h, n)
+// for filter tap (kx, ky), 64 channels from channel c; the tensor map carries the padding
+// box and the conv stride.
+__device__ __forceinline__ void tma_load_im2col(uint32_t dst, const CUtensorMap* map,
+                                                uint32_t bar, int c, int w, int h, int n,
+                                                uint16_t kx, uint16_t ky) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(kx), "h"(ky)
+      : "memory");
+}
+
+// 2-D tiled TMA load into this CTA's shared memory, completing `bytes` on the mbarrier.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"((uint64_t)map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a) {
+__global__ void __launch_bounds__(kThreads, 1)
+conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmA) {
   using Cfg = TcCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t bar_base = base + STAGES * Cfg::kStage;
-  // barriers: full[0..S), empty[S..2S), accum[2S]; tmem slot after them
+  // barriers: full[S], empty[S], tfull[NACC], tempty[NACC]; the TMEM slot, the abort flag;
+  // then the bias cache
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
-  const uint32_t accum_bar = bar_base + 8u * (2 * STAGES);
-  const uint32_t tslot = bar_base + 8u * (2 * STAGES + 1);
-  uint32_t* tslot_ptr = (uint32_t*)(smem_raw + (tslot - raw));
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * STAGES + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * STAGES + Cfg::kNacc + b); };
+  const uint32_t tslot = bar_base + 8u * (2 * STAGES + 2 * Cfg::kNacc);
+  volatile uint32_t* tslot_ptr = (volatile uint32_t*)(smem_raw + (tslot - raw));
+  volatile int* abort_flag = (volatile int*)(smem_raw + (tslot - raw) + 8);
+  float* bias_s = (float*)(smem_raw + (base - raw) + STAGES * Cfg::kStage + 256);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int nt = blockIdx.x % a.ntn;
-  const int mt = blockIdx.x / a.ntn;
-  const int m0 = mt * 128, n0 = nt * BN;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; s++) {
-      mbar_init(full_bar(s), kProducers);
+      mbar_init(full_bar(s), a.tmaA ? 1 : kProducers + 1);
       mbar_init(empty_bar(s), 1);
     }
-    mbar_init(accum_bar, 1);
+    for (int b = 0; b < Cfg::kNacc; b++) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), kEpiGroup);
+    }
+    *abort_flag = 0;
     mbar_fence_init();
   }
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tslot, Cfg::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *(volatile uint32_t*)tslot_ptr;
+  const uint32_t tmem = *tslot_ptr;
 
   if (warp < 4) {
     // ---------------- producers ----------------
     const int c = tid & 7, r0 = tid >> 3;
     const int HWo = a.Ho * a.Wo;
-    int ybase[8], xbase[8];
-    const __half* rowp[8];
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      int m = m0 + r0 + 16 * i;
-      bool ok = m < a.M;
-      int mm = ok ? m : 0;
-      int img = mm / HWo, rem = mm - img * HWo;
-      int oy = rem / a.Wo, ox = rem - oy * a.Wo;
-      ybase[i] = ok ? oy * a.s - a.p : -(1 << 28);   // invalid rows never pass the bounds test
-      xbase[i] = ox * a.s - a.p;
-      rowp[i] = a.x + (size_t)img * a.H * a.W * a.xs;
-    }
     const uint32_t offA = sw_off(r0, c);
-    bool ok_all = true;
-    int kb = 0;
-    for (; kb < a.nk; kb++) {
-      const int s = kb % STAGES, u = kb / STAGES;
-      if (u > 0 && !mbar_wait(empty_bar(s), (u - 1) & 1, 0x101)) { ok_all = false; break; }
-      const uint32_t sA = base + s * Cfg::kStage, sB = sA + Cfg::kABytes;
-      const int kk = kb * 64 + c * 8;
-      const bool kval = kk < a.Ktot;
-      const int tap = kval ? kk / a.Cin : 0;
-      const int ci = kk - tap * a.Cin;
-      const int ky = tap / a.k, kx = tap - ky * a.k;
+    uint32_t g = 0;   // global stage counter across tiles
+    const bool gather = !a.tmaA;
+    for (int t = blockIdx.x; t < a.ntiles && !*abort_flag && (gather || tid == 0); t += gridDim.x) {
+      const int m0 = (t / a.ntn) * 128, n0 = (t % a.ntn) * BN;
+      int w0 = 0, h0 = 0, i0 = 0;      // im2col start: input coords of output pixel m0
+      if (a.tmaA == 2) {
+        i0 = m0 / HWo;
+        const int rem = m0 - i0 * HWo, oy = rem / a.Wo;
+        h0 = oy * a.s - a.p;
+        w0 = (rem - oy * a.Wo) * a.s - a.p;
+      }
+      int ybase[8], xbase[8];
+      const __half* rowp[8];
 #pragma unroll
       for (int i = 0; i < 8; i++) {
-        const int iy = ybase[i] + ky, ix = xbase[i] + kx;
-        const bool ok = kval && (unsigned)iy < (unsigned)a.H && (unsigned)ix < (unsigned)a.W;
-        const __half* src = ok ? rowp[i] + ((size_t)iy * a.W + ix) * a.xs + ci : a.x;
-        cp_async16(sA + offA + (uint32_t)(i * 2048), src, ok ? 16u : 0u);
+        const int m = m0 + r0 + 16 * i;
+        const bool ok = m < a.M;
+        const int mm = ok ? m : 0;
+        const int img = mm / HWo, rem = mm - img * HWo;
+        const int oy = rem / a.Wo, ox = rem - oy * a.Wo;
+        ybase[i] = ok ? oy * a.s - a.p : -(1 << 28);   // invalid rows fail the bounds test
+        xbase[i] = ox * a.s - a.p;
+        rowp[i] = a.x + (size_t)img * a.H * a.W * a.xs;
       }
+      for (int kb = 0; kb < a.nk; kb++, g++) {
+        const int s = g % STAGES;
+        const uint32_t u = g / STAGES;
+        if (u > 0 && !mbar_wait(empty_bar(s), (u - 1) & 1, 0x101)) { *abort_flag = 1; break; }
+        const uint32_t sA = base + s * Cfg::kStage, sB = sA + Cfg::kABytes;
+        if (tid == 0) {
+          mbar_expect_tx(full_bar(s), Cfg::kBBytes + (gather ? 0 : Cfg::kABytes));
+          if (a.tmaA == 2) {
+            const int tap = kb / a.ncb, cb = kb - tap * a.ncb;
+            const int ky = tap / a.k, kx = tap - ky * a.k;
+            tma_load_2d(sB, &tmB, full_bar(s), tap * a.Cin + cb * 64, n0);
+            tma_load_im2col(sA, &tmA, full_bar(s), cb * 64, w0, h0, i0, (uint16_t)kx, (uint16_t)ky);
+          } else {
+            tma_load_2d(sB, &tmB, full_bar(s), kb * 64, n0);
+            if (!gather) tma_load_2d(sA, &tmA, full_bar(s), kb * 64, m0);
+          }
+        }
+        if (!gather) continue;
+        if (a.dbg & 2) { mbar_arrive(full_bar(s)); continue; }
+        const int kk = kb * 64 + c * 8;
+        const bool kval = kk < a.Ktot;
+        const int tap = kval ? kk / a.Cin : 0;
+        const int ci = kk - tap * a.Cin;
+        const int ky = tap / a.k, kx = tap - ky * a.k;
 #pragma unroll
-      for (int j = 0; j < BN / 16; j++) {
-        const int n = n0 + r0 + 16 * j;
-        const bool ok = kval && n < a.Cout;
-        const __half* src = ok ? a.w + (size_t)n * a.Ktot + kk : a.w;
-        cp_async16(sB + sw_off(r0 + 16 * j, c), src, ok ? 16u : 0u);
-      }
-      cp_async_commit();
-      // signal stage kb-2 once its copies have landed (two stages stay in flight)
-      if (kb >= 2) {
-        cp_async_wait<2>();
-        fence_proxy_async();
-        mbar_arrive(full_bar((kb - 2) % STAGES));
+        for (int i = 0; i < 8; i++) {
+          const int iy = ybase[i] + ky, ix = xbase[i] + kx;
+          const bool ok = kval && (unsigned)iy < (unsigned)a.H && (unsigned)ix < (unsigned)a.W;
+          const __half* src = ok ? rowp[i] + ((size_t)iy * a.W + ix) * a.xs + ci : a.x;
+          cp_async16(sA + offA + (uint32_t)(i * 2048), src, ok ? 16u : 0u);
+        }
+        cp_async_arrive_noinc(full_bar(s));   // arrives when this thread's copies land
       }
     }
     cp_async_wait<0>();
-    fence_proxy_async();
-    if (ok_all) {
-      for (int t = (kb >= 2 ? kb - 2 : 0); t < kb; t++) mbar_arrive(full_bar(t % STAGES));
-    }
-
+  } else if (warp < kMmaWarp) {
     // ---------------- epilogue ----------------
-    const bool acc_ok = mbar_wait(accum_bar, 0, 0x103);
-    tc_fence_after();
-    const int row = warp * 32 + lane;
-    const int m = m0 + row;
-    const bool mok = m < a.M && acc_ok;
-    __half* yrow = a.y + (size_t)(mok ? m : 0) * a.ys;
-    const __half* rrow = a.res ? a.res + (size_t)(mok ? m : 0) * a.rs : nullptr;
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-    if (acc_ok) {
+    const int sp = warp & 3;              // TMEM sub-partition this warp may read
+    const int grp = (warp - 4) >> 2;      // epilogue group: takes every other tile
+    const int row = sp * 32 + lane;
+    const bool bias_cached = a.Cout <= kBiasSmem;
+    if (bias_cached)
+      for (int i = tid - 128; i < a.Cout; i += 256) bias_s[i] = a.bias[i];
+    asm volatile("bar.sync 1, 256;" ::: "memory");   // epilogue warps only
+    const float* bias = bias_cached ? bias_s : a.bias;
+    uint32_t li = 0;
+    for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, li++) {
+      if ((int)(li & 1) != grp) continue;
+      const int acc = li % Cfg::kNacc;
+      const uint32_t use = li / Cfg::kNacc;
+      if (!mbar_wait(tfull_bar(acc), use & 1, 0x103)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const int m0 = (t / a.ntn) * 128, n0 = (t % a.ntn) * BN;
+      const int m = m0 + row;
+      const bool mok = m < a.M;
+      __half* yrow = a.y + (size_t)(mok ? m : 0) * a.ys;
+      const __half* rrow = a.res ? a.res + (size_t)(mok ? m : 0) * a.rs : nullptr;
+      const uint32_t trow = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kAccCols;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 16; cc++) {
         const int n = n0 + cc * 16;
@@ -163,27 +243,27 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a) 
         uint32_t r[16];
         tmem_ld16(trow + cc * 16, r);
         tmem_ld_wait();
-        if (!mok) continue;
+        if (!mok || (a.dbg & 1)) continue;
 #pragma unroll
         for (int h = 0; h < 2; h++) {
           const int nn = n + 8 * h;
           if (nn >= a.Cout) break;
-          const float4 b0 = __ldg((const float4*)(a.bias + nn));
-          const float4 b1 = __ldg((const float4*)(a.bias + nn + 4));
+          const float4 b0 = *(const float4*)(bias + nn);
+          const float4 b1 = *(const float4*)(bias + nn + 4);
           float v[8] = {__uint_as_float(r[8 * h + 0]) + b0.x, __uint_as_float(r[8 * h + 1]) + b0.y,
                         __uint_as_float(r[8 * h + 2]) + b0.z, __uint_as_float(r[8 * h + 3]) + b0.w,
                         __uint_as_float(r[8 * h + 4]) + b1.x, __uint_as_float(r[8 * h + 5]) + b1.y,
                         __uint_as_float(r[8 * h + 6]) + b1.z, __uint_as_float(r[8 * h + 7]) + b1.w};
           if (a.act == 1) {
 #pragma unroll
-            for (int q = 0; q < 8; q++) v[q] = silu(v[q]);
+            for (int q = 0; q < 8; q++) v[q] = __fdividef(v[q], 1.f + __expf(-v[q]));
           }
           if (rrow) {
-            uint4 rv = *(const uint4*)(rrow + nn);
+            const uint4 rv = *(const uint4*)(rrow + nn);
             const __half2* rh = (const __half2*)&rv;
 #pragma unroll
             for (int q = 0; q < 4; q++) {
-              float2 f = __half22float2(rh[q]);
+              const float2 f = __half22float2(rh[q]);
               v[2 * q] += f.x;
               v[2 * q + 1] += f.y;
             }
@@ -195,37 +275,106 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a) 
           *(uint4*)(yrow + nn) = o;
         }
       }
+      tc_fence_before();
+      mbar_arrive(tempty_bar(acc));
     }
-    tc_fence_before();
   } else if (lane == 0) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer (warp 12) ----------------
     constexpr uint32_t idesc = idesc_f16_m128(BN);
-    bool ok = true;
-    for (int kb = 0; kb < a.nk; kb++) {
-      const int s = kb % STAGES;
-      if (!mbar_wait(full_bar(s), (kb / STAGES) & 1, 0x102)) { ok = false; break; }
+    uint32_t g = 0, li = 0;
+    for (int t = blockIdx.x; t < a.ntiles && !*abort_flag; t += gridDim.x, li++) {
+      const int acc = li % Cfg::kNacc;
+      const uint32_t use = li / Cfg::kNacc;
+      if (use > 0 && !mbar_wait(tempty_bar(acc), (use - 1) & 1, 0x104)) { *abort_flag = 1; break; }
       tc_fence_after();
-      const uint32_t sA = base + s * Cfg::kStage, sB = sA + Cfg::kABytes;
+      const uint32_t d = tmem + acc * Cfg::kAccCols;
+      bool ok = true;
+      for (int kb = 0; kb < a.nk; kb++, g++) {
+        const int s = g % STAGES;
+        if (!mbar_wait(full_bar(s), (g / STAGES) & 1, 0x102)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sA = base + s * Cfg::kStage, sB = sA + Cfg::kABytes;
 #pragma unroll
-      for (int kk = 0; kk < 4; kk++)
-        tc_mma_f16(tmem, sw128_desc(sA + kk * 32), sw128_desc(sB + kk * 32), idesc,
-                   (kb | kk) != 0);
-      tc_commit(empty_bar(s));
+        for (int kk = 0; kk < 4; kk++)
+          tc_mma_f16(d, sw128_desc(sA + kk * 32), sw128_desc(sB + kk * 32), idesc,
+                     (kb | kk) != 0);
+        tc_commit(empty_bar(s));
+      }
+      if (!ok) { *abort_flag = 1; break; }
+      tc_commit(tfull_bar(acc));
     }
-    if (ok) tc_commit(accum_bar);
   }
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
 }
 
+static int g_num_sms[64] = {};
+
+// 2-D fp16 tensor map with a 64-element (128-byte) inner box and the 128-byte swizzle that
+// matches the UMMA K-major layout; out-of-range elements read as zero.
+static bool encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
+                      uint64_t row_bytes, uint32_t box_outer) {
+  static PFN_cuTensorMapEncodeTiled encode = nullptr;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+              cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return false;
+      encode = (PFN_cuTensorMapEncodeTiled)fn;
+    }
+  }
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {64, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// im2col tensor map over the NHWC input view: dims {C, W, H, N}, the padding bounding box
+// [-p, W-1+p-(k-1)] per spatial dim, conv stride as the traversal stride, 64 channels x 128
+// output pixels per load, 128-byte swizzle; outside the image reads as zero.
+static bool encode_im2col(CUtensorMap* m, const ConvArgs& a) {
+  static PFN_cuTensorMapEncodeIm2col encode = nullptr;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &fn, cudaEnableDefault, &q) !=
+              cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return false;
+      encode = (PFN_cuTensorMapEncodeIm2col)fn;
+    }
+  }
+  const uint64_t batch = (uint64_t)a.M / ((uint64_t)a.Ho * a.Wo);
+  const cuuint64_t dims[4] = {(cuuint64_t)a.Cin, (cuuint64_t)a.W, (cuuint64_t)a.H, batch};
+  const cuuint64_t strides[3] = {(cuuint64_t)a.xs * 2, (cuuint64_t)a.W * a.xs * 2,
+                                 (cuuint64_t)a.H * a.W * a.xs * 2};
+  const int lower[2] = {-a.p, -a.p};
+  const int upper[2] = {a.p - (a.k - 1), a.p - (a.k - 1)};
+  const cuuint32_t estr[4] = {1, (cuuint32_t)a.s, (cuuint32_t)a.s, 1};
+  return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(a.x), dims, strides,
+                lower, upper, 64, 128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int STAGES>
 static int launch_tc(const ConvArgs& a, cudaStream_t st) {
   using Cfg = TcCfg<BN, STAGES>;
-  static bool attr_set = false;   // per process; the attribute is per function, all devices
+  static bool attr_set = false;   // the attribute is per function, for all devices
   if (!attr_set) {
     if (cudaFuncSetAttribute(conv_tc_kernel<BN, STAGES>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -233,16 +382,26 @@ static int launch_tc(const ConvArgs& a, cudaStream_t st) {
       return check_launch("conv_tc attr");
     attr_set = true;
   }
-  const long long mtiles = (a.M + 127) / 128;
-  const long long blocks = mtiles * a.ntn;
-  if (blocks > 0x7fffffffLL) return YK_EUNSUP;
-  conv_tc_kernel<BN, STAGES><<<(unsigned)blocks, kThreads, Cfg::kSmem, st>>>(a);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return YK_EUNSUP;
+  if (!g_num_sms[dev]) cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int grid = a.ntiles < g_num_sms[dev] ? a.ntiles : g_num_sms[dev];
+  CUtensorMap tmB, tmA;
+  memset(&tmA, 0, sizeof tmA);
+  if (!encode_2d(&tmB, a.w, (uint64_t)a.Ktot, (uint64_t)a.Cout, (uint64_t)a.Ktot * 2, BN))
+    return YK_EUNSUP;
+  if (a.tmaA == 1 && !encode_2d(&tmA, a.x, (uint64_t)a.Cin, (uint64_t)a.M, (uint64_t)a.xs * 2, 128))
+    return YK_EUNSUP;
+  if (a.tmaA == 2 && !encode_im2col(&tmA, a))
+    return YK_EUNSUP;
+  conv_tc_kernel<BN, STAGES><<<grid, kThreads, Cfg::kSmem, st>>>(a, tmB, tmA);
   note_launch();
   return check_launch("conv_tc");
 }
 
-// Heuristic N tile: widest tile that does not waste half of it, shrunk when the grid would
-// leave most of the 148 SMs idle.
+// Heuristic N tile: widest tile that does not waste half of it, shrunk when the tile count
+// would leave most of the 148 SMs idle.
 int pick_tile(int M, int Cout) {
   int bn = Cout <= 32 ? 32 : Cout <= 64 ? 64 : Cout <= 128 ? 128 : (Cout % 256 == 0 ? 256 : 128);
   long long mt = (M + 127) / 128;
@@ -267,10 +426,22 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   a.nk = (a.Ktot + 63) / 64;
   int bn = p->tile ? p->tile : pick_tile(a.M, a.Cout);
   a.ntn = (a.Cout + bn - 1) / bn;
+  const long long nt = (long long)((a.M + 127) / 128) * a.ntn;
+  if (nt > 0x7fffffffLL) return YK_EUNSUP;
+  a.ntiles = (int)nt;
+  { const char* e = getenv("YK_DBG"); a.dbg = e ? atoi(e) : 0; }
+  const bool tma_ok = p->Cin >= 64 && ((uintptr_t)a.x & 15) == 0 && (a.xs % 8) == 0;
+  a.tmaA = 0;
+  a.ncb = (p->Cin + 63) / 64;
+  if (tma_ok && p->k == 1 && p->s == 1 && p->p == 0) a.tmaA = 1;
+  else if (tma_ok && p->p < 128 && p->k - 1 - p->p < 128 && p->s <= 8 && !(a.dbg & 4)) {
+    a.tmaA = 2;
+    a.nk = p->k * p->k * a.ncb;   // one 64-channel block of one filter tap per stage
+  }
   switch (bn) {
-    case 32: return launch_tc<32, 5>(a, st);
-    case 64: return launch_tc<64, 4>(a, st);
-    case 128: return launch_tc<128, 4>(a, st);
+    case 32: return launch_tc<32, 8>(a, st);
+    case 64: return launch_tc<64, 8>(a, st);
+    case 128: return launch_tc<128, 6>(a, st);
     case 256: return launch_tc<256, 4>(a, st);
     default: return YK_EINVAL;
   }
