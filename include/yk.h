@@ -42,7 +42,7 @@ typedef struct {
   int act;              // 0 identity, 1 SiLU
   int Cin, Cout;
   int tile;             // tensor-core N tile (0 = heuristic, else 32/64/128/256)
-  int splitk;           // reserved, 0
+  int msub;             // stacked 128-row sub-tiles per CTA tile (0 = heuristic, 1/2/4)
 } YkConv;
 
 // Convolution with bias, activation, optional residual (y = act(conv(x)+b) + res) written

@@ -28,7 +28,8 @@ def vw(rt, buf, coff, Cv):
     return rt.view(buf.data_ptr(), B, H, W, Ct, coff, Cv)
 
 
-def run_conv(lib, rt, x, w, b, k, s, p, act, groups=1, res=None, tile=0, xc=(0, None), yc=(0, 0)):
+def run_conv(lib, rt, x, w, b, k, s, p, act, groups=1, res=None, tile=0, msub=0, xc=(0, None),
+             yc=(0, 0)):
     """x: NHWC fp16 buffer (view = channels xc[0]:xc[0]+Cin); output written into a fresh
     buffer with yc = (coff, extra channels) to exercise channel-slice stores."""
     B, H, W, _ = x.shape
@@ -38,7 +39,7 @@ def run_conv(lib, rt, x, w, b, k, s, p, act, groups=1, res=None, tile=0, xc=(0, 
     ybuf = torch.full((B, Ho, Wo, yc[0] + Cout + yc[1]), 7.0, dtype=torch.half, device=x.device)
     wt = w.permute(0, 2, 3, 1).contiguous().half()            # OHWI
     bt = b.float().contiguous()
-    prm = rt.YkConv(wt.data_ptr(), bt.data_ptr(), k, s, p, groups, act, Cin, Cout, tile, 0)
+    prm = rt.YkConv(wt.data_ptr(), bt.data_ptr(), k, s, p, groups, act, Cin, Cout, tile, msub)
     xv = vw(rt, x, xc[0], Cin)
     yv = vw(rt, ybuf, yc[0], Cout)
     rv = vw(rt, res, 0, Cout) if res is not None else None
@@ -77,12 +78,16 @@ CONV_CASES = [
     (2, 12, 12, 96, 64, 3, 1, 1),      # im2col TMA, Cin not a multiple of 64
     (3, 13, 9, 64, 64, 3, 2, 1),       # im2col TMA, stride 2, odd sizes, tiles across images
     (2, 7, 7, 128, 32, 3, 1, 1),
+    (2, 20, 20, 32, 64, 1, 1, 0),      # narrow-block TMA, 1x1
+    (2, 21, 19, 16, 32, 3, 2, 1),      # narrow-block TMA im2col, stride 2
+    (3, 16, 16, 32, 32, 3, 1, 1),
 ]
 
 
 @pytest.mark.parametrize("case", CONV_CASES)
-@pytest.mark.parametrize("tile", [0, 64, 128, 256])
-def test_conv_tc(lib, cuda, case, tile):
+@pytest.mark.parametrize("tile,msub", [(0, 0), (32, 4), (64, 1), (64, 2), (64, 4), (128, 1),
+                                       (128, 2), (256, 1)])
+def test_conv_tc(lib, cuda, case, tile, msub):
     from yolo11_cu_b200 import runtime as rt
     B, H, W, Cin, Cout, k, s, p = case
     g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000)
@@ -90,7 +95,7 @@ def test_conv_tc(lib, cuda, case, tile):
     w = (torch.randn(Cout, Cin, k, k, generator=g) / (Cin * k * k) ** 0.5)
     b = torch.randn(Cout, generator=g) * 0.1
     out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), k, s, p, act=1, tile=tile,
-                        xc=(8, None), yc=(8, 8))
+                        msub=msub, xc=(8, None), yc=(8, 8))
     assert rel(out, ref) < TOL
 
 

@@ -159,6 +159,15 @@ __device__ __forceinline__ void tmem_ld_wait() {
 
 // Shared-memory matrix descriptor: K-major operand in the 128-byte swizzle layout
 // (8-row x 128-byte atoms, 1024-byte aligned; SBO = 1024 B between 8-row groups).
+// Same for a K-major operand whose rows are cb_bytes = 128 / 64 / 32 wide (swizzle span equal
+// to the row): atoms of 8 rows, SBO = 8 * cb_bytes.
+template <int CB_BYTES>
+__device__ __forceinline__ uint64_t swz_desc(uint32_t saddr) {
+  constexpr uint64_t layout = CB_BYTES == 128 ? 2 : CB_BYTES == 64 ? 4 : 6;
+  constexpr uint64_t sbo = (8 * CB_BYTES) >> 4;
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (sbo << 32) | (1ull << 46) |
+         (layout << 61);
+}
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
          (2ull << 61);

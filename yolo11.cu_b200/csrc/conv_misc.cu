@@ -191,6 +191,96 @@ __global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restric
   *(uint4*)(y.p + (size_t)pix * y.stride + c) = o;
 }
 
+// 3x3 depthwise conv, register-blocked: thread = 8 channels x 4 consecutive output pixels
+// of one row.  The 72 filter weights of its channels live in registers, each input column of
+// the 3 x (3*S + 1 ... ) window is loaded once (16 bytes) and feeds every output it touches.
+// Index arithmetic is 32-bit (I = unsigned) whenever the element count allows it.
+template <int S, typename I>
+__global__ void __launch_bounds__(256) dwconv3_kernel(DView x, DView y, DView r,
+                                                      const __half* __restrict__ w,
+                                                      const float* __restrict__ b, int act,
+                                                      int batch) {
+  constexpr int PX = 4, NIN = (PX - 1) * S + 3;
+  const int cg = y.C >> 3, nxb = (y.W + PX - 1) / PX;
+  const I total = (I)batch * y.H * nxb * cg;
+  const I idx = (I)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int g = (int)(idx % cg);
+  I rr = idx / cg;
+  const int xb = (int)(rr % nxb);
+  rr /= nxb;
+  const int oy = (int)(rr % y.H), img = (int)(rr / y.H);
+  const int c = g << 3, ox0 = xb * PX;
+  float wr[9][8];
+#pragma unroll
+  for (int q = 0; q < 8; q++)
+#pragma unroll
+    for (int t = 0; t < 9; t++) wr[t][q] = __half2float(w[(c + q) * 9 + t]);
+  float acc[PX][8];
+  {
+    const float4 b0 = *(const float4*)(b + c), b1 = *(const float4*)(b + c + 4);
+#pragma unroll
+    for (int j = 0; j < PX; j++) {
+      acc[j][0] = b0.x; acc[j][1] = b0.y; acc[j][2] = b0.z; acc[j][3] = b0.w;
+      acc[j][4] = b1.x; acc[j][5] = b1.y; acc[j][6] = b1.z; acc[j][7] = b1.w;
+    }
+  }
+  const int ix0 = ox0 * S - 1;
+#pragma unroll
+  for (int ky = 0; ky < 3; ky++) {
+    const int iy = oy * S - 1 + ky;
+    if (iy < 0 || iy >= x.H) continue;
+    const __half* xrow = x.p + x.pix(img, iy, 0) + c;
+#pragma unroll
+    for (int u = 0; u < NIN; u++) {
+      const int ix = ix0 + u;
+      if (ix < 0 || ix >= x.W) continue;
+      const uint4 xv = *(const uint4*)(xrow + (size_t)ix * x.stride);
+      const __half2* xh = (const __half2*)&xv;
+      float xf[8];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const float2 f = __half22float2(xh[q]);
+        xf[2 * q] = f.x;
+        xf[2 * q + 1] = f.y;
+      }
+#pragma unroll
+      for (int j = 0; j < PX; j++) {
+        const int kx = u - j * S;   // compile-time after unrolling
+        if (kx < 0 || kx > 2) continue;
+#pragma unroll
+        for (int q = 0; q < 8; q++) acc[j][q] = fmaf(xf[q], wr[ky * 3 + kx][q], acc[j][q]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < PX; j++) {
+    const int ox = ox0 + j;
+    if (ox >= y.W) break;
+    const size_t pix = ((size_t)img * y.H + oy) * y.W + ox;
+    float rv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (r.p) {
+      const uint4 v = *(const uint4*)(r.p + pix * r.stride + c);
+      const __half2* h = (const __half2*)&v;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const float2 f = __half22float2(h[q]);
+        rv[2 * q] = f.x;
+        rv[2 * q + 1] = f.y;
+      }
+    }
+    uint4 o;
+    __half2* oh = (__half2*)&o;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      float a0 = acc[j][2 * q], a1 = acc[j][2 * q + 1];
+      if (act == 1) { a0 = silu(a0); a1 = silu(a1); }
+      oh[q] = __floats2half2_rn(a0 + rv[2 * q], a1 + rv[2 * q + 1]);
+    }
+    *(uint4*)(y.p + pix * y.stride + c) = o;
+  }
+}
+
 // ---------------- SPPF max pools ----------------
 __device__ __forceinline__ void hmax8(uint4& m, const uint4 v) {
   __half2* a = (__half2*)&m;
@@ -202,15 +292,16 @@ __device__ __forceinline__ void hmax8(uint4& m, const uint4 v) {
 // nr outputs: output j (j < nr) is the max over the (5+4j) x (5+4j) window clipped to the
 // image, i.e. j+1 chained 5x5/s1/p2 pools (max pooling composes: pool5(pool5(x)) = pool9(x)
 // with -inf padding).  Replaces k_maxpool5 (engine/engine.cu:672-695).
-__global__ void maxpool_kernel(DView x, DView y1, DView y2, DView y3, int nr, long long total) {
-  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+template <typename I>
+__global__ void maxpool_kernel(DView x, DView y1, DView y2, DView y3, int nr, I total) {
+  const I idx = (I)blockIdx.x * blockDim.x + threadIdx.x;
   const int cg = x.C >> 3;
   if (idx >= total) return;
   const int g = (int)(idx % cg);
-  const long long pix = idx / cg;
+  const I pix = idx / cg;
   const int c = g << 3;
   const int HW = x.H * x.W;
-  const int img = (int)(pix / HW), rem = (int)(pix - (long long)img * HW);
+  const int img = (int)(pix / HW), rem = (int)(pix - (I)img * HW);
   const int y0 = rem / x.W, x0 = rem - y0 * x.W;
   const uint4 ninf = make_uint4(0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u);
   uint4 m1 = ninf, m2 = ninf, m3 = ninf;
@@ -239,15 +330,16 @@ __global__ void maxpool_kernel(DView x, DView y1, DView y2, DView y3, int nr, lo
 // mode 0: nearest 2x upsample (engine/engine.cu:697-708); mode 1: pixel shuffle r=2 from
 // quadrant blocks (engine/engine.cu:713-725); mode 2: channel-slice copy (727-732).
 // Thread = one output pixel x 8 channels.
-__global__ void move8_kernel(DView x, DView y, int mode, long long total) {
-  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+template <typename I>
+__global__ void move8_kernel(DView x, DView y, int mode, I total) {
+  const I idx = (I)blockIdx.x * blockDim.x + threadIdx.x;
   const int cg = y.C >> 3;
   if (idx >= total) return;
   const int g = (int)(idx % cg);
-  const long long pix = idx / cg;
+  const I pix = idx / cg;
   const int c = g << 3;
   const int HW = y.H * y.W;
-  const int img = (int)(pix / HW), rem = (int)(pix - (long long)img * HW);
+  const int img = (int)(pix / HW), rem = (int)(pix - (I)img * HW);
   const int oy = rem / y.W, ox = rem - oy * y.W;
   const __half* src;
   if (mode == 0) src = x.p + x.pix(img, oy >> 1, ox >> 1) + c;
@@ -264,12 +356,13 @@ __global__ void copy_scalar_kernel(DView x, DView y, long long total) {
   y.p[(size_t)pix * y.stride + c] = x.p[(size_t)pix * x.stride + c];
 }
 
-__global__ void add8_kernel(DView a, DView b, DView y, long long total) {
-  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+template <typename I>
+__global__ void add8_kernel(DView a, DView b, DView y, I total) {
+  const I idx = (I)blockIdx.x * blockDim.x + threadIdx.x;
   const int cg = y.C >> 3;
   if (idx >= total) return;
   const int c = (int)(idx % cg) << 3;
-  const long long pix = idx / cg;
+  const I pix = idx / cg;
   const uint4 va = *(const uint4*)(a.p + (size_t)pix * a.stride + c);
   const uint4 vb = *(const uint4*)(b.p + (size_t)pix * b.stride + c);
   const __half2* ha = (const __half2*)&va;
@@ -341,6 +434,20 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     if (!view_vec8(x)) return YK_EINVAL;
     DView r = res ? dview(*res) : DView{nullptr, 0, 0, 0, 0};
     const long long total = npix * (p->Cout / 8);
+    if (p->k == 3 && p->p == 1 && (p->s == 1 || p->s == 2)) {
+      const long long t3 = (long long)y->batch * y->H * ((y->W + 3) / 4) * (p->Cout / 8);
+      const unsigned nb = nblk(t3, 256);
+      const __half* wp = (const __half*)p->weight;
+      if (t3 < (1LL << 31)) {
+        if (p->s == 1) dwconv3_kernel<1, unsigned><<<nb, 256, 0, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+        else dwconv3_kernel<2, unsigned><<<nb, 256, 0, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+      } else {
+        if (p->s == 1) dwconv3_kernel<1, long long><<<nb, 256, 0, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+        else dwconv3_kernel<2, long long><<<nb, 256, 0, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+      }
+      note_launch();
+      return check_launch("dwconv3");
+    }
     const size_t smem = (size_t)p->Cout * p->k * p->k * sizeof(__half);
     if (smem > 96 * 1024) return YK_EUNSUP;
     static bool attr = false;
@@ -361,7 +468,8 @@ int yk_maxpool5(const YkView* x, const YkView* y, yk_stream_t st) {
   if (!view_vec8(x) || !view_vec8(y) || !same_shape(x, y)) return YK_EINVAL;
   const long long total = (long long)x->batch * x->H * x->W * (x->C / 8);
   DView Y = dview(*y);
-  maxpool_kernel<<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), Y, Y, Y, 1, total);
+  if (total < (1LL << 31)) maxpool_kernel<unsigned><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), Y, Y, Y, 1, (unsigned)total);
+  else maxpool_kernel<long long><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), Y, Y, Y, 1, total);
   note_launch();
   return check_launch("maxpool5");
 }
@@ -372,15 +480,22 @@ int yk_maxpool5x3(const YkView* x, const YkView* y1, const YkView* y2, const YkV
       !same_shape(x, y1) || !same_shape(x, y2) || !same_shape(x, y3))
     return YK_EINVAL;
   const long long total = (long long)x->batch * x->H * x->W * (x->C / 8);
-  maxpool_kernel<<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y1),
-                                                                 dview(*y2), dview(*y3), 3, total);
+  if (total < (1LL << 31))
+    maxpool_kernel<unsigned><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(
+        dview(*x), dview(*y1), dview(*y2), dview(*y3), 3, (unsigned)total);
+  else
+    maxpool_kernel<long long><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(
+        dview(*x), dview(*y1), dview(*y2), dview(*y3), 3, total);
   note_launch();
   return check_launch("maxpool5x3");
 }
 
 static int move8(const YkView* x, const YkView* y, int mode, yk_stream_t st) {
   const long long total = (long long)y->batch * y->H * y->W * (y->C / 8);
-  move8_kernel<<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), mode, total);
+  if (total < (1LL << 31))
+    move8_kernel<unsigned><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), mode, (unsigned)total);
+  else
+    move8_kernel<long long><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), mode, total);
   note_launch();
   return check_launch("move8");
 }
@@ -412,7 +527,10 @@ int yk_add(const YkView* a, const YkView* b, const YkView* y, yk_stream_t st) {
   if (!view_vec8(a) || !view_vec8(b) || !view_vec8(y) || !same_shape(a, b) || !same_shape(a, y))
     return YK_EINVAL;
   const long long total = (long long)y->batch * y->H * y->W * (y->C / 8);
-  add8_kernel<<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*a), dview(*b), dview(*y), total);
+  if (total < (1LL << 31))
+    add8_kernel<unsigned><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*a), dview(*b), dview(*y), (unsigned)total);
+  else
+    add8_kernel<long long><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*a), dview(*b), dview(*y), total);
   note_launch();
   return check_launch("add");
 }

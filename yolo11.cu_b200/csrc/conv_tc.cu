@@ -7,8 +7,8 @@
 // engine/engine.cu:270-358), so Cin = 8/16 layers waste nothing.  W is the OHWI weight
 // tensor, already [N][K] K-contiguous.
 //
-// Persistent, warp-specialised CTA (416 threads, one per SM), 128 x BN output tiles taken
-// round-robin:
+// Persistent, warp-specialised CTA (416 threads, one per SM); a CTA tile is MT stacked
+// 128-row sub-tiles x BN columns, taken round-robin:
 //   warps 0-3  producers, into a STAGES-deep ring of 128-byte-swizzled K-major tiles (BK=64):
 //              W tiles come by TMA (2-D tensor map over [Cout][K], zero fill past the edges,
 //              no cluster sharing); A tiles with Cin >= 64 come by TMA too (2-D for 1x1
@@ -16,9 +16,10 @@
 //              one 64-channel block of one filter tap); thinner A tiles are gathered in 16-byte
 //              cp.async chunks whose completion arrives on the stage's mbarrier in hardware
 //              (cp.async.mbarrier.arrive.noinc), so producers never stall on their own loads.
-//   warp 12    allocates TMEM (two BN-column fp32 accumulators) and one lane issues
-//              tcgen05.mma (M=128, N=BN, K=16, four per stage), releasing each stage with
-//              tcgen05.commit and handing a finished accumulator to the epilogue.
+//   warp 12    allocates TMEM and one lane issues tcgen05.mma (M=128, N=BN, K=16): per stage
+//              four K steps x MT independent sub-tile accumulators (independent chains keep
+//              the tensor pipe busy when BN is small), then tcgen05.commit releases the stage;
+//              a finished tile's accumulators are handed to the epilogue.
 //   warps 4-11 epilogue, two groups of four warps taking alternate tiles (warp w reads TMEM
 //              lanes 32(w%4)..): tcgen05.ld of the accumulator, bias (cached in shared
 //              memory), SiLU, residual, fp16 store into the output channel slice; then free the
@@ -48,25 +49,28 @@ struct ConvArgs {
   int Cin, Cout, k, s, p, act;
   int Ktot, M, nk, ntn, ntiles;
   int tmaA;          // A tiles: 0 cp.async gather, 1 TMA 2-D (1x1 s1 p0), 2 TMA im2col
-  int ncb;           // im2col mode: 64-channel blocks per filter tap
-  int dbg;           // experiment switches (0 in production)
+  int ncb;           // TMA modes: CB-channel blocks per filter tap
 };
 
 constexpr int kProducers = 128;
-constexpr int kEpiGroup = 128;      // one epilogue group = 4 warps = all 128 tile rows
+constexpr int kEpiGroup = 128;      // one epilogue group = 4 warps = all 128 sub-tile rows
 constexpr int kBiasSmem = 2048;     // bias floats cached in shared memory
 constexpr int kThreads = 416;
 constexpr int kMmaWarp = 12;
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int MT, int CB>
 struct TcCfg {
-  static constexpr int kABytes = 128 * 128;
+  static constexpr int kTPS = 64 / CB;                      // K blocks (CB wide) per stage
+  static constexpr int kABytes = 128 * 128;                 // one 128-row sub-tile
   static constexpr int kBBytes = BN * 128;
-  static constexpr int kStage = kABytes + kBBytes;
-  static constexpr int kAccCols = BN < 32 ? 32 : BN;
-  static constexpr int kNacc = BN >= 256 ? 2 : 4;        // TMEM accumulator ring
-  static constexpr int kTmemCols = kNacc * kAccCols;     // <= 512
+  static constexpr int kStage = MT * kABytes + kBBytes;
+  static constexpr int kAccCols = BN < 32 ? 32 : BN;         // one sub-tile accumulator
+  static constexpr int kTileCols = MT * kAccCols;
+  static constexpr int kNacc = 512 / kTileCols >= 4 ? 4 : 2; // TMEM accumulator ring
+  static constexpr int kTmemCols = kNacc * kTileCols;        // <= 512, power of two
   static constexpr size_t kSmem = (size_t)STAGES * kStage + 1024 + 256 + kBiasSmem * 4;
+  static_assert(kTmemCols <= 512, "TMEM budget");
+  static_assert((size_t)STAGES * kStage + 1024 + 256 + kBiasSmem * 4 <= 232448, "smem budget");
 };
 
 __device__ __forceinline__ uint32_t sw_off(int r, int c) {
@@ -90,8 +94,7 @@ __device__ __forceinline__ void tma_load_im2col(uint32_t dst, const CUtensorMap*
       "l"((uint64_t)map), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(kx), "h"(ky)
       : "memory");
 }
-
-// 2-D tiled TMA load into this CTA's shared memory, completing `bytes` on the mbarrier.
+// 2-D tiled TMA load into this CTA's shared memory, completing its bytes on the mbarrier.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y) {
   asm volatile(
@@ -105,11 +108,12 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int MT, int CB>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmA) {
-  using Cfg = TcCfg<BN, STAGES>;
+  using Cfg = TcCfg<BN, STAGES, MT, CB>;
+  constexpr int kTM = 128 * MT;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -154,59 +158,84 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
     const int c = tid & 7, r0 = tid >> 3;
     const int HWo = a.Ho * a.Wo;
     const uint32_t offA = sw_off(r0, c);
+    const int batch = a.M / HWo;
     uint32_t g = 0;   // global stage counter across tiles
     const bool gather = !a.tmaA;
     for (int t = blockIdx.x; t < a.ntiles && !*abort_flag && (gather || tid == 0); t += gridDim.x) {
-      const int m0 = (t / a.ntn) * 128, n0 = (t % a.ntn) * BN;
-      int w0 = 0, h0 = 0, i0 = 0;      // im2col start: input coords of output pixel m0
+      const int m0 = (t / a.ntn) * kTM, n0 = (t % a.ntn) * BN;
+      int w0[MT], h0[MT], i0[MT];      // im2col start of each sub-tile (input coords of its pixel 0)
       if (a.tmaA == 2) {
-        i0 = m0 / HWo;
-        const int rem = m0 - i0 * HWo, oy = rem / a.Wo;
-        h0 = oy * a.s - a.p;
-        w0 = (rem - oy * a.Wo) * a.s - a.p;
-      }
-      int ybase[8], xbase[8];
-      const __half* rowp[8];
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const int m = m0 + r0 + 16 * i;
-        const bool ok = m < a.M;
-        const int mm = ok ? m : 0;
-        const int img = mm / HWo, rem = mm - img * HWo;
-        const int oy = rem / a.Wo, ox = rem - oy * a.Wo;
-        ybase[i] = ok ? oy * a.s - a.p : -(1 << 28);   // invalid rows fail the bounds test
-        xbase[i] = ox * a.s - a.p;
-        rowp[i] = a.x + (size_t)img * a.H * a.W * a.xs;
+        for (int mt = 0; mt < MT; mt++) {
+          const int m = m0 + mt * 128;
+          if (m < a.M) {
+            i0[mt] = m / HWo;
+            const int rem = m - i0[mt] * HWo, oy = rem / a.Wo;
+            h0[mt] = oy * a.s - a.p;
+            w0[mt] = (rem - oy * a.Wo) * a.s - a.p;
+          } else {
+            i0[mt] = batch; h0[mt] = 0; w0[mt] = 0;   // past the last image: reads zeros
+          }
+        }
+      }
+      // gather: per row, the pixel offset of its image and the packed (y, x) window origin
+      int rowpix[8 * MT], yx[8 * MT];
+      if (gather) {
+#pragma unroll
+        for (int i = 0; i < 8 * MT; i++) {
+          const int m = m0 + r0 + 16 * i;
+          const bool ok = m < a.M;
+          const int mm = ok ? m : 0;
+          const int img = mm / HWo, rem = mm - img * HWo;
+          const int oy = rem / a.Wo, ox = rem - oy * a.Wo;
+          rowpix[i] = img * a.H * a.W;
+          const int yb = ok ? oy * a.s - a.p : -30000;   // invalid rows fail the bounds test
+          yx[i] = (yb << 16) | ((ox * a.s - a.p) & 0xffff);
+        }
       }
       for (int kb = 0; kb < a.nk; kb++, g++) {
         const int s = g % STAGES;
         const uint32_t u = g / STAGES;
         if (u > 0 && !mbar_wait(empty_bar(s), (u - 1) & 1, 0x101)) { *abort_flag = 1; break; }
-        const uint32_t sA = base + s * Cfg::kStage, sB = sA + Cfg::kABytes;
+        const uint32_t sA = base + s * Cfg::kStage, sB = sA + MT * Cfg::kABytes;
         if (tid == 0) {
-          mbar_expect_tx(full_bar(s), Cfg::kBBytes + (gather ? 0 : Cfg::kABytes));
-          if (a.tmaA == 2) {
-            const int tap = kb / a.ncb, cb = kb - tap * a.ncb;
-            const int ky = tap / a.k, kx = tap - ky * a.k;
-            tma_load_2d(sB, &tmB, full_bar(s), tap * a.Cin + cb * 64, n0);
-            tma_load_im2col(sA, &tmA, full_bar(s), cb * 64, w0, h0, i0, (uint16_t)kx, (uint16_t)ky);
-          } else {
-            tma_load_2d(sB, &tmB, full_bar(s), kb * 64, n0);
-            if (!gather) tma_load_2d(sA, &tmA, full_bar(s), kb * 64, m0);
+          mbar_expect_tx(full_bar(s), Cfg::kBBytes + (gather ? 0 : MT * Cfg::kABytes));
+          // stage kb holds K blocks q = kb*TPS + j (j < TPS), each CB channels of one tap;
+          // blocks past the end read weights out of range (zeros), so they add nothing
+          constexpr uint32_t kABlk = 128 * CB * 2, kBBlk = BN * CB * 2;
+#pragma unroll
+          for (int j = 0; j < Cfg::kTPS; j++) {
+            const int q = kb * Cfg::kTPS + j;
+            if (a.tmaA == 2) {
+              const int tap = q / a.ncb, cbi = q - tap * a.ncb;
+              const int tapc = tap < a.k * a.k ? tap : a.k * a.k - 1;
+              const int ky = tapc / a.k, kx = tapc - ky * a.k;
+              tma_load_2d(sB + j * kBBlk, &tmB, full_bar(s), tap * a.Cin + cbi * CB, n0);
+#pragma unroll
+              for (int mt = 0; mt < MT; mt++)
+                tma_load_im2col(sA + (mt * Cfg::kTPS + j) * kABlk, &tmA, full_bar(s), cbi * CB,
+                                w0[mt], h0[mt], i0[mt], (uint16_t)kx, (uint16_t)ky);
+            } else {
+              tma_load_2d(sB + j * kBBlk, &tmB, full_bar(s), q * CB, n0);
+              if (!gather)
+#pragma unroll
+                for (int mt = 0; mt < MT; mt++)
+                  tma_load_2d(sA + (mt * Cfg::kTPS + j) * kABlk, &tmA, full_bar(s), q * CB,
+                              m0 + mt * 128);
+            }
           }
         }
         if (!gather) continue;
-        if (a.dbg & 2) { mbar_arrive(full_bar(s)); continue; }
         const int kk = kb * 64 + c * 8;
         const bool kval = kk < a.Ktot;
         const int tap = kval ? kk / a.Cin : 0;
         const int ci = kk - tap * a.Cin;
         const int ky = tap / a.k, kx = tap - ky * a.k;
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-          const int iy = ybase[i] + ky, ix = xbase[i] + kx;
+        for (int i = 0; i < 8 * MT; i++) {
+          const int iy = (yx[i] >> 16) + ky, ix = (int)(short)(yx[i] & 0xffff) + kx;
           const bool ok = kval && (unsigned)iy < (unsigned)a.H && (unsigned)ix < (unsigned)a.W;
-          const __half* src = ok ? rowp[i] + ((size_t)iy * a.W + ix) * a.xs + ci : a.x;
+          const __half* src = ok ? a.x + (size_t)(rowpix[i] + iy * a.W + ix) * a.xs + ci : a.x;
           cp_async16(sA + offA + (uint32_t)(i * 2048), src, ok ? 16u : 0u);
         }
         cp_async_arrive_noinc(full_bar(s));   // arrives when this thread's copies land
@@ -230,49 +259,53 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
       const uint32_t use = li / Cfg::kNacc;
       if (!mbar_wait(tfull_bar(acc), use & 1, 0x103)) { *abort_flag = 1; break; }
       tc_fence_after();
-      const int m0 = (t / a.ntn) * 128, n0 = (t % a.ntn) * BN;
-      const int m = m0 + row;
-      const bool mok = m < a.M;
-      __half* yrow = a.y + (size_t)(mok ? m : 0) * a.ys;
-      const __half* rrow = a.res ? a.res + (size_t)(mok ? m : 0) * a.rs : nullptr;
-      const uint32_t trow = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kAccCols;
+      const int m0 = (t / a.ntn) * kTM, n0 = (t % a.ntn) * BN;
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 16; cc++) {
-        const int n = n0 + cc * 16;
-        if (n >= a.Cout) break;  // uniform across the warp
-        uint32_t r[16];
-        tmem_ld16(trow + cc * 16, r);
-        tmem_ld_wait();
-        if (!mok || (a.dbg & 1)) continue;
+      for (int mt = 0; mt < MT; mt++) {
+        const int m = m0 + mt * 128 + row;
+        const bool mok = m < a.M;
+        __half* yrow = a.y + (size_t)(mok ? m : 0) * a.ys;
+        const __half* rrow = a.res ? a.res + (size_t)(mok ? m : 0) * a.rs : nullptr;
+        const uint32_t trow = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kTileCols +
+                              mt * Cfg::kAccCols;
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 16; cc++) {
+          const int n = n0 + cc * 16;
+          if (n >= a.Cout) break;  // uniform across the warp
+          uint32_t r[16];
+          tmem_ld16(trow + cc * 16, r);
+          tmem_ld_wait();
+          if (!mok) continue;
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-          const int nn = n + 8 * h;
-          if (nn >= a.Cout) break;
-          const float4 b0 = *(const float4*)(bias + nn);
-          const float4 b1 = *(const float4*)(bias + nn + 4);
-          float v[8] = {__uint_as_float(r[8 * h + 0]) + b0.x, __uint_as_float(r[8 * h + 1]) + b0.y,
-                        __uint_as_float(r[8 * h + 2]) + b0.z, __uint_as_float(r[8 * h + 3]) + b0.w,
-                        __uint_as_float(r[8 * h + 4]) + b1.x, __uint_as_float(r[8 * h + 5]) + b1.y,
-                        __uint_as_float(r[8 * h + 6]) + b1.z, __uint_as_float(r[8 * h + 7]) + b1.w};
-          if (a.act == 1) {
+          for (int h = 0; h < 2; h++) {
+            const int nn = n + 8 * h;
+            if (nn >= a.Cout) break;
+            const float4 b0 = *(const float4*)(bias + nn);
+            const float4 b1 = *(const float4*)(bias + nn + 4);
+            float v[8] = {__uint_as_float(r[8 * h + 0]) + b0.x, __uint_as_float(r[8 * h + 1]) + b0.y,
+                          __uint_as_float(r[8 * h + 2]) + b0.z, __uint_as_float(r[8 * h + 3]) + b0.w,
+                          __uint_as_float(r[8 * h + 4]) + b1.x, __uint_as_float(r[8 * h + 5]) + b1.y,
+                          __uint_as_float(r[8 * h + 6]) + b1.z, __uint_as_float(r[8 * h + 7]) + b1.w};
+            if (a.act == 1) {
 #pragma unroll
-            for (int q = 0; q < 8; q++) v[q] = __fdividef(v[q], 1.f + __expf(-v[q]));
-          }
-          if (rrow) {
-            const uint4 rv = *(const uint4*)(rrow + nn);
-            const __half2* rh = (const __half2*)&rv;
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-              const float2 f = __half22float2(rh[q]);
-              v[2 * q] += f.x;
-              v[2 * q + 1] += f.y;
+              for (int q = 0; q < 8; q++) v[q] = __fdividef(v[q], 1.f + __expf(-v[q]));
             }
-          }
-          uint4 o;
-          __half2* oh = (__half2*)&o;
+            if (rrow) {
+              const uint4 rv = *(const uint4*)(rrow + nn);
+              const __half2* rh = (const __half2*)&rv;
 #pragma unroll
-          for (int q = 0; q < 4; q++) oh[q] = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
-          *(uint4*)(yrow + nn) = o;
+              for (int q = 0; q < 4; q++) {
+                const float2 f = __half22float2(rh[q]);
+                v[2 * q] += f.x;
+                v[2 * q + 1] += f.y;
+              }
+            }
+            uint4 o;
+            __half2* oh = (__half2*)&o;
+#pragma unroll
+            for (int q = 0; q < 4; q++) oh[q] = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
+            *(uint4*)(yrow + nn) = o;
+          }
         }
       }
       tc_fence_before();
@@ -287,17 +320,23 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
       const uint32_t use = li / Cfg::kNacc;
       if (use > 0 && !mbar_wait(tempty_bar(acc), (use - 1) & 1, 0x104)) { *abort_flag = 1; break; }
       tc_fence_after();
-      const uint32_t d = tmem + acc * Cfg::kAccCols;
+      const uint32_t d = tmem + acc * Cfg::kTileCols;
       bool ok = true;
       for (int kb = 0; kb < a.nk; kb++, g++) {
         const int s = g % STAGES;
         if (!mbar_wait(full_bar(s), (g / STAGES) & 1, 0x102)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sA = base + s * Cfg::kStage, sB = sA + Cfg::kABytes;
+        const uint32_t sA = base + s * Cfg::kStage, sB = sA + MT * Cfg::kABytes;
+        constexpr uint32_t kABlk = 128 * CB * 2, kBBlk = BN * CB * 2;
 #pragma unroll
-        for (int kk = 0; kk < 4; kk++)
-          tc_mma_f16(d, sw128_desc(sA + kk * 32), sw128_desc(sB + kk * 32), idesc,
-                     (kb | kk) != 0);
+        for (int j = 0; j < Cfg::kTPS; j++)
+#pragma unroll
+          for (int kk = 0; kk < CB / 16; kk++)
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++)
+              tc_mma_f16(d + mt * Cfg::kAccCols,
+                         swz_desc<CB * 2>(sA + (mt * Cfg::kTPS + j) * kABlk + kk * 32),
+                         swz_desc<CB * 2>(sB + j * kBBlk + kk * 32), idesc, (kb | j | kk) != 0);
         tc_commit(empty_bar(s));
       }
       if (!ok) { *abort_flag = 1; break; }
@@ -314,10 +353,15 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
 
 static int g_num_sms[64] = {};
 
+static CUtensorMapSwizzle swizzle_of(int cb) {
+  return cb == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : cb == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                          : CU_TENSOR_MAP_SWIZZLE_32B;
+}
+
 // 2-D fp16 tensor map with a 64-element (128-byte) inner box and the 128-byte swizzle that
 // matches the UMMA K-major layout; out-of-range elements read as zero.
 static bool encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
-                      uint64_t row_bytes, uint32_t box_outer) {
+                      uint64_t row_bytes, uint32_t box_outer, int cb) {
   static PFN_cuTensorMapEncodeTiled encode = nullptr;
   static std::mutex mu;
   {
@@ -333,10 +377,10 @@ static bool encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t
   }
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_bytes};
-  const cuuint32_t box[2] = {64, box_outer};
+  const cuuint32_t box[2] = {(cuuint32_t)cb, box_outer};
   const cuuint32_t estr[2] = {1, 1};
   return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
-                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_of(cb),
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -344,7 +388,7 @@ static bool encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t
 // im2col tensor map over the NHWC input view: dims {C, W, H, N}, the padding bounding box
 // [-p, W-1+p-(k-1)] per spatial dim, conv stride as the traversal stride, 64 channels x 128
 // output pixels per load, 128-byte swizzle; outside the image reads as zero.
-static bool encode_im2col(CUtensorMap* m, const ConvArgs& a) {
+static bool encode_im2col(CUtensorMap* m, const ConvArgs& a, int cb) {
   static PFN_cuTensorMapEncodeIm2col encode = nullptr;
   static std::mutex mu;
   {
@@ -366,17 +410,17 @@ static bool encode_im2col(CUtensorMap* m, const ConvArgs& a) {
   const int upper[2] = {a.p - (a.k - 1), a.p - (a.k - 1)};
   const cuuint32_t estr[4] = {1, (cuuint32_t)a.s, (cuuint32_t)a.s, 1};
   return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(a.x), dims, strides,
-                lower, upper, 64, 128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                lower, upper, (cuuint32_t)cb, 128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                swizzle_of(cb), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int MT, int CB = 64>
 static int launch_tc(const ConvArgs& a, cudaStream_t st) {
-  using Cfg = TcCfg<BN, STAGES>;
+  using Cfg = TcCfg<BN, STAGES, MT, CB>;
   static bool attr_set = false;   // the attribute is per function, for all devices
   if (!attr_set) {
-    if (cudaFuncSetAttribute(conv_tc_kernel<BN, STAGES>,
+    if (cudaFuncSetAttribute(conv_tc_kernel<BN, STAGES, MT, CB>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)Cfg::kSmem) != cudaSuccess)
       return check_launch("conv_tc attr");
@@ -389,13 +433,14 @@ static int launch_tc(const ConvArgs& a, cudaStream_t st) {
   const int grid = a.ntiles < g_num_sms[dev] ? a.ntiles : g_num_sms[dev];
   CUtensorMap tmB, tmA;
   memset(&tmA, 0, sizeof tmA);
-  if (!encode_2d(&tmB, a.w, (uint64_t)a.Ktot, (uint64_t)a.Cout, (uint64_t)a.Ktot * 2, BN))
+  if (!encode_2d(&tmB, a.w, (uint64_t)a.Ktot, (uint64_t)a.Cout, (uint64_t)a.Ktot * 2, BN, CB))
     return YK_EUNSUP;
-  if (a.tmaA == 1 && !encode_2d(&tmA, a.x, (uint64_t)a.Cin, (uint64_t)a.M, (uint64_t)a.xs * 2, 128))
+  if (a.tmaA == 1 &&
+      !encode_2d(&tmA, a.x, (uint64_t)a.Cin, (uint64_t)a.M, (uint64_t)a.xs * 2, 128, CB))
     return YK_EUNSUP;
-  if (a.tmaA == 2 && !encode_im2col(&tmA, a))
+  if (a.tmaA == 2 && !encode_im2col(&tmA, a, CB))
     return YK_EUNSUP;
-  conv_tc_kernel<BN, STAGES><<<grid, kThreads, Cfg::kSmem, st>>>(a, tmB, tmA);
+  conv_tc_kernel<BN, STAGES, MT, CB><<<grid, kThreads, Cfg::kSmem, st>>>(a, tmB, tmA);
   note_launch();
   return check_launch("conv_tc");
 }
@@ -409,6 +454,15 @@ int pick_tile(int M, int Cout) {
   return bn;
 }
 
+// Heuristic M sub-tiles per CTA tile: narrow N tiles stack 2-4 sub-tiles so independent
+// accumulation chains keep the tensor pipe busy, as long as the grid still fills the SMs.
+int pick_msub(int M, int Cout, int bn) {
+  int ms = bn <= 32 ? 4 : bn <= 64 ? 2 : 1;
+  const long long nt = (Cout + bn - 1) / bn;
+  while (ms > 1 && ((M + 128LL * ms - 1) / (128LL * ms)) * nt < 2 * 148) ms >>= 1;
+  return ms;
+}
+
 int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p,
             cudaStream_t st) {
   ConvArgs a;
@@ -420,29 +474,60 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   a.w = (const __half*)p->weight; a.bias = p->bias;
   a.Cin = p->Cin; a.Cout = p->Cout; a.k = p->k; a.s = p->s; a.p = p->p; a.act = p->act;
   a.Ktot = p->k * p->k * p->Cin;
-  long long M = (long long)y->batch * y->H * y->W;
-  if (M > 0x7fffffffLL) return YK_EUNSUP;
+  const long long M = (long long)y->batch * y->H * y->W;
+  if (M > 0x7fffffffLL || (long long)x->batch * x->H * x->W > 0x7fffffffLL) return YK_EUNSUP;
+  if (x->H > 30000 || x->W > 30000) return YK_EUNSUP;   // packed 16-bit window origins
   a.M = (int)M;
   a.nk = (a.Ktot + 63) / 64;
-  int bn = p->tile ? p->tile : pick_tile(a.M, a.Cout);
+  const int bn = p->tile ? p->tile : pick_tile(a.M, a.Cout);
+  if (bn != 32 && bn != 64 && bn != 128 && bn != 256) return YK_EINVAL;
+  int ms = p->msub ? p->msub : pick_msub(a.M, a.Cout, bn);
+  if (bn == 256) ms = 1;
+  if (bn == 128 && ms > 2) ms = 2;
+  if (ms != 1 && ms != 2 && ms != 4) return YK_EINVAL;
   a.ntn = (a.Cout + bn - 1) / bn;
-  const long long nt = (long long)((a.M + 127) / 128) * a.ntn;
+  const long long nt = ((M + 128LL * ms - 1) / (128LL * ms)) * a.ntn;
   if (nt > 0x7fffffffLL) return YK_EUNSUP;
   a.ntiles = (int)nt;
-  { const char* e = getenv("YK_DBG"); a.dbg = e ? atoi(e) : 0; }
-  const bool tma_ok = p->Cin >= 64 && ((uintptr_t)a.x & 15) == 0 && (a.xs % 8) == 0;
+  // A by TMA when the view allows it: CB = 64-channel blocks (128-byte rows) for Cin >= 64,
+  // 32 / 16-channel blocks (64 / 32-byte rows, matching swizzle) for Cin = 32 / 16
+  const int cb = p->Cin >= 64 ? 64 : ((p->Cin == 32 || p->Cin == 16) && bn <= 64) ? p->Cin : 0;
+  const bool tma_ok = cb && ((uintptr_t)a.x & 15) == 0 && (a.xs % 8) == 0;
   a.tmaA = 0;
-  a.ncb = (p->Cin + 63) / 64;
+  a.ncb = cb ? (p->Cin + cb - 1) / cb : 0;
   if (tma_ok && p->k == 1 && p->s == 1 && p->p == 0) a.tmaA = 1;
-  else if (tma_ok && p->p < 128 && p->k - 1 - p->p < 128 && p->s <= 8 && !(a.dbg & 4)) {
-    a.tmaA = 2;
-    a.nk = p->k * p->k * a.ncb;   // one 64-channel block of one filter tap per stage
+  else if (tma_ok && p->p < 128 && p->k - 1 - p->p < 128 && p->s <= 8) a.tmaA = 2;
+  if (a.tmaA) {
+    const int tps = 64 / cb;                      // K blocks per stage
+    a.nk = (p->k * p->k * a.ncb + tps - 1) / tps;
   }
-  switch (bn) {
-    case 32: return launch_tc<32, 8>(a, st);
-    case 64: return launch_tc<64, 8>(a, st);
-    case 128: return launch_tc<128, 6>(a, st);
-    case 256: return launch_tc<256, 4>(a, st);
+  if (a.tmaA && cb < 64) {
+    switch (bn * 1000 + ms * 100 + cb) {
+      case 32116: return launch_tc<32, 8, 1, 16>(a, st);
+      case 32216: return launch_tc<32, 5, 2, 16>(a, st);
+      case 32416: return launch_tc<32, 3, 4, 16>(a, st);
+      case 64116: return launch_tc<64, 8, 1, 16>(a, st);
+      case 64216: return launch_tc<64, 5, 2, 16>(a, st);
+      case 64416: return launch_tc<64, 2, 4, 16>(a, st);
+      case 32132: return launch_tc<32, 8, 1, 32>(a, st);
+      case 32232: return launch_tc<32, 5, 2, 32>(a, st);
+      case 32432: return launch_tc<32, 3, 4, 32>(a, st);
+      case 64132: return launch_tc<64, 8, 1, 32>(a, st);
+      case 64232: return launch_tc<64, 5, 2, 32>(a, st);
+      case 64432: return launch_tc<64, 2, 4, 32>(a, st);
+      default: return YK_EINVAL;
+    }
+  }
+  switch (bn * 10 + ms) {
+    case 321: return launch_tc<32, 8, 1>(a, st);
+    case 322: return launch_tc<32, 5, 2>(a, st);
+    case 324: return launch_tc<32, 3, 4>(a, st);
+    case 641: return launch_tc<64, 8, 1>(a, st);
+    case 642: return launch_tc<64, 5, 2>(a, st);
+    case 644: return launch_tc<64, 2, 4>(a, st);
+    case 1281: return launch_tc<128, 6, 1>(a, st);
+    case 1282: return launch_tc<128, 3, 2>(a, st);
+    case 2561: return launch_tc<256, 4, 1>(a, st);
     default: return YK_EINVAL;
   }
 }

@@ -60,6 +60,7 @@ struct Op {
   int res = -1;                   // fused residual tensor
   int y2 = -1, y3 = -1;           // POOLX3 outputs 2 and 3
   int tile = 0;                   // tensor-core N tile chosen by the planner / autotuner
+  int msub = 0;                   // tensor-core stacked M sub-tiles (0 = heuristic)
 };
 
 struct SlotGeom { float scale = 1.f; int top = 0, left = 0; };
@@ -361,7 +362,7 @@ void Engine::run_op(const Op& op, int B) {
       p.weight = (const uint16_t*)dweights + op.woff;
       p.bias = dbias + op.boff;
       p.k = op.k; p.s = op.s; p.p = op.p; p.groups = op.g; p.act = op.act;
-      p.Cin = op.Cin; p.Cout = op.Cout; p.tile = op.tile; p.splitk = 0;
+      p.Cin = op.Cin; p.Cout = op.Cout; p.tile = op.tile; p.msub = op.msub;
       YkView x = view(op.a, B), y = view(op.out, B);
       YkView r;
       if (op.res >= 0) r = view(op.res, B);
@@ -441,13 +442,18 @@ void Engine::autotune() {
   cudaEvent_t e0, e1;
   CKE(cudaEventCreate(&e0));
   CKE(cudaEventCreate(&e1));
+  static const int combos[][2] = {{32, 1}, {32, 2}, {32, 4}, {64, 1}, {64, 2}, {64, 4},
+                                  {128, 1}, {128, 2}, {256, 1}};
   for (Op& op : ops) {
     if (op.kind != CONV || op.g != 1 || op.Cin % 8) continue;
-    int best = 0;
+    int best_t = 0, best_m = 0;
     float tbest = 1e30f;
-    for (int tile : {64, 128, 256}) {
-      if (tile > 64 && tile / 2 >= op.Cout) continue;
+    for (const auto& cm : combos) {
+      const int tile = cm[0];
+      if (tile > 32 && tile / 2 >= op.Cout) continue;   // more than half the tile wasted
+      if (tile == 32 && op.Cout > 64) continue;
       op.tile = tile;
+      op.msub = cm[1];
       run_op(op, maxB);
       CKE(cudaEventRecord(e0, st));
       for (int r = 0; r < 5; r++) run_op(op, maxB);
@@ -455,13 +461,14 @@ void Engine::autotune() {
       CKE(cudaEventSynchronize(e1));
       float ms = 0;
       CKE(cudaEventElapsedTime(&ms, e0, e1));
-      if (ms < tbest) { tbest = ms; best = tile; }
+      if (ms < tbest) { tbest = ms; best_t = tile; best_m = cm[1]; }
     }
-    op.tile = op.Cout <= 32 ? 32 : best;
+    op.tile = best_t;
+    op.msub = best_m;
   }
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
-  // the tuning runs overwrote activations; nothing downstream depends on them
+  // the tuning runs overwrote activations; every forward recomputes them
 }
 
 cudaGraphExec_t Engine::graph_for(int B) {
@@ -702,7 +709,7 @@ int yolo_run_op(void* h, int op_index, int B) {
     Op o = op;
     if (o.kind == CONV && o.g == 1 && o.Cin % 8 == 0) {
       for (const Op& f : e->ops)   // reuse the tuned tile of the matching planned conv
-        if (f.kind == CONV && f.woff == o.woff) o.tile = f.tile;
+        if (f.kind == CONV && f.woff == o.woff) { o.tile = f.tile; o.msub = f.msub; }
     }
     e->run_op(o, B);
     CKE(cudaStreamSynchronize(e->st));
