@@ -81,6 +81,8 @@ CONV_CASES = [
     (2, 20, 20, 32, 64, 1, 1, 0),      # narrow-block TMA, 1x1
     (2, 21, 19, 16, 32, 3, 2, 1),      # narrow-block TMA im2col, stride 2
     (3, 16, 16, 32, 32, 3, 1, 1),
+    (2, 32, 24, 8, 16, 3, 2, 1),       # 8-channel blocks (unswizzled TMA im2col)
+    (1, 15, 15, 8, 64, 3, 1, 1),
 ]
 
 

@@ -142,6 +142,146 @@ static int launch_attn(const YkView* qkv, const YkView* y, int heads, int N, siz
   return check_launch("attn");
 }
 
+
+// ---------------- tensor-core path (kd = 32, hd = 64) ----------------
+// Flash-style: a warp owns 16 queries; keys stream through shared memory in chunks of 192
+// (K rows padded to 40 halves, V rows to 72, so fragment loads are bank-conflict free).
+// Per 16-key block: S = Q K^T with four m16n8k16 MMAs (fp32 accumulate), online softmax in
+// registers (row max / sum shared by the 4 lanes of a row through shuffles), then the fp16
+// probabilities are reused in place as the A operand of O += P V (eight MMAs, V fragments by
+// ldmatrix.trans).  The FLOPs are ~0.2 % of the network, so the warp-level MMA is enough.
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *(uint32_t*)&h;
+}
+
+constexpr int kAttnChunk = 192, kKs = 40, kVs = 72;
+
+__global__ void __launch_bounds__(128) attn_mma_kernel(DView qkv, DView y, int N, float scale) {
+  __shared__ __align__(16) __half Ks[kAttnChunk * kKs];
+  __shared__ __align__(16) __half Vs[kAttnChunk * kVs];
+  const int h = blockIdx.y, img = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const __half* base = qkv.p + (size_t)img * N * qkv.stride + h * 128;   // per head: q32 k32 v64
+  const int q0 = blockIdx.x * 64 + warp * 16;
+  // Q fragments (2 K-steps of 16 over kd = 32), rows beyond N are zero
+  uint32_t qa[2][4];
+  {
+    const int r0 = q0 + g, r1 = q0 + g + 8;
+#pragma unroll
+    for (int ks = 0; ks < 2; ks++) {
+      const int c = ks * 16 + 2 * t;
+      qa[ks][0] = r0 < N ? *(const uint32_t*)(base + (size_t)r0 * qkv.stride + c) : 0u;
+      qa[ks][1] = r1 < N ? *(const uint32_t*)(base + (size_t)r1 * qkv.stride + c) : 0u;
+      qa[ks][2] = r0 < N ? *(const uint32_t*)(base + (size_t)r0 * qkv.stride + c + 8) : 0u;
+      qa[ks][3] = r1 < N ? *(const uint32_t*)(base + (size_t)r1 * qkv.stride + c + 8) : 0u;
+    }
+  }
+  float o[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;   // rows g and g+8
+  for (int c0 = 0; c0 < N; c0 += kAttnChunk) {
+    const int cn = min(kAttnChunk, N - c0);
+    __syncthreads();
+    const int cn16 = (cn + 15) & ~15;   // rows past the last key are zero (P = 0 there)
+    for (int i = threadIdx.x; i < cn16 * 12; i += 128) {   // 4 K + 8 V 16-byte chunks per key
+      const int j = i / 12, cc = i - j * 12;
+      const uint4 v = j < cn ? *(const uint4*)(base + (size_t)(c0 + j) * qkv.stride + 32 + cc * 8)
+                             : make_uint4(0, 0, 0, 0);
+      if (cc < 4) *(uint4*)(Ks + j * kKs + cc * 8) = v;
+      else *(uint4*)(Vs + j * kVs + (cc - 4) * 8) = v;
+    }
+    __syncthreads();
+    for (int kb = 0; kb < cn; kb += 16) {
+      // S = Q K^T for 16 keys: two n-tiles of 8 keys
+      float sc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+        const int key = kb + nt * 8 + g;
+#pragma unroll
+        for (int ks = 0; ks < 2; ks++) {
+          const __half* kp = Ks + key * kKs + ks * 16 + 2 * t;
+          mma16816(sc[nt], qa[ks], *(const uint32_t*)kp, *(const uint32_t*)(kp + 8));
+        }
+      }
+      // scale, mask keys past the end, online softmax per row
+      float mx0 = m0, mx1 = m1;
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const bool ok = kb + nt * 8 + 2 * t + e < cn;
+          sc[nt][e] = ok ? sc[nt][e] * scale : -INFINITY;
+          sc[nt][2 + e] = ok ? sc[nt][2 + e] * scale : -INFINITY;
+          mx0 = fmaxf(mx0, sc[nt][e]);
+          mx1 = fmaxf(mx1, sc[nt][2 + e]);
+        }
+#pragma unroll
+      for (int off = 1; off < 4; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(~0u, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(~0u, mx1, off));
+      }
+      const float cor0 = __expf(m0 - mx0), cor1 = __expf(m1 - mx1);
+      m0 = mx0;
+      m1 = mx1;
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          sc[nt][e] = __expf(sc[nt][e] - mx0);
+          sc[nt][2 + e] = __expf(sc[nt][2 + e] - mx1);
+          ps0 += sc[nt][e];
+          ps1 += sc[nt][2 + e];
+        }
+      l0 = l0 * cor0 + ps0;   // per-lane partial sums; the row total is reduced at the end
+      l1 = l1 * cor1 + ps1;
+#pragma unroll
+      for (int n = 0; n < 8; n++) {
+        o[n][0] *= cor0; o[n][1] *= cor0;
+        o[n][2] *= cor1; o[n][3] *= cor1;
+      }
+      // O += P V: P (16 q x 16 keys) as the A operand, V via ldmatrix.trans
+      uint32_t pa[4] = {pack_half2(sc[0][0], sc[0][1]), pack_half2(sc[0][2], sc[0][3]),
+                        pack_half2(sc[1][0], sc[1][1]), pack_half2(sc[1][2], sc[1][3])};
+#pragma unroll
+      for (int np = 0; np < 4; np++) {   // pairs of 8-column n-tiles
+        const __half* vp = Vs + (kb + (lane & 7) + ((lane >> 3) & 1) * 8) * kVs + np * 16 + (lane >> 4) * 8;
+        uint32_t r0, r1, r2, r3;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                     : "r"(smem_u32(vp)));
+        mma16816(o[2 * np], pa, r0, r1);
+        mma16816(o[2 * np + 1], pa, r2, r3);
+      }
+    }
+  }
+  l0 += __shfl_xor_sync(~0u, l0, 1);
+  l0 += __shfl_xor_sync(~0u, l0, 2);
+  l1 += __shfl_xor_sync(~0u, l1, 1);
+  l1 += __shfl_xor_sync(~0u, l1, 2);
+  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+  const int r0 = q0 + g, r1 = q0 + g + 8;
+  __half* y0 = y.p + ((size_t)img * N + r0) * y.stride + h * 64;
+  __half* y1 = y.p + ((size_t)img * N + r1) * y.stride + h * 64;
+#pragma unroll
+  for (int n = 0; n < 8; n++) {
+    if (r0 < N) *(__half2*)(y0 + n * 8 + 2 * t) = __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
+    if (r1 < N) *(__half2*)(y1 + n * 8 + 2 * t) = __floats2half2_rn(o[n][2] * inv1, o[n][3] * inv1);
+  }
+}
+
 }  // namespace yk
 
 using namespace yk;
@@ -153,6 +293,13 @@ extern "C" int yk_attn(const YkView* qkv, const YkView* y, int heads, int kd, in
     return YK_EINVAL;
   if (kd != 32 || hd != 64) return YK_EUNSUP;
   const int N = qkv->H * qkv->W;
+  if (!getenv("YK_ATTN_SIMT")) {
+    dim3 grid((N + 63) / 64, heads, qkv->batch);
+    attn_mma_kernel<<<grid, 128, 0, (cudaStream_t)st>>>(dview(*qkv), dview(*y), N,
+                                                        rsqrtf((float)kd));
+    note_launch();
+    return check_launch("attn_mma");
+  }
   const size_t smem = (size_t)N * (kd + hd) * sizeof(__half);
   if (smem > 227 * 1024) return YK_EUNSUP;
   // enough blocks to cover the SMs: split keys further when batch x heads is small

@@ -192,7 +192,8 @@ __global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restric
 }
 
 // 3x3 depthwise conv, register-blocked: thread = 8 channels x 4 consecutive output pixels
-// of one row.  The 72 filter weights of its channels live in registers, each input column of
+// of one row.  The block stages the filter transposed to [9][C] in shared memory; the 72
+// weights of a thread's channels then live in registers, each input column of
 // the 3 x (3*S + 1 ... ) window is loaded once (16 bytes) and feeds every output it touches.
 // Index arithmetic is 32-bit (I = unsigned) whenever the element count allows it.
 template <int S, typename I>
@@ -201,6 +202,12 @@ __global__ void __launch_bounds__(256) dwconv3_kernel(DView x, DView y, DView r,
                                                       const float* __restrict__ b, int act,
                                                       int batch) {
   constexpr int PX = 4, NIN = (PX - 1) * S + 3;
+  extern __shared__ __align__(16) __half dw_wsm[];   // weights transposed to [9][C]
+  for (int i = threadIdx.x; i < y.C * 9; i += blockDim.x) {
+    const int ch = i / 9, t = i - ch * 9;
+    dw_wsm[t * y.C + ch] = w[i];
+  }
+  __syncthreads();
   const int cg = y.C >> 3, nxb = (y.W + PX - 1) / PX;
   const I total = (I)batch * y.H * nxb * cg;
   const I idx = (I)blockIdx.x * blockDim.x + threadIdx.x;
@@ -213,9 +220,16 @@ __global__ void __launch_bounds__(256) dwconv3_kernel(DView x, DView y, DView r,
   const int c = g << 3, ox0 = xb * PX;
   float wr[9][8];
 #pragma unroll
-  for (int q = 0; q < 8; q++)
+  for (int t = 0; t < 9; t++) {
+    const uint4 v = *(const uint4*)(dw_wsm + t * y.C + c);
+    const __half2* h = (const __half2*)&v;
 #pragma unroll
-    for (int t = 0; t < 9; t++) wr[t][q] = __half2float(w[(c + q) * 9 + t]);
+    for (int q = 0; q < 4; q++) {
+      const float2 f = __half22float2(h[q]);
+      wr[t][2 * q] = f.x;
+      wr[t][2 * q + 1] = f.y;
+    }
+  }
   float acc[PX][8];
   {
     const float4 b0 = *(const float4*)(b + c), b1 = *(const float4*)(b + c + 4);
@@ -437,13 +451,15 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     if (p->k == 3 && p->p == 1 && (p->s == 1 || p->s == 2)) {
       const long long t3 = (long long)y->batch * y->H * ((y->W + 3) / 4) * (p->Cout / 8);
       const unsigned nb = nblk(t3, 256);
+      const size_t wsmem = (size_t)p->Cout * 9 * sizeof(__half);
+      if (wsmem > 48 * 1024) return YK_EUNSUP;
       const __half* wp = (const __half*)p->weight;
       if (t3 < (1LL << 31)) {
-        if (p->s == 1) dwconv3_kernel<1, unsigned><<<nb, 256, 0, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
-        else dwconv3_kernel<2, unsigned><<<nb, 256, 0, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+        if (p->s == 1) dwconv3_kernel<1, unsigned><<<nb, 256, wsmem, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+        else dwconv3_kernel<2, unsigned><<<nb, 256, wsmem, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
       } else {
-        if (p->s == 1) dwconv3_kernel<1, long long><<<nb, 256, 0, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
-        else dwconv3_kernel<2, long long><<<nb, 256, 0, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+        if (p->s == 1) dwconv3_kernel<1, long long><<<nb, 256, wsmem, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+        else dwconv3_kernel<2, long long><<<nb, 256, wsmem, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
       }
       note_launch();
       return check_launch("dwconv3");

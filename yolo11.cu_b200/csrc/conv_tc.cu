@@ -328,15 +328,26 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
         tc_fence_after();
         const uint32_t sA = base + s * Cfg::kStage, sB = sA + MT * Cfg::kABytes;
         constexpr uint32_t kABlk = 128 * CB * 2, kBBlk = BN * CB * 2;
+        if constexpr (CB == 8) {
+          // 16-byte blocks, no swizzle: one K=16 step spans blocks 2i and 2i+1 (LBO apart)
 #pragma unroll
-        for (int j = 0; j < Cfg::kTPS; j++)
-#pragma unroll
-          for (int kk = 0; kk < CB / 16; kk++)
+          for (int i = 0; i < Cfg::kTPS / 2; i++)
 #pragma unroll
             for (int mt = 0; mt < MT; mt++)
               tc_mma_f16(d + mt * Cfg::kAccCols,
-                         swz_desc<CB * 2>(sA + (mt * Cfg::kTPS + j) * kABlk + kk * 32),
-                         swz_desc<CB * 2>(sB + j * kBBlk + kk * 32), idesc, (kb | j | kk) != 0);
+                         nosw_desc(sA + (mt * Cfg::kTPS + 2 * i) * kABlk, kABlk, 128),
+                         nosw_desc(sB + 2 * i * kBBlk, kBBlk, 128), idesc, (kb | i) != 0);
+        } else {
+#pragma unroll
+          for (int j = 0; j < Cfg::kTPS; j++)
+#pragma unroll
+            for (int kk = 0; kk < CB / 16; kk++)
+#pragma unroll
+              for (int mt = 0; mt < MT; mt++)
+                tc_mma_f16(d + mt * Cfg::kAccCols,
+                           swz_desc<CB * 2>(sA + (mt * Cfg::kTPS + j) * kABlk + kk * 32),
+                           swz_desc<CB * 2>(sB + j * kBBlk + kk * 32), idesc, (kb | j | kk) != 0);
+        }
         tc_commit(empty_bar(s));
       }
       if (!ok) { *abort_flag = 1; break; }
@@ -355,7 +366,7 @@ static int g_num_sms[64] = {};
 
 static CUtensorMapSwizzle swizzle_of(int cb) {
   return cb == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : cb == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                                          : CU_TENSOR_MAP_SWIZZLE_32B;
+         : cb == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
 }
 
 // 2-D fp16 tensor map with a 64-element (128-byte) inner box and the 128-byte swizzle that
@@ -490,8 +501,10 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   if (nt > 0x7fffffffLL) return YK_EUNSUP;
   a.ntiles = (int)nt;
   // A by TMA when the view allows it: CB = 64-channel blocks (128-byte rows) for Cin >= 64,
-  // 32 / 16-channel blocks (64 / 32-byte rows, matching swizzle) for Cin = 32 / 16
-  const int cb = p->Cin >= 64 ? 64 : ((p->Cin == 32 || p->Cin == 16) && bn <= 64) ? p->Cin : 0;
+  // 32 / 16 / 8-channel blocks (64 / 32-byte swizzled rows, 16-byte unswizzled core matrices)
+  // for Cin = 32 / 16 / 8
+  const int cb = p->Cin >= 64 ? 64
+                 : ((p->Cin == 32 || p->Cin == 16 || p->Cin == 8) && bn <= 64) ? p->Cin : 0;
   const bool tma_ok = cb && ((uintptr_t)a.x & 15) == 0 && (a.xs % 8) == 0;
   a.tmaA = 0;
   a.ncb = cb ? (p->Cin + cb - 1) / cb : 0;
@@ -515,6 +528,12 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
       case 64132: return launch_tc<64, 8, 1, 32>(a, st);
       case 64232: return launch_tc<64, 5, 2, 32>(a, st);
       case 64432: return launch_tc<64, 2, 4, 32>(a, st);
+      case 32108: return launch_tc<32, 8, 1, 8>(a, st);
+      case 32208: return launch_tc<32, 5, 2, 8>(a, st);
+      case 32408: return launch_tc<32, 3, 4, 8>(a, st);
+      case 64108: return launch_tc<64, 8, 1, 8>(a, st);
+      case 64208: return launch_tc<64, 5, 2, 8>(a, st);
+      case 64408: return launch_tc<64, 2, 4, 8>(a, st);
       default: return YK_EINVAL;
     }
   }

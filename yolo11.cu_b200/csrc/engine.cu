@@ -61,6 +61,7 @@ struct Op {
   int y2 = -1, y3 = -1;           // POOLX3 outputs 2 and 3
   int tile = 0;                   // tensor-core N tile chosen by the planner / autotuner
   int msub = 0;                   // tensor-core stacked M sub-tiles (0 = heuristic)
+  const void* wpad = nullptr;     // stem conv on the 8-channel padded input: padded weights
 };
 
 struct SlotGeom { float scale = 1.f; int top = 0, left = 0; };
@@ -87,6 +88,7 @@ struct Engine {
   std::vector<Ten> tens;
   std::vector<Op> raw, ops;       // unfused (dump order) and planned (fused) op lists
   void* dweights = nullptr;
+  void* dstem = nullptr;          // zero-padded (Cin 3 -> 8) weights of convs reading the input
   float* dbias = nullptr;
   size_t nweights = 0, nbias = 0;
   // head
@@ -116,6 +118,7 @@ struct Engine {
     for (auto& b : bufs)
       if (b.p) cudaFree(b.p), b.p = nullptr;
     if (dweights) cudaFree(dweights);
+    if (dstem) cudaFree(dstem);
     if (dbias) cudaFree(dbias);
     if (post.ws) cudaFree(post.ws);
     if (post.outdets) cudaFree(post.outdets);
@@ -127,7 +130,7 @@ struct Engine {
     if (h_cnt) cudaFreeHost(h_cnt);
     if (h_raw) cudaFreeHost(h_raw);
     if (st) cudaStreamDestroy(st);
-    dweights = nullptr; dbias = nullptr; post = YkPost{}; dmasks = nullptr;
+    dweights = nullptr; dstem = nullptr; dbias = nullptr; post = YkPost{}; dmasks = nullptr;
     h_out = nullptr; h_cnt = nullptr; h_raw = nullptr; st = nullptr;
     if (prev >= 0) cudaSetDevice(prev);
   }
@@ -288,6 +291,12 @@ void Engine::validate(const std::string& dir) {
 void Engine::allocate(const std::string& dir) {
   CKE(cudaSetDevice(device));
   CKE(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  // The 3-channel input is stored with a stride of 8 channels (pad channels stay zero), so the
+  // dense convs that read it run on the tensor cores with zero-padded weights (Cin 3 -> 8).
+  bool stem = false;
+  for (const Op& op : raw)
+    if (op.kind == CONV && op.a == 0 && op.g == 1 && op.Cin == 3) stem = true;
+  if (stem) bufs[tens[0].buf].C = 8;
   for (auto& b : bufs) {
     const size_t bytes = (size_t)maxB * b.H * b.W * b.C * 2;
     CKE(cudaMalloc(&b.p, bytes));
@@ -303,6 +312,24 @@ void Engine::allocate(const std::string& dir) {
       if (op.woff + wcount > nweights || op.boff + (size_t)op.Cout > nbias)
         throw Error("weights.f16 / bias.f32 too small for the graph");
     }
+  if (stem) {
+    const uint16_t* w16 = (const uint16_t*)wf.data();
+    std::vector<uint16_t> pad;
+    std::vector<size_t> offs;
+    for (const Op& op : raw)
+      if (op.kind == CONV && op.a == 0 && op.g == 1 && op.Cin == 3) {
+        offs.push_back(pad.size());
+        const size_t taps = (size_t)op.Cout * op.k * op.k;
+        for (size_t t = 0; t < taps; t++)
+          for (int c = 0; c < 8; c++) pad.push_back(c < 3 ? w16[op.woff + t * 3 + c] : 0);
+      }
+    CKE(cudaMalloc(&dstem, pad.size() * 2));
+    CKE(cudaMemcpy(dstem, pad.data(), pad.size() * 2, cudaMemcpyHostToDevice));
+    size_t i = 0;
+    for (Op& op : raw)
+      if (op.kind == CONV && op.a == 0 && op.g == 1 && op.Cin == 3)
+        op.wpad = (const uint16_t*)dstem + offs[i++];
+  }
   CKE(cudaMalloc(&dweights, std::max<size_t>(wf.size(), 16)));
   CKE(cudaMemcpy(dweights, wf.data(), wf.size(), cudaMemcpyHostToDevice));
   CKE(cudaMalloc(&dbias, std::max<size_t>(bf.size(), 16)));
@@ -364,6 +391,11 @@ void Engine::run_op(const Op& op, int B) {
       p.k = op.k; p.s = op.s; p.p = op.p; p.groups = op.g; p.act = op.act;
       p.Cin = op.Cin; p.Cout = op.Cout; p.tile = op.tile; p.msub = op.msub;
       YkView x = view(op.a, B), y = view(op.out, B);
+      if (op.wpad) {            // padded stem: 8-channel input view, padded weights
+        p.weight = op.wpad;
+        p.Cin = 8;
+        x.C = 8;
+      }
       YkView r;
       if (op.res >= 0) r = view(op.res, B);
       CKY(yk_conv(&x, &y, op.res >= 0 ? &r : nullptr, &p, (yk_stream_t)st));
@@ -445,7 +477,7 @@ void Engine::autotune() {
   static const int combos[][2] = {{32, 1}, {32, 2}, {32, 4}, {64, 1}, {64, 2}, {64, 4},
                                   {128, 1}, {128, 2}, {256, 1}};
   for (Op& op : ops) {
-    if (op.kind != CONV || op.g != 1 || op.Cin % 8) continue;
+    if (op.kind != CONV || op.g != 1 || (op.Cin % 8 && !op.wpad)) continue;
     int best_t = 0, best_m = 0;
     float tbest = 1e30f;
     for (const auto& cm : combos) {
