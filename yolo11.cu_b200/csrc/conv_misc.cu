@@ -2,6 +2,7 @@
 // upsample, pixel shuffle, channel-slice copy and add, plus the yk_conv dispatcher.
 // All activation accesses are 16-byte vectors of 8 channels where the view allows it
 // (channel counts, offsets and strides are multiples of 8 in every exported graph).
+#include <algorithm>
 #include <atomic>
 #include <string.h>
 
@@ -192,8 +193,8 @@ __global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restric
 }
 
 // 3x3 depthwise conv, register-blocked: thread = 8 channels x 4 consecutive output pixels
-// of one row.  The block stages the filter transposed to [9][C] in shared memory; the 72
-// weights of a thread's channels then live in registers, each input column of
+// of one row.  The block stages the filter transposed to [9][C] in shared memory and each
+// filter row's 24 weights of a thread's channels are loaded to registers per row, each input column of
 // the 3 x (3*S + 1 ... ) window is loaded once (16 bytes) and feeds every output it touches.
 // Index arithmetic is 32-bit (I = unsigned) whenever the element count allows it.
 template <int S, typename I>
@@ -204,32 +205,20 @@ __global__ void __launch_bounds__(256) dwconv3_kernel(DView x, DView y, DView r,
   constexpr int PX = 4, NIN = (PX - 1) * S + 3;
   extern __shared__ __align__(16) __half dw_wsm[];   // weights transposed to [9][C]
   for (int i = threadIdx.x; i < y.C * 9; i += blockDim.x) {
-    const int ch = i / 9, t = i - ch * 9;
-    dw_wsm[t * y.C + ch] = w[i];
+    const int t = i / y.C, ch = i - t * y.C;
+    dw_wsm[i] = w[ch * 9 + t];
   }
   __syncthreads();
   const int cg = y.C >> 3, nxb = (y.W + PX - 1) / PX;
   const I total = (I)batch * y.H * nxb * cg;
-  const I idx = (I)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= total) return;
+  for (I idx = (I)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (I)gridDim.x * blockDim.x) {
   const int g = (int)(idx % cg);
   I rr = idx / cg;
   const int xb = (int)(rr % nxb);
   rr /= nxb;
   const int oy = (int)(rr % y.H), img = (int)(rr / y.H);
   const int c = g << 3, ox0 = xb * PX;
-  float wr[9][8];
-#pragma unroll
-  for (int t = 0; t < 9; t++) {
-    const uint4 v = *(const uint4*)(dw_wsm + t * y.C + c);
-    const __half2* h = (const __half2*)&v;
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const float2 f = __half22float2(h[q]);
-      wr[t][2 * q] = f.x;
-      wr[t][2 * q + 1] = f.y;
-    }
-  }
   float acc[PX][8];
   {
     const float4 b0 = *(const float4*)(b + c), b1 = *(const float4*)(b + c + 4);
@@ -245,12 +234,28 @@ __global__ void __launch_bounds__(256) dwconv3_kernel(DView x, DView y, DView r,
     const int iy = oy * S - 1 + ky;
     if (iy < 0 || iy >= x.H) continue;
     const __half* xrow = x.p + x.pix(img, iy, 0) + c;
+    float wr[3][8];   // this filter row's weights for the thread's 8 channels
+#pragma unroll
+    for (int kx = 0; kx < 3; kx++) {
+      const uint4 v = *(const uint4*)(dw_wsm + (ky * 3 + kx) * y.C + c);
+      const __half2* hw = (const __half2*)&v;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const float2 f = __half22float2(hw[q]);
+        wr[kx][2 * q] = f.x;
+        wr[kx][2 * q + 1] = f.y;
+      }
+    }
+    uint4 xin[NIN];   // issue the whole row of loads first: one latency per filter row
 #pragma unroll
     for (int u = 0; u < NIN; u++) {
       const int ix = ix0 + u;
-      if (ix < 0 || ix >= x.W) continue;
-      const uint4 xv = *(const uint4*)(xrow + (size_t)ix * x.stride);
-      const __half2* xh = (const __half2*)&xv;
+      xin[u] = (ix >= 0 && ix < x.W) ? *(const uint4*)(xrow + (size_t)ix * x.stride)
+                                     : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < NIN; u++) {
+      const __half2* xh = (const __half2*)&xin[u];
       float xf[8];
 #pragma unroll
       for (int q = 0; q < 4; q++) {
@@ -263,7 +268,7 @@ __global__ void __launch_bounds__(256) dwconv3_kernel(DView x, DView y, DView r,
         const int kx = u - j * S;   // compile-time after unrolling
         if (kx < 0 || kx > 2) continue;
 #pragma unroll
-        for (int q = 0; q < 8; q++) acc[j][q] = fmaf(xf[q], wr[ky * 3 + kx][q], acc[j][q]);
+        for (int q = 0; q < 8; q++) acc[j][q] = fmaf(xf[q], wr[kx][q], acc[j][q]);
       }
     }
   }
@@ -292,6 +297,7 @@ __global__ void __launch_bounds__(256) dwconv3_kernel(DView x, DView y, DView r,
       oh[q] = __floats2half2_rn(a0 + rv[2 * q], a1 + rv[2 * q + 1]);
     }
     *(uint4*)(y.p + pix * y.stride + c) = o;
+  }
   }
 }
 
@@ -344,22 +350,22 @@ __global__ void maxpool_kernel(DView x, DView y1, DView y2, DView y3, int nr, I 
 // mode 0: nearest 2x upsample (engine/engine.cu:697-708); mode 1: pixel shuffle r=2 from
 // quadrant blocks (engine/engine.cu:713-725); mode 2: channel-slice copy (727-732).
 // Thread = one output pixel x 8 channels.
-template <typename I>
-__global__ void move8_kernel(DView x, DView y, int mode, I total) {
-  const I idx = (I)blockIdx.x * blockDim.x + threadIdx.x;
+// One block row per output image row (blockIdx.y strides over batch x H), threads over
+// (x, 8-channel group): no 64-bit or per-thread image/row divisions.
+__global__ void move8_kernel(DView x, DView y, int mode, int rows) {
   const int cg = y.C >> 3;
-  if (idx >= total) return;
-  const int g = (int)(idx % cg);
-  const I pix = idx / cg;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= y.W * cg) return;
+  const int g = i % cg, ox = i / cg;
   const int c = g << 3;
-  const int HW = y.H * y.W;
-  const int img = (int)(pix / HW), rem = (int)(pix - (I)img * HW);
-  const int oy = rem / y.W, ox = rem - oy * y.W;
-  const __half* src;
-  if (mode == 0) src = x.p + x.pix(img, oy >> 1, ox >> 1) + c;
-  else if (mode == 1) src = x.p + x.pix(img, oy >> 1, ox >> 1) + (((oy & 1) << 1) | (ox & 1)) * y.C + c;
-  else src = x.p + x.pix(img, oy, ox) + c;
-  *(uint4*)(y.p + (size_t)pix * y.stride + c) = *(const uint4*)src;
+  for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int img = row / y.H, oy = row - img * y.H;
+    const __half* src;
+    if (mode == 0) src = x.p + x.pix(img, oy >> 1, ox >> 1) + c;
+    else if (mode == 1) src = x.p + x.pix(img, oy >> 1, ox >> 1) + (((oy & 1) << 1) | (ox & 1)) * y.C + c;
+    else src = x.p + x.pix(img, oy, ox) + c;
+    *(uint4*)(y.p + y.pix(img, oy, ox) + c) = *(const uint4*)src;
+  }
 }
 
 __global__ void copy_scalar_kernel(DView x, DView y, long long total) {
@@ -450,7 +456,7 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     const long long total = npix * (p->Cout / 8);
     if (p->k == 3 && p->p == 1 && (p->s == 1 || p->s == 2)) {
       const long long t3 = (long long)y->batch * y->H * ((y->W + 3) / 4) * (p->Cout / 8);
-      const unsigned nb = nblk(t3, 256);
+      const unsigned nb = (unsigned)std::min<long long>(nblk(t3, 256), 148 * 8);  // grid-stride
       const size_t wsmem = (size_t)p->Cout * 9 * sizeof(__half);
       if (wsmem > 48 * 1024) return YK_EUNSUP;
       const __half* wp = (const __half*)p->weight;
@@ -506,12 +512,28 @@ int yk_maxpool5x3(const YkView* x, const YkView* y1, const YkView* y2, const YkV
   return check_launch("maxpool5x3");
 }
 
+// Nearest 2x upsample: thread = one input pixel x 8 channels, one 16-byte load, four stores.
+__global__ void upsample2_kernel(DView x, DView y, int rows) {
+  const int cg = x.C >> 3;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= x.W * cg) return;
+  const int c = (i % cg) << 3, ix = i / cg;
+  for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int img = row / x.H, iy = row - img * x.H;
+    const uint4 v = *(const uint4*)(x.p + x.pix(img, iy, ix) + c);
+    __half* o = y.p + y.pix(img, 2 * iy, 2 * ix) + c;
+    const size_t rs = (size_t)y.W * y.stride;
+    *(uint4*)o = v;
+    *(uint4*)(o + y.stride) = v;
+    *(uint4*)(o + rs) = v;
+    *(uint4*)(o + rs + y.stride) = v;
+  }
+}
+
 static int move8(const YkView* x, const YkView* y, int mode, yk_stream_t st) {
-  const long long total = (long long)y->batch * y->H * y->W * (y->C / 8);
-  if (total < (1LL << 31))
-    move8_kernel<unsigned><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), mode, (unsigned)total);
-  else
-    move8_kernel<long long><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), mode, total);
+  const int rows = y->batch * y->H;
+  dim3 grid(nblk((long long)y->W * (y->C / 8), 256), rows < 65535 ? rows : 65535);
+  move8_kernel<<<grid, 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), mode, rows);
   note_launch();
   return check_launch("move8");
 }
@@ -520,7 +542,11 @@ int yk_upsample2(const YkView* x, const YkView* y, yk_stream_t st) {
   if (!view_vec8(x) || !view_vec8(y) || x->batch != y->batch || x->C != y->C ||
       y->H != 2 * x->H || y->W != 2 * x->W)
     return YK_EINVAL;
-  return move8(x, y, 0, st);
+  const int rows = x->batch * x->H;
+  dim3 grid(nblk((long long)x->W * (x->C / 8), 256), rows < 65535 ? rows : 65535);
+  upsample2_kernel<<<grid, 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), rows);
+  note_launch();
+  return check_launch("upsample2");
 }
 
 int yk_ps2(const YkView* x, const YkView* y, yk_stream_t st) {
