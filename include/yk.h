@@ -51,6 +51,12 @@ typedef struct {
 // Replaces the CONV dispatch of runOp (engine/engine.cu:1263-1336).
 int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, yk_stream_t st);
 
+// im2col of a thin input (x->C <= 8) for a k x k / stride s / pad p conv: row (n, oy, ox) of
+// col gets the k*k*x->C taps in (ky, kx, c) order, zero past the image and past k*k*C
+// (col->C >= k*k*x->C, a multiple of 8).  With it the first conv (Cin = 3, k*k*C = 27 -> 32)
+// runs as a 1x1 tensor-core GEMM.  Replaces the reference's direct k_conv0 (engine/engine.cu:487-532).
+int yk_im2col(const YkView* x, const YkView* col, int k, int s, int p, yk_stream_t st);
+
 // 5x5 stride-1 pad-2 max pool (SPPF), engine/engine.cu:672-695.
 int yk_maxpool5(const YkView* x, const YkView* y, yk_stream_t st);
 // The SPPF chain y1 = pool5(x), y2 = pool5(y1), y3 = pool5(y2) in one pass over x.

@@ -215,3 +215,23 @@ def test_bad_arguments_rejected(lib, cuda):
     bad = rt.tview(x, 4, 16)       # coff + C > stride
     assert lib.yk_copyc(C.byref(bad), C.byref(rt.tview(y)), st) != 0
     assert lib.yk_attn(C.byref(rt.tview(x)), C.byref(rt.tview(y)), 1, 4, 8, st) != 0
+
+
+@pytest.mark.parametrize("k,s,p", [(3, 2, 1), (3, 1, 1), (1, 1, 0)])
+def test_im2col_thin(lib, cuda, k, s, p):
+    from yolo11_cu_b200 import runtime as rt
+    B, H, W, Cin = 2, 17, 12, 3
+    x = torch.randn(B, H, W, Cin, device=cuda).half()
+    Ho, Wo = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
+    kp = (k * k * Cin + 7) // 8 * 8
+    col = torch.full((B, Ho, Wo, kp), 5.0, device=cuda).half()
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.yk_im2col(C.byref(rt.tview(x)), C.byref(rt.tview(col)), k, s, p, st) == 0
+    torch.cuda.synchronize()
+    xp = F.pad(x.permute(0, 3, 1, 2).float(), (p, p, p, p))
+    ref = torch.zeros(B, Ho, Wo, kp, device=cuda)
+    for ky in range(k):
+        for kx in range(k):
+            patch = xp[:, :, ky:ky + s * (Ho - 1) + 1:s, kx:kx + s * (Wo - 1) + 1:s]
+            ref[..., (ky * k + kx) * Cin:(ky * k + kx + 1) * Cin] = patch.permute(0, 2, 3, 1)
+    assert torch.equal(col.float(), ref)

@@ -126,6 +126,39 @@ __global__ void __launch_bounds__(128) conv_stem3_kernel(DView x, DView y,
   }
 }
 
+// ---------------- im2col for thin inputs (stem) ----------------
+// Thread = one output pixel: gathers its k*k*C taps (C <= 8) and writes the padded row as
+// 16-byte stores.
+__global__ void im2col_kernel(DView x, DView col, int k, int s, int p, long long npix) {
+  const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= npix) return;
+  const int HW = col.H * col.W;
+  const int img = (int)(pix / HW), rem = (int)(pix - (long long)img * HW);
+  const int oy = rem / col.W, ox = rem - oy * col.W;
+  __half* o = col.p + (size_t)pix * col.stride;
+  __half buf[8];
+  int n = 0, base = 0;
+  const __half zero = __float2half(0.f);
+  for (int ky = 0; ky < k; ky++) {
+    const int iy = oy * s - p + ky;
+    for (int kx = 0; kx < k; kx++) {
+      const int ix = ox * s - p + kx;
+      const bool ok = iy >= 0 && iy < x.H && ix >= 0 && ix < x.W;
+      const __half* xp = x.p + x.pix(img, ok ? iy : 0, ok ? ix : 0);
+      for (int c = 0; c < x.C; c++) {
+        buf[n++] = ok ? xp[c] : zero;
+        if (n == 8) { *(uint4*)(o + base) = *(uint4*)buf; base += 8; n = 0; }
+      }
+    }
+  }
+  while (base < col.C) {
+    while (n < 8) buf[n++] = zero;
+    *(uint4*)(o + base) = *(uint4*)buf;
+    base += 8;
+    n = 0;
+  }
+}
+
 // ---------------- depthwise conv ----------------
 // Thread = one output pixel x 8 channels, 16-byte activation loads.  The block first stages
 // the OHWI [C][k][k][1] weights transposed to [k*k][C] in shared memory, so each tap's 8
@@ -484,6 +517,17 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     return check_launch("dwconv");
   }
   return YK_EUNSUP;
+}
+
+int yk_im2col(const YkView* x, const YkView* col, int k, int s, int p, yk_stream_t st) {
+  if (!view_ok(x) || !view_vec8(col) || x->C > 8 || k < 1 || s < 1 || p < 0 ||
+      x->batch != col->batch || col->C < k * k * x->C ||
+      (x->H + 2 * p - k) / s + 1 != col->H || (x->W + 2 * p - k) / s + 1 != col->W)
+    return YK_EINVAL;
+  const long long npix = (long long)col->batch * col->H * col->W;
+  im2col_kernel<<<nblk(npix, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*col), k, s, p, npix);
+  note_launch();
+  return check_launch("im2col");
 }
 
 int yk_maxpool5(const YkView* x, const YkView* y, yk_stream_t st) {

@@ -61,7 +61,9 @@ struct Op {
   int y2 = -1, y3 = -1;           // POOLX3 outputs 2 and 3
   int tile = 0;                   // tensor-core N tile chosen by the planner / autotuner
   int msub = 0;                   // tensor-core stacked M sub-tiles (0 = heuristic)
-  const void* wpad = nullptr;     // stem conv on the 8-channel padded input: padded weights
+  const void* wpad = nullptr;     // stem conv as GEMM over an im2col buffer: padded weights
+  void* col = nullptr;            // its im2col buffer [maxB][Ho][Wo][kpad]
+  int kpad = 0;
 };
 
 struct SlotGeom { float scale = 1.f; int top = 0, left = 0; };
@@ -88,7 +90,8 @@ struct Engine {
   std::vector<Ten> tens;
   std::vector<Op> raw, ops;       // unfused (dump order) and planned (fused) op lists
   void* dweights = nullptr;
-  void* dstem = nullptr;          // zero-padded (Cin 3 -> 8) weights of convs reading the input
+  void* dstem = nullptr;          // stem convs: zero-padded [Cout][kpad] weights
+  std::vector<void*> dcols;       // stem convs: im2col buffers
   float* dbias = nullptr;
   size_t nweights = 0, nbias = 0;
   // head
@@ -119,6 +122,8 @@ struct Engine {
       if (b.p) cudaFree(b.p), b.p = nullptr;
     if (dweights) cudaFree(dweights);
     if (dstem) cudaFree(dstem);
+    for (void* c : dcols) cudaFree(c);
+    dcols.clear();
     if (dbias) cudaFree(dbias);
     if (post.ws) cudaFree(post.ws);
     if (post.outdets) cudaFree(post.outdets);
@@ -291,12 +296,14 @@ void Engine::validate(const std::string& dir) {
 void Engine::allocate(const std::string& dir) {
   CKE(cudaSetDevice(device));
   CKE(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
-  // The 3-channel input is stored with a stride of 8 channels (pad channels stay zero), so the
-  // dense convs that read it run on the tensor cores with zero-padded weights (Cin 3 -> 8).
+  // Dense convs on the 3-channel input (the stem) run as a tensor-core GEMM over an im2col
+  // buffer: each output pixel's k*k*3 taps padded to a multiple of 8 (27 -> 32), one
+  // contiguous row per pixel, so the GEMM's A operand streams by 2-D TMA.
+  auto is_stem = [&](const Op& op) {
+    return op.kind == CONV && op.g == 1 && op.Cin == 3 && op.k * op.k * 3 <= 64;
+  };
   bool stem = false;
-  for (const Op& op : raw)
-    if (op.kind == CONV && op.a == 0 && op.g == 1 && op.Cin == 3) stem = true;
-  if (stem) bufs[tens[0].buf].C = 8;
+  for (const Op& op : raw) stem = stem || is_stem(op);
   for (auto& b : bufs) {
     const size_t bytes = (size_t)maxB * b.H * b.W * b.C * 2;
     CKE(cudaMalloc(&b.p, bytes));
@@ -317,18 +324,25 @@ void Engine::allocate(const std::string& dir) {
     std::vector<uint16_t> pad;
     std::vector<size_t> offs;
     for (const Op& op : raw)
-      if (op.kind == CONV && op.a == 0 && op.g == 1 && op.Cin == 3) {
+      if (is_stem(op)) {
+        const int kk = op.k * op.k * 3, kp = (kk + 7) / 8 * 8;
         offs.push_back(pad.size());
-        const size_t taps = (size_t)op.Cout * op.k * op.k;
-        for (size_t t = 0; t < taps; t++)
-          for (int c = 0; c < 8; c++) pad.push_back(c < 3 ? w16[op.woff + t * 3 + c] : 0);
+        for (int o = 0; o < op.Cout; o++)
+          for (int i = 0; i < kp; i++) pad.push_back(i < kk ? w16[op.woff + (size_t)o * kk + i] : 0);
       }
     CKE(cudaMalloc(&dstem, pad.size() * 2));
     CKE(cudaMemcpy(dstem, pad.data(), pad.size() * 2, cudaMemcpyHostToDevice));
     size_t i = 0;
     for (Op& op : raw)
-      if (op.kind == CONV && op.a == 0 && op.g == 1 && op.Cin == 3)
+      if (is_stem(op)) {
         op.wpad = (const uint16_t*)dstem + offs[i++];
+        op.kpad = (op.k * op.k * 3 + 7) / 8 * 8;
+        const Buf& yb = bufs[tens[op.out].buf];
+        void* col = nullptr;
+        CKE(cudaMalloc(&col, (size_t)maxB * yb.H * yb.W * op.kpad * 2));
+        dcols.push_back(col);
+        op.col = col;
+      }
   }
   CKE(cudaMalloc(&dweights, std::max<size_t>(wf.size(), 16)));
   CKE(cudaMemcpy(dweights, wf.data(), wf.size(), cudaMemcpyHostToDevice));
@@ -391,10 +405,15 @@ void Engine::run_op(const Op& op, int B) {
       p.k = op.k; p.s = op.s; p.p = op.p; p.groups = op.g; p.act = op.act;
       p.Cin = op.Cin; p.Cout = op.Cout; p.tile = op.tile; p.msub = op.msub;
       YkView x = view(op.a, B), y = view(op.out, B);
-      if (op.wpad) {            // padded stem: 8-channel input view, padded weights
+      if (op.wpad) {            // stem: im2col into the padded buffer, then a 1x1 GEMM
+        YkView col;
+        col.ptr = op.col; col.batch = B; col.H = y.H; col.W = y.W;
+        col.stride = op.kpad; col.coff = 0; col.C = op.kpad;
+        CKY(yk_im2col(&x, &col, op.k, op.s, op.p, (yk_stream_t)st));
+        x = col;
         p.weight = op.wpad;
-        p.Cin = 8;
-        x.C = 8;
+        p.Cin = op.kpad;
+        p.k = 1; p.s = 1; p.p = 0;
       }
       YkView r;
       if (op.res >= 0) r = view(op.res, B);

@@ -48,6 +48,7 @@ _P = C.POINTER
 _SIGS = {
     # kernel ABI (include/yk.h)
     "yk_conv": (C.c_int, [_P(YkView), _P(YkView), _P(YkView), _P(YkConv), C.c_void_p]),
+    "yk_im2col": (C.c_int, [_P(YkView), _P(YkView), C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "yk_maxpool5": (C.c_int, [_P(YkView), _P(YkView), C.c_void_p]),
     "yk_maxpool5x3": (C.c_int, [_P(YkView)] * 4 + [C.c_void_p]),
     "yk_upsample2": (C.c_int, [_P(YkView), _P(YkView), C.c_void_p]),
