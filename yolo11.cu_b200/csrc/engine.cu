@@ -153,6 +153,9 @@ struct Engine {
   void allocate(const std::string& dir);
   void plan();
   void autotune();
+  std::string tuning_key() const;
+  bool load_tuning(const char* path);
+  void save_tuning(const char* path) const;
   void run_op(const Op& op, int B);
   void run_post(int B);
   void forward(int B);
@@ -522,6 +525,50 @@ void Engine::autotune() {
   // the tuning runs overwrote activations; every forward recomputes them
 }
 
+std::string Engine::tuning_key() const {
+  cudaDeviceProp pr;
+  cudaGetDeviceProperties(&pr, device);
+  std::string k = std::string(pr.name) + "|B" + std::to_string(maxB);
+  for (const Op& op : ops)
+    if (op.kind == CONV)
+      k += "|" + std::to_string(op.Cin) + "," + std::to_string(op.Cout) + "," +
+           std::to_string(op.k) + "," + std::to_string(op.s) + "," +
+           std::to_string(bufs[tens[op.out].buf].H);
+  return k;
+}
+
+bool Engine::load_tuning(const char* path) {
+  FILE* f = fopen(path, "r");
+  if (!f) return false;
+  std::unique_ptr<FILE, int (*)(FILE*)> g(f, fclose);
+  std::string key = tuning_key();
+  std::vector<char> line(key.size() + 16);
+  if (!fgets(line.data(), (int)line.size(), f)) return false;
+  std::string got(line.data());
+  while (!got.empty() && (got.back() == '\n' || got.back() == '\r')) got.pop_back();
+  if (got != key) return false;
+  std::vector<std::pair<int, int>> tiles;
+  int t, m;
+  while (fscanf(f, "%d %d", &t, &m) == 2) tiles.push_back({t, m});
+  size_t i = 0;
+  for (const Op& op : ops)
+    if (op.kind == CONV) i++;
+  if (tiles.size() != i) return false;
+  i = 0;
+  for (Op& op : ops)
+    if (op.kind == CONV) { op.tile = tiles[i].first; op.msub = tiles[i].second; i++; }
+  return true;
+}
+
+void Engine::save_tuning(const char* path) const {
+  FILE* f = fopen(path, "w");
+  if (!f) return;
+  fprintf(f, "%s\n", tuning_key().c_str());
+  for (const Op& op : ops)
+    if (op.kind == CONV) fprintf(f, "%d %d\n", op.tile, op.msub);
+  fclose(f);
+}
+
 cudaGraphExec_t Engine::graph_for(int B) {
   auto it = graphs.find(B);
   if (it != graphs.end()) return it->second;
@@ -612,7 +659,15 @@ void* yolo_create_ex(const char* model_dir, int max_batch, const YoloOptions* op
     DeviceScope ds(dev);
     e->allocate(model_dir);
     e->plan();
-    if (e->opt.autotune) e->autotune();
+    if (e->opt.autotune) {
+      // optional tuning cache (env YOLO_TUNE_CACHE=path): tiles keyed by device name, batch
+      // and the conv list; a miss tunes and rewrites the file
+      const char* cache = getenv("YOLO_TUNE_CACHE");
+      if (!(cache && e->load_tuning(cache))) {
+        e->autotune();
+        if (cache) e->save_tuning(cache);
+      }
+    }
     CKE(cudaStreamSynchronize(e->st));
     int derr = yk_fetch_device_error();
     if (derr) throw Error("device error word set during create: " + std::to_string(derr));
