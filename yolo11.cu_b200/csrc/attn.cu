@@ -15,6 +15,8 @@ namespace yk {
 
 template <int KD, int HD, int KS>
 __global__ void __launch_bounds__(128) attn_kernel(DView qkv, DView y, int N) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   extern __shared__ __align__(16) __half kv[];   // [N][KD] keys then [N][HD] values
   __half* ks = kv;
   __half* vs = kv + (size_t)N * KD;
@@ -137,7 +139,7 @@ static int launch_attn(const YkView* qkv, const YkView* y, int heads, int N, siz
     attr = true;
   }
   dim3 grid((N + 128 / KS - 1) / (128 / KS), heads, qkv->batch);
-  attn_kernel<32, 64, KS><<<grid, 128, smem, st>>>(dview(*qkv), dview(*y), N);
+  launch_k(attn_kernel<32, 64, KS>, grid, 128, smem, (cudaStream_t)st, dview(*qkv), dview(*y), N);
   note_launch();
   return check_launch("attn");
 }
@@ -166,6 +168,8 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 constexpr int kAttnChunk = 192, kKs = 40, kVs = 72;
 
 __global__ void __launch_bounds__(128) attn_mma_kernel(DView qkv, DView y, int N, float scale) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   __shared__ __align__(16) __half Ks[kAttnChunk * kKs];
   __shared__ __align__(16) __half Vs[kAttnChunk * kVs];
   const int h = blockIdx.y, img = blockIdx.z;
@@ -295,7 +299,7 @@ extern "C" int yk_attn(const YkView* qkv, const YkView* y, int heads, int kd, in
   const int N = qkv->H * qkv->W;
   if (!getenv("YK_ATTN_SIMT")) {
     dim3 grid((N + 63) / 64, heads, qkv->batch);
-    attn_mma_kernel<<<grid, 128, 0, (cudaStream_t)st>>>(dview(*qkv), dview(*y), N,
+    launch_k(attn_mma_kernel, grid, 128, 0, (cudaStream_t)st, dview(*qkv), dview(*y), N,
                                                         rsqrtf((float)kd));
     note_launch();
     return check_launch("attn_mma");

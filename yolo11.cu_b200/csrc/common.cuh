@@ -6,6 +6,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <utility>
+
 #include "../../include/yk.h"
 
 namespace yk {
@@ -43,6 +45,40 @@ __device__ int g_device_error = 0;         // set by bounded waits that give up 
 // Bounded-wait budget: a wait that has not completed after this many nanoseconds of
 // %globaltimer gives up, sets g_device_error and lets the kernel unwind.
 constexpr unsigned long long kWaitNs = 2000000000ull;
+
+// ---------------- programmatic dependent launch ----------------
+// Every kernel is launched with programmatic stream serialisation, so the next kernel in
+// the stream (or graph) may be scheduled while this one still runs and do its set-up
+// (barrier init, tensor-map prefetch) in the shadow of our tail.  The contract each kernel
+// keeps: pdl_wait() before its first access to memory that an earlier kernel writes or
+// reads (it returns once the previous grid has completed and flushed), then pdl_trigger()
+// to let the following kernel start its own set-up.  With the wait placed before the
+// trigger, at most one kernel waits behind the running one.  YK_NO_PDL=1 launches plainly.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+bool pdl_enabled();
+// Per host thread: -1 follows pdl_enabled(), 0 / 1 force plain / programmatic launches (the
+// engine captures its graphs both ways and keeps the faster).
+static thread_local int g_pdl_override = -1;
+
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                                   size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed =
+      g_pdl_override >= 0 ? g_pdl_override : pdl_enabled() ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;

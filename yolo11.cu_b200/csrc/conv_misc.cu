@@ -4,6 +4,7 @@
 // (channel counts, offsets and strides are multiples of 8 in every exported graph).
 #include <algorithm>
 #include <atomic>
+#include <stdlib.h>
 #include <string.h>
 
 #include "common.cuh"
@@ -12,6 +13,14 @@ namespace yk {
 
 static std::atomic<long long> g_launches{0};
 static thread_local char g_cuda_err[256];
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("YK_NO_PDL");
+    return !(e && *e && *e != '0');
+  }();
+  return on;
+}
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 int check_launch(const char* what) {
@@ -31,6 +40,8 @@ static inline unsigned nblk(long long n, int tb) { return (unsigned)((n + tb - 1
 __global__ void conv_small_cin_kernel(DView x, DView y, const __half* __restrict__ w,
                                       const float* __restrict__ b, int Cin, int k, int s, int p,
                                       int act, long long npix) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   extern __shared__ float wsm[];   // [8][k*k*Cin] then bias[8]
   const int KK = k * k * Cin;
   const int co0 = blockIdx.y * 8;
@@ -80,6 +91,8 @@ __global__ void __launch_bounds__(128) conv_stem3_kernel(DView x, DView y,
                                                          const __half* __restrict__ w,
                                                          const float* __restrict__ b, int Cout,
                                                          int s, int p, int act, long long npix) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   extern __shared__ __align__(16) float wst[];   // [Cout][K*K*3] then bias[Cout]
   constexpr int KK = K * K * 3;
   for (int i = threadIdx.x; i < Cout * KK; i += blockDim.x) wst[i] = __half2float(w[i]);
@@ -130,6 +143,8 @@ __global__ void __launch_bounds__(128) conv_stem3_kernel(DView x, DView y,
 // Thread = one output pixel: gathers its k*k*C taps (C <= 8) and writes the padded row as
 // 16-byte stores.
 __global__ void im2col_kernel(DView x, DView col, int k, int s, int p, long long npix) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (pix >= npix) return;
   const int HW = col.H * col.W;
@@ -167,6 +182,8 @@ __global__ void im2col_kernel(DView x, DView col, int k, int s, int p, long long
 __global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restrict__ w,
                               const float* __restrict__ b, int k, int s, int p, int act,
                               long long total) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   extern __shared__ __align__(16) __half wt[];   // [k*k][C]
   const int C = y.C, KK = k * k;
   for (int i = threadIdx.x; i < C * KK; i += blockDim.x) {
@@ -235,6 +252,8 @@ __global__ void __launch_bounds__(256) dwconv3_kernel(DView x, DView y, DView r,
                                                       const __half* __restrict__ w,
                                                       const float* __restrict__ b, int act,
                                                       int batch) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   constexpr int PX = 4, NIN = (PX - 1) * S + 3;
   extern __shared__ __align__(16) __half dw_wsm[];   // weights transposed to [9][C]
   for (int i = threadIdx.x; i < y.C * 9; i += blockDim.x) {
@@ -347,6 +366,8 @@ __device__ __forceinline__ void hmax8(uint4& m, const uint4 v) {
 // with -inf padding).  Replaces k_maxpool5 (engine/engine.cu:672-695).
 template <typename I>
 __global__ void maxpool_kernel(DView x, DView y1, DView y2, DView y3, int nr, I total) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   const I idx = (I)blockIdx.x * blockDim.x + threadIdx.x;
   const int cg = x.C >> 3;
   if (idx >= total) return;
@@ -386,6 +407,8 @@ __global__ void maxpool_kernel(DView x, DView y1, DView y2, DView y3, int nr, I 
 // One block row per output image row (blockIdx.y strides over batch x H), threads over
 // (x, 8-channel group): no 64-bit or per-thread image/row divisions.
 __global__ void move8_kernel(DView x, DView y, int mode, int rows) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   const int cg = y.C >> 3;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= y.W * cg) return;
@@ -402,6 +425,8 @@ __global__ void move8_kernel(DView x, DView y, int mode, int rows) {
 }
 
 __global__ void copy_scalar_kernel(DView x, DView y, long long total) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
   const int c = (int)(idx % y.C);
@@ -411,6 +436,8 @@ __global__ void copy_scalar_kernel(DView x, DView y, long long total) {
 
 template <typename I>
 __global__ void add8_kernel(DView a, DView b, DView y, I total) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   const I idx = (I)blockIdx.x * blockDim.x + threadIdx.x;
   const int cg = y.C >> 3;
   if (idx >= total) return;
@@ -467,7 +494,7 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   if (p->groups == 1 && p->Cin == 3 && p->k == 3 && !res && p->Cout % 8 == 0 &&
       p->Cout <= 256) {
     const size_t smem = ((size_t)p->Cout * 27 + p->Cout) * sizeof(float);
-    conv_stem3_kernel<3><<<nblk(npix, 128), 128, smem, st>>>(
+    launch_k(conv_stem3_kernel<3>, nblk(npix, 128), 128, smem, (cudaStream_t)st, 
         dview(*x), dview(*y), (const __half*)p->weight, p->bias, p->Cout, p->s, p->p, p->act,
         npix);
     note_launch();
@@ -477,7 +504,7 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     if (res || p->Cout % 8) return YK_EUNSUP;
     const int KK = p->k * p->k * p->Cin;
     dim3 grid(nblk(npix, 256), p->Cout / 8);
-    conv_small_cin_kernel<<<grid, 256, (8 * KK + 8) * sizeof(float), st>>>(
+    launch_k(conv_small_cin_kernel, grid, 256, (8 * KK + 8) * sizeof(float), (cudaStream_t)st, 
         dview(*x), dview(*y), (const __half*)p->weight, p->bias, p->Cin, p->k, p->s, p->p,
         p->act, npix);
     note_launch();
@@ -494,11 +521,11 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
       if (wsmem > 48 * 1024) return YK_EUNSUP;
       const __half* wp = (const __half*)p->weight;
       if (t3 < (1LL << 31)) {
-        if (p->s == 1) dwconv3_kernel<1, unsigned><<<nb, 256, wsmem, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
-        else dwconv3_kernel<2, unsigned><<<nb, 256, wsmem, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+        if (p->s == 1) launch_k(dwconv3_kernel<1, unsigned>, nb, 256, wsmem, (cudaStream_t)st, dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+        else launch_k(dwconv3_kernel<2, unsigned>, nb, 256, wsmem, (cudaStream_t)st, dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
       } else {
-        if (p->s == 1) dwconv3_kernel<1, long long><<<nb, 256, wsmem, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
-        else dwconv3_kernel<2, long long><<<nb, 256, wsmem, st>>>(dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+        if (p->s == 1) launch_k(dwconv3_kernel<1, long long>, nb, 256, wsmem, (cudaStream_t)st, dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
+        else launch_k(dwconv3_kernel<2, long long>, nb, 256, wsmem, (cudaStream_t)st, dview(*x), dview(*y), r, wp, p->bias, p->act, y->batch);
       }
       note_launch();
       return check_launch("dwconv3");
@@ -510,7 +537,7 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
       cudaFuncSetAttribute(dwconv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
       attr = true;
     }
-    dwconv_kernel<<<nblk(total, 256), 256, smem, st>>>(dview(*x), dview(*y), r,
+    launch_k(dwconv_kernel, nblk(total, 256), 256, smem, (cudaStream_t)st, dview(*x), dview(*y), r,
                                                     (const __half*)p->weight, p->bias, p->k,
                                                     p->s, p->p, p->act, total);
     note_launch();
@@ -525,7 +552,7 @@ int yk_im2col(const YkView* x, const YkView* col, int k, int s, int p, yk_stream
       (x->H + 2 * p - k) / s + 1 != col->H || (x->W + 2 * p - k) / s + 1 != col->W)
     return YK_EINVAL;
   const long long npix = (long long)col->batch * col->H * col->W;
-  im2col_kernel<<<nblk(npix, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*col), k, s, p, npix);
+  launch_k(im2col_kernel, nblk(npix, 256), 256, 0, (cudaStream_t)st, dview(*x), dview(*col), k, s, p, npix);
   note_launch();
   return check_launch("im2col");
 }
@@ -534,8 +561,8 @@ int yk_maxpool5(const YkView* x, const YkView* y, yk_stream_t st) {
   if (!view_vec8(x) || !view_vec8(y) || !same_shape(x, y)) return YK_EINVAL;
   const long long total = (long long)x->batch * x->H * x->W * (x->C / 8);
   DView Y = dview(*y);
-  if (total < (1LL << 31)) maxpool_kernel<unsigned><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), Y, Y, Y, 1, (unsigned)total);
-  else maxpool_kernel<long long><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), Y, Y, Y, 1, total);
+  if (total < (1LL << 31)) launch_k(maxpool_kernel<unsigned>, nblk(total, 256), 256, 0, (cudaStream_t)st, dview(*x), Y, Y, Y, 1, (unsigned)total);
+  else launch_k(maxpool_kernel<long long>, nblk(total, 256), 256, 0, (cudaStream_t)st, dview(*x), Y, Y, Y, 1, total);
   note_launch();
   return check_launch("maxpool5");
 }
@@ -547,10 +574,10 @@ int yk_maxpool5x3(const YkView* x, const YkView* y1, const YkView* y2, const YkV
     return YK_EINVAL;
   const long long total = (long long)x->batch * x->H * x->W * (x->C / 8);
   if (total < (1LL << 31))
-    maxpool_kernel<unsigned><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(
+    launch_k(maxpool_kernel<unsigned>, nblk(total, 256), 256, 0, (cudaStream_t)st, 
         dview(*x), dview(*y1), dview(*y2), dview(*y3), 3, (unsigned)total);
   else
-    maxpool_kernel<long long><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(
+    launch_k(maxpool_kernel<long long>, nblk(total, 256), 256, 0, (cudaStream_t)st, 
         dview(*x), dview(*y1), dview(*y2), dview(*y3), 3, total);
   note_launch();
   return check_launch("maxpool5x3");
@@ -558,6 +585,8 @@ int yk_maxpool5x3(const YkView* x, const YkView* y1, const YkView* y2, const YkV
 
 // Nearest 2x upsample: thread = one input pixel x 8 channels, one 16-byte load, four stores.
 __global__ void upsample2_kernel(DView x, DView y, int rows) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   const int cg = x.C >> 3;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= x.W * cg) return;
@@ -577,7 +606,7 @@ __global__ void upsample2_kernel(DView x, DView y, int rows) {
 static int move8(const YkView* x, const YkView* y, int mode, yk_stream_t st) {
   const int rows = y->batch * y->H;
   dim3 grid(nblk((long long)y->W * (y->C / 8), 256), rows < 65535 ? rows : 65535);
-  move8_kernel<<<grid, 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), mode, rows);
+  launch_k(move8_kernel, grid, 256, 0, (cudaStream_t)st, dview(*x), dview(*y), mode, rows);
   note_launch();
   return check_launch("move8");
 }
@@ -588,7 +617,7 @@ int yk_upsample2(const YkView* x, const YkView* y, yk_stream_t st) {
     return YK_EINVAL;
   const int rows = x->batch * x->H;
   dim3 grid(nblk((long long)x->W * (x->C / 8), 256), rows < 65535 ? rows : 65535);
-  upsample2_kernel<<<grid, 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), rows);
+  launch_k(upsample2_kernel, grid, 256, 0, (cudaStream_t)st, dview(*x), dview(*y), rows);
   note_launch();
   return check_launch("upsample2");
 }
@@ -604,7 +633,7 @@ int yk_copyc(const YkView* x, const YkView* y, yk_stream_t st) {
   if (!view_ok(x) || !view_ok(y) || !same_shape(x, y)) return YK_EINVAL;
   if (view_vec8(x) && view_vec8(y)) return move8(x, y, 2, st);
   const long long total = (long long)y->batch * y->H * y->W * y->C;
-  copy_scalar_kernel<<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*x), dview(*y), total);
+  launch_k(copy_scalar_kernel, nblk(total, 256), 256, 0, (cudaStream_t)st, dview(*x), dview(*y), total);
   note_launch();
   return check_launch("copyc");
 }
@@ -614,9 +643,9 @@ int yk_add(const YkView* a, const YkView* b, const YkView* y, yk_stream_t st) {
     return YK_EINVAL;
   const long long total = (long long)y->batch * y->H * y->W * (y->C / 8);
   if (total < (1LL << 31))
-    add8_kernel<unsigned><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*a), dview(*b), dview(*y), (unsigned)total);
+    launch_k(add8_kernel<unsigned>, nblk(total, 256), 256, 0, (cudaStream_t)st, dview(*a), dview(*b), dview(*y), (unsigned)total);
   else
-    add8_kernel<long long><<<nblk(total, 256), 256, 0, (cudaStream_t)st>>>(dview(*a), dview(*b), dview(*y), total);
+    launch_k(add8_kernel<long long>, nblk(total, 256), 256, 0, (cudaStream_t)st, dview(*a), dview(*b), dview(*y), total);
   note_launch();
   return check_launch("add");
 }

@@ -143,7 +143,13 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
     }
     *abort_flag = 0;
     mbar_fence_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
+    if (a.tmaA) asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
   }
+  // everything above overlaps the previous kernel; activations, the output and TMEM (which a
+  // co-resident predecessor may still hold) are touched only after it has completed
+  pdl_wait();
+  pdl_trigger();
   if (warp == kMmaWarp) {
     tmem_alloc(tslot, Cfg::kTmemCols);
     tmem_relinquish();
@@ -451,7 +457,7 @@ static int launch_tc(const ConvArgs& a, cudaStream_t st) {
     return YK_EUNSUP;
   if (a.tmaA == 2 && !encode_im2col(&tmA, a, CB))
     return YK_EUNSUP;
-  conv_tc_kernel<BN, STAGES, MT, CB><<<grid, kThreads, Cfg::kSmem, st>>>(a, tmB, tmA);
+  launch_k(conv_tc_kernel<BN, STAGES, MT, CB>, grid, kThreads, Cfg::kSmem, (cudaStream_t)st, a, tmB, tmA);
   note_launch();
   return check_launch("conv_tc");
 }

@@ -17,6 +17,8 @@ namespace yk {
 __global__ void letterbox_kernel(const uint8_t* __restrict__ src, int sh, int sw, __half* dst,
                                  int dh, int dw, int dstride, float scale, int top, int left,
                                  int nh, int nw) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= dh * dw) return;
   const int x = idx % dw, y = idx / dw;
@@ -91,6 +93,8 @@ static inline WsLayout ws_layout(int A) {
 
 __global__ void decode_kernel(DevLevels lv, int batch, int nc, float conf, uint8_t* ws,
                               WsLayout L) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (gid >= (long long)batch * lv.A) return;
   const int img = (int)(gid / lv.A), a = (int)(gid - (long long)img * lv.A);
@@ -142,6 +146,7 @@ __global__ void decode_kernel(DevLevels lv, int batch, int nc, float conf, uint8
 constexpr int kNmsThreads = 1024;
 constexpr int kNmsSmemKeys = 16384;    // keys sorted in shared memory up to this count
 constexpr int kMaxClasses = 1024;
+constexpr int kKeptSmem = 48;          // kept boxes per class held in shared memory
 
 __device__ __forceinline__ unsigned lanemask_lt() {
   unsigned m;
@@ -195,10 +200,13 @@ __device__ void bitonic_sort(unsigned long long* keys, int P) {
 __global__ void __launch_bounds__(kNmsThreads, 1)
 nms_kernel(int A, float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets,
            int* outidx, int* outcnt, int* rawcnt) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   extern __shared__ __align__(16) unsigned long long skeys[];
   __shared__ int wsum[32];
   __shared__ int segs[kMaxClasses + 1];
   __shared__ int s_total;
+  __shared__ float kept_s[32][kKeptSmem][5];
   const int img = blockIdx.x, tid = threadIdx.x;
   uint8_t* wimg = ws + (size_t)img * L.per_img;
   const float* rec = (const float*)(wimg + L.rec);
@@ -206,31 +214,51 @@ nms_kernel(int A, float iou, int max_out, uint8_t* ws, WsLayout L, float* outdet
   float* kept = (float*)(wimg + L.kept);
   int* surv = (int*)(wimg + L.surv);
 
-  // 1. count the candidates, pick the key store
+  // 1. count the candidates per warp (each warp owns a contiguous anchor range, ballots)
+  const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int span = ((A + nwarps - 1) / nwarps + 31) & ~31;
+  const int a_lo = warp * span, a_hi = min(A, a_lo + span);
   int cnt = 0;
-  for (int a = tid; a < A; a += blockDim.x) cnt += flag[a];
-  int tot;
-  block_scan(cnt, wsum, &tot);
-  const int n = tot;
+  for (int a0 = a_lo; a0 < a_hi; a0 += 32) {
+    const int a = a0 + lane;
+    cnt += __popc(__ballot_sync(~0u, a < a_hi && flag[a]));
+  }
+  if (lane == 0) wsum[warp] = cnt;
+  __syncthreads();
+  if (warp == 0) {
+    const int v = lane < nwarps ? wsum[lane] : 0;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y2 = __shfl_up_sync(~0u, x, o);
+      if (lane >= o) x += y2;
+    }
+    wsum[lane] = x - v;                       // exclusive prefix
+    if (lane == 31) s_total = x;
+  }
+  __syncthreads();
+  const int n = s_total;
   int P = 2;
   while (P < n) P <<= 1;
   unsigned long long* keys = P <= kNmsSmemKeys ? skeys : (unsigned long long*)(wimg + L.keys);
 
   // 2. keys in anchor order: class | ~score bits | anchor
-  int running = 0;
-  for (int a0 = 0; a0 < A; a0 += blockDim.x) {
-    const int a = a0 + tid;
-    const int f = a < A ? flag[a] : 0;
-    int t;
-    const int pos = running + block_scan(f, wsum, &t);
-    if (f) {
-      const float* r = rec + (size_t)a * 6;
-      const unsigned long long cls = (unsigned long long)(int)r[5];
-      const unsigned long long sb = (~dm_f2bits(r[4])) & 0xffffffffull;
-      keys[pos] = (cls << 52) | (sb << 20) | (unsigned long long)a;
+  {
+    int pos = wsum[warp];
+    for (int a0 = a_lo; a0 < a_hi; a0 += 32) {
+      const int a = a0 + lane;
+      const bool f = a < a_hi && flag[a];
+      const unsigned m = __ballot_sync(~0u, f);
+      if (f) {
+        const float* r = rec + (size_t)a * 6;
+        const unsigned long long cls = (unsigned long long)(int)r[5];
+        const unsigned long long sb = (~dm_f2bits(r[4])) & 0xffffffffull;
+        keys[pos + __popc(m & lanemask_lt())] = (cls << 52) | (sb << 20) | (unsigned long long)a;
+      }
+      pos += __popc(m);
     }
-    running += t;
   }
+  __syncthreads();
   for (int i = n + tid; i < P; i += blockDim.x) keys[i] = ~0ull;
   __syncthreads();
   bitonic_sort(keys, P);
@@ -253,8 +281,8 @@ nms_kernel(int A, float iou, int max_out, uint8_t* ws, WsLayout L, float* outdet
   if (tid == 0) segs[nseg] = n;
   __syncthreads();
 
-  // 4. greedy suppression per class, one warp per class, 32 candidates per step
-  const int lane = tid & 31, warp = tid >> 5;
+  // 4. greedy suppression per class, one warp per class, 32 candidates per step; the first
+  // kKeptSmem kept boxes of the class live in shared memory, later ones in the workspace
   for (int sg = warp; sg < nseg; sg += blockDim.x >> 5) {
     const int s = segs[sg], e = segs[sg + 1];
     int nk = 0;
@@ -270,7 +298,7 @@ nms_kernel(int A, float iou, int max_out, uint8_t* ws, WsLayout L, float* outdet
       bool alive = valid;
       for (int t = 0; t < nk; t++) {
         if (!__any_sync(~0u, alive)) break;
-        const float* kb = kept + (size_t)(s + t) * 5;
+        const float* kb = t < kKeptSmem ? kept_s[warp][t] : kept + (size_t)(s + t) * 5;
         if (alive && dm_iou_gt(kb[0], kb[1], kb[2], kb[3], kb[4], x1, y1, x2, y2, iou)) alive = false;
       }
       for (int l = 0; l < 32; l++) {
@@ -284,7 +312,8 @@ nms_kernel(int A, float iou, int max_out, uint8_t* ws, WsLayout L, float* outdet
       }
       const unsigned m = __ballot_sync(~0u, alive);
       if (alive) {
-        float* kb = kept + (size_t)(s + nk + __popc(m & lanemask_lt())) * 5;
+        const int t = nk + __popc(m & lanemask_lt());
+        float* kb = t < kKeptSmem ? kept_s[warp][t] : kept + (size_t)(s + t) * 5;
         kb[0] = x1; kb[1] = y1; kb[2] = x2; kb[3] = y2; kb[4] = ar;
       }
       if (valid) surv[i] = alive ? 1 : 0;
@@ -301,6 +330,7 @@ nms_kernel(int A, float iou, int max_out, uint8_t* ws, WsLayout L, float* outdet
     keys[i] = sv ? (keys[i] & ((1ull << 52) - 1)) : ~0ull;
     ns += sv;
   }
+  int tot;
   block_scan(ns, wsum, &tot);
   const int nsurv = tot;
   bitonic_sort(keys, P);
@@ -329,6 +359,8 @@ struct DevCoefs {
 __global__ void masks_kernel(DevCoefs cf, DView proto, int nm, float rx, float ry, int max_out,
                              const float* __restrict__ outdets, const int* __restrict__ outidx,
                              const int* __restrict__ outcnt, uint8_t* __restrict__ masks) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
   const int img = blockIdx.y, d = blockIdx.x;
   if (d >= outcnt[img]) return;
   __shared__ float co[64];
@@ -387,7 +419,7 @@ int yk_letterbox(const uint8_t* bgr, int sh, int sw, const YkView* y, int slot,
   if (left_out) *left_out = left;
   __half* dst = (__half*)y->ptr + y->coff + (size_t)slot * y->H * y->W * y->stride;
   const int npx = y->H * y->W;
-  letterbox_kernel<<<(npx + 255) / 256, 256, 0, (cudaStream_t)st>>>(
+  launch_k(letterbox_kernel, (npx + 255) / 256, 256, 0, (cudaStream_t)st, 
       bgr, sh, sw, dst, y->H, y->W, y->stride, scale, top, left, nh, nw);
   note_launch();
   return check_launch("letterbox");
@@ -417,7 +449,7 @@ int yk_decode(const YkLevel* levels, int nlevels, int batch, int nc, float conf,
   WsLayout L = ws_layout(A);
   if (post->ws_bytes < (size_t)batch * L.per_img) return YK_EINVAL;
   const long long total = (long long)batch * A;
-  decode_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)st>>>(
+  launch_k(decode_kernel, (unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)st, 
       lv, batch, nc, conf, (uint8_t*)post->ws, L);
   note_launch();
   return check_launch("decode");
@@ -436,7 +468,7 @@ int yk_nms(int batch, int anchors, float iou, int max_out, const YkPost* post, y
                          kNmsSmemKeys * 8);
     attr = true;
   }
-  nms_kernel<<<batch, kNmsThreads, smem, (cudaStream_t)st>>>(
+  launch_k(nms_kernel, batch, kNmsThreads, smem, (cudaStream_t)st, 
       anchors, iou, max_out, (uint8_t*)post->ws, L, post->outdets, post->outidx, post->outcnt,
       post->rawcnt);
   note_launch();
@@ -460,7 +492,7 @@ int yk_masks(const YkLevel* levels, int nlevels, const YkView* proto, int in_h, 
   }
   cf.n = nlevels;
   dim3 grid(max_out, proto->batch);
-  masks_kernel<<<grid, 256, 0, (cudaStream_t)st>>>(
+  launch_k(masks_kernel, grid, 256, 0, (cudaStream_t)st, 
       cf, dview(*proto), proto->C, (float)proto->W / in_w, (float)proto->H / in_h, max_out,
       post->outdets, post->outidx, post->outcnt, masks);
   note_launch();

@@ -264,7 +264,8 @@ int main(int argc, char** argv) {
     for (int i = 0; i < n; i++) { order[i] = i; tot += ms[i]; }
     std::sort(order.begin(), order.end(), [&](int a, int b) { return ms[a] > ms[b]; });
     printf("total %.3f ms/iter (B=%d) - top ops:\n", tot, batch);
-    for (int i = 0; i < 25 && i < n; i++) {
+    const int top = getenv("YOLO_PROFILE_ALL") ? n : 25;
+    for (int i = 0; i < top && i < n; i++) {
       int k = order[i], tile = 0;
       const char* kind = k == n - 1 ? "POST" : yolo_op_desc(h, k, &tile);
       printf("op%03d %-9s tile=%-3d %8.1f us (%4.1f%%)\n", k, kind, tile, ms[k] * 1000.0,
