@@ -34,14 +34,15 @@ def test_letterbox_bitexact(lib, cuda, pkg, hw, S):
     assert torch.all(out[0] == 0)
 
 
-def _levels(S, B, g, cls_bias, box_scale=1.0):
+def _levels(S, B, g, cls_bias, box_scale=1.0, nc=80):
     sizes = [(S // 8, 8), (S // 16, 16), (S // 32, 32)]
     box = [(torch.randn(B, n, n, 64, generator=g) * box_scale).half() for n, _ in sizes]
-    cls = [(torch.randn(B, n, n, 80, generator=g) + cls_bias).half() for n, _ in sizes]
+    cls = [(torch.randn(B, n, n, nc, generator=g) + cls_bias).half() for n, _ in sizes]
     return sizes, box, cls
 
 
-def _run_gpu_post(lib, rt, cuda, sizes, box, cls, B, iou, max_out, coef=None, proto=None, S=None):
+def _run_gpu_post(lib, rt, cuda, sizes, box, cls, B, iou, max_out, coef=None, proto=None, S=None,
+                  nc=80):
     A = sum(n * n for n, _ in sizes)
     dev = [(b.to(cuda), c.to(cuda)) for b, c in zip(box, cls)]
     lv = (rt.YkLevel * 3)()
@@ -62,7 +63,7 @@ def _run_gpu_post(lib, rt, cuda, sizes, box, cls, B, iou, max_out, coef=None, pr
     rc = torch.zeros(B, dtype=torch.int32, device=cuda)
     post = rt.YkPost(ws.data_ptr(), wsb, od.data_ptr(), oi.data_ptr(), oc.data_ptr(), rc.data_ptr())
     st = torch.cuda.current_stream().cuda_stream
-    assert lib.yk_decode(lv, 3, B, 80, 0.25, C.byref(post), st) == 0
+    assert lib.yk_decode(lv, 3, B, nc, 0.25, C.byref(post), st) == 0
     assert lib.yk_nms(B, A, iou, max_out, C.byref(post), st) == 0
     masks = None
     if coef is not None:
@@ -76,19 +77,21 @@ def _run_gpu_post(lib, rt, cuda, sizes, box, cls, B, iou, max_out, coef=None, pr
         (masks.cpu().numpy() if masks is not None else None)
 
 
-def _oracle(sizes, box, cls, img, iou, max_out):
+def _oracle(sizes, box, cls, img, iou, max_out, nc=80):
     lv = [(b[img].numpy(), c[img].numpy(), st) for (n, st), b, c in zip(sizes, box, cls)]
-    recs = graph_ref.decode(lv, 80, 0.25)
+    recs = graph_ref.decode(lv, nc, 0.25)
     return recs, graph_ref.nms(recs, iou, max_out)
 
 
 @pytest.mark.parametrize("S,B,cls_bias,iou,max_out", [
-    (640, 2, -4.0, 0.45, 300),     # a few hundred candidates
+    (640, 2, -5.0, 0.45, 300),     # tens of candidates: rank sort
+    (640, 2, -4.0, 0.45, 300),     # about a thousand candidates: radix sort in shared memory
     (640, 1, -4.0, 0.7, 300),
     (320, 3, -20.0, 0.45, 300),    # no candidates
     (320, 1, 6.0, 0.45, 300),      # every anchor is a candidate
     (640, 1, 6.0, 0.45, 50),       # max_out truncation
-    (1024, 1, 6.0, 0.45, 300),     # 21504 candidates: global-memory sort path
+    (640, 1, 6.0, 0.7, 300),       # 8400 candidates: candidate arrays in the workspace
+    (1024, 1, 6.0, 0.45, 300),     # 21504 candidates: candidate arrays in the workspace
 ])
 def test_decode_nms_bitexact(lib, cuda, S, B, cls_bias, iou, max_out):
     from yolo11_cu_b200 import runtime as rt
@@ -102,6 +105,36 @@ def test_decode_nms_bitexact(lib, cuda, S, B, cls_bias, iou, max_out):
         n = len(keep)
         assert np.array_equal(oi[img, :n], keep[:, 6].astype(np.int32))
         assert np.array_equal(od[img, :n].view(np.uint32), keep[:, :6].view(np.uint32))
+
+
+@pytest.mark.parametrize("S,nc,bias", [(320, 600, 1.0), (640, 304, -1.0)])
+def test_decode_nms_many_classes(lib, cuda, S, nc, bias):
+    """More than 256 classes: the class order takes two radix digits."""
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(S + nc)
+    sizes, box, cls = _levels(S, 1, g, bias, nc=nc)
+    od, oi, oc, rc, _ = _run_gpu_post(lib, rt, cuda, sizes, box, cls, 1, 0.45, 300, nc=nc)
+    recs, keep = _oracle(sizes, box, cls, 0, 0.45, 300, nc=nc)
+    assert rc[0] == len(recs) and oc[0] == len(keep)
+    assert np.array_equal(oi[0, :oc[0]], keep[:, 6].astype(np.int32))
+    assert np.array_equal(od[0, :oc[0]].view(np.uint32), keep[:, :6].view(np.uint32))
+
+
+def test_decode_nms_one_class(lib, cuda):
+    """Every candidate in one class: one long class segment and many kept boxes (the
+    kept list spills past the shared-memory cache into the workspace)."""
+    from yolo11_cu_b200 import runtime as rt
+    S = 320
+    g = torch.Generator().manual_seed(77)
+    sizes, box, cls = _levels(S, 1, g, -12.0, box_scale=0.5)
+    for c in cls:
+        c[..., 5] = (torch.randn(c.shape[:-1], generator=g) + 2.0).half()
+    od, oi, oc, rc, _ = _run_gpu_post(lib, rt, cuda, sizes, box, cls, 1, 0.45, 300)
+    recs, keep = _oracle(sizes, box, cls, 0, 0.45, 300)
+    assert rc[0] == len(recs) > 1000
+    assert oc[0] == len(keep) > 32
+    assert np.array_equal(oi[0, :oc[0]], keep[:, 6].astype(np.int32))
+    assert np.array_equal(od[0, :oc[0]].view(np.uint32), keep[:, :6].view(np.uint32))
 
 
 def test_nms_ties_deterministic(lib, cuda):

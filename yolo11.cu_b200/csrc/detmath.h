@@ -141,6 +141,7 @@ DM_HD int dm_iou_gt(float ax1, float ay1, float ax2, float ay2, float aarea,
   w = w > 0.f ? w : 0.f;
   h = h > 0.f ? h : 0.f;
   float inter = DM_MUL(w, h);
+  if (inter == 0.f && thr >= 0.f) return 0;   // 0 / ua is 0, or ua > 0 fails: never > thr
   float barea = DM_MUL(DM_SUB(bx2, bx1), DM_SUB(by2, by1));
   float ua = DM_SUB(DM_ADD(aarea, barea), inter);
   return ua > 0.f && DM_DIV(inter, ua) > thr;

@@ -67,48 +67,64 @@ struct DevLevels {
   int n, A;
 };
 
-// Per-image workspace layout (all 16-byte aligned): rec[A][6] f32, flag[A] i32,
-// keys[P2] u64 (P2 = next pow2 of A; global fallback of the shared-memory sort),
-// kept[A][5] f32, surv[A] i32.
+// Per-image workspace layout (all 16-byte aligned): rec[A][6] f32 and flag[A] i32 from
+// decode; then the NMS candidate arrays, used in place of shared memory when an image has
+// more candidates than shared memory holds: anchor[A] u32, box[A] float4, skey[A] u32,
+// cls[A] u32, ord[3][A] u32, surv[A] u8; kept[A][5] f32 (kept boxes past the shared cache).
 struct WsLayout {
-  size_t rec, flag, keys, kept, surv, per_img;
+  size_t rec, flag, anch, box, skey, cls, ord, surv, kept, per_img;
+  int A;
 };
 static inline size_t al16(size_t v) { return (v + 15) & ~(size_t)15; }
-static inline int pow2ge(int v) {
-  int p = 1;
-  while (p < v) p <<= 1;
-  return p;
-}
 static inline WsLayout ws_layout(int A) {
   WsLayout L;
   size_t o = 0;
+  L.A = A;
   L.rec = o;  o = al16(o + (size_t)A * 6 * 4);
   L.flag = o; o = al16(o + (size_t)A * 4);
-  L.keys = o; o = al16(o + (size_t)pow2ge(A) * 8);
+  L.anch = o; o = al16(o + (size_t)A * 4);
+  L.box = o;  o = al16(o + (size_t)A * 16);
+  L.skey = o; o = al16(o + (size_t)A * 4);
+  L.cls = o;  o = al16(o + (size_t)A * 4);
+  L.ord = o;  o = al16(o + (size_t)A * 12);
+  L.surv = o; o = al16(o + (size_t)A);
   L.kept = o; o = al16(o + (size_t)A * 5 * 4);
-  L.surv = o; o = al16(o + (size_t)A * 4);
   L.per_img = o;
   return L;
 }
 
-__global__ void decode_kernel(DevLevels lv, int batch, int nc, float conf, uint8_t* ws,
-                              WsLayout L) {
-  pdl_wait();     // inputs come from the previous kernel
-  pdl_trigger();
-  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (gid >= (long long)batch * lv.A) return;
-  const int img = (int)(gid / lv.A), a = (int)(gid - (long long)img * lv.A);
+// Anchor -> (level, y, x) and its element offsets in the level's views.
+struct AnchorLoc {
+  int li, y, x;
+};
+__device__ __forceinline__ AnchorLoc locate(const DevLevels& lv, int a) {
   int li = 0;
   while (li + 1 < lv.n && a >= lv.l[li + 1].abase) li++;
-  const DevLevel& L0 = lv.l[li];
-  const int rem = a - L0.abase;
-  const int y = rem / L0.W, x = rem - y * L0.W;
+  const int rem = a - lv.l[li].abase;
+  const int y = rem / lv.l[li].W;
+  return {li, y, rem - y * lv.l[li].W};
+}
+
+// One 4-lane group per anchor.  Class scores: the lanes take interleaved 16-byte chunks of
+// the logits and reduce (max, then the lowest class index: the reference's first-max-wins
+// scan).  For a candidate, lane k runs the DFL expectation of box side k, so all four lanes
+// share the 64 exponentials.
+__global__ void __launch_bounds__(256) decode_kernel(DevLevels lv, int batch, int nc, float conf,
+                                                     uint8_t* ws, WsLayout L) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
+  const long long ga = (long long)blockIdx.x * (blockDim.x >> 2) + (threadIdx.x >> 2);
+  if (ga >= (long long)batch * lv.A) return;   // whole 4-lane groups leave together
+  const int sub = threadIdx.x & 3, g0 = threadIdx.x & 28;
+  const unsigned gm = 0xfu << g0;
+  const int img = (int)(ga / lv.A), a = (int)(ga - (long long)img * lv.A);
+  const AnchorLoc p = locate(lv, a);
+  const DevLevel& L0 = lv.l[p.li];
   uint8_t* wimg = ws + (size_t)img * L.per_img;
-  int* flag = (int*)(wimg + L.flag);
-  const __half* cp = L0.cls.p + L0.cls.pix(img, y, x);
+  const __half* cp = L0.cls.p + L0.cls.pix(img, p.y, p.x);
   float best = -INFINITY;
   int bcls = 0;
-  for (int c0 = 0; c0 < nc; c0 += 8) {
+  for (int c0 = sub * 8; c0 < nc; c0 += 32) {
     const uint4 v = *(const uint4*)(cp + c0);
     const __half* h = (const __half*)&v;
 #pragma unroll
@@ -117,36 +133,56 @@ __global__ void decode_kernel(DevLevels lv, int batch, int nc, float conf, uint8
       if (c0 + i < nc && f > best) { best = f; bcls = c0 + i; }   // first max wins
     }
   }
-  const float score = dm_sigmoid(best);
-  if (!(score >= conf)) { flag[a] = 0; return; }
-  const __half* bp = L0.box.p + L0.box.pix(img, y, x);
-  float d[4];
 #pragma unroll
-  for (int side = 0; side < 4; side++) {
-    const uint4 v0 = *(const uint4*)(bp + side * 16), v1 = *(const uint4*)(bp + side * 16 + 8);
-    const __half* h0 = (const __half*)&v0;
-    const __half* h1 = (const __half*)&v1;
-    float l[16];
-#pragma unroll
-    for (int i = 0; i < 8; i++) { l[i] = __half2float(h0[i]); l[i + 8] = __half2float(h1[i]); }
-    d[side] = dm_dfl16(l);
+  for (int o = 1; o < 4; o <<= 1) {
+    const float ob = __shfl_xor_sync(gm, best, o);
+    const int oc = __shfl_xor_sync(gm, bcls, o);
+    if (ob > best || (ob == best && oc < bcls)) { best = ob; bcls = oc; }
   }
-  const float cx = DM_ADD((float)x, 0.5f), cy = DM_ADD((float)y, 0.5f), st = (float)L0.stride;
+  int* flag = (int*)(wimg + L.flag);
+  const float score = dm_sigmoid(best);
+  if (!(score >= conf)) {
+    if (sub == 0) flag[a] = 0;
+    return;
+  }
+  const __half* bp = L0.box.p + L0.box.pix(img, p.y, p.x) + sub * 16;
+  const uint4 v0 = *(const uint4*)bp, v1 = *(const uint4*)(bp + 8);
+  const __half* h0 = (const __half*)&v0;
+  const __half* h1 = (const __half*)&v1;
+  float l[16];
+#pragma unroll
+  for (int i = 0; i < 8; i++) { l[i] = __half2float(h0[i]); l[i + 8] = __half2float(h1[i]); }
+  const float d = dm_dfl16(l);
+  const float d0 = __shfl_sync(gm, d, g0), d1 = __shfl_sync(gm, d, g0 + 1);
+  const float d2 = __shfl_sync(gm, d, g0 + 2), d3 = __shfl_sync(gm, d, g0 + 3);
+  if (sub != 0) return;
+  const float cx = DM_ADD((float)p.x, 0.5f), cy = DM_ADD((float)p.y, 0.5f), st = (float)L0.stride;
   float* o = (float*)(wimg + L.rec) + (size_t)a * 6;
-  o[0] = DM_MUL(DM_SUB(cx, d[0]), st);
-  o[1] = DM_MUL(DM_SUB(cy, d[1]), st);
-  o[2] = DM_MUL(DM_ADD(cx, d[2]), st);
-  o[3] = DM_MUL(DM_ADD(cy, d[3]), st);
+  o[0] = DM_MUL(DM_SUB(cx, d0), st);
+  o[1] = DM_MUL(DM_SUB(cy, d1), st);
+  o[2] = DM_MUL(DM_ADD(cx, d2), st);
+  o[3] = DM_MUL(DM_ADD(cy, d3), st);
   o[4] = score;
   o[5] = (float)bcls;
   flag[a] = 1;
 }
 
 // ---------------- NMS (engine/engine.cu:1051-1123, exact + deterministic) ----------------
+// Order of work, one 1024-thread block per image:
+//   1. compaction of the decode flags into the candidate list (anchor order);
+//   2. a stable sort by score (descending; anchor order breaks ties) and, from that, a stable
+//      sort by class: a rank sort for small lists, LSD radix passes (8-bit digits, only the
+//      bytes that vary) otherwise;
+//   3. greedy suppression per class, one warp per class, 32 candidates per step;
+//   4. survivors in score order, the first max_out written out.
+// Up to kNmsSmemCand candidates live in shared memory, more in the workspace.
 constexpr int kNmsThreads = 1024;
-constexpr int kNmsSmemKeys = 16384;    // keys sorted in shared memory up to this count
+constexpr int kNmsSmemCand = 4096;
+constexpr int kRankSortMax = 256;
 constexpr int kMaxClasses = 1024;
-constexpr int kKeptSmem = 48;          // kept boxes per class held in shared memory
+constexpr int kKeptSmem = 32;          // kept boxes per class held in shared memory
+constexpr int kHistStride = 33;        // per-warp digit counters, [digit][warp] padded
+constexpr size_t kNmsDynSmem = (size_t)kNmsSmemCand * (16 + 4 + 4 + 12 + 1) + 256 * kHistStride * 4;
 
 __device__ __forceinline__ unsigned lanemask_lt() {
   unsigned m;
@@ -181,97 +217,216 @@ __device__ int block_scan(int v, int* wsum, int* total) {
   return pre;
 }
 
-__device__ void bitonic_sort(unsigned long long* keys, int P) {
-  for (int k = 2; k <= P; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < P; i += blockDim.x) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const bool asc = (i & k) == 0;
-          const unsigned long long a = keys[i], b = keys[ixj];
-          if ((a > b) == asc) { keys[i] = b; keys[ixj] = a; }
-        }
-      }
-      __syncthreads();
-    }
+// Lanes of the warp (among those in `valid`) whose 8-bit digit equals this lane's: the
+// intersection over the 8 bits of the ballot of lanes agreeing on that bit.
+__device__ __forceinline__ unsigned digit_peers(unsigned d, unsigned valid) {
+  unsigned m = valid;
+#pragma unroll
+  for (int b = 0; b < 8; b++) {
+    const unsigned bb = __ballot_sync(~0u, (d >> b) & 1u);
+    m &= ((d >> b) & 1u) ? bb : ~bb;
   }
+  return m;
+}
+
+// One stable LSD radix pass (8-bit digit of karr[item] at `shift`) from src to dst.  Warp w
+// owns a contiguous slice of src; within a warp, lanes of one 32-item step that share a
+// digit are ranked by lane (digit_peers), so the (digit, warp, position) order is the input
+// order.
+// Needs exactly 1024 threads (the scan gives each thread 8 of the 256 x 32 counters).
+__device__ void radix_pass(const uint32_t* src, uint32_t* dst, int n, const uint32_t* karr,
+                           int shift, uint32_t* hist, int* wsum) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < 256 * kHistStride; i += kNmsThreads) hist[i] = 0;
+  __syncthreads();
+  const int chunk = (((n + 31) >> 5) + 31) & ~31;
+  const int lo = warp * chunk, hi = min(n, lo + chunk);
+  for (int j = lo; j < hi; j += 32) {
+    const int it = j + lane;
+    const bool v = it < hi;
+    const unsigned vm = __ballot_sync(~0u, v);
+    const unsigned d = v ? (karr[src[it]] >> shift) & 255u : 0u;
+    const unsigned peers = digit_peers(d, vm);
+    if (v && lane == __ffs(peers) - 1) hist[d * kHistStride + warp] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  {
+    const int d = tid >> 2, w0 = (tid & 3) * 8;
+    uint32_t loc[8];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) { loc[k] = hist[d * kHistStride + w0 + k]; sum += (int)loc[k]; }
+    int tot;
+    int pre = block_scan(sum, wsum, &tot);
+#pragma unroll
+    for (int k = 0; k < 8; k++) { hist[d * kHistStride + w0 + k] = (uint32_t)pre; pre += (int)loc[k]; }
+  }
+  __syncthreads();
+  for (int j = lo; j < hi; j += 32) {
+    const int it = j + lane;
+    const bool v = it < hi;
+    const unsigned vm = __ballot_sync(~0u, v);
+    const uint32_t item = v ? src[it] : 0u;
+    const unsigned d = v ? (karr[item] >> shift) & 255u : 0u;
+    const unsigned peers = digit_peers(d, vm);
+    unsigned base = 0;
+    if (v) {
+      base = hist[d * kHistStride + warp];
+      dst[base + __popc(peers & lanemask_lt())] = item;
+    }
+    __syncwarp();
+    if (v && lane == __ffs(peers) - 1) hist[d * kHistStride + warp] = base + __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ unsigned warp_or(unsigned v) {
+  return __reduce_or_sync(~0u, v);
+}
+__device__ __forceinline__ unsigned warp_and(unsigned v) {
+  return __reduce_and_sync(~0u, v);
 }
 
 __global__ void __launch_bounds__(kNmsThreads, 1)
-nms_kernel(int A, float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets,
-           int* outidx, int* outcnt, int* rawcnt) {
+nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int* outidx,
+           int* outcnt, int* rawcnt) {
   pdl_wait();     // inputs come from the previous kernel
   pdl_trigger();
-  extern __shared__ __align__(16) unsigned long long skeys[];
+  extern __shared__ __align__(16) uint8_t nsm[];
   __shared__ int wsum[32];
   __shared__ int segs[kMaxClasses + 1];
   __shared__ int s_total;
+  __shared__ unsigned s_bits[4];        // OR / AND of the score keys, OR / AND of the classes
   __shared__ float kept_s[32][kKeptSmem][5];
-  const int img = blockIdx.x, tid = threadIdx.x;
+  const int img = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int A = L.A;
   uint8_t* wimg = ws + (size_t)img * L.per_img;
   const float* rec = (const float*)(wimg + L.rec);
   const int* flag = (const int*)(wimg + L.flag);
+  uint32_t* canch = (uint32_t*)(wimg + L.anch);
   float* kept = (float*)(wimg + L.kept);
-  int* surv = (int*)(wimg + L.surv);
+  if (tid == 0) { s_bits[0] = 0u; s_bits[1] = ~0u; s_bits[2] = 0u; s_bits[3] = ~0u; }
 
-  // 1. count the candidates per warp (each warp owns a contiguous anchor range, ballots)
-  const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-  const int span = ((A + nwarps - 1) / nwarps + 31) & ~31;
-  const int a_lo = warp * span, a_hi = min(A, a_lo + span);
+  // 1. count: thread t owns anchors [t*per, t*per + per), per a multiple of 4 (int4 loads)
+  const int per = ((A + kNmsThreads - 1) / kNmsThreads + 3) & ~3;
+  const int a0 = tid * per;
   int cnt = 0;
-  for (int a0 = a_lo; a0 < a_hi; a0 += 32) {
-    const int a = a0 + lane;
-    cnt += __popc(__ballot_sync(~0u, a < a_hi && flag[a]));
+  for (int q = 0; q < per; q += 4) {
+    const int a = a0 + q;
+    if (a < A) {
+      const int4 f = *(const int4*)(flag + a);
+      cnt += (f.x != 0) + (a + 1 < A && f.y != 0) + (a + 2 < A && f.z != 0) + (a + 3 < A && f.w != 0);
+    }
   }
-  if (lane == 0) wsum[warp] = cnt;
-  __syncthreads();
-  if (warp == 0) {
-    const int v = lane < nwarps ? wsum[lane] : 0;
-    int x = v;
+  int n;
+  int pos = block_scan(cnt, wsum, &n);
+  const bool in_smem = n <= kNmsSmemCand;
+  const int cap = in_smem ? kNmsSmemCand : A;
+  uint8_t* cb = in_smem ? nsm : wimg + L.box;
+  // shared layout: box | skey | cls | ord0..2 | hist | surv ; workspace: the same arrays
+  float4* box = (float4*)cb;
+  uint32_t* skey = in_smem ? (uint32_t*)(nsm + (size_t)cap * 16) : (uint32_t*)(wimg + L.skey);
+  uint32_t* ccls = in_smem ? (uint32_t*)(nsm + (size_t)cap * 20) : (uint32_t*)(wimg + L.cls);
+  uint32_t* ord = in_smem ? (uint32_t*)(nsm + (size_t)cap * 24) : (uint32_t*)(wimg + L.ord);
+  uint32_t* hist = (uint32_t*)(nsm + (size_t)kNmsSmemCand * 36);
+  uint8_t* surv = in_smem ? nsm + (size_t)kNmsSmemCand * 36 + 256 * kHistStride * 4
+                          : wimg + L.surv;
+  uint32_t* ord0 = ord;
+  uint32_t* ord1 = ord + cap;
+  uint32_t* ord2 = ord + 2 * cap;
+
+  // 1b. gather the candidates in anchor order
+  unsigned kor = 0, kand = ~0u, cor = 0, cand_ = ~0u;
+  for (int q0 = 0; q0 < per; q0 += 32) {
+    unsigned fm = 0;   // bit q: anchor a0 + q0 + q is a candidate
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y2 = __shfl_up_sync(~0u, x, o);
-      if (lane >= o) x += y2;
-    }
-    wsum[lane] = x - v;                       // exclusive prefix
-    if (lane == 31) s_total = x;
-  }
-  __syncthreads();
-  const int n = s_total;
-  int P = 2;
-  while (P < n) P <<= 1;
-  unsigned long long* keys = P <= kNmsSmemKeys ? skeys : (unsigned long long*)(wimg + L.keys);
-
-  // 2. keys in anchor order: class | ~score bits | anchor
-  {
-    int pos = wsum[warp];
-    for (int a0 = a_lo; a0 < a_hi; a0 += 32) {
-      const int a = a0 + lane;
-      const bool f = a < a_hi && flag[a];
-      const unsigned m = __ballot_sync(~0u, f);
-      if (f) {
-        const float* r = rec + (size_t)a * 6;
-        const unsigned long long cls = (unsigned long long)(int)r[5];
-        const unsigned long long sb = (~dm_f2bits(r[4])) & 0xffffffffull;
-        keys[pos + __popc(m & lanemask_lt())] = (cls << 52) | (sb << 20) | (unsigned long long)a;
+    for (int q = 0; q < 32; q += 4) {
+      const int a = a0 + q0 + q;
+      if (q0 + q < per && a < A) {
+        const int4 f = *(const int4*)(flag + a);
+        fm |= (unsigned)(f.x != 0) << q | (unsigned)(a + 1 < A && f.y != 0) << (q + 1) |
+              (unsigned)(a + 2 < A && f.z != 0) << (q + 2) |
+              (unsigned)(a + 3 < A && f.w != 0) << (q + 3);
       }
-      pos += __popc(m);
+    }
+    while (fm) {
+      const int q = __ffs(fm) - 1;
+      fm &= fm - 1;
+      const int a = a0 + q0 + q;
+      const float* r = rec + (size_t)a * 6;
+      const uint32_t sk = ~dm_f2bits(r[4]);
+      const uint32_t c = (uint32_t)(int)r[5];
+      box[pos] = make_float4(r[0], r[1], r[2], r[3]);
+      skey[pos] = sk;
+      ccls[pos] = c;
+      canch[pos] = (uint32_t)a;
+      ord0[pos] = (uint32_t)pos;
+      surv[pos] = 0;
+      kor |= sk; kand &= sk; cor |= c; cand_ &= c;
+      pos++;
     }
   }
+  kor = warp_or(kor); kand = warp_and(kand); cor = warp_or(cor); cand_ = warp_and(cand_);
+  if (lane == 0) {
+    atomicOr(&s_bits[0], kor); atomicAnd(&s_bits[1], kand);
+    atomicOr(&s_bits[2], cor); atomicAnd(&s_bits[3], cand_);
+  }
   __syncthreads();
-  for (int i = n + tid; i < P; i += blockDim.x) keys[i] = ~0ull;
-  __syncthreads();
-  bitonic_sort(keys, P);
 
-  // 3. class segments of the sorted list
+  // 2. score order (ordS) and class order (ordC), both stable on the anchor order
+  const uint32_t* ordS;
+  const uint32_t* ordC;
+  if (n <= kRankSortMax) {
+    if (tid < n) {
+      const unsigned long long ks = ((unsigned long long)skey[tid] << 20) | (unsigned)tid;
+      const unsigned long long kc = ((unsigned long long)ccls[tid] << 52) | ks;
+      int rs = 0, rc = 0;
+      for (int j = 0; j < n; j++) {
+        const unsigned long long js = ((unsigned long long)skey[j] << 20) | (unsigned)j;
+        const unsigned long long jc = ((unsigned long long)ccls[j] << 52) | js;
+        rs += js < ks;
+        rc += jc < kc;
+      }
+      ord1[rs] = (uint32_t)tid;
+      ord2[rc] = (uint32_t)tid;
+    }
+    __syncthreads();
+    ordS = ord1;
+    ordC = ord2;
+  } else {
+    uint32_t* bufs[3] = {ord0, ord1, ord2};
+    int cur = 0;
+    const unsigned kvar = s_bits[0] ^ s_bits[1], cvar = s_bits[2] ^ s_bits[3];
+    for (int sh = 0; sh < 32; sh += 8) {
+      if (!((kvar >> sh) & 255u)) continue;
+      radix_pass(bufs[cur], bufs[cur ^ 1], n, skey, sh, hist, wsum);
+      cur ^= 1;
+    }
+    const int sidx = cur, o1 = sidx == 0 ? 1 : 0, o2 = 2;
+    // class passes never overwrite the score order: they run over the other two buffers
+    int ccur = sidx;
+    int nxt = o1;
+    for (int sh = 0; sh < 16; sh += 8) {
+      if (!((cvar >> sh) & 255u)) continue;
+      radix_pass(bufs[ccur], bufs[nxt], n, ccls, sh, hist, wsum);
+      ccur = nxt;
+      nxt = nxt == o1 ? o2 : o1;
+    }
+    ordS = bufs[sidx];
+    ordC = bufs[ccur];
+  }
+
+  // 3. class segments of the class order
   {
     int nseg_running = 0;
-    for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+    for (int i0 = 0; i0 < n; i0 += kNmsThreads) {
       const int i = i0 + tid;
-      const int st = i < n && (i == 0 || (keys[i] >> 52) != (keys[i - 1] >> 52));
+      const int st = i < n && (i == 0 || ccls[ordC[i]] != ccls[ordC[i - 1]]);
       int t;
-      const int pos = nseg_running + block_scan(st, wsum, &t);
-      if (st && pos < kMaxClasses) segs[pos] = i;
+      const int p = nseg_running + block_scan(st, wsum, &t);
+      if (st && p < kMaxClasses) segs[p] = i;
       nseg_running += t;
     }
     if (tid == 0) s_total = min(nseg_running, kMaxClasses);
@@ -283,16 +438,17 @@ nms_kernel(int A, float iou, int max_out, uint8_t* ws, WsLayout L, float* outdet
 
   // 4. greedy suppression per class, one warp per class, 32 candidates per step; the first
   // kKeptSmem kept boxes of the class live in shared memory, later ones in the workspace
-  for (int sg = warp; sg < nseg; sg += blockDim.x >> 5) {
+  for (int sg = warp; sg < nseg; sg += kNmsThreads >> 5) {
     const int s = segs[sg], e = segs[sg + 1];
     int nk = 0;
     for (int c0 = s; c0 < e; c0 += 32) {
       const int i = c0 + lane;
       const bool valid = i < e;
+      const uint32_t ci = valid ? ordC[i] : 0u;
       float x1 = 0, y1 = 0, x2 = 0, y2 = 0, ar = 0;
       if (valid) {
-        const float* r = rec + (size_t)(keys[i] & 0xfffffull) * 6;
-        x1 = r[0]; y1 = r[1]; x2 = r[2]; y2 = r[3];
+        const float4 b = box[ci];
+        x1 = b.x; y1 = b.y; x2 = b.z; y2 = b.w;
         ar = dm_area(x1, y1, x2, y2);
       }
       bool alive = valid;
@@ -303,6 +459,7 @@ nms_kernel(int A, float iou, int max_out, uint8_t* ws, WsLayout L, float* outdet
       }
       for (int l = 0; l < 32; l++) {
         const unsigned m = __ballot_sync(~0u, alive);
+        if (!(m >> l)) break;
         const float bx1 = __shfl_sync(~0u, x1, l), by1 = __shfl_sync(~0u, y1, l);
         const float bx2 = __shfl_sync(~0u, x2, l), by2 = __shfl_sync(~0u, y2, l);
         const float bar = __shfl_sync(~0u, ar, l);
@@ -316,35 +473,33 @@ nms_kernel(int A, float iou, int max_out, uint8_t* ws, WsLayout L, float* outdet
         float* kb = t < kKeptSmem ? kept_s[warp][t] : kept + (size_t)(s + t) * 5;
         kb[0] = x1; kb[1] = y1; kb[2] = x2; kb[3] = y2; kb[4] = ar;
       }
-      if (valid) surv[i] = alive ? 1 : 0;
+      if (valid) surv[ci] = alive ? 1 : 0;
       nk += __popc(m);
       __syncwarp();
     }
   }
   __syncthreads();
 
-  // 5. survivors in (score desc, anchor asc) order, first max_out kept
-  int ns = 0;
-  for (int i = tid; i < n; i += blockDim.x) {
-    const bool sv = surv[i] != 0;
-    keys[i] = sv ? (keys[i] & ((1ull << 52) - 1)) : ~0ull;
-    ns += sv;
-  }
-  int tot;
-  block_scan(ns, wsum, &tot);
-  const int nsurv = tot;
-  bitonic_sort(keys, P);
-  const int nout = min(nsurv, max_out);
-  for (int i = tid; i < nout; i += blockDim.x) {
-    const int a = (int)(keys[i] & 0xfffffull);
-    const float* r = rec + (size_t)a * 6;
-    float* o = outdets + ((size_t)img * max_out + i) * 6;
+  // 5. survivors in score order, the first max_out kept
+  int base = 0;
+  for (int i0 = 0; i0 < n && base < max_out; i0 += kNmsThreads) {
+    const int i = i0 + tid;
+    const uint32_t ci = i < n ? ordS[i] : 0u;
+    const bool sv = i < n && surv[ci];
+    int tot;
+    const int p = base + block_scan(sv ? 1 : 0, wsum, &tot);
+    if (sv && p < max_out) {
+      const int a = (int)canch[ci];
+      const float* r = rec + (size_t)a * 6;
+      float* o = outdets + ((size_t)img * max_out + p) * 6;
 #pragma unroll
-    for (int q = 0; q < 6; q++) o[q] = r[q];
-    outidx[(size_t)img * max_out + i] = a;
+      for (int q = 0; q < 6; q++) o[q] = r[q];
+      outidx[(size_t)img * max_out + p] = a;
+    }
+    base += tot;
   }
   if (tid == 0) {
-    outcnt[img] = nout;
+    outcnt[img] = min(base, max_out);
     rawcnt[img] = n;
   }
 }
@@ -433,6 +588,7 @@ int yk_decode(const YkLevel* levels, int nlevels, int batch, int nc, float conf,
               const YkPost* post, yk_stream_t st) {
   if (!levels || nlevels < 1 || nlevels > 4 || batch < 1 || nc < 1 || !post || !post->ws)
     return YK_EINVAL;
+  if (nc > kMaxClasses) return YK_EUNSUP;
   DevLevels lv;
   int A = 0;
   for (int i = 0; i < nlevels; i++) {
@@ -449,7 +605,7 @@ int yk_decode(const YkLevel* levels, int nlevels, int batch, int nc, float conf,
   WsLayout L = ws_layout(A);
   if (post->ws_bytes < (size_t)batch * L.per_img) return YK_EINVAL;
   const long long total = (long long)batch * A;
-  launch_k(decode_kernel, (unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)st, 
+  launch_k(decode_kernel, (unsigned)((total + 63) / 64), 256, 0, (cudaStream_t)st,
       lv, batch, nc, conf, (uint8_t*)post->ws, L);
   note_launch();
   return check_launch("decode");
@@ -461,16 +617,14 @@ int yk_nms(int batch, int anchors, float iou, int max_out, const YkPost* post, y
     return YK_EINVAL;
   WsLayout L = ws_layout(anchors);
   if (post->ws_bytes < (size_t)batch * L.per_img) return YK_EINVAL;
-  const size_t smem = (size_t)std::min(pow2ge(std::max(anchors, 2)), kNmsSmemKeys) * 8;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(nms_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kNmsSmemKeys * 8);
+                         (int)kNmsDynSmem);
     attr = true;
   }
-  launch_k(nms_kernel, batch, kNmsThreads, smem, (cudaStream_t)st, 
-      anchors, iou, max_out, (uint8_t*)post->ws, L, post->outdets, post->outidx, post->outcnt,
-      post->rawcnt);
+  launch_k(nms_kernel, batch, kNmsThreads, kNmsDynSmem, (cudaStream_t)st, iou, max_out,
+           (uint8_t*)post->ws, L, post->outdets, post->outidx, post->outcnt, post->rawcnt);
   note_launch();
   return check_launch("nms");
 }
