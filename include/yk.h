@@ -43,6 +43,8 @@ typedef struct {
   int Cin, Cout;
   int tile;             // tensor-core N tile (0 = heuristic, else 32/64/128/256)
   int msub;             // stacked 128-row sub-tiles per CTA tile (0 = heuristic, 1/2/4)
+  int algo;             // 0 heuristic, 1 implicit GEMM (TMA im2col / gather), 2 halo patches
+                        // (3x3 stride 1 pad 1, Cin % 64 == 0; tile 64/128/256, msub 1/2)
 } YkConv;
 
 // Convolution with bias, activation, optional residual (y = act(conv(x)+b) + res) written

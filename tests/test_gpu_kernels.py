@@ -29,7 +29,7 @@ def vw(rt, buf, coff, Cv):
 
 
 def run_conv(lib, rt, x, w, b, k, s, p, act, groups=1, res=None, tile=0, msub=0, xc=(0, None),
-             yc=(0, 0)):
+             yc=(0, 0), algo=0):
     """x: NHWC fp16 buffer (view = channels xc[0]:xc[0]+Cin); output written into a fresh
     buffer with yc = (coff, extra channels) to exercise channel-slice stores."""
     B, H, W, _ = x.shape
@@ -39,7 +39,8 @@ def run_conv(lib, rt, x, w, b, k, s, p, act, groups=1, res=None, tile=0, msub=0,
     ybuf = torch.full((B, Ho, Wo, yc[0] + Cout + yc[1]), 7.0, dtype=torch.half, device=x.device)
     wt = w.permute(0, 2, 3, 1).contiguous().half()            # OHWI
     bt = b.float().contiguous()
-    prm = rt.YkConv(wt.data_ptr(), bt.data_ptr(), k, s, p, groups, act, Cin, Cout, tile, msub)
+    prm = rt.YkConv(wt.data_ptr(), bt.data_ptr(), k, s, p, groups, act, Cin, Cout, tile, msub,
+                    algo)
     xv = vw(rt, x, xc[0], Cin)
     yv = vw(rt, ybuf, yc[0], Cout)
     rv = vw(rt, res, 0, Cout) if res is not None else None
@@ -101,6 +102,45 @@ def test_conv_tc(lib, cuda, case, tile, msub):
     assert rel(out, ref) < TOL
 
 
+PATCH_CASES = [
+    # B, H, W, Cin, Cout
+    (1, 20, 20, 64, 64),
+    (2, 40, 40, 128, 128),
+    (1, 13, 29, 64, 96),       # ragged patch rows and columns, Cout not a tile multiple
+    (2, 80, 80, 64, 64),
+    (1, 9, 9, 256, 128),       # several 64-channel blocks
+    (3, 7, 7, 512, 64),        # small images: one patch per image, 8 channel blocks
+]
+
+
+@pytest.mark.parametrize("case", PATCH_CASES)
+@pytest.mark.parametrize("tile,msub", [(64, 1), (64, 2), (128, 1), (128, 2), (256, 1)])
+def test_conv_patch(lib, cuda, case, tile, msub):
+    """3x3 stride-1 convs on halo patches (algo 2), channel-slice input and output views."""
+    from yolo11_cu_b200 import runtime as rt
+    B, H, W, Cin, Cout = case
+    if tile // 2 >= Cout:
+        pytest.skip("tile more than twice Cout")
+    g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000)
+    x = torch.randn(B, H, W, Cin + 16, generator=g).half().to(cuda)
+    w = (torch.randn(Cout, Cin, 3, 3, generator=g) / (Cin * 9) ** 0.5)
+    b = torch.randn(Cout, generator=g) * 0.1
+    out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), 3, 1, 1, act=1, tile=tile,
+                        msub=msub, xc=(8, None), yc=(8, 8), algo=2)
+    assert rel(out, ref) < TOL
+
+
+def test_conv_patch_residual(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(2, 30, 30, 128, generator=g).half().to(cuda)
+    w = (torch.randn(128, 128, 3, 3, generator=g) / 34).to(cuda)
+    b = (torch.randn(128, generator=g) * 0.1).to(cuda)
+    res = torch.randn(2, 30, 30, 128, generator=g).half().to(cuda)
+    out, ref = run_conv(lib, rt, x, w, b, 3, 1, 1, act=1, res=res, tile=128, msub=2, algo=2)
+    assert rel(out, ref) < TOL
+
+
 def test_conv_tc_residual_and_inplace(lib, cuda):
     from yolo11_cu_b200 import runtime as rt
     g = torch.Generator().manual_seed(3)
@@ -135,6 +175,23 @@ def test_dwconv(lib, cuda, s):
     if s == 1:
         res = torch.randn(2, 20, 20, C_, generator=g).half().to(cuda)
     out, ref = run_conv(lib, rt, x, w, b, 3, s, 1, act=1, groups=C_, res=res)
+    assert rel(out, ref) < TOL
+
+
+@pytest.mark.parametrize("B,H,W,C_,res", [(1, 13, 21, 96, False), (2, 80, 80, 256, False),
+                                          (1, 17, 9, 512, True), (3, 8, 16, 64, True),
+                                          (1, 1, 1, 8, False)])
+def test_dwconv_tiles(lib, cuda, B, H, W, C_, res):
+    """3x3 stride-1 depthwise on shared-memory tiles: partial channel tiles, ragged edges,
+    channel-slice input / output views, residual."""
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(H * W + C_)
+    x = torch.randn(B, H, W, C_ + 16, generator=g).half().to(cuda)
+    w = (torch.randn(C_, 1, 3, 3, generator=g) / 3).to(cuda)
+    b = (torch.randn(C_, generator=g) * 0.1).to(cuda)
+    r = torch.randn(B, H, W, C_, generator=g).half().to(cuda) if res else None
+    out, ref = run_conv(lib, rt, x, w, b, 3, 1, 1, act=1, groups=C_, res=r, xc=(8, None),
+                        yc=(8, 8))
     assert rel(out, ref) < TOL
 
 

@@ -59,6 +59,7 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 bool pdl_enabled();
+bool patch_enabled();   // halo-patch 3x3 convs offered to the autotuner (YK_NO_PATCH=1: no)
 // Per host thread: -1 follows pdl_enabled(), 0 / 1 force plain / programmatic launches (the
 // engine captures its graphs both ways and keeps the faster).
 static thread_local int g_pdl_override = -1;
@@ -114,7 +115,7 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 // Returns false (and sets the device error word to `code`) if the phase did not complete
 // within kWaitNs.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int code) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int code) {
   if (mbar_try(bar, parity)) return true;
   unsigned long long t0 = globaltimer();
   while (!mbar_try(bar, parity)) {
@@ -125,6 +126,23 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int cod
   }
   return true;
 }
+#ifdef YK_CONV_PROF
+// Role timing of the tensor-core kernels (diagnostic builds only): cycles spent in each wait,
+// summed over lane 0 of every waiting warp, indexed by the low 4 bits of the wait's code.
+__device__ unsigned long long g_prof[16];
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int code) {
+  const long long t0 = clock64();
+  const bool r = mbar_wait_bounded(bar, parity, code);
+  if ((threadIdx.x & 31) == 0) atomicAdd(&g_prof[code & 15], (unsigned long long)(clock64() - t0));
+  return r;
+}
+#define YK_PROF_ADD(i, v) atomicAdd(&g_prof[i], (unsigned long long)(v))
+#else
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int code) {
+  return mbar_wait_bounded(bar, parity, code);
+}
+#define YK_PROF_ADD(i, v) ((void)0)
+#endif
 
 // ---------------- cp.async ----------------
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -189,8 +207,88 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr)
       : "memory");
 }
+__device__ __forceinline__ void tmem_ld16p(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Packed fp32 pair FMA (one instruction for two lanes, each rounded like fmaf).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("{\n\t.reg .b64 pa, pb, pc;\n\t"
+      "mov.b64 pa, {%1, %2};\n\tmov.b64 pb, {%3, %4};\n\tmov.b64 pc, {%5, %6};\n\t"
+      "fma.rn.f32x2 %0, pa, pb, pc;\n\t}"
+      : "=l"(d)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+  return r;
+}
+
+// SiLU with one special-function op: v * sigmoid(v), sigmoid(v) = 0.5 + 0.5 * tanh(v / 2)
+// (the hardware tanh approximation, relative error about 2^-11, below fp16 output rounding).
+__device__ __forceinline__ float silu_fast(float v) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * v));
+  return v * fmaf(0.5f, t, 0.5f);
+}
+
+// Epilogue of one accumulator row (this thread's TMEM lane) of a BN-column tile: output
+// channels n0 .. n0+BN-1 (those < Cout) get bias, SiLU (act == 1), the residual row, and are
+// stored as fp16 into yrow.  TMEM columns come in batches of up to 64 with one wait each.
+template <int BN>
+__device__ __forceinline__ void epi_row(uint32_t trow, int n0, int Cout, bool mok, __half* yrow,
+                                        const __half* rrow, const float* bias, int act) {
+  constexpr int kBatch = BN < 64 ? BN : 64;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += kBatch) {
+    if (n0 + c0 >= Cout) break;   // uniform across the warp
+    uint32_t r[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch / 16; j++)
+      if (n0 + c0 + 16 * j < Cout) tmem_ld16p(trow + c0 + 16 * j, r + 16 * j);
+    tmem_ld_wait();
+    if (!mok) continue;
+#pragma unroll
+    for (int h = 0; h < kBatch / 8; h++) {
+      const int nn = n0 + c0 + 8 * h;
+      if (nn >= Cout) break;
+      const float4 b0 = *(const float4*)(bias + nn);
+      const float4 b1 = *(const float4*)(bias + nn + 4);
+      float v[8] = {__uint_as_float(r[8 * h + 0]) + b0.x, __uint_as_float(r[8 * h + 1]) + b0.y,
+                    __uint_as_float(r[8 * h + 2]) + b0.z, __uint_as_float(r[8 * h + 3]) + b0.w,
+                    __uint_as_float(r[8 * h + 4]) + b1.x, __uint_as_float(r[8 * h + 5]) + b1.y,
+                    __uint_as_float(r[8 * h + 6]) + b1.z, __uint_as_float(r[8 * h + 7]) + b1.w};
+      if (act == 1) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) v[q] = silu_fast(v[q]);
+      }
+      if (rrow) {
+        const uint4 rv = *(const uint4*)(rrow + nn);
+        const __half2* rh = (const __half2*)&rv;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float2 f = __half22float2(rh[q]);
+          v[2 * q] += f.x;
+          v[2 * q + 1] += f.y;
+        }
+      }
+      uint4 o;
+      __half2* oh = (__half2*)&o;
+#pragma unroll
+      for (int q = 0; q < 4; q++) oh[q] = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
+      *(uint4*)(yrow + nn) = o;
+    }
+  }
 }
 
 // Shared-memory matrix descriptor: K-major operand in the 128-byte swizzle layout

@@ -14,6 +14,22 @@ namespace yk {
 static std::atomic<long long> g_launches{0};
 static thread_local char g_cuda_err[256];
 
+static bool dw_tiled_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("YK_DW_ROWS");   // 1: the register-blocked row kernel instead
+    return !(e && *e && *e != '0');
+  }();
+  return on;
+}
+
+bool patch_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("YK_NO_PATCH");
+    return !(e && *e && *e != '0');
+  }();
+  return on;
+}
+
 bool pdl_enabled() {
   static const bool on = [] {
     const char* e = getenv("YK_NO_PDL");
@@ -240,6 +256,143 @@ __global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restric
     oh[q] = __floats2half2_rn(a0 + rv[2 * q], a1 + rv[2 * q + 1]);
   }
   *(uint4*)(y.p + (size_t)pix * y.stride + c) = o;
+}
+
+// 3x3 stride-1 depthwise conv on shared-memory tiles.  A tile is 64 channels x 8 output rows
+// x 16 output columns; its 10 x 18 input window comes into shared memory by 16-byte cp.async
+// (zero outside the image), so every input element is read from L2 about 1.4 times instead
+// of once per tap.  Persistent blocks, each with a fixed channel tile (the grid is a multiple
+// of the channel-tile count, so the fp32 [9][64] filter is staged once), double-buffer the
+// windows: the next tile's loads are in flight while the current one is computed.  Thread =
+// 8 channels x 2 output rows x 4 output columns, so each loaded input row feeds two output
+// rows; packed fp32 pair FMAs, taps accumulated in (ky, kx) order like the other depthwise
+// kernels.
+constexpr int kDwTY = 8, kDwTX = 16, kDwCh = 64, kDwThreads = 128;
+constexpr int kDwIW = kDwTX + 2, kDwIH = kDwTY + 2;
+constexpr int kDwWin = kDwIH * kDwIW * kDwCh;   // halves per window buffer
+__global__ void __launch_bounds__(kDwThreads, 4) dwconv3t_kernel(DView x, DView y, DView r,
+                                                                 const __half* __restrict__ w,
+                                                                 const float* __restrict__ b,
+                                                                 int act, int tiles_c,
+                                                                 int tiles_x, int tiles_y,
+                                                                 int ntiles) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
+  extern __shared__ __align__(16) __half dw_smem[];   // [2][window] + fp32 [9][64] filter
+  float* wsm = (float*)(dw_smem + 2 * kDwWin);
+  const int tid = threadIdx.x;
+  const int tc = blockIdx.x % tiles_c;                  // fixed: gridDim.x % tiles_c == 0
+  const int c0 = tc * kDwCh;
+  const int cvalid = min(kDwCh, y.C - c0);
+  for (int i = tid; i < 9 * kDwCh; i += kDwThreads) {
+    const int t = i / kDwCh, c = i - t * kDwCh;
+    wsm[i] = c < cvalid ? __half2float(w[(size_t)(c0 + c) * 9 + t]) : 0.f;
+  }
+  const int per_img = tiles_y * tiles_x * tiles_c;
+  auto stage = [&](int t, __half* buf) {
+    const int img = t / per_img;
+    const int q = (t - img * per_img) / tiles_c;
+    const int ty = q / tiles_x, tx = q - ty * tiles_x;
+    const int oy0 = ty * kDwTY, ox0 = tx * kDwTX;
+    for (int i = tid; i < kDwIH * kDwIW * 8; i += kDwThreads) {
+      const int ch = i & 7, pos = i >> 3;
+      const int rr = pos / kDwIW, cc = pos - rr * kDwIW;
+      const int iy = oy0 - 1 + rr, ix = ox0 - 1 + cc;
+      const bool ok = iy >= 0 && iy < x.H && ix >= 0 && ix < x.W && ch * 8 < cvalid;
+      const __half* src = ok ? x.p + x.pix(img, iy, ix) + c0 + ch * 8 : x.p;
+      cp_async16(smem_u32(buf + pos * kDwCh + ch * 8), src, ok ? 16u : 0u);
+    }
+  };
+  const int cg = tid & 7, q16 = tid >> 3;                // q16: 4 row pairs x 4 column quads
+  const int r0 = (q16 >> 2) * 2, xq = (q16 & 3) * 4;
+  const int c = c0 + cg * 8;
+  const bool cok = cg * 8 < cvalid;
+  float2 bias[4] = {};
+  if (cok) {
+    const float4 b0 = *(const float4*)(b + c), b1 = *(const float4*)(b + c + 4);
+    bias[0] = make_float2(b0.x, b0.y); bias[1] = make_float2(b0.z, b0.w);
+    bias[2] = make_float2(b1.x, b1.y); bias[3] = make_float2(b1.z, b1.w);
+  }
+  int t = blockIdx.x;
+  if (t < ntiles) stage(t, dw_smem);
+  cp_async_commit();
+  for (int it = 0; t < ntiles; t += gridDim.x, it++) {
+    __half* cur = dw_smem + (it & 1) * kDwWin;
+    if (t + (int)gridDim.x < ntiles) stage(t + gridDim.x, dw_smem + ((it + 1) & 1) * kDwWin);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int img = t / per_img;
+    const int q = (t - img * per_img) / tiles_c;
+    const int ty = q / tiles_x, tx = q - ty * tiles_x;
+    const int oy = ty * kDwTY + r0, ox0 = tx * kDwTX + xq;
+    if (cok && oy < y.H) {
+      float2 acc[2][4][4];   // [output row][pixel][channel pair]
+#pragma unroll
+      for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+          for (int e = 0; e < 4; e++) acc[h][j][e] = bias[e];
+      // input rows r0 .. r0+3 of the window; input row ir feeds output row h with ky = ir - h
+#pragma unroll
+      for (int ir = 0; ir < 4; ir++) {
+        const __half* trow = cur + ((r0 + ir) * kDwIW + xq) * kDwCh + cg * 8;
+        float2 xf[6][4];
+#pragma unroll
+        for (int u = 0; u < 6; u++) {
+          const uint4 v = *(const uint4*)(trow + u * kDwCh);
+          const __half2* xh = (const __half2*)&v;
+#pragma unroll
+          for (int e = 0; e < 4; e++) xf[u][e] = __half22float2(xh[e]);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int ky = ir - h;
+          if (ky < 0 || ky > 2) continue;
+#pragma unroll
+          for (int kx = 0; kx < 3; kx++) {
+            const float4 w0 = *(const float4*)(wsm + (ky * 3 + kx) * kDwCh + cg * 8);
+            const float4 w1 = *(const float4*)(wsm + (ky * 3 + kx) * kDwCh + cg * 8 + 4);
+            const float2 wv[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w),
+                                  make_float2(w1.x, w1.y), make_float2(w1.z, w1.w)};
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+              for (int e = 0; e < 4; e++) acc[h][j][e] = ffma2(xf[j + kx][e], wv[e], acc[h][j][e]);
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        if (oy + h >= y.H) break;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int ox = ox0 + j;
+          if (ox >= y.W) break;
+          const size_t pix = ((size_t)img * y.H + oy + h) * y.W + ox;
+          float2 rv[4] = {};
+          if (r.p) {
+            const uint4 v = *(const uint4*)(r.p + pix * r.stride + c);
+            const __half2* hr = (const __half2*)&v;
+#pragma unroll
+            for (int e = 0; e < 4; e++) rv[e] = __half22float2(hr[e]);
+          }
+          uint4 o;
+          __half2* oh = (__half2*)&o;
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            float a0 = acc[h][j][e].x, a1 = acc[h][j][e].y;
+            if (act == 1) { a0 = silu_fast(a0); a1 = silu_fast(a1); }
+            oh[e] = __floats2half2_rn(a0 + rv[e].x, a1 + rv[e].y);
+          }
+          *(uint4*)(y.p + pix * y.stride + c) = o;
+        }
+      }
+    }
+    __syncthreads();   // the buffer is refilled two tiles later
+  }
+  cp_async_wait<0>();
 }
 
 // 3x3 depthwise conv, register-blocked: thread = 8 channels x 4 consecutive output pixels
@@ -514,6 +667,33 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     if (!view_vec8(x)) return YK_EINVAL;
     DView r = res ? dview(*res) : DView{nullptr, 0, 0, 0, 0};
     const long long total = npix * (p->Cout / 8);
+    if (p->k == 3 && p->p == 1 && p->s == 1 && dw_tiled_enabled()) {
+      const int tcn = (p->Cout + kDwCh - 1) / kDwCh, txn = (y->W + kDwTX - 1) / kDwTX;
+      const int tyn = (y->H + kDwTY - 1) / kDwTY;
+      const long long nt = (long long)y->batch * tyn * txn * tcn;
+      if (nt >= (1LL << 31)) return YK_EUNSUP;
+      static int nsm = 0;
+      if (!nsm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        if (nsm <= 0) nsm = 148;
+      }
+      // persistent grid, a multiple of the channel-tile count (each block keeps its filter)
+      long long grid = std::min<long long>(nt, (long long)nsm * 4);
+      grid = std::max<long long>(tcn, grid / tcn * tcn);
+      const size_t smem = 2 * (size_t)kDwWin * sizeof(__half) + 9 * kDwCh * sizeof(float);
+      static bool attr = false;
+      if (!attr) {
+        cudaFuncSetAttribute(dwconv3t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+        attr = true;
+      }
+      launch_k(dwconv3t_kernel, (unsigned)grid, kDwThreads, smem, (cudaStream_t)st, dview(*x),
+               dview(*y), r, (const __half*)p->weight, p->bias, p->act, tcn, txn, tyn, (int)nt);
+      note_launch();
+      return check_launch("dwconv3t");
+    }
     if (p->k == 3 && p->p == 1 && (p->s == 1 || p->s == 2)) {
       const long long t3 = (long long)y->batch * y->H * ((y->W + 3) / 4) * (p->Cout / 8);
       const unsigned nb = (unsigned)std::min<long long>(nblk(t3, 256), 148 * 8);  // grid-stride

@@ -108,11 +108,12 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-template <int BN, int STAGES, int MT, int CB>
+template <int BN, int STAGES, int MT, int CB, int G>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmA) {
   using Cfg = TcCfg<BN, STAGES, MT, CB>;
+  static_assert(STAGES % G == 0 && STAGES / G >= 2, "stage groups");
   constexpr int kTM = 128 * MT;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -135,7 +136,7 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
   if (tid == 0) {
     for (int s = 0; s < STAGES; s++) {
       mbar_init(full_bar(s), a.tmaA ? 1 : kProducers + 1);
-      mbar_init(empty_bar(s), 1);
+      if (s < STAGES / G) mbar_init(empty_bar(s), 1);
     }
     for (int b = 0; b < Cfg::kNacc; b++) {
       mbar_init(tfull_bar(b), 1);
@@ -158,6 +159,7 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot_ptr;
+  const long long t_role = clock64();
 
   if (warp < 4) {
     // ---------------- producers ----------------
@@ -202,7 +204,11 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
       for (int kb = 0; kb < a.nk; kb++, g++) {
         const int s = g % STAGES;
         const uint32_t u = g / STAGES;
-        if (u > 0 && !mbar_wait(empty_bar(s), (u - 1) & 1, 0x101)) { *abort_flag = 1; break; }
+        // stages are released G at a time (one tcgen05.commit per group)
+        if (u > 0 && s % G == 0 && !mbar_wait(empty_bar(s / G), (u - 1) & 1, 0x101)) {
+          *abort_flag = 1;
+          break;
+        }
         const uint32_t sA = base + s * Cfg::kStage, sB = sA + MT * Cfg::kABytes;
         if (tid == 0) {
           mbar_expect_tx(full_bar(s), Cfg::kBBytes + (gather ? 0 : MT * Cfg::kABytes));
@@ -248,6 +254,7 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
       }
     }
     cp_async_wait<0>();
+    if (tid == 0) YK_PROF_ADD(10, clock64() - t_role);
   } else if (warp < kMmaWarp) {
     // ---------------- epilogue ----------------
     const int sp = warp & 3;              // TMEM sub-partition this warp may read
@@ -274,49 +281,12 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
         const __half* rrow = a.res ? a.res + (size_t)(mok ? m : 0) * a.rs : nullptr;
         const uint32_t trow = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kTileCols +
                               mt * Cfg::kAccCols;
-#pragma unroll 1
-        for (int cc = 0; cc < BN / 16; cc++) {
-          const int n = n0 + cc * 16;
-          if (n >= a.Cout) break;  // uniform across the warp
-          uint32_t r[16];
-          tmem_ld16(trow + cc * 16, r);
-          tmem_ld_wait();
-          if (!mok) continue;
-#pragma unroll
-          for (int h = 0; h < 2; h++) {
-            const int nn = n + 8 * h;
-            if (nn >= a.Cout) break;
-            const float4 b0 = *(const float4*)(bias + nn);
-            const float4 b1 = *(const float4*)(bias + nn + 4);
-            float v[8] = {__uint_as_float(r[8 * h + 0]) + b0.x, __uint_as_float(r[8 * h + 1]) + b0.y,
-                          __uint_as_float(r[8 * h + 2]) + b0.z, __uint_as_float(r[8 * h + 3]) + b0.w,
-                          __uint_as_float(r[8 * h + 4]) + b1.x, __uint_as_float(r[8 * h + 5]) + b1.y,
-                          __uint_as_float(r[8 * h + 6]) + b1.z, __uint_as_float(r[8 * h + 7]) + b1.w};
-            if (a.act == 1) {
-#pragma unroll
-              for (int q = 0; q < 8; q++) v[q] = __fdividef(v[q], 1.f + __expf(-v[q]));
-            }
-            if (rrow) {
-              const uint4 rv = *(const uint4*)(rrow + nn);
-              const __half2* rh = (const __half2*)&rv;
-#pragma unroll
-              for (int q = 0; q < 4; q++) {
-                const float2 f = __half22float2(rh[q]);
-                v[2 * q] += f.x;
-                v[2 * q + 1] += f.y;
-              }
-            }
-            uint4 o;
-            __half2* oh = (__half2*)&o;
-#pragma unroll
-            for (int q = 0; q < 4; q++) oh[q] = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
-            *(uint4*)(yrow + nn) = o;
-          }
-        }
+        epi_row<BN>(trow, n0, a.Cout, mok, yrow, rrow, bias, a.act);
       }
       tc_fence_before();
       mbar_arrive(tempty_bar(acc));
     }
+    if (lane == 0) YK_PROF_ADD(9, clock64() - t_role);
   } else if (lane == 0) {
     // ---------------- MMA issuer (warp 12) ----------------
     constexpr uint32_t idesc = idesc_f16_m128(BN);
@@ -354,11 +324,13 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
                            swz_desc<CB * 2>(sA + (mt * Cfg::kTPS + j) * kABlk + kk * 32),
                            swz_desc<CB * 2>(sB + j * kBBlk + kk * 32), idesc, (kb | j | kk) != 0);
         }
-        tc_commit(empty_bar(s));
+        if (s % G == G - 1) tc_commit(empty_bar(s / G));
       }
       if (!ok) { *abort_flag = 1; break; }
       tc_commit(tfull_bar(acc));
     }
+    YK_PROF_ADD(8, clock64() - t_role);
+    YK_PROF_ADD(11, 1);
   }
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -432,12 +404,12 @@ static bool encode_im2col(CUtensorMap* m, const ConvArgs& a, int cb) {
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, int MT, int CB = 64>
+template <int BN, int STAGES, int MT, int G, int CB = 64>
 static int launch_tc(const ConvArgs& a, cudaStream_t st) {
   using Cfg = TcCfg<BN, STAGES, MT, CB>;
   static bool attr_set = false;   // the attribute is per function, for all devices
   if (!attr_set) {
-    if (cudaFuncSetAttribute(conv_tc_kernel<BN, STAGES, MT, CB>,
+    if (cudaFuncSetAttribute(conv_tc_kernel<BN, STAGES, MT, CB, G>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)Cfg::kSmem) != cudaSuccess)
       return check_launch("conv_tc attr");
@@ -457,7 +429,7 @@ static int launch_tc(const ConvArgs& a, cudaStream_t st) {
     return YK_EUNSUP;
   if (a.tmaA == 2 && !encode_im2col(&tmA, a, CB))
     return YK_EUNSUP;
-  launch_k(conv_tc_kernel<BN, STAGES, MT, CB>, grid, kThreads, Cfg::kSmem, (cudaStream_t)st, a, tmB, tmA);
+  launch_k(conv_tc_kernel<BN, STAGES, MT, CB, G>, grid, kThreads, Cfg::kSmem, (cudaStream_t)st, a, tmB, tmA);
   note_launch();
   return check_launch("conv_tc");
 }
@@ -480,8 +452,27 @@ int pick_msub(int M, int Cout, int bn) {
   return ms;
 }
 
+#ifdef YK_CONV_PROF
+extern "C" void yk_conv_prof(unsigned long long* out, int reset) {
+  cudaMemcpyFromSymbol(out, g_prof, sizeof(unsigned long long) * 16);
+  if (reset) {
+    unsigned long long z[16] = {};
+    cudaMemcpyToSymbol(g_prof, z, sizeof z);
+  }
+}
+#endif
+
+int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, int bn,
+               int ms, cudaStream_t st);
+
 int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p,
             cudaStream_t st) {
+  if (p->algo == 2) {
+    const int bn = p->tile ? p->tile : p->Cout <= 64 ? 64 : p->Cout <= 128 ? 128 : 256;
+    const int ms = p->msub ? p->msub : 1;
+    return conv_patch(x, y, res, p, bn, ms, st);
+  }
+  if (p->algo != 0 && p->algo != 1) return YK_EINVAL;
   ConvArgs a;
   DView X = dview(*x), Y = dview(*y);
   a.x = X.p; a.H = x->H; a.W = x->W; a.xs = x->stride;
@@ -520,39 +511,41 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     const int tps = 64 / cb;                      // K blocks per stage
     a.nk = (p->k * p->k * a.ncb + tps - 1) / tps;
   }
+  // (STAGES, G): a tcgen05.commit costs about as much issue time as ten MMAs, so stages are
+  // released in groups of G with at least 16 MMAs per commit where shared memory allows
   if (a.tmaA && cb < 64) {
     switch (bn * 1000 + ms * 100 + cb) {
-      case 32116: return launch_tc<32, 8, 1, 16>(a, st);
-      case 32216: return launch_tc<32, 5, 2, 16>(a, st);
-      case 32416: return launch_tc<32, 3, 4, 16>(a, st);
-      case 64116: return launch_tc<64, 8, 1, 16>(a, st);
-      case 64216: return launch_tc<64, 5, 2, 16>(a, st);
-      case 64416: return launch_tc<64, 2, 4, 16>(a, st);
-      case 32132: return launch_tc<32, 8, 1, 32>(a, st);
-      case 32232: return launch_tc<32, 5, 2, 32>(a, st);
-      case 32432: return launch_tc<32, 3, 4, 32>(a, st);
-      case 64132: return launch_tc<64, 8, 1, 32>(a, st);
-      case 64232: return launch_tc<64, 5, 2, 32>(a, st);
-      case 64432: return launch_tc<64, 2, 4, 32>(a, st);
-      case 32108: return launch_tc<32, 8, 1, 8>(a, st);
-      case 32208: return launch_tc<32, 5, 2, 8>(a, st);
-      case 32408: return launch_tc<32, 3, 4, 8>(a, st);
-      case 64108: return launch_tc<64, 8, 1, 8>(a, st);
-      case 64208: return launch_tc<64, 5, 2, 8>(a, st);
-      case 64408: return launch_tc<64, 2, 4, 8>(a, st);
+      case 32116: return launch_tc<32, 8, 1, 4, 16>(a, st);
+      case 32216: return launch_tc<32, 4, 2, 2, 16>(a, st);
+      case 32416: return launch_tc<32, 3, 4, 1, 16>(a, st);
+      case 64116: return launch_tc<64, 8, 1, 4, 16>(a, st);
+      case 64216: return launch_tc<64, 4, 2, 2, 16>(a, st);
+      case 64416: return launch_tc<64, 2, 4, 1, 16>(a, st);
+      case 32132: return launch_tc<32, 8, 1, 4, 32>(a, st);
+      case 32232: return launch_tc<32, 4, 2, 2, 32>(a, st);
+      case 32432: return launch_tc<32, 3, 4, 1, 32>(a, st);
+      case 64132: return launch_tc<64, 8, 1, 4, 32>(a, st);
+      case 64232: return launch_tc<64, 4, 2, 2, 32>(a, st);
+      case 64432: return launch_tc<64, 2, 4, 1, 32>(a, st);
+      case 32108: return launch_tc<32, 8, 1, 4, 8>(a, st);
+      case 32208: return launch_tc<32, 4, 2, 2, 8>(a, st);
+      case 32408: return launch_tc<32, 3, 4, 1, 8>(a, st);
+      case 64108: return launch_tc<64, 8, 1, 4, 8>(a, st);
+      case 64208: return launch_tc<64, 4, 2, 2, 8>(a, st);
+      case 64408: return launch_tc<64, 2, 4, 1, 8>(a, st);
       default: return YK_EINVAL;
     }
   }
   switch (bn * 10 + ms) {
-    case 321: return launch_tc<32, 8, 1>(a, st);
-    case 322: return launch_tc<32, 5, 2>(a, st);
-    case 324: return launch_tc<32, 3, 4>(a, st);
-    case 641: return launch_tc<64, 8, 1>(a, st);
-    case 642: return launch_tc<64, 5, 2>(a, st);
-    case 644: return launch_tc<64, 2, 4>(a, st);
-    case 1281: return launch_tc<128, 6, 1>(a, st);
-    case 1282: return launch_tc<128, 3, 2>(a, st);
-    case 2561: return launch_tc<256, 4, 1>(a, st);
+    case 321: return launch_tc<32, 8, 1, 4>(a, st);
+    case 322: return launch_tc<32, 4, 2, 2>(a, st);
+    case 324: return launch_tc<32, 3, 4, 1>(a, st);
+    case 641: return launch_tc<64, 8, 1, 4>(a, st);
+    case 642: return launch_tc<64, 4, 2, 2>(a, st);
+    case 644: return launch_tc<64, 2, 4, 1>(a, st);
+    case 1281: return launch_tc<128, 6, 1, 3>(a, st);
+    case 1282: return launch_tc<128, 4, 2, 2>(a, st);
+    case 2561: return launch_tc<256, 4, 1, 2>(a, st);
     default: return YK_EINVAL;
   }
 }

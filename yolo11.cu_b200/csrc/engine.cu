@@ -61,6 +61,7 @@ struct Op {
   int y2 = -1, y3 = -1;           // POOLX3 outputs 2 and 3
   int tile = 0;                   // tensor-core N tile chosen by the planner / autotuner
   int msub = 0;                   // tensor-core stacked M sub-tiles (0 = heuristic)
+  int algo = 0;                   // tensor-core conv algorithm (YkConv::algo)
   const void* wpad = nullptr;     // stem conv as GEMM over an im2col buffer: padded weights
   void* col = nullptr;            // its im2col buffer [maxB][Ho][Wo][kpad]
   int kpad = 0;
@@ -406,7 +407,7 @@ void Engine::run_op(const Op& op, int B) {
       p.weight = (const uint16_t*)dweights + op.woff;
       p.bias = dbias + op.boff;
       p.k = op.k; p.s = op.s; p.p = op.p; p.groups = op.g; p.act = op.act;
-      p.Cin = op.Cin; p.Cout = op.Cout; p.tile = op.tile; p.msub = op.msub;
+      p.Cin = op.Cin; p.Cout = op.Cout; p.tile = op.tile; p.msub = op.msub; p.algo = op.algo;
       YkView x = view(op.a, B), y = view(op.out, B);
       if (op.wpad) {            // stem: im2col into the padded buffer, then a 1x1 GEMM
         YkView col;
@@ -496,18 +497,24 @@ void Engine::autotune() {
   cudaEvent_t e0, e1;
   CKE(cudaEventCreate(&e0));
   CKE(cudaEventCreate(&e1));
-  static const int combos[][2] = {{32, 1}, {32, 2}, {32, 4}, {64, 1}, {64, 2}, {64, 4},
-                                  {128, 1}, {128, 2}, {256, 1}};
+  // {algo, tile, msub}: implicit GEMM, then halo patches (3x3 stride-1 convs, Cin % 64 == 0)
+  static const int combos[][3] = {{1, 32, 1}, {1, 32, 2}, {1, 32, 4}, {1, 64, 1}, {1, 64, 2},
+                                  {1, 64, 4}, {1, 128, 1}, {1, 128, 2}, {1, 256, 1},
+                                  {2, 64, 1}, {2, 64, 2}, {2, 128, 1}, {2, 128, 2}, {2, 256, 1}};
   for (Op& op : ops) {
     if (op.kind != CONV || op.g != 1 || (op.Cin % 8 && !op.wpad)) continue;
-    int best_t = 0, best_m = 0;
+    const bool patch_ok = !op.wpad && op.k == 3 && op.s == 1 && op.p == 1 && op.Cin % 64 == 0 &&
+                          patch_enabled();
+    int best_t = 0, best_m = 0, best_a = 1;
     float tbest = 1e30f;
     for (const auto& cm : combos) {
-      const int tile = cm[0];
+      const int tile = cm[1];
+      if (cm[0] == 2 && !patch_ok) continue;
       if (tile > 32 && tile / 2 >= op.Cout) continue;   // more than half the tile wasted
       if (tile == 32 && op.Cout > 64) continue;
+      op.algo = cm[0];
       op.tile = tile;
-      op.msub = cm[1];
+      op.msub = cm[2];
       run_op(op, maxB);
       CKE(cudaEventRecord(e0, st));
       for (int r = 0; r < 5; r++) run_op(op, maxB);
@@ -515,8 +522,9 @@ void Engine::autotune() {
       CKE(cudaEventSynchronize(e1));
       float ms = 0;
       CKE(cudaEventElapsedTime(&ms, e0, e1));
-      if (ms < tbest) { tbest = ms; best_t = tile; best_m = cm[1]; }
+      if (ms < tbest) { tbest = ms; best_t = tile; best_m = cm[2]; best_a = cm[0]; }
     }
+    op.algo = best_a;
     op.tile = best_t;
     op.msub = best_m;
   }
@@ -528,7 +536,7 @@ void Engine::autotune() {
 std::string Engine::tuning_key() const {
   cudaDeviceProp pr;
   cudaGetDeviceProperties(&pr, device);
-  std::string k = std::string(pr.name) + "|B" + std::to_string(maxB);
+  std::string k = "v2|" + std::string(pr.name) + "|B" + std::to_string(maxB);
   for (const Op& op : ops)
     if (op.kind == CONV)
       k += "|" + std::to_string(op.Cin) + "," + std::to_string(op.Cout) + "," +
@@ -547,16 +555,20 @@ bool Engine::load_tuning(const char* path) {
   std::string got(line.data());
   while (!got.empty() && (got.back() == '\n' || got.back() == '\r')) got.pop_back();
   if (got != key) return false;
-  std::vector<std::pair<int, int>> tiles;
-  int t, m;
-  while (fscanf(f, "%d %d", &t, &m) == 2) tiles.push_back({t, m});
+  struct Tuned { int algo, tile, msub; };
+  std::vector<Tuned> tiles;
+  int al, t, m;
+  while (fscanf(f, "%d %d %d", &al, &t, &m) == 3) tiles.push_back({al, t, m});
   size_t i = 0;
   for (const Op& op : ops)
     if (op.kind == CONV) i++;
   if (tiles.size() != i) return false;
   i = 0;
   for (Op& op : ops)
-    if (op.kind == CONV) { op.tile = tiles[i].first; op.msub = tiles[i].second; i++; }
+    if (op.kind == CONV) {
+      op.algo = tiles[i].algo; op.tile = tiles[i].tile; op.msub = tiles[i].msub;
+      i++;
+    }
   return true;
 }
 
@@ -565,7 +577,7 @@ void Engine::save_tuning(const char* path) const {
   if (!f) return;
   fprintf(f, "%s\n", tuning_key().c_str());
   for (const Op& op : ops)
-    if (op.kind == CONV) fprintf(f, "%d %d\n", op.tile, op.msub);
+    if (op.kind == CONV) fprintf(f, "%d %d %d\n", op.algo, op.tile, op.msub);
   fclose(f);
 }
 
@@ -851,7 +863,7 @@ int yolo_run_op(void* h, int op_index, int B) {
     Op o = op;
     if (o.kind == CONV && o.g == 1 && o.Cin % 8 == 0) {
       for (const Op& f : e->ops)   // reuse the tuned tile of the matching planned conv
-        if (f.kind == CONV && f.woff == o.woff) { o.tile = f.tile; o.msub = f.msub; }
+        if (f.kind == CONV && f.woff == o.woff) { o.tile = f.tile; o.msub = f.msub; o.algo = f.algo; }
     }
     e->run_op(o, B);
     CKE(cudaStreamSynchronize(e->st));

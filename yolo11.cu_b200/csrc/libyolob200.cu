@@ -2,6 +2,7 @@
 // device error word) then need no relocatable device code.
 #include "conv_misc.cu"
 #include "conv_tc.cu"
+#include "conv_patch.cu"
 #include "attn.cu"
 #include "post.cu"
 #include "engine.cu"

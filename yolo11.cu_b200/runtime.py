@@ -22,7 +22,8 @@ class YkView(C.Structure):
 class YkConv(C.Structure):
     _fields_ = [("weight", C.c_void_p), ("bias", C.c_void_p), ("k", C.c_int), ("s", C.c_int),
                 ("p", C.c_int), ("groups", C.c_int), ("act", C.c_int), ("Cin", C.c_int),
-                ("Cout", C.c_int), ("tile", C.c_int), ("msub", C.c_int)]
+                ("Cout", C.c_int), ("tile", C.c_int), ("msub", C.c_int),
+                ("algo", C.c_int)]
 
 
 class YkLevel(C.Structure):
