@@ -130,6 +130,58 @@ def test_conv_patch(lib, cuda, case, tile, msub):
     assert rel(out, ref) < TOL
 
 
+@pytest.mark.parametrize("case", [c for c in CONV_CASES if c[3] >= 64])
+@pytest.mark.parametrize("msub", [1, 2])
+def test_conv_transposed(lib, cuda, case, msub):
+    """Transposed tiles (algo 3): output channels on the MMA's M side, pixels on N."""
+    from yolo11_cu_b200 import runtime as rt
+    B, H, W, Cin, Cout, k, s, p = case
+    g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000 + 7)
+    x = torch.randn(B, H, W, Cin + 16, generator=g).half().to(cuda)
+    w = (torch.randn(Cout, Cin, k, k, generator=g) / (Cin * k * k) ** 0.5)
+    b = torch.randn(Cout, generator=g) * 0.1
+    out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), k, s, p, act=1, msub=msub,
+                        xc=(8, None), yc=(8, 8), algo=3)
+    assert rel(out, ref) < TOL
+
+
+def test_conv_transposed_residual(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(2, 30, 30, 128, generator=g).half().to(cuda)
+    w = (torch.randn(192, 128, 3, 3, generator=g) / 34).to(cuda)
+    b = (torch.randn(192, generator=g) * 0.1).to(cuda)
+    res = torch.randn(2, 30, 30, 192, generator=g).half().to(cuda)
+    out, ref = run_conv(lib, rt, x, w, b, 3, 1, 1, act=1, res=res, msub=2, algo=3)
+    assert rel(out, ref) < TOL
+
+
+@pytest.mark.parametrize("case", PATCH_CASES)
+@pytest.mark.parametrize("tile,msub", [(64, 1), (64, 2), (128, 1), (128, 2)])
+def test_conv_patch_transposed(lib, cuda, case, tile, msub):
+    """Halo patches with transposed tiles (algo 4): 64 (M = 64 MMA) or 128 output channels."""
+    from yolo11_cu_b200 import runtime as rt
+    B, H, W, Cin, Cout = case
+    g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000 + 11)
+    x = torch.randn(B, H, W, Cin + 16, generator=g).half().to(cuda)
+    w = (torch.randn(Cout, Cin, 3, 3, generator=g) / (Cin * 9) ** 0.5)
+    b = torch.randn(Cout, generator=g) * 0.1
+    out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), 3, 1, 1, act=1, tile=tile,
+                        msub=msub, xc=(8, None), yc=(8, 8), algo=4)
+    assert rel(out, ref) < TOL
+
+
+def test_conv_patch_transposed_residual(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(8)
+    x = torch.randn(2, 30, 30, 64, generator=g).half().to(cuda)
+    w = (torch.randn(64, 64, 3, 3, generator=g) / 24).to(cuda)
+    b = (torch.randn(64, generator=g) * 0.1).to(cuda)
+    res = torch.randn(2, 30, 30, 64, generator=g).half().to(cuda)
+    out, ref = run_conv(lib, rt, x, w, b, 3, 1, 1, act=1, res=res, tile=64, msub=2, algo=4)
+    assert rel(out, ref) < TOL
+
+
 def test_conv_patch_residual(lib, cuda):
     from yolo11_cu_b200 import runtime as rt
     g = torch.Generator().manual_seed(5)

@@ -34,20 +34,27 @@ struct PatchArgs {
 constexpr int kPatchCols = 16;     // positions per patch row (row pitch)
 constexpr int kPatchUse = 14;      // real output columns per patch row
 
-template <int BN, int MT, int BST, int WST>
+template <int BN, int MT, int BST, int WST, bool T = false>
 struct PatchCfg {
   static constexpr int kRows = 8 * MT + 2;                        // window rows
   static constexpr int kWinTx = kRows * kPatchCols * 128;         // bytes one TMA box brings
-  static constexpr int kWin = (kWinTx + 256 + 1023) & ~1023;      // + the junk columns' overrun
+  // The junk columns of the last window row read 2 positions past the box: inside the next
+  // buffer (the next window or the weight ring), so no padding is needed.
+  static constexpr int kWin = (kWinTx + 1023) & ~1023;
   static constexpr int kB = BN * 128;                             // one tap's weights, 64 ch
   static constexpr int kAccCols = BN;
-  static constexpr int kTileCols = MT * BN;
+  // transposed tiles: one accumulator of 128*MT columns (positions) x BN lanes (channels)
+  static constexpr int kTileCols = T ? 128 * MT : MT * BN;
   static constexpr int kNacc = 512 / kTileCols >= 4 ? 4 : 2;
   static constexpr int kTmemCols = kNacc * kTileCols;
-  static constexpr size_t kSmem =
-      (size_t)WST * kWin + (size_t)BST * kB + 1024 + 256 + kBiasSmem * 4;
+  // transposed: per epilogue warp a [32 positions][32 or 16 channels] fp16 staging block and
+  // no bias cache (each lane holds its channel's bias); otherwise the bias cache
+  static constexpr int kStg = T ? 8 * 32 * (BN == 128 ? 32 : 16) * 2 : kBiasSmem * 4;
+  static constexpr int kBars = 512;   // mbarriers, TMEM slot, abort flag
+  static_assert(8 * (2 * WST + 2 * BST + 2 * kNacc) + 16 <= kBars, "barrier area");
+  static constexpr size_t kSmem = (size_t)WST * kWin + (size_t)BST * kB + 1024 + kBars + kStg;
   static_assert(kTmemCols <= 512, "TMEM budget");
-  static_assert((size_t)WST * kWin + (size_t)BST * kB + 1024 + 256 + kBiasSmem * 4 <= 232448,
+  static_assert((size_t)WST * kWin + (size_t)BST * kB + 1024 + kBars + kStg <= 232448,
                 "smem budget");
 };
 
@@ -60,11 +67,12 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-template <int BN, int MT, int BST, int WST, int G>
+template <int BN, int MT, int BST, int WST, int G, bool T>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmX) {
-  using Cfg = PatchCfg<BN, MT, BST, WST>;
+  using Cfg = PatchCfg<BN, MT, BST, WST, T>;
+  static_assert(!T || BN == 64 || BN == 128, "transposed tiles: 64 or 128 channels");
   static_assert(BST % G == 0 && BST / G >= 2, "weight stage groups");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -81,7 +89,12 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
   const uint32_t tslot = bar_base + 8u * (2 * WST + 2 * BST + 2 * Cfg::kNacc);
   volatile uint32_t* tslot_ptr = (volatile uint32_t*)(smem_raw + (tslot - raw));
   volatile int* abort_flag = (volatile int*)(smem_raw + (tslot - raw) + 8);
-  float* bias_s = (float*)(smem_raw + (bar_base - raw) + 256);
+  float* bias_s = (float*)(smem_raw + (bar_base - raw) + Cfg::kBars);   // plain tiles
+  __half* stg_s = (__half*)(smem_raw + (bar_base - raw) + Cfg::kBars);   // transposed tiles
+  // G == 9: the weight stages of a window are its 9 taps in slots 9*ws .. 9*ws+8, released
+  // with the window by one commit (the ring holds BST = 9*WST stages)
+  constexpr bool kFused = G == 9;
+  static_assert(!kFused || BST == 9 * WST, "fused weight stages");
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -108,6 +121,7 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
   tc_fence_after();
   const uint32_t tmem = *tslot_ptr;
   const int per_img = a.nty * a.ntx;
+  const long long t_role = clock64();
 
   if (warp == 0) {
     // ---------------- producer (one thread, all loads by TMA) ----------------
@@ -126,10 +140,11 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
           tma_load_4d(wbase + ws * Cfg::kWin, &tmX, wfull(ws), cb * 64, tx * kPatchUse - 1,
                       ty * 8 * MT - 1, img);
           for (int tap = 0; tap < 9; tap++, gb++) {
-            const int bs = gb % BST;
+            const int bs = kFused ? ws * 9 + tap : gb % BST;
             const uint32_t ub = gb / BST;
             // weight stages are released G at a time (one tcgen05.commit per group)
-            if (ub > 0 && bs % G == 0 && !mbar_wait(bempty(bs / G), (ub - 1) & 1, 0x202)) {
+            if (!kFused && ub > 0 && bs % G == 0 &&
+                !mbar_wait(bempty(bs / G), (ub - 1) & 1, 0x202)) {
               ok = false;
               break;
             }
@@ -139,7 +154,79 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
         }
         if (!ok) { *abort_flag = 1; break; }
       }
+      YK_PROF_ADD(10, clock64() - t_role);
     }
+  } else if (warp >= 4 && warp < kMmaWarp && T) {
+    // ---------------- epilogue, transposed tiles ----------------
+    // TMEM column = window position (sub-tile position + 128*mt), lane = output channel: for
+    // 128 channels lane = channel, for 64 channels (M = 64 MMA) channel c sits in lane
+    // 32*(c/16) + c%16, so each warp owns 16 channels in its lanes 0-15.  Per 32 positions
+    // (two patch rows): bias + SiLU per lane, fp16 into the warp's [position][channel]
+    // staging block, then 16-byte rows of 8 channels stored for the real output pixels.
+    constexpr int kCw = BN == 128 ? 32 : 16;    // channels per warp
+    const int sp = warp & 3, grp = (warp - 4) >> 2;
+    __half* stg = stg_s + (warp - 4) * 32 * kCw;   // kStg = 8 warps x 32 x kCw halves
+    const bool lane_ok = lane < kCw;
+    uint32_t li = 0;
+    for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, li++) {
+      if ((int)(li & 1) != grp) continue;
+      const int acc = li % Cfg::kNacc;
+      const uint32_t use = li / Cfg::kNacc;
+      if (!mbar_wait(tfull(acc), use & 1, 0x203)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const int mtile = t / a.ntn, n0 = (t - mtile * a.ntn) * BN;
+      const int img = mtile / per_img, r = mtile - img * per_img;
+      const int ty = r / a.ntx, tx = r - ty * a.ntx;
+      const int cw0 = n0 + sp * kCw;                 // first channel of this warp
+      const int ch = cw0 + lane;
+      const float bc = lane_ok && ch < a.Cout ? a.bias[ch] : 0.f;
+      const uint32_t tcol = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kTileCols;
+      const bool any_ch = cw0 < a.Cout;              // uniform
+#pragma unroll 1
+      for (int pc = 0; pc < MT * 4 && any_ch; pc++) {   // 32 positions per chunk
+        uint32_t rg[32];
+        tmem_ld16p(tcol + pc * 32, rg);
+        tmem_ld16p(tcol + pc * 32 + 16, rg + 16);
+        tmem_ld_wait();
+        if (lane_ok) {
+#pragma unroll
+          for (int k = 0; k < 32; k++) {
+            float v = __uint_as_float(rg[k]) + bc;
+            if (a.act == 1) v = silu_fast(v);
+            stg[k * kCw + lane] = __float2half_rn(v);
+          }
+        }
+        __syncwarp();
+        constexpr int kChunks = 32 * kCw / 8;          // 16-byte pieces in the block
+#pragma unroll
+        for (int i = 0; i < kChunks / 32; i++) {
+          const int q = lane + 32 * i, pos = q / (kCw / 8), cc = q % (kCw / 8);
+          const int gpos = pc * 32 + pos;               // position within the tile
+          const int mt = gpos >> 7, pr = (gpos & 127) >> 4, pcol = gpos & 15;
+          const int y = ty * 8 * MT + mt * 8 + pr, x = tx * kPatchUse + pcol;
+          const int c8 = cw0 + cc * 8;
+          if (pcol < kPatchUse && x < a.W && y < a.H && c8 < a.Cout) {
+            const size_t m = ((size_t)img * a.H + y) * a.W + x;
+            uint4 o = *(const uint4*)(stg + pos * kCw + cc * 8);
+            if (a.res) {
+              const uint4 rv = *(const uint4*)(a.res + m * a.rs + c8);
+              __half2* oh = (__half2*)&o;
+              const __half2* rh = (const __half2*)&rv;
+#pragma unroll
+              for (int e = 0; e < 4; e++) {
+                const float2 f = __half22float2(oh[e]), g2 = __half22float2(rh[e]);
+                oh[e] = __floats2half2_rn(f.x + g2.x, f.y + g2.y);
+              }
+            }
+            *(uint4*)(a.y + m * a.ys + c8) = o;
+          }
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      mbar_arrive(tempty(acc));
+    }
+    if (lane == 0) YK_PROF_ADD(9, clock64() - t_role);
   } else if (warp >= 4 && warp < kMmaWarp) {
     // ---------------- epilogue ----------------
     const int sp = warp & 3;
@@ -193,11 +280,24 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
         tc_fence_after();
         const uint32_t win = wbase + ws * Cfg::kWin;
         for (int tap = 0; tap < 9; tap++, gb++) {
-          const int bs = gb % BST;
-          if (!mbar_wait(bfull(bs), (gb / BST) & 1, 0x206)) { ok = false; break; }
+          const int bs = kFused ? ws * 9 + tap : gb % BST;
+          const uint32_t bpar = kFused ? (gw / WST) & 1 : (gb / BST) & 1;
+          if (!mbar_wait(bfull(bs), bpar, 0x206)) { ok = false; break; }
           tc_fence_after();
           const int ky = tap / 3, kx = tap - ky * 3;
           const uint32_t sb = bbase + bs * Cfg::kB;
+          if constexpr (T) {
+            // transposed: A = BN weight rows (channels), B = 128*MT window positions from
+            // the tap's shift (sub-tiles are 128 positions apart, so one operand covers all)
+            constexpr uint32_t idt = (1u << 4) | ((uint32_t)((128 * MT) >> 3) << 17) |
+                                     ((uint32_t)(BN >> 4) << 24);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+              const uint32_t sa = win + (uint32_t)((ky * kPatchCols + kx) * 128 + kk * 32);
+              tc_mma_f16(d, swz_desc<128>(sb + kk * 32), swz_desc<128>(sa), idt,
+                         (cb | tap | kk) != 0);
+            }
+          } else
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
 #pragma unroll
@@ -208,13 +308,15 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
               tc_mma_f16(d + mt * Cfg::kAccCols, swz_desc<128>(sa), swz_desc<128>(sb + kk * 32),
                          idesc, (cb | tap | kk) != 0);
             }
-          if (bs % G == G - 1) tc_commit(bempty(bs / G));
+          if (!kFused && bs % G == G - 1) tc_commit(bempty(bs / G));
         }
         if (ok) tc_commit(wempty(ws));
       }
       if (!ok) { *abort_flag = 1; break; }
       tc_commit(tfull(acc));
     }
+    YK_PROF_ADD(8, clock64() - t_role);
+    YK_PROF_ADD(11, 1);
   }
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -252,12 +354,12 @@ static bool encode_patch_x(CUtensorMap* m, const __half* x, int C, int W, int H,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int MT, int BST, int WST, int G>
+template <int BN, int MT, int BST, int WST, int G, bool T = false>
 static int launch_patch(const PatchArgs& a, const YkView* x, cudaStream_t st) {
-  using Cfg = PatchCfg<BN, MT, BST, WST>;
+  using Cfg = PatchCfg<BN, MT, BST, WST, T>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(conv_patch_kernel<BN, MT, BST, WST, G>,
+    if (cudaFuncSetAttribute(conv_patch_kernel<BN, MT, BST, WST, G, T>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)Cfg::kSmem) != cudaSuccess)
       return check_launch("conv_patch attr");
@@ -273,7 +375,7 @@ static int launch_patch(const PatchArgs& a, const YkView* x, cudaStream_t st) {
     return YK_EUNSUP;
   if (!encode_patch_x(&tmX, a.x, a.Cin, a.W, a.H, x->batch, x->stride, Cfg::kRows))
     return YK_EUNSUP;
-  launch_k(conv_patch_kernel<BN, MT, BST, WST, G>, grid, kThreads, Cfg::kSmem, st, a, tmB, tmX);
+  launch_k(conv_patch_kernel<BN, MT, BST, WST, G, T>, grid, kThreads, Cfg::kSmem, st, a, tmB, tmX);
   note_launch();
   return check_launch("conv_patch");
 }
@@ -281,7 +383,7 @@ static int launch_patch(const PatchArgs& a, const YkView* x, cudaStream_t st) {
 // Halo-patch 3x3 stride-1 pad-1 conv; Cin a multiple of 64, 16-byte aligned view.
 // bn in {64, 128, 256}, ms (stacked 8x16 sub-tiles) in {1, 2}.
 int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, int bn,
-               int ms, cudaStream_t st) {
+               int ms, bool trans, cudaStream_t st) {
   if (p->k != 3 || p->s != 1 || p->p != 1 || p->groups != 1 || p->Cin % 64 ||
       ((uintptr_t)x->ptr & 15) || x->stride % 8 || (x->coff % 8))
     return YK_EUNSUP;
@@ -301,6 +403,15 @@ int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv
   const long long nt = (long long)y->batch * a.nty * a.ntx * a.ntn;
   if (nt > 0x7fffffffLL) return YK_EUNSUP;
   a.ntiles = (int)nt;
+  if (trans) {
+    switch (bn * 10 + ms) {
+      case 641: return launch_patch<64, 1, 18, 2, 9, true>(a, x, st);
+      case 642: return launch_patch<64, 2, 18, 2, 9, true>(a, x, st);
+      case 1281: return launch_patch<128, 1, 6, 3, 3, true>(a, x, st);
+      case 1282: return launch_patch<128, 2, 6, 2, 3, true>(a, x, st);
+      default: return YK_EINVAL;
+    }
+  }
   switch (bn * 10 + ms) {
     case 641: return launch_patch<64, 1, 6, 3, 3>(a, x, st);
     case 642: return launch_patch<64, 2, 6, 2, 3>(a, x, st);

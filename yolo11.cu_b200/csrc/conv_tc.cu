@@ -58,7 +58,7 @@ constexpr int kBiasSmem = 2048;     // bias floats cached in shared memory
 constexpr int kThreads = 416;
 constexpr int kMmaWarp = 12;
 
-template <int BN, int STAGES, int MT, int CB>
+template <int BN, int STAGES, int MT, int CB, bool T = false>
 struct TcCfg {
   static constexpr int kTPS = 64 / CB;                      // K blocks (CB wide) per stage
   static constexpr int kABytes = 128 * 128;                 // one 128-row sub-tile
@@ -68,9 +68,12 @@ struct TcCfg {
   static constexpr int kTileCols = MT * kAccCols;
   static constexpr int kNacc = 512 / kTileCols >= 4 ? 4 : 2; // TMEM accumulator ring
   static constexpr int kTmemCols = kNacc * kTileCols;        // <= 512, power of two
-  static constexpr size_t kSmem = (size_t)STAGES * kStage + 1024 + 256 + kBiasSmem * 4;
+  // transposed tiles: per epilogue warp a [32 pixels][32 channels] fp16 staging block
+  static constexpr int kStg = T ? 8 * 32 * 32 * 2 : 0;
+  static constexpr size_t kSmem = (size_t)STAGES * kStage + 1024 + 256 + kBiasSmem * 4 + kStg;
   static_assert(kTmemCols <= 512, "TMEM budget");
-  static_assert((size_t)STAGES * kStage + 1024 + 256 + kBiasSmem * 4 <= 232448, "smem budget");
+  static_assert((size_t)STAGES * kStage + 1024 + 256 + kBiasSmem * 4 + kStg <= 232448,
+                "smem budget");
 };
 
 __device__ __forceinline__ uint32_t sw_off(int r, int c) {
@@ -108,11 +111,12 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-template <int BN, int STAGES, int MT, int CB, int G>
+template <int BN, int STAGES, int MT, int CB, int G, bool T>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmA) {
-  using Cfg = TcCfg<BN, STAGES, MT, CB>;
+  using Cfg = TcCfg<BN, STAGES, MT, CB, T>;
+  static_assert(!T || (BN == 128 && CB == 64), "transposed tiles: 128 channels, 64-ch blocks");
   static_assert(STAGES % G == 0 && STAGES / G >= 2, "stage groups");
   constexpr int kTM = 128 * MT;
   extern __shared__ uint8_t smem_raw[];
@@ -129,6 +133,7 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
   volatile uint32_t* tslot_ptr = (volatile uint32_t*)(smem_raw + (tslot - raw));
   volatile int* abort_flag = (volatile int*)(smem_raw + (tslot - raw) + 8);
   float* bias_s = (float*)(smem_raw + (base - raw) + STAGES * Cfg::kStage + 256);
+  __half* stg_s = (__half*)(bias_s + kBiasSmem);   // transposed tiles only
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -255,6 +260,63 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
     }
     cp_async_wait<0>();
     if (tid == 0) YK_PROF_ADD(10, clock64() - t_role);
+  } else if (warp < kMmaWarp && T) {
+    // ---------------- epilogue, transposed tiles ----------------
+    // TMEM lane = output channel n0 + 32*sp + lane, column = pixel m0 + col.  Per 32-pixel
+    // chunk: bias + SiLU per lane, fp16 into the warp's [pixel][channel] staging block, then
+    // 16-byte rows of 8 channels (residual added) stored pixel by pixel.
+    const int sp = warp & 3, grp = (warp - 4) >> 2;
+    __half* stg = stg_s + (warp - 4) * 32 * 32;
+    uint32_t li = 0;
+    for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, li++) {
+      if ((int)(li & 1) != grp) continue;
+      const int acc = li % Cfg::kNacc;
+      const uint32_t use = li / Cfg::kNacc;
+      if (!mbar_wait(tfull_bar(acc), use & 1, 0x103)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const int m0 = (t / a.ntn) * kTM, n0 = (t % a.ntn) * BN;
+      const int ch = n0 + sp * 32 + lane;
+      const float bc = ch < a.Cout ? a.bias[ch] : 0.f;
+      const uint32_t tcol = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kTileCols;
+      const bool any_ch = n0 + sp * 32 < a.Cout;   // uniform
+#pragma unroll 1
+      for (int pc = 0; pc < kTM / 32 && any_ch; pc++) {
+        uint32_t r[32];
+        tmem_ld16p(tcol + pc * 32, r);
+        tmem_ld16p(tcol + pc * 32 + 16, r + 16);
+        tmem_ld_wait();
+#pragma unroll
+        for (int k = 0; k < 32; k++) {
+          float v = __uint_as_float(r[k]) + bc;
+          if (a.act == 1) v = silu_fast(v);
+          stg[k * 32 + lane] = __float2half_rn(v);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int q = lane + 32 * i, px = q >> 2, cc = q & 3;
+          const int m = m0 + pc * 32 + px, c8 = n0 + sp * 32 + cc * 8;
+          if (m < a.M && c8 < a.Cout) {
+            uint4 o = *(const uint4*)(stg + px * 32 + cc * 8);
+            if (a.res) {
+              const uint4 rv = *(const uint4*)(a.res + (size_t)m * a.rs + c8);
+              __half2* oh = (__half2*)&o;
+              const __half2* rh = (const __half2*)&rv;
+#pragma unroll
+              for (int e = 0; e < 4; e++) {
+                const float2 f = __half22float2(oh[e]), g2 = __half22float2(rh[e]);
+                oh[e] = __floats2half2_rn(f.x + g2.x, f.y + g2.y);
+              }
+            }
+            *(uint4*)(a.y + (size_t)m * a.ys + c8) = o;
+          }
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      mbar_arrive(tempty_bar(acc));
+    }
+    if (lane == 0) YK_PROF_ADD(9, clock64() - t_role);
   } else if (warp < kMmaWarp) {
     // ---------------- epilogue ----------------
     const int sp = warp & 3;              // TMEM sub-partition this warp may read
@@ -304,7 +366,14 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
         tc_fence_after();
         const uint32_t sA = base + s * Cfg::kStage, sB = sA + MT * Cfg::kABytes;
         constexpr uint32_t kABlk = 128 * CB * 2, kBBlk = BN * CB * 2;
-        if constexpr (CB == 8) {
+        if constexpr (T) {
+          // transposed: A = 128 weight rows (output channels), B = all MT*128 pixel rows
+          constexpr uint32_t idt = idesc_f16_m128(MT * 128);
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            tc_mma_f16(d, swz_desc<128>(sB + kk * 32), swz_desc<128>(sA + kk * 32), idt,
+                       (kb | kk) != 0);
+        } else if constexpr (CB == 8) {
           // 16-byte blocks, no swizzle: one K=16 step spans blocks 2i and 2i+1 (LBO apart)
 #pragma unroll
           for (int i = 0; i < Cfg::kTPS / 2; i++)
@@ -404,12 +473,12 @@ static bool encode_im2col(CUtensorMap* m, const ConvArgs& a, int cb) {
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, int MT, int G, int CB = 64>
+template <int BN, int STAGES, int MT, int G, int CB = 64, bool T = false>
 static int launch_tc(const ConvArgs& a, cudaStream_t st) {
-  using Cfg = TcCfg<BN, STAGES, MT, CB>;
+  using Cfg = TcCfg<BN, STAGES, MT, CB, T>;
   static bool attr_set = false;   // the attribute is per function, for all devices
   if (!attr_set) {
-    if (cudaFuncSetAttribute(conv_tc_kernel<BN, STAGES, MT, CB, G>,
+    if (cudaFuncSetAttribute(conv_tc_kernel<BN, STAGES, MT, CB, G, T>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)Cfg::kSmem) != cudaSuccess)
       return check_launch("conv_tc attr");
@@ -429,7 +498,7 @@ static int launch_tc(const ConvArgs& a, cudaStream_t st) {
     return YK_EUNSUP;
   if (a.tmaA == 2 && !encode_im2col(&tmA, a, CB))
     return YK_EUNSUP;
-  launch_k(conv_tc_kernel<BN, STAGES, MT, CB, G>, grid, kThreads, Cfg::kSmem, (cudaStream_t)st, a, tmB, tmA);
+  launch_k(conv_tc_kernel<BN, STAGES, MT, CB, G, T>, grid, kThreads, Cfg::kSmem, (cudaStream_t)st, a, tmB, tmA);
   note_launch();
   return check_launch("conv_tc");
 }
@@ -463,16 +532,18 @@ extern "C" void yk_conv_prof(unsigned long long* out, int reset) {
 #endif
 
 int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, int bn,
-               int ms, cudaStream_t st);
+               int ms, bool trans, cudaStream_t st);
 
 int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p,
             cudaStream_t st) {
-  if (p->algo == 2) {
-    const int bn = p->tile ? p->tile : p->Cout <= 64 ? 64 : p->Cout <= 128 ? 128 : 256;
-    const int ms = p->msub ? p->msub : 1;
-    return conv_patch(x, y, res, p, bn, ms, st);
+  if (p->algo == 2 || p->algo == 4) {
+    const bool trans = p->algo == 4;
+    const int bn = p->tile ? p->tile
+                   : p->Cout <= 64 ? 64 : (p->Cout <= 128 || trans) ? 128 : 256;
+    const int ms = p->msub ? p->msub : trans ? 2 : 1;
+    return conv_patch(x, y, res, p, bn, ms, trans, st);
   }
-  if (p->algo != 0 && p->algo != 1) return YK_EINVAL;
+  if (p->algo < 0 || p->algo > 4) return YK_EINVAL;
   ConvArgs a;
   DView X = dview(*x), Y = dview(*y);
   a.x = X.p; a.H = x->H; a.W = x->W; a.xs = x->stride;
@@ -487,9 +558,9 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   if (x->H > 30000 || x->W > 30000) return YK_EUNSUP;   // packed 16-bit window origins
   a.M = (int)M;
   a.nk = (a.Ktot + 63) / 64;
-  const int bn = p->tile ? p->tile : pick_tile(a.M, a.Cout);
+  const int bn = p->algo == 3 ? 128 : p->tile ? p->tile : pick_tile(a.M, a.Cout);
   if (bn != 32 && bn != 64 && bn != 128 && bn != 256) return YK_EINVAL;
-  int ms = p->msub ? p->msub : pick_msub(a.M, a.Cout, bn);
+  int ms = p->msub ? p->msub : p->algo == 3 ? 2 : pick_msub(a.M, a.Cout, bn);
   if (bn == 256) ms = 1;
   if (bn == 128 && ms > 2) ms = 2;
   if (ms != 1 && ms != 2 && ms != 4) return YK_EINVAL;
@@ -513,6 +584,12 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   }
   // (STAGES, G): a tcgen05.commit costs about as much issue time as ten MMAs, so stages are
   // released in groups of G with at least 16 MMAs per commit where shared memory allows
+  if (p->algo == 3) {   // transposed tiles: 128 output channels x 128*ms pixels
+    if (cb != 64 || bn != 128) return YK_EINVAL;
+    if (ms == 1) return launch_tc<128, 6, 1, 3, 64, true>(a, st);
+    if (ms == 2) return launch_tc<128, 4, 2, 2, 64, true>(a, st);
+    return YK_EINVAL;
+  }
   if (a.tmaA && cb < 64) {
     switch (bn * 1000 + ms * 100 + cb) {
       case 32116: return launch_tc<32, 8, 1, 4, 16>(a, st);

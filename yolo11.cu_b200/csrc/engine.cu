@@ -497,20 +497,24 @@ void Engine::autotune() {
   cudaEvent_t e0, e1;
   CKE(cudaEventCreate(&e0));
   CKE(cudaEventCreate(&e1));
-  // {algo, tile, msub}: implicit GEMM, then halo patches (3x3 stride-1 convs, Cin % 64 == 0)
+  // {algo, tile, msub}: implicit GEMM; implicit GEMM with transposed tiles (Cin >= 64);
+  // halo patches with transposed tiles (3x3 stride-1 convs, Cin % 64 == 0)
   static const int combos[][3] = {{1, 32, 1}, {1, 32, 2}, {1, 32, 4}, {1, 64, 1}, {1, 64, 2},
                                   {1, 64, 4}, {1, 128, 1}, {1, 128, 2}, {1, 256, 1},
-                                  {2, 64, 1}, {2, 64, 2}, {2, 128, 1}, {2, 128, 2}, {2, 256, 1}};
+                                  {3, 128, 1}, {3, 128, 2},
+                                  {4, 64, 1}, {4, 64, 2}, {4, 128, 1}, {4, 128, 2}};
   for (Op& op : ops) {
     if (op.kind != CONV || op.g != 1 || (op.Cin % 8 && !op.wpad)) continue;
     const bool patch_ok = !op.wpad && op.k == 3 && op.s == 1 && op.p == 1 && op.Cin % 64 == 0 &&
                           patch_enabled();
+    const bool trans_ok = !op.wpad && op.Cin >= 64;
     int best_t = 0, best_m = 0, best_a = 1;
     float tbest = 1e30f;
     for (const auto& cm : combos) {
       const int tile = cm[1];
-      if (cm[0] == 2 && !patch_ok) continue;
-      if (tile > 32 && tile / 2 >= op.Cout) continue;   // more than half the tile wasted
+      if (cm[0] == 4 && (!patch_ok || (tile == 128 && op.Cout <= 64))) continue;
+      if (cm[0] == 3 && !trans_ok) continue;
+      if (cm[0] == 1 && tile > 32 && tile / 2 >= op.Cout) continue;   // half the tile wasted
       if (tile == 32 && op.Cout > 64) continue;
       op.algo = cm[0];
       op.tile = tile;
