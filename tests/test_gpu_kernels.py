@@ -204,11 +204,17 @@ def test_conv_tc_residual_and_inplace(lib, cuda):
     assert rel(out, ref) < TOL
 
 
-@pytest.mark.parametrize("cout,k,s", [(16, 3, 2), (64, 3, 2), (96, 3, 2), (16, 3, 1), (16, 1, 1)])
-def test_conv_first_layer(lib, cuda, cout, k, s):
+@pytest.mark.parametrize("cout,k,s,hw", [(16, 3, 2, (64, 48)), (64, 3, 2, (64, 48)),
+                                         (96, 3, 2, (64, 48)), (16, 3, 1, (64, 48)),
+                                         (16, 1, 1, (64, 48)), (32, 3, 2, (90, 122)),
+                                         (48, 3, 2, (33, 17)), (80, 3, 2, (160, 160)),
+                                         (64, 3, 2, (640, 640))])
+def test_conv_first_layer(lib, cuda, cout, k, s, hw):
+    """The 3-channel first conv: the warp-MMA stem kernel (k = 3, Cout <= 96) and the direct
+    small-Cin kernel (other k)."""
     from yolo11_cu_b200 import runtime as rt
     g = torch.Generator().manual_seed(4)
-    x = torch.rand(2, 64, 48, 3, generator=g).half().to(cuda)
+    x = torch.rand(2, hw[0], hw[1], 3, generator=g).half().to(cuda)
     w = (torch.randn(cout, 3, k, k, generator=g) / 5).to(cuda)
     b = (torch.randn(cout, generator=g) * 0.1).to(cuda)
     out, ref = run_conv(lib, rt, x, w, b, k, s, k // 2, act=1)

@@ -152,18 +152,6 @@ static int launch_attn(const YkView* qkv, const YkView* y, int heads, int N, siz
 // registers (row max / sum shared by the 4 lanes of a row through shuffles), then the fp16
 // probabilities are reused in place as the A operand of O += P V (eight MMAs, V fragments by
 // ldmatrix.trans).  The FLOPs are ~0.2 % of the network, so the warp-level MMA is enough.
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *(uint32_t*)&h;
-}
 
 constexpr int kAttnChunk = 192, kKs = 40, kVs = 72;
 

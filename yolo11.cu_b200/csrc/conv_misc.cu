@@ -98,61 +98,134 @@ __global__ void conv_small_cin_kernel(DView x, DView y, const __half* __restrict
   *(uint4*)(y.p + (size_t)pix * y.stride + co0) = o;
 }
 
-// First conv specialised for k=3, Cin=3 (every YOLO stem): thread = one output pixel, all
-// Cout channels.  The 27 input taps are loaded once into registers; weights (fp32) and bias
-// sit in shared memory and are read as broadcast float4s; the pixel's Cout outputs are
-// written as contiguous 16-byte chunks.
-template <int K>
-__global__ void __launch_bounds__(128) conv_stem3_kernel(DView x, DView y,
-                                                         const __half* __restrict__ w,
-                                                         const float* __restrict__ b, int Cout,
-                                                         int s, int p, int act, long long npix) {
+// First conv of every YOLO (k = 3, Cin = 3, stride s, pad p <= 2) on the warp-level tensor
+// cores.  The layer is bound by its output writes (Cout channels per pixel from 27 taps).
+// Persistent blocks walk output rows; each row's 3 input rows come into a double-buffered
+// shared window by 16-byte cp.async (packed stride-3 rows; element loads otherwise), the
+// borders staying zero.  Each warp builds the m16n8k16 A fragments of 16 output pixels
+// straight from the window (K = 27 taps padded to 32), multiplies by the filter held in
+// B-fragment registers for the whole kernel (NF = Cout / 8 fragments), and writes bias + SiLU
+// through a padded [16][Cout] staging block as whole 16-byte channel groups per pixel.
+// Replaces k_conv0 (engine/engine.cu:487-532).
+template <int NF>
+__global__ void __launch_bounds__(128) conv_stem_mma_kernel(DView x, DView y,
+                                                            const __half* __restrict__ w,
+                                                            const float* __restrict__ b, int s,
+                                                            int p, int act, int pitch, int vec,
+                                                            int rows) {
   pdl_wait();     // inputs come from the previous kernel
   pdl_trigger();
-  extern __shared__ __align__(16) float wst[];   // [Cout][K*K*3] then bias[Cout]
-  constexpr int KK = K * K * 3;
-  for (int i = threadIdx.x; i < Cout * KK; i += blockDim.x) wst[i] = __half2float(w[i]);
-  for (int i = threadIdx.x; i < Cout; i += blockDim.x) wst[Cout * KK + i] = b[i];
-  __syncthreads();
-  const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (pix >= npix) return;
-  const int HW = y.H * y.W;
-  const int img = (int)(pix / HW), rem = (int)(pix - (long long)img * HW);
-  const int oy = rem / y.W, ox = rem - oy * y.W;
-  float in[KK];
+  constexpr int Cout = NF * 8, kStgRow = Cout + 8;
+  // [2 buffers][3 rows][pitch]: element (input column ix >= -p, channel c) of a row sits at
+  // 8 + 3*ix + c; then the per-warp staging blocks
+  extern __shared__ __align__(16) __half stem_sm[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __half* stg = stem_sm + 6 * pitch + warp * 16 * kStgRow;
+  for (int i = tid; i < 6 * pitch / 8; i += 128) ((uint4*)stem_sm)[i] = make_uint4(0, 0, 0, 0);
+  // this lane's K indices per k-step: 2t, 2t+1, 2t+8, 2t+9 (+16); tap-major (ky, kx, ci) order
+  const int g = lane >> 2, t = lane & 3;
+  int koff[2][4];
 #pragma unroll
-  for (int ky = 0; ky < K; ky++) {
-    const int iy = oy * s - p + ky;
+  for (int ks = 0; ks < 2; ks++)
 #pragma unroll
-    for (int kx = 0; kx < K; kx++) {
-      const int ix = ox * s - p + kx;
-      const bool ok = iy >= 0 && iy < x.H && ix >= 0 && ix < x.W;
-      const __half* xp = x.p + x.pix(img, ok ? iy : 0, ok ? ix : 0);
-#pragma unroll
-      for (int ci = 0; ci < 3; ci++) in[(ky * K + kx) * 3 + ci] = ok ? __half2float(xp[ci]) : 0.f;
+    for (int j = 0; j < 4; j++) {
+      const int k = 16 * ks + 2 * t + (j & 1) + (j >> 1) * 8;
+      const int tap = k / 3, ci = k - tap * 3, ky = tap / 3, kx = tap - ky * 3;
+      koff[ks][j] = k < 27 ? ky * pitch + 8 + (kx - p) * 3 + ci : -1;
     }
+  uint32_t bf[2][NF][2];
+  float bias2[NF][2];
+#pragma unroll
+  for (int f = 0; f < NF; f++) {
+    const int n = 8 * f + g;
+#pragma unroll
+    for (int ks = 0; ks < 2; ks++)
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int k0 = 16 * ks + 2 * t + 8 * h;
+        const float lo = k0 < 27 ? __half2float(w[n * 27 + k0]) : 0.f;
+        const float hi = k0 + 1 < 27 ? __half2float(w[n * 27 + k0 + 1]) : 0.f;
+        bf[ks][f][h] = pack_half2(lo, hi);
+      }
+    bias2[f][0] = b[8 * f + 2 * t];
+    bias2[f][1] = b[8 * f + 2 * t + 1];
   }
-  __half* yp = y.p + (size_t)pix * y.stride;
-  for (int c0 = 0; c0 < Cout; c0 += 8) {
-    float acc[8];
-#pragma unroll
-    for (int c = 0; c < 8; c++) acc[c] = wst[Cout * KK + c0 + c];
-#pragma unroll
-    for (int c = 0; c < 8; c++) {
-      const float* wr = wst + (c0 + c) * KK;
-#pragma unroll
-      for (int t = 0; t < KK; t++) acc[c] = fmaf(in[t], wr[t], acc[c]);
+  __syncthreads();   // zeroed window before the first fill
+  auto stage = [&](int r, __half* buf) {
+    const int img = r / y.H, oy = r - img * y.H;
+    if (vec) {
+      const int cpr = x.W * 3 / 8;
+      for (int i = tid; i < 3 * cpr; i += 128) {
+        const int ky = i / cpr, c = i - ky * cpr, iy = oy * s - p + ky;
+        const bool ok = iy >= 0 && iy < x.H;
+        const __half* src = ok ? x.p + ((size_t)img * x.H + iy) * x.W * 3 + c * 8 : x.p;
+        cp_async16(smem_u32(buf + ky * pitch + 8 + c * 8), src, ok ? 16u : 0u);
+      }
+    } else {
+      for (int i = tid; i < 3 * x.W * 3; i += 128) {
+        const int ky = i / (x.W * 3), rem = i - ky * x.W * 3, col = rem / 3, ch = rem - col * 3;
+        const int iy = oy * s - p + ky;
+        buf[ky * pitch + 8 + rem] = (iy >= 0 && iy < x.H) ? x.p[x.pix(img, iy, col) + ch]
+                                                          : __float2half(0.f);
+      }
     }
-    uint4 o;
-    __half2* oh = (__half2*)&o;
+  };
+  int r = blockIdx.x;
+  if (r < rows) stage(r, stem_sm);
+  cp_async_commit();
+  const int ntile = (y.W + 15) / 16;
+  for (int it = 0; r < rows; r += gridDim.x, it++) {
+    const __half* cur = stem_sm + (it & 1) * 3 * pitch;
+    if (r + (int)gridDim.x < rows) stage(r + gridDim.x, stem_sm + ((it + 1) & 1) * 3 * pitch);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int img = r / y.H, oy = r - img * y.H;
+    for (int mt = warp; mt < ntile; mt += 4) {
+      const int ox0 = mt * 16;
+      const int oxa = min(ox0 + g, y.W - 1), oxb = min(ox0 + g + 8, y.W - 1);
+      const __half* pa = cur + oxa * s * 3;
+      const __half* pb = cur + oxb * s * 3;
+      float acc[NF][4];
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      float a0 = acc[2 * q], a1 = acc[2 * q + 1];
-      if (act == 1) { a0 = __fdividef(a0, 1.f + __expf(-a0)); a1 = __fdividef(a1, 1.f + __expf(-a1)); }
-      oh[q] = __floats2half2_rn(a0, a1);
+      for (int f = 0; f < NF; f++) acc[f][0] = acc[f][1] = acc[f][2] = acc[f][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 2; ks++) {
+        __half va[4], vb[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          va[j] = koff[ks][j] >= 0 ? pa[koff[ks][j]] : __float2half(0.f);
+          vb[j] = koff[ks][j] >= 0 ? pb[koff[ks][j]] : __float2half(0.f);
+        }
+        uint32_t a[4];
+        a[0] = (uint32_t)__half_as_ushort(va[0]) | ((uint32_t)__half_as_ushort(va[1]) << 16);
+        a[1] = (uint32_t)__half_as_ushort(vb[0]) | ((uint32_t)__half_as_ushort(vb[1]) << 16);
+        a[2] = (uint32_t)__half_as_ushort(va[2]) | ((uint32_t)__half_as_ushort(va[3]) << 16);
+        a[3] = (uint32_t)__half_as_ushort(vb[2]) | ((uint32_t)__half_as_ushort(vb[3]) << 16);
+#pragma unroll
+        for (int f = 0; f < NF; f++) mma16816(acc[f], a, bf[ks][f][0], bf[ks][f][1]);
+      }
+#pragma unroll
+      for (int f = 0; f < NF; f++) {
+        float v0 = acc[f][0] + bias2[f][0], v1 = acc[f][1] + bias2[f][1];
+        float v2 = acc[f][2] + bias2[f][0], v3 = acc[f][3] + bias2[f][1];
+        if (act == 1) {
+          v0 = silu_fast(v0); v1 = silu_fast(v1); v2 = silu_fast(v2); v3 = silu_fast(v3);
+        }
+        *(uint32_t*)(stg + g * kStgRow + 8 * f + 2 * t) = pack_half2(v0, v1);
+        *(uint32_t*)(stg + (g + 8) * kStgRow + 8 * f + 2 * t) = pack_half2(v2, v3);
+      }
+      __syncwarp();
+      for (int q = lane; q < 16 * NF; q += 32) {
+        const int px = q / NF, f = q - px * NF, ox = ox0 + px;
+        if (ox < y.W)
+          *(uint4*)(y.p + y.pix(img, oy, ox) + 8 * f) = *(const uint4*)(stg + px * kStgRow + 8 * f);
+      }
+      __syncwarp();
     }
-    *(uint4*)(yp + c0) = o;
+    __syncthreads();   // the buffer is refilled two rows later
   }
+  cp_async_wait<0>();
 }
 
 // ---------------- im2col for thin inputs (stem) ----------------
@@ -645,13 +718,43 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     return conv_tc(x, y, res, p, st);
   }
   if (p->groups == 1 && p->Cin == 3 && p->k == 3 && !res && p->Cout % 8 == 0 &&
-      p->Cout <= 256) {
-    const size_t smem = ((size_t)p->Cout * 27 + p->Cout) * sizeof(float);
-    launch_k(conv_stem3_kernel<3>, nblk(npix, 128), 128, smem, (cudaStream_t)st, 
-        dview(*x), dview(*y), (const __half*)p->weight, p->bias, p->Cout, p->s, p->p, p->act,
-        npix);
-    note_launch();
-    return check_launch("conv_stem3");
+      p->Cout <= 96 && x->stride >= 3 && x->C == 3) {
+    // a window row holds input columns [-p, max(W, (Wo-1)*s + 3 - p)) after an 8-half lead
+    const int cols = std::max(x->W + 2 * p->p, (y->W - 1) * p->s + 3);
+    const int pitch = (8 + 3 * cols + 8 + 7) & ~7;
+    const size_t smem = (size_t)6 * pitch * 2 + 4 * 16 * (p->Cout + 8) * 2;
+    const long long rows = (long long)y->batch * y->H;
+    if (rows >= (1LL << 31) || smem > 200 * 1024 || p->p > 2) return YK_EUNSUP;
+    static int nsm = 0;
+    if (!nsm) {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+      if (nsm <= 0) nsm = 148;
+    }
+    const unsigned grid = (unsigned)std::min<long long>(rows, (long long)nsm * 4);
+    const int vec = x->stride == 3 && (x->W * 3) % 8 == 0 &&
+                    (((uintptr_t)x->ptr + (size_t)x->coff * 2) & 15) == 0;
+    void (*kern)(DView, DView, const __half*, const float*, int, int, int, int, int, int) = nullptr;
+    switch (p->Cout / 8) {
+      case 2: kern = conv_stem_mma_kernel<2>; break;
+      case 4: kern = conv_stem_mma_kernel<4>; break;
+      case 6: kern = conv_stem_mma_kernel<6>; break;
+      case 8: kern = conv_stem_mma_kernel<8>; break;
+      case 10: kern = conv_stem_mma_kernel<10>; break;
+      case 12: kern = conv_stem_mma_kernel<12>; break;
+      default: break;
+    }
+    if (kern) {
+      if (smem > 48 * 1024 &&
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+              cudaSuccess)
+        return check_launch("conv_stem attr");
+      launch_k(kern, grid, 128, smem, (cudaStream_t)st, dview(*x), dview(*y),
+               (const __half*)p->weight, p->bias, p->s, p->p, p->act, pitch, vec, (int)rows);
+      note_launch();
+      return check_launch("conv_stem");
+    }
   }
   if (p->groups == 1 && p->Cin <= 4) {
     if (res || p->Cout % 8) return YK_EUNSUP;

@@ -300,11 +300,18 @@ void Engine::validate(const std::string& dir) {
 void Engine::allocate(const std::string& dir) {
   CKE(cudaSetDevice(device));
   CKE(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
-  // Dense convs on the 3-channel input (the stem) run as a tensor-core GEMM over an im2col
-  // buffer: each output pixel's k*k*3 taps padded to a multiple of 8 (27 -> 32), one
-  // contiguous row per pixel, so the GEMM's A operand streams by 2-D TMA.
+  // Dense 3x3 convs on the 3-channel input (the stem) with Cout <= 96 run on the direct
+  // warp-MMA stem kernel (yk_conv).  Other convs on the 3-channel input run as a tensor-core
+  // GEMM over an im2col buffer: each output pixel's k*k*3 taps padded to a multiple of 8
+  // (27 -> 32), one contiguous row per pixel, so the GEMM's A operand streams by 2-D TMA
+  // (YK_STEM_GEMM=1 forces this path for every stem).
+  static const bool force_gemm = [] {
+    const char* e = getenv("YK_STEM_GEMM");
+    return e && *e && *e != '0';
+  }();
   auto is_stem = [&](const Op& op) {
-    return op.kind == CONV && op.g == 1 && op.Cin == 3 && op.k * op.k * 3 <= 64;
+    const bool direct = op.k == 3 && op.Cout % 8 == 0 && op.Cout <= 96 && !force_gemm;
+    return op.kind == CONV && op.g == 1 && op.Cin == 3 && op.k * op.k * 3 <= 64 && !direct;
   };
   bool stem = false;
   for (const Op& op : raw) stem = stem || is_stem(op);
