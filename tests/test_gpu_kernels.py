@@ -156,7 +156,8 @@ def test_conv_transposed_residual(lib, cuda):
     assert rel(out, ref) < TOL
 
 
-@pytest.mark.parametrize("case", PATCH_CASES)
+@pytest.mark.parametrize("case", PATCH_CASES + [(2, 40, 40, 32, 32), (1, 19, 23, 96, 64),
+                                                (1, 160, 160, 32, 32)])
 @pytest.mark.parametrize("tile,msub", [(64, 1), (64, 2), (128, 1), (128, 2)])
 def test_conv_patch_transposed(lib, cuda, case, tile, msub):
     """Halo patches with transposed tiles (algo 4): 64 (M = 64 MMA) or 128 output channels."""

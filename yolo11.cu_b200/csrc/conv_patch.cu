@@ -1,5 +1,8 @@
 // 3x3 stride-1 convolution on tcgen05 with halo patches: each input element crosses from L2
-// into shared memory about 1.3-1.4 times instead of 9 times.
+// into shared memory about 1.3-1.4 times instead of 9 times.  Channel blocks (CB) are 64
+// channels (128-byte rows, 128-byte swizzle) or, for the transposed tiles of inputs whose
+// channel count is a multiple of 32 only, 32 channels (64-byte rows, 64-byte swizzle); the
+// text below says 64.
 //
 // The CTA tile is MT sub-tiles of 8 x 16 output positions (one 128-row UMMA operand each),
 // stacked vertically, of which the first 14 columns are real outputs (the last two of each
@@ -34,14 +37,15 @@ struct PatchArgs {
 constexpr int kPatchCols = 16;     // positions per patch row (row pitch)
 constexpr int kPatchUse = 14;      // real output columns per patch row
 
-template <int BN, int MT, int BST, int WST, bool T = false>
+template <int BN, int MT, int BST, int WST, bool T = false, int CB = 64>
 struct PatchCfg {
   static constexpr int kRows = 8 * MT + 2;                        // window rows
-  static constexpr int kWinTx = kRows * kPatchCols * 128;         // bytes one TMA box brings
+  static constexpr int kRB = CB * 2;                              // bytes per position row
+  static constexpr int kWinTx = kRows * kPatchCols * kRB;         // bytes one TMA box brings
   // The junk columns of the last window row read 2 positions past the box: inside the next
   // buffer (the next window or the weight ring), so no padding is needed.
   static constexpr int kWin = (kWinTx + 1023) & ~1023;
-  static constexpr int kB = BN * 128;                             // one tap's weights, 64 ch
+  static constexpr int kB = BN * kRB;                             // one tap's weights, CB ch
   static constexpr int kAccCols = BN;
   // transposed tiles: one accumulator of 128*MT columns (positions) x BN lanes (channels)
   static constexpr int kTileCols = T ? 128 * MT : MT * BN;
@@ -67,11 +71,13 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-template <int BN, int MT, int BST, int WST, int G, bool T>
+template <int BN, int MT, int BST, int WST, int G, bool T, int CB>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmX) {
-  using Cfg = PatchCfg<BN, MT, BST, WST, T>;
+  using Cfg = PatchCfg<BN, MT, BST, WST, T, CB>;
+  constexpr int kRB = Cfg::kRB;
+  static_assert(CB == 64 || (CB == 32 && T), "32-channel blocks: transposed tiles only");
   static_assert(!T || BN == 64 || BN == 128, "transposed tiles: 64 or 128 channels");
   static_assert(BST % G == 0 && BST / G >= 2, "weight stage groups");
   extern __shared__ uint8_t smem_raw[];
@@ -137,7 +143,7 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
           const uint32_t uw = gw / WST;
           if (uw > 0 && !mbar_wait(wempty(ws), (uw - 1) & 1, 0x201)) { ok = false; break; }
           mbar_expect_tx(wfull(ws), Cfg::kWinTx);
-          tma_load_4d(wbase + ws * Cfg::kWin, &tmX, wfull(ws), cb * 64, tx * kPatchUse - 1,
+          tma_load_4d(wbase + ws * Cfg::kWin, &tmX, wfull(ws), cb * CB, tx * kPatchUse - 1,
                       ty * 8 * MT - 1, img);
           for (int tap = 0; tap < 9; tap++, gb++) {
             const int bs = kFused ? ws * 9 + tap : gb % BST;
@@ -149,7 +155,7 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
               break;
             }
             mbar_expect_tx(bfull(bs), Cfg::kB);
-            tma_load_2d(bbase + bs * Cfg::kB, &tmB, bfull(bs), tap * a.Cin + cb * 64, n0);
+            tma_load_2d(bbase + bs * Cfg::kB, &tmB, bfull(bs), tap * a.Cin + cb * CB, n0);
           }
         }
         if (!ok) { *abort_flag = 1; break; }
@@ -292,9 +298,9 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
             constexpr uint32_t idt = (1u << 4) | ((uint32_t)((128 * MT) >> 3) << 17) |
                                      ((uint32_t)(BN >> 4) << 24);
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-              const uint32_t sa = win + (uint32_t)((ky * kPatchCols + kx) * 128 + kk * 32);
-              tc_mma_f16(d, swz_desc<128>(sb + kk * 32), swz_desc<128>(sa), idt,
+            for (int kk = 0; kk < CB / 16; kk++) {
+              const uint32_t sa = win + (uint32_t)((ky * kPatchCols + kx) * kRB + kk * 32);
+              tc_mma_f16(d, swz_desc<kRB>(sb + kk * 32), swz_desc<kRB>(sa), idt,
                          (cb | tap | kk) != 0);
             }
           } else
@@ -329,7 +335,7 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
 // 4-D tiled map over the NHWC input view {C, W, H, N}: box {64, 16, rows, 1}, 128-byte
 // swizzle; coordinates outside the image (the 1-pixel border) read as zero.
 static bool encode_patch_x(CUtensorMap* m, const __half* x, int C, int W, int H, int N,
-                           int xs, int rows) {
+                           int xs, int rows, int cb) {
   static PFN_cuTensorMapEncodeTiled encode = nullptr;
   static std::mutex mu;
   {
@@ -346,20 +352,20 @@ static bool encode_patch_x(CUtensorMap* m, const __half* x, int C, int W, int H,
   const cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N};
   const cuuint64_t strides[3] = {(cuuint64_t)xs * 2, (cuuint64_t)W * xs * 2,
                                  (cuuint64_t)H * W * xs * 2};
-  const cuuint32_t box[4] = {64, (cuuint32_t)kPatchCols, (cuuint32_t)rows, 1};
+  const cuuint32_t box[4] = {(cuuint32_t)cb, (cuuint32_t)kPatchCols, (cuuint32_t)rows, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(x), dims, strides,
-                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_of(cb),
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int MT, int BST, int WST, int G, bool T = false>
+template <int BN, int MT, int BST, int WST, int G, bool T = false, int CB = 64>
 static int launch_patch(const PatchArgs& a, const YkView* x, cudaStream_t st) {
-  using Cfg = PatchCfg<BN, MT, BST, WST, T>;
+  using Cfg = PatchCfg<BN, MT, BST, WST, T, CB>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(conv_patch_kernel<BN, MT, BST, WST, G, T>,
+    if (cudaFuncSetAttribute(conv_patch_kernel<BN, MT, BST, WST, G, T, CB>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)Cfg::kSmem) != cudaSuccess)
       return check_launch("conv_patch attr");
@@ -371,11 +377,11 @@ static int launch_patch(const PatchArgs& a, const YkView* x, cudaStream_t st) {
   if (!g_num_sms[dev]) cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
   const int grid = a.ntiles < g_num_sms[dev] ? a.ntiles : g_num_sms[dev];
   CUtensorMap tmB, tmX;
-  if (!encode_2d(&tmB, a.w, (uint64_t)9 * a.Cin, (uint64_t)a.Cout, (uint64_t)9 * a.Cin * 2, BN, 64))
+  if (!encode_2d(&tmB, a.w, (uint64_t)9 * a.Cin, (uint64_t)a.Cout, (uint64_t)9 * a.Cin * 2, BN, CB))
     return YK_EUNSUP;
-  if (!encode_patch_x(&tmX, a.x, a.Cin, a.W, a.H, x->batch, x->stride, Cfg::kRows))
+  if (!encode_patch_x(&tmX, a.x, a.Cin, a.W, a.H, x->batch, x->stride, Cfg::kRows, CB))
     return YK_EUNSUP;
-  launch_k(conv_patch_kernel<BN, MT, BST, WST, G, T>, grid, kThreads, Cfg::kSmem, st, a, tmB, tmX);
+  launch_k(conv_patch_kernel<BN, MT, BST, WST, G, T, CB>, grid, kThreads, Cfg::kSmem, st, a, tmB, tmX);
   note_launch();
   return check_launch("conv_patch");
 }
@@ -384,7 +390,9 @@ static int launch_patch(const PatchArgs& a, const YkView* x, cudaStream_t st) {
 // bn in {64, 128, 256}, ms (stacked 8x16 sub-tiles) in {1, 2}.
 int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, int bn,
                int ms, bool trans, cudaStream_t st) {
-  if (p->k != 3 || p->s != 1 || p->p != 1 || p->groups != 1 || p->Cin % 64 ||
+  // 64-channel blocks when Cin allows them; 32-channel blocks (transposed tiles) otherwise
+  const int cbw = p->Cin % 64 == 0 ? 64 : p->Cin % 32 == 0 && trans ? 32 : 0;
+  if (p->k != 3 || p->s != 1 || p->p != 1 || p->groups != 1 || !cbw ||
       ((uintptr_t)x->ptr & 15) || x->stride % 8 || (x->coff % 8))
     return YK_EUNSUP;
   if (y->H != x->H || y->W != x->W) return YK_EINVAL;
@@ -396,13 +404,22 @@ int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv
   a.rs = res ? res->stride : 0;
   a.w = (const __half*)p->weight; a.bias = p->bias;
   a.Cin = p->Cin; a.Cout = p->Cout; a.act = p->act;
-  a.ncb = p->Cin / 64;
+  a.ncb = p->Cin / cbw;
   a.nty = (x->H + 8 * ms - 1) / (8 * ms);
   a.ntx = (x->W + kPatchUse - 1) / kPatchUse;
   a.ntn = (p->Cout + bn - 1) / bn;
   const long long nt = (long long)y->batch * a.nty * a.ntx * a.ntn;
   if (nt > 0x7fffffffLL) return YK_EUNSUP;
   a.ntiles = (int)nt;
+  if (trans && cbw == 32) {
+    switch (bn * 10 + ms) {
+      case 641: return launch_patch<64, 1, 18, 2, 9, true, 32>(a, x, st);
+      case 642: return launch_patch<64, 2, 18, 2, 9, true, 32>(a, x, st);
+      case 1281: return launch_patch<128, 1, 6, 3, 3, true, 32>(a, x, st);
+      case 1282: return launch_patch<128, 2, 6, 2, 3, true, 32>(a, x, st);
+      default: return YK_EINVAL;
+    }
+  }
   if (trans) {
     switch (bn * 10 + ms) {
       case 641: return launch_patch<64, 1, 18, 2, 9, true>(a, x, st);

@@ -505,14 +505,14 @@ void Engine::autotune() {
   CKE(cudaEventCreate(&e0));
   CKE(cudaEventCreate(&e1));
   // {algo, tile, msub}: implicit GEMM; implicit GEMM with transposed tiles (Cin >= 64);
-  // halo patches with transposed tiles (3x3 stride-1 convs, Cin % 64 == 0)
+  // halo patches with transposed tiles (3x3 stride-1 convs, Cin % 32 == 0)
   static const int combos[][3] = {{1, 32, 1}, {1, 32, 2}, {1, 32, 4}, {1, 64, 1}, {1, 64, 2},
                                   {1, 64, 4}, {1, 128, 1}, {1, 128, 2}, {1, 256, 1},
                                   {3, 128, 1}, {3, 128, 2},
                                   {4, 64, 1}, {4, 64, 2}, {4, 128, 1}, {4, 128, 2}};
   for (Op& op : ops) {
     if (op.kind != CONV || op.g != 1 || (op.Cin % 8 && !op.wpad)) continue;
-    const bool patch_ok = !op.wpad && op.k == 3 && op.s == 1 && op.p == 1 && op.Cin % 64 == 0 &&
+    const bool patch_ok = !op.wpad && op.k == 3 && op.s == 1 && op.p == 1 && op.Cin % 32 == 0 &&
                           patch_enabled();
     const bool trans_ok = !op.wpad && op.Cin >= 64;
     int best_t = 0, best_m = 0, best_a = 1;
