@@ -33,6 +33,11 @@ PKG_DIR = os.path.join(ROOT, "yolo11.cu_b200")
 MODELS = os.path.join(ROOT, "models")
 MODEL, S, FRAME_HW, PER_GPU = "yolo11m", 640, (720, 1280), 32
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) of the tcgen05 conv launches of one 32-frame yolo11m forward, from
+# one ncu capture of the current kernels, and the algorithmic bytes of the same convs (input,
+# weights, output, residual once each): profiles/dram_conv_yolo11m_bs32.md.
+CONV_DRAM_BYTES_PER_STEP = 7.485e9
+CONV_ALG_BYTES_PER_STEP = 9.469e9
 
 
 def load_pkg():
@@ -387,8 +392,14 @@ def run_ours(args):
         "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": (achieved / peak) if achieved else None, "traffic": None,
-                     "kernel": "conv_tc_kernel (tcgen05 implicit-GEMM conv), all launches of one step",
+                     "frac": (achieved / peak) if achieved else None,
+                     "traffic": CONV_DRAM_BYTES_PER_STEP,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over the "
+                                       "104 tcgen05 conv launches of one 32-frame forward "
+                                       "(profiles/dram_conv_yolo11m_bs32.md); algorithmic bytes "
+                                       f"{CONV_ALG_BYTES_PER_STEP:.4g}",
+                     "kernel": "conv_tc_kernel + conv_patch_kernel (tcgen05 convs), all launches "
+                               "of one step",
                      "flops_per_step": flops, "conv_ms_per_step": conv_ms,
                      "conv_launches_per_step": conv_launches, "step_ms_profiled": total_ms,
                      "peak_source": f"{pk_kind} bf16_tflops_sustained"},
