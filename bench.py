@@ -82,26 +82,62 @@ def barrier(world: int):
 
 # ---------------- clocks ----------------
 class ClockSampler:
-    """nvidia-smi clock / throttle samples every 200 ms while the timed region runs."""
-    Q = ("index,clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle-reason samples while the timed region runs: NVML every 10 ms on
+    the GPU this process drives (matched by UUID, so CUDA_VISIBLE_DEVICES cannot mislead it),
+    else nvidia-smi every 200 ms.  Read-only queries."""
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpu: int):
         self.gpu, self.samples, self._stop = gpu, [], threading.Event()
+        self.sm_max, self.source = None, None
+        self._nvml = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(gpu).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.sm_max = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            bits = [pynvml.nvmlClocksEventReasonHwSlowdown,
+                    pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                    pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                    pynvml.nvmlClocksEventReasonSwPowerCap]
+            self._nvml = (pynvml, h, bits)
+            self.source = "nvml"
+        except Exception:
+            self._nvml = None
+            self.source = "nvidia-smi"
         self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _sample_nvml(self):
+        pynvml, h, bits = self._nvml
+        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+        r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+        self.samples.append((sm, [n for n, b in zip(self.NAMES, bits) if r & b]))
+
+    def _sample_smi(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + q,
+                              "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                             timeout=5).stdout.strip()
+        if out:
+            v = [x.strip() for x in out.split(",")]
+            if v[1].replace(".", "").isdigit():
+                self.sm_max = float(v[1])
+            if v[0].replace(".", "").isdigit():
+                self.samples.append((float(v[0]),
+                                     [n for n, a in zip(self.NAMES, v[2:6]) if a == "Active"]))
 
     def _run(self):
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.Q,
-                                      "--format=csv,noheader,nounits"], capture_output=True,
-                                     text=True, timeout=5).stdout.strip()
-                if out:
-                    self.samples.append([v.strip() for v in out.split(",")])
+                self._sample_nvml() if self._nvml else self._sample_smi()
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(0.01 if self._nvml else 0.2)
 
     def __enter__(self):
         self._t.start()
@@ -113,13 +149,12 @@ class ClockSampler:
 
     def summary(self):
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for s in self.samples for n, v in zip(names, s[3:7]) if v.strip() == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(self.samples[0][2]) if self.samples[0][2].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(self.samples)}
+            return {"sm_mhz": None, "sm_max_mhz": self.sm_max, "reasons": ["no samples"],
+                    "source": self.source}
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": self.sm_max,
+                "reasons": sorted({n for s in self.samples for n in s[1]}),
+                "samples": len(self.samples), "source": self.source}
 
 
 def peaks():
