@@ -48,7 +48,10 @@ typedef struct {
                         // 3 implicit GEMM with transposed tiles (128 output channels x
                         // 128*msub pixels per MMA; Cin >= 64; msub 1/2; tile ignored),
                         // 4 halo patches with transposed tiles (as 2 but Cin % 32 == 0;
-                        // tile = output channels per MMA, 64 or 128; msub 1/2)
+                        // tile = output channels per MMA, 64 or 128; msub 1/2),
+                        // 5 halo patches with the 3 horizontal taps folded into the MMA's N
+                        // (3x3 stride 1 pad 1, Cin % 32 == 0; tile 32/64 output channels,
+                        // N = 3*tile; msub 1/2 for tile 32, 1 for 64)
 } YkConv;
 
 // Convolution with bias, activation, optional residual (y = act(conv(x)+b) + res) written

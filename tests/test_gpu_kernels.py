@@ -113,14 +113,16 @@ PATCH_CASES = [
 ]
 
 
-@pytest.mark.parametrize("case", PATCH_CASES)
-@pytest.mark.parametrize("tile,msub", [(64, 1), (64, 2), (128, 1), (128, 2), (256, 1)])
+@pytest.mark.parametrize("case", PATCH_CASES + [(2, 40, 40, 32, 32), (1, 19, 23, 96, 64),
+                                                (1, 33, 30, 32, 48)])
+@pytest.mark.parametrize("tile,msub", [(32, 1), (32, 2), (64, 1), (64, 2), (128, 1), (128, 2),
+                                       (256, 1)])
 def test_conv_patch(lib, cuda, case, tile, msub):
     """3x3 stride-1 convs on halo patches (algo 2), channel-slice input and output views."""
     from yolo11_cu_b200 import runtime as rt
     B, H, W, Cin, Cout = case
-    if tile // 2 >= Cout:
-        pytest.skip("tile more than twice Cout")
+    if tile // 2 >= Cout or (tile == 32 and Cout > 64) or (Cin % 64 and tile > 64):
+        pytest.skip("tile more than twice Cout, or no such configuration")
     g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000)
     x = torch.randn(B, H, W, Cin + 16, generator=g).half().to(cuda)
     w = (torch.randn(Cout, Cin, 3, 3, generator=g) / (Cin * 9) ** 0.5)
@@ -180,6 +182,33 @@ def test_conv_patch_transposed_residual(lib, cuda):
     b = (torch.randn(64, generator=g) * 0.1).to(cuda)
     res = torch.randn(2, 30, 30, 64, generator=g).half().to(cuda)
     out, ref = run_conv(lib, rt, x, w, b, 3, 1, 1, act=1, res=res, tile=64, msub=2, algo=4)
+    assert rel(out, ref) < TOL
+
+
+@pytest.mark.parametrize("case", PATCH_CASES + [(2, 40, 40, 32, 32), (1, 19, 23, 96, 64),
+                                                (1, 160, 160, 32, 32), (1, 33, 30, 32, 48)])
+@pytest.mark.parametrize("tile,msub", [(32, 1), (32, 2), (64, 1)])
+def test_conv_kx_folded(lib, cuda, case, tile, msub):
+    """Halo patches with the horizontal taps folded into N (algo 5)."""
+    from yolo11_cu_b200 import runtime as rt
+    B, H, W, Cin, Cout = case
+    g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000 + 13)
+    x = torch.randn(B, H, W, Cin + 16, generator=g).half().to(cuda)
+    w = (torch.randn(Cout, Cin, 3, 3, generator=g) / (Cin * 9) ** 0.5)
+    b = torch.randn(Cout, generator=g) * 0.1
+    out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), 3, 1, 1, act=1, tile=tile,
+                        msub=msub, xc=(8, None), yc=(8, 8), algo=5)
+    assert rel(out, ref) < TOL
+
+
+def test_conv_kx_folded_residual(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(2, 30, 30, 64, generator=g).half().to(cuda)
+    w = (torch.randn(64, 64, 3, 3, generator=g) / 24).to(cuda)
+    b = (torch.randn(64, generator=g) * 0.1).to(cuda)
+    res = torch.randn(2, 30, 30, 64, generator=g).half().to(cuda)
+    out, ref = run_conv(lib, rt, x, w, b, 3, 1, 1, act=1, res=res, tile=64, msub=1, algo=5)
     assert rel(out, ref) < TOL
 
 

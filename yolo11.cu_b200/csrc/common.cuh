@@ -256,6 +256,21 @@ __device__ __forceinline__ float silu_fast(float v) {
   return v * fmaf(0.5f, t, 0.5f);
 }
 
+// Bias + optional SiLU of a pair of fp32 accumulators with packed pair arithmetic, rounded to
+// a half2: v = acc + bias; act: v * (0.5 + 0.5 * tanh(v / 2)).
+__device__ __forceinline__ __half2 bias_act2(float2 acc, float2 bias, int act) {
+  float2 v = ffma2(acc, make_float2(1.f, 1.f), bias);
+  if (act == 1) {
+    const float2 h = ffma2(v, make_float2(0.5f, 0.5f), make_float2(0.f, 0.f));
+    float2 t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t.x) : "f"(h.x));
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t.y) : "f"(h.y));
+    const float2 sg = ffma2(t, make_float2(0.5f, 0.5f), make_float2(0.5f, 0.5f));
+    v = ffma2(v, sg, make_float2(0.f, 0.f));
+  }
+  return __floats2half2_rn(v.x, v.y);
+}
+
 // Epilogue of one accumulator row (this thread's TMEM lane) of a BN-column tile: output
 // channels n0 .. n0+BN-1 (those < Cout) get bias, SiLU (act == 1), the residual row, and are
 // stored as fp16 into yrow.  TMEM columns come in batches of up to 64 with one wait each.
@@ -278,28 +293,28 @@ __device__ __forceinline__ void epi_row(uint32_t trow, int n0, int Cout, bool mo
       if (nn >= Cout) break;
       const float4 b0 = *(const float4*)(bias + nn);
       const float4 b1 = *(const float4*)(bias + nn + 4);
-      float v[8] = {__uint_as_float(r[8 * h + 0]) + b0.x, __uint_as_float(r[8 * h + 1]) + b0.y,
-                    __uint_as_float(r[8 * h + 2]) + b0.z, __uint_as_float(r[8 * h + 3]) + b0.w,
-                    __uint_as_float(r[8 * h + 4]) + b1.x, __uint_as_float(r[8 * h + 5]) + b1.y,
-                    __uint_as_float(r[8 * h + 6]) + b1.z, __uint_as_float(r[8 * h + 7]) + b1.w};
-      if (act == 1) {
+      const float2 bb[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
+                            make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
+      uint4 o;
+      __half2* oh = (__half2*)&o;
+      if (!rrow) {
 #pragma unroll
-        for (int q = 0; q < 8; q++) v[q] = silu_fast(v[q]);
-      }
-      if (rrow) {
+        for (int q = 0; q < 4; q++)
+          oh[q] = bias_act2(make_float2(__uint_as_float(r[8 * h + 2 * q]),
+                                        __uint_as_float(r[8 * h + 2 * q + 1])), bb[q], act);
+      } else {
+        // residual: act(acc + bias) + res in fp32, one rounding
         const uint4 rv = *(const uint4*)(rrow + nn);
         const __half2* rh = (const __half2*)&rv;
 #pragma unroll
         for (int q = 0; q < 4; q++) {
+          float v0 = __uint_as_float(r[8 * h + 2 * q]) + bb[q].x;
+          float v1 = __uint_as_float(r[8 * h + 2 * q + 1]) + bb[q].y;
+          if (act == 1) { v0 = silu_fast(v0); v1 = silu_fast(v1); }
           const float2 f = __half22float2(rh[q]);
-          v[2 * q] += f.x;
-          v[2 * q + 1] += f.y;
+          oh[q] = __floats2half2_rn(v0 + f.x, v1 + f.y);
         }
       }
-      uint4 o;
-      __half2* oh = (__half2*)&o;
-#pragma unroll
-      for (int q = 0; q < 4; q++) oh[q] = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
       *(uint4*)(yrow + nn) = o;
     }
   }

@@ -77,7 +77,7 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmX) {
   using Cfg = PatchCfg<BN, MT, BST, WST, T, CB>;
   constexpr int kRB = Cfg::kRB;
-  static_assert(CB == 64 || (CB == 32 && T), "32-channel blocks: transposed tiles only");
+  static_assert(CB == 64 || CB == 32, "64- or 32-channel blocks");
   static_assert(!T || BN == 64 || BN == 128, "transposed tiles: 64 or 128 channels");
   static_assert(BST % G == 0 && BST / G >= 2, "weight stage groups");
   extern __shared__ uint8_t smem_raw[];
@@ -196,10 +196,12 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
         tmem_ld_wait();
         if (lane_ok) {
 #pragma unroll
-          for (int k = 0; k < 32; k++) {
-            float v = __uint_as_float(rg[k]) + bc;
-            if (a.act == 1) v = silu_fast(v);
-            stg[k * kCw + lane] = __float2half_rn(v);
+          for (int k = 0; k < 32; k += 2) {
+            const __half2 h = bias_act2(
+                make_float2(__uint_as_float(rg[k]), __uint_as_float(rg[k + 1])),
+                make_float2(bc, bc), a.act);
+            stg[k * kCw + lane] = __low2half(h);
+            stg[(k + 1) * kCw + lane] = __high2half(h);
           }
         }
         __syncwarp();
@@ -305,13 +307,14 @@ conv_patch_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmB,
             }
           } else
 #pragma unroll
-          for (int kk = 0; kk < 4; kk++)
+          for (int kk = 0; kk < CB / 16; kk++)
 #pragma unroll
             for (int mt = 0; mt < MT; mt++) {
               // the swizzle follows the absolute shared-memory address, so a start shifted
-              // by whole 128-byte rows needs no base offset in the descriptor
-              const uint32_t sa = win + (uint32_t)(((mt * 8 + ky) * kPatchCols + kx) * 128 + kk * 32);
-              tc_mma_f16(d + mt * Cfg::kAccCols, swz_desc<128>(sa), swz_desc<128>(sb + kk * 32),
+              // by whole rows needs no base offset in the descriptor
+              const uint32_t sa =
+                  win + (uint32_t)(((mt * 8 + ky) * kPatchCols + kx) * kRB + kk * 32);
+              tc_mma_f16(d + mt * Cfg::kAccCols, swz_desc<kRB>(sa), swz_desc<kRB>(sb + kk * 32),
                          idesc, (cb | tap | kk) != 0);
             }
           if (!kFused && bs % G == G - 1) tc_commit(bempty(bs / G));
@@ -391,7 +394,7 @@ static int launch_patch(const PatchArgs& a, const YkView* x, cudaStream_t st) {
 int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, int bn,
                int ms, bool trans, cudaStream_t st) {
   // 64-channel blocks when Cin allows them; 32-channel blocks (transposed tiles) otherwise
-  const int cbw = p->Cin % 64 == 0 ? 64 : p->Cin % 32 == 0 && trans ? 32 : 0;
+  const int cbw = p->Cin % 64 == 0 ? 64 : p->Cin % 32 == 0 ? 32 : 0;
   if (p->k != 3 || p->s != 1 || p->p != 1 || p->groups != 1 || !cbw ||
       ((uintptr_t)x->ptr & 15) || x->stride % 8 || (x->coff % 8))
     return YK_EUNSUP;
@@ -429,7 +432,18 @@ int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv
       default: return YK_EINVAL;
     }
   }
+  if (cbw == 32) {
+    switch (bn * 10 + ms) {
+      case 321: return launch_patch<32, 1, 18, 2, 9, false, 32>(a, x, st);
+      case 322: return launch_patch<32, 2, 18, 2, 9, false, 32>(a, x, st);
+      case 641: return launch_patch<64, 1, 18, 2, 9, false, 32>(a, x, st);
+      case 642: return launch_patch<64, 2, 18, 2, 9, false, 32>(a, x, st);
+      default: return YK_EINVAL;
+    }
+  }
   switch (bn * 10 + ms) {
+    case 321: return launch_patch<32, 1, 18, 2, 9>(a, x, st);
+    case 322: return launch_patch<32, 2, 18, 2, 9>(a, x, st);
     case 641: return launch_patch<64, 1, 6, 3, 3>(a, x, st);
     case 642: return launch_patch<64, 2, 6, 2, 3>(a, x, st);
     case 1281: return launch_patch<128, 1, 6, 3, 3>(a, x, st);

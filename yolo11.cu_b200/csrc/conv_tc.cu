@@ -55,7 +55,8 @@ struct ConvArgs {
 constexpr int kProducers = 128;
 constexpr int kEpiGroup = 128;      // one epilogue group = 4 warps = all 128 sub-tile rows
 constexpr int kBiasSmem = 2048;     // bias floats cached in shared memory
-constexpr int kThreads = 416;
+constexpr int kThreads = 416;      // halo-patch kernel: 13 warps
+constexpr int kTcThreads = 448;    // implicit GEMM: 14 warps (warp 13 = second MMA issuer)
 constexpr int kMmaWarp = 12;
 
 template <int BN, int STAGES, int MT, int CB, bool T = false>
@@ -112,11 +113,15 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
 }
 
 template <int BN, int STAGES, int MT, int CB, int G, bool T>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, 1)
 conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmA) {
   using Cfg = TcCfg<BN, STAGES, MT, CB, T>;
   static_assert(!T || (BN == 128 && CB == 64), "transposed tiles: 128 channels, 64-ch blocks");
+  // Plain tiles with stacked sub-tiles have two MMA issuers (warps 12 and 13), each owning half
+  // of the sub-tiles: a single thread issues a narrow MMA only every ~50-80 cycles, below the
+  // tensor pipe's rate, and each issuer's commits stall only itself.
+  constexpr int kNMma = (!T && MT >= 2) ? 2 : 1;
   static_assert(STAGES % G == 0 && STAGES / G >= 2, "stage groups");
   constexpr int kTM = 128 * MT;
   extern __shared__ uint8_t smem_raw[];
@@ -141,10 +146,10 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
   if (tid == 0) {
     for (int s = 0; s < STAGES; s++) {
       mbar_init(full_bar(s), a.tmaA ? 1 : kProducers + 1);
-      if (s < STAGES / G) mbar_init(empty_bar(s), 1);
+      if (s < STAGES / G) mbar_init(empty_bar(s), kNMma);
     }
     for (int b = 0; b < Cfg::kNacc; b++) {
-      mbar_init(tfull_bar(b), 1);
+      mbar_init(tfull_bar(b), kNMma);
       mbar_init(tempty_bar(b), kEpiGroup);
     }
     *abort_flag = 0;
@@ -286,10 +291,11 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
         tmem_ld16p(tcol + pc * 32 + 16, r + 16);
         tmem_ld_wait();
 #pragma unroll
-        for (int k = 0; k < 32; k++) {
-          float v = __uint_as_float(r[k]) + bc;
-          if (a.act == 1) v = silu_fast(v);
-          stg[k * 32 + lane] = __float2half_rn(v);
+        for (int k = 0; k < 32; k += 2) {
+          const __half2 h = bias_act2(make_float2(__uint_as_float(r[k]), __uint_as_float(r[k + 1])),
+                                      make_float2(bc, bc), a.act);
+          stg[k * 32 + lane] = __low2half(h);
+          stg[(k + 1) * 32 + lane] = __high2half(h);
         }
         __syncwarp();
 #pragma unroll
@@ -349,9 +355,11 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
       mbar_arrive(tempty_bar(acc));
     }
     if (lane == 0) YK_PROF_ADD(9, clock64() - t_role);
-  } else if (lane == 0) {
-    // ---------------- MMA issuer (warp 12) ----------------
+  } else if (lane == 0 && warp - kMmaWarp < kNMma) {
+    // ---------------- MMA issuers (warp 12, and 13 for stacked plain tiles) ----------------
     constexpr uint32_t idesc = idesc_f16_m128(BN);
+    constexpr int kMtPer = MT / kNMma;
+    const int mt0 = (warp - kMmaWarp) * kMtPer;
     uint32_t g = 0, li = 0;
     for (int t = blockIdx.x; t < a.ntiles && !*abort_flag; t += gridDim.x, li++) {
       const int acc = li % Cfg::kNacc;
@@ -378,28 +386,34 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
 #pragma unroll
           for (int i = 0; i < Cfg::kTPS / 2; i++)
 #pragma unroll
-            for (int mt = 0; mt < MT; mt++)
+            for (int q = 0; q < kMtPer; q++) {
+              const int mt = mt0 + q;
               tc_mma_f16(d + mt * Cfg::kAccCols,
                          nosw_desc(sA + (mt * Cfg::kTPS + 2 * i) * kABlk, kABlk, 128),
                          nosw_desc(sB + 2 * i * kBBlk, kBBlk, 128), idesc, (kb | i) != 0);
+            }
         } else {
 #pragma unroll
           for (int j = 0; j < Cfg::kTPS; j++)
 #pragma unroll
             for (int kk = 0; kk < CB / 16; kk++)
 #pragma unroll
-              for (int mt = 0; mt < MT; mt++)
+              for (int q = 0; q < kMtPer; q++) {
+                const int mt = mt0 + q;
                 tc_mma_f16(d + mt * Cfg::kAccCols,
                            swz_desc<CB * 2>(sA + (mt * Cfg::kTPS + j) * kABlk + kk * 32),
                            swz_desc<CB * 2>(sB + j * kBBlk + kk * 32), idesc, (kb | j | kk) != 0);
+              }
         }
         if (s % G == G - 1) tc_commit(empty_bar(s / G));
       }
       if (!ok) { *abort_flag = 1; break; }
       tc_commit(tfull_bar(acc));
     }
-    YK_PROF_ADD(8, clock64() - t_role);
-    YK_PROF_ADD(11, 1);
+    if (warp == kMmaWarp) {
+      YK_PROF_ADD(8, clock64() - t_role);
+      YK_PROF_ADD(11, 1);
+    }
   }
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -498,7 +512,8 @@ static int launch_tc(const ConvArgs& a, cudaStream_t st) {
     return YK_EUNSUP;
   if (a.tmaA == 2 && !encode_im2col(&tmA, a, CB))
     return YK_EUNSUP;
-  launch_k(conv_tc_kernel<BN, STAGES, MT, CB, G, T>, grid, kThreads, Cfg::kSmem, (cudaStream_t)st, a, tmB, tmA);
+  launch_k(conv_tc_kernel<BN, STAGES, MT, CB, G, T>, grid, kTcThreads, Cfg::kSmem,
+           (cudaStream_t)st, a, tmB, tmA);
   note_launch();
   return check_launch("conv_tc");
 }
@@ -534,8 +549,16 @@ extern "C" void yk_conv_prof(unsigned long long* out, int reset) {
 int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, int bn,
                int ms, bool trans, cudaStream_t st);
 
+int conv_kxn(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, int bn,
+             int ms, cudaStream_t st);
+
 int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p,
             cudaStream_t st) {
+  if (p->algo == 5) {
+    const int bn = p->tile ? p->tile : p->Cout <= 32 ? 32 : 64;
+    const int ms = p->msub ? p->msub : 1;
+    return conv_kxn(x, y, res, p, bn, ms, st);
+  }
   if (p->algo == 2 || p->algo == 4) {
     const bool trans = p->algo == 4;
     const int bn = p->tile ? p->tile
@@ -543,7 +566,7 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     const int ms = p->msub ? p->msub : trans ? 2 : 1;
     return conv_patch(x, y, res, p, bn, ms, trans, st);
   }
-  if (p->algo < 0 || p->algo > 4) return YK_EINVAL;
+  if (p->algo < 0 || p->algo > 5) return YK_EINVAL;
   ConvArgs a;
   DView X = dview(*x), Y = dview(*y);
   a.x = X.p; a.H = x->H; a.W = x->W; a.xs = x->stride;

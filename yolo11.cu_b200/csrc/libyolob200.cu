@@ -3,6 +3,7 @@
 #include "conv_misc.cu"
 #include "conv_tc.cu"
 #include "conv_patch.cu"
+#include "conv_kxn.cu"
 #include "attn.cu"
 #include "post.cu"
 #include "engine.cu"
