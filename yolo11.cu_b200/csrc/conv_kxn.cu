@@ -23,6 +23,12 @@
 
 namespace yk {
 
+// 21 warps: 0 producer, 4-19 epilogue (four groups of four), 20 MMA.  The kx sums make the
+// epilogue the long pole for small Cin, so each accumulator is drained by two groups, each
+// taking alternate 16-channel blocks.
+constexpr int kKxMma = 20;
+constexpr int kKxThreads = 32 * (kKxMma + 1);
+
 template <int BN, int MT, int CB>
 struct KxnCfg {
   static constexpr int kWST = 2;                                  // window ring
@@ -45,7 +51,7 @@ struct KxnCfg {
 };
 
 template <int BN, int MT, int CB>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kKxThreads, 1)
 conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
                 const __grid_constant__ CUtensorMap tmX) {
   using Cfg = KxnCfg<BN, MT, CB>;
@@ -72,7 +78,7 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
   if (tid == 0) {
     for (int s = 0; s < WST; s++) { mbar_init(wfull(s), 1); mbar_init(wempty(s), 1); }
     for (int s = 0; s < Cfg::kBST; s++) mbar_init(bfull(s), 1);
-    for (int b = 0; b < Cfg::kNacc; b++) { mbar_init(tfull(b), 1); mbar_init(tempty(b), kEpiGroup); }
+    for (int b = 0; b < Cfg::kNacc; b++) { mbar_init(tfull(b), 1); mbar_init(tempty(b), 2 * kEpiGroup); }
     *abort_flag = 0;
     mbar_fence_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmW) : "memory");
@@ -80,7 +86,7 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
   }
   pdl_wait();
   pdl_trigger();
-  if (warp == kMmaWarp) {
+  if (warp == kKxMma) {
     tmem_alloc(tslot, Cfg::kTmemCols);
     tmem_relinquish();
   }
@@ -116,16 +122,17 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
         if (!ok) { *abort_flag = 1; break; }
       }
     }
-  } else if (warp >= 4 && warp < kMmaWarp) {
+  } else if (warp >= 4 && warp < kKxMma) {
     // ---------------- epilogue ----------------
     const int sp = warp & 3;
-    const int grp = (warp - 4) >> 2;
+    const int grp = (warp - 4) >> 3;          // accumulator parity this group pair drains
+    const int half = ((warp - 4) >> 2) & 1;   // which alternate 16-channel blocks
     const int row = sp * 32 + lane;
     const int pr = row >> 4, pc = row & 15;
     const bool bias_cached = a.Cout <= kBiasSmem;
     if (bias_cached)
-      for (int i = tid - 128; i < a.Cout; i += 256) bias_s[i] = a.bias[i];
-    asm volatile("bar.sync 1, 256;" ::: "memory");
+      for (int i = tid - 128; i < a.Cout; i += 512) bias_s[i] = a.bias[i];
+    asm volatile("bar.sync 1, 512;" ::: "memory");
     const float* bias = bias_cached ? bias_s : a.bias;
     uint32_t li = 0;
     for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, li++) {
@@ -148,7 +155,7 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
         const uint32_t trow = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kTileCols +
                               mt * Cfg::kSub;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {     // 16 channels = 48 accumulator columns
+        for (int c0 = 16 * half; c0 < BN; c0 += 32) {   // 16 channels = 48 columns
           if (n0 + c0 >= a.Cout) break;           // uniform
           uint32_t rg[48];
           tmem_ld16p(trow + 3 * c0, rg);
@@ -196,7 +203,7 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
       tc_fence_before();
       mbar_arrive(tempty(acc));
     }
-  } else if (warp == kMmaWarp && lane == 0) {
+  } else if (warp == kKxMma && lane == 0) {
     // ---------------- MMA issuer ----------------
     constexpr uint32_t idesc = idesc_f16_m128(3 * BN);
     uint32_t gw = 0, li = 0;
@@ -237,7 +244,7 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
     }
   }
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kKxMma) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
@@ -291,7 +298,7 @@ static int launch_kxn(const PatchArgs& a, const YkView* x, cudaStream_t st) {
   if (!encode_kxn_w(&tmW, a.w, a.Cin, a.Cout, BN, CB)) return YK_EUNSUP;
   if (!encode_patch_x(&tmX, a.x, a.Cin, a.W, a.H, x->batch, x->stride, Cfg::kRows, CB))
     return YK_EUNSUP;
-  launch_k(conv_kxn_kernel<BN, MT, CB>, grid, kThreads, Cfg::kSmem, st, a, tmW, tmX);
+  launch_k(conv_kxn_kernel<BN, MT, CB>, grid, kKxThreads, Cfg::kSmem, st, a, tmW, tmX);
   note_launch();
   return check_launch("conv_kxn");
 }
