@@ -133,8 +133,8 @@ def test_conv_patch(lib, cuda, case, tile, msub):
 
 
 @pytest.mark.parametrize("case", [c for c in CONV_CASES if c[3] >= 64])
-@pytest.mark.parametrize("msub", [1, 2])
-def test_conv_transposed(lib, cuda, case, msub):
+@pytest.mark.parametrize("tile,msub", [(128, 1), (128, 2), (256, 2)])
+def test_conv_transposed(lib, cuda, case, tile, msub):
     """Transposed tiles (algo 3): output channels on the MMA's M side, pixels on N."""
     from yolo11_cu_b200 import runtime as rt
     B, H, W, Cin, Cout, k, s, p = case
@@ -142,8 +142,8 @@ def test_conv_transposed(lib, cuda, case, msub):
     x = torch.randn(B, H, W, Cin + 16, generator=g).half().to(cuda)
     w = (torch.randn(Cout, Cin, k, k, generator=g) / (Cin * k * k) ** 0.5)
     b = torch.randn(Cout, generator=g) * 0.1
-    out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), k, s, p, act=1, msub=msub,
-                        xc=(8, None), yc=(8, 8), algo=3)
+    out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), k, s, p, act=1, tile=tile,
+                        msub=msub, xc=(8, None), yc=(8, 8), algo=3)
     assert rel(out, ref) < TOL
 
 

@@ -67,7 +67,7 @@ struct TcCfg {
   static constexpr int kStage = MT * kABytes + kBBytes;
   static constexpr int kAccCols = BN < 32 ? 32 : BN;         // one sub-tile accumulator
   static constexpr int kTileCols = MT * kAccCols;
-  static constexpr int kNacc = 512 / kTileCols >= 4 ? 4 : 2; // TMEM accumulator ring
+  static constexpr int kNacc = 512 / kTileCols >= 4 ? 4 : 512 / kTileCols;  // TMEM ring
   static constexpr int kTmemCols = kNacc * kTileCols;        // <= 512, power of two
   // transposed tiles: per epilogue warp a [32 pixels][32 channels] fp16 staging block
   static constexpr int kStg = T ? 8 * 32 * 32 * 2 : 0;
@@ -117,7 +117,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmA) {
   using Cfg = TcCfg<BN, STAGES, MT, CB, T>;
-  static_assert(!T || (BN == 128 && CB == 64), "transposed tiles: 128 channels, 64-ch blocks");
+  static_assert(!T || ((BN == 128 || BN == 256) && CB == 64),
+                "transposed tiles: 128 or 256 channels, 64-channel blocks");
+  // 256 transposed channels: two M = 128 MMAs per K step share the pixel operand (half the
+  // operand bytes per FLOP of 128-channel tiles); one accumulator fills TMEM, and the two
+  // epilogue groups drain its channel halves together
+  constexpr bool kT2 = T && BN == 256;
   // Plain tiles with stacked sub-tiles have two MMA issuers (warps 12 and 13), each owning half
   // of the sub-tiles: a single thread issues a narrow MMA only every ~50-80 cycles, below the
   // tensor pipe's rate, and each issuer's commits stall only itself.
@@ -150,7 +155,7 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
     }
     for (int b = 0; b < Cfg::kNacc; b++) {
       mbar_init(tfull_bar(b), kNMma);
-      mbar_init(tempty_bar(b), kEpiGroup);
+      mbar_init(tempty_bar(b), kT2 ? 2 * kEpiGroup : kEpiGroup);
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -274,15 +279,17 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
     __half* stg = stg_s + (warp - 4) * 32 * 32;
     uint32_t li = 0;
     for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, li++) {
-      if ((int)(li & 1) != grp) continue;
+      if (!kT2 && (int)(li & 1) != grp) continue;
       const int acc = li % Cfg::kNacc;
       const uint32_t use = li / Cfg::kNacc;
       if (!mbar_wait(tfull_bar(acc), use & 1, 0x103)) { *abort_flag = 1; break; }
       tc_fence_after();
-      const int m0 = (t / a.ntn) * kTM, n0 = (t % a.ntn) * BN;
+      const int m0 = (t / a.ntn) * kTM;
+      const int n0 = (t % a.ntn) * BN + (kT2 ? 128 * grp : 0);
       const int ch = n0 + sp * 32 + lane;
       const float bc = ch < a.Cout ? a.bias[ch] : 0.f;
-      const uint32_t tcol = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kTileCols;
+      const uint32_t tcol = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kTileCols +
+                            (kT2 ? 256 * grp : 0);
       const bool any_ch = n0 + sp * 32 < a.Cout;   // uniform
 #pragma unroll 1
       for (int pc = 0; pc < kTM / 32 && any_ch; pc++) {
@@ -378,9 +385,13 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
           // transposed: A = 128 weight rows (output channels), B = all MT*128 pixel rows
           constexpr uint32_t idt = idesc_f16_m128(MT * 128);
 #pragma unroll
-          for (int kk = 0; kk < 4; kk++)
+          for (int kk = 0; kk < 4; kk++) {
             tc_mma_f16(d, swz_desc<128>(sB + kk * 32), swz_desc<128>(sA + kk * 32), idt,
                        (kb | kk) != 0);
+            if constexpr (kT2)   // channels 128-255: weight rows 128-255, columns 256-511
+              tc_mma_f16(d + 256, swz_desc<128>(sB + 128 * 128 + kk * 32),
+                         swz_desc<128>(sA + kk * 32), idt, (kb | kk) != 0);
+          }
         } else if constexpr (CB == 8) {
           // 16-byte blocks, no swizzle: one K=16 step spans blocks 2i and 2i+1 (LBO apart)
 #pragma unroll
@@ -581,10 +592,11 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   if (x->H > 30000 || x->W > 30000) return YK_EUNSUP;   // packed 16-bit window origins
   a.M = (int)M;
   a.nk = (a.Ktot + 63) / 64;
-  const int bn = p->algo == 3 ? 128 : p->tile ? p->tile : pick_tile(a.M, a.Cout);
+  const int bn = p->algo == 3 ? (p->tile == 256 ? 256 : 128)
+                 : p->tile ? p->tile : pick_tile(a.M, a.Cout);
   if (bn != 32 && bn != 64 && bn != 128 && bn != 256) return YK_EINVAL;
   int ms = p->msub ? p->msub : p->algo == 3 ? 2 : pick_msub(a.M, a.Cout, bn);
-  if (bn == 256) ms = 1;
+  if (bn == 256 && p->algo != 3) ms = 1;
   if (bn == 128 && ms > 2) ms = 2;
   if (ms != 1 && ms != 2 && ms != 4) return YK_EINVAL;
   a.ntn = (a.Cout + bn - 1) / bn;
@@ -608,7 +620,8 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   // (STAGES, G): a tcgen05.commit costs about as much issue time as ten MMAs, so stages are
   // released in groups of G with at least 16 MMAs per commit where shared memory allows
   if (p->algo == 3) {   // transposed tiles: 128 output channels x 128*ms pixels
-    if (cb != 64 || bn != 128) return YK_EINVAL;
+    if (cb != 64) return YK_EINVAL;
+    if (bn == 256) return ms == 2 ? launch_tc<256, 3, 2, 1, 64, true>(a, st) : YK_EINVAL;
     if (ms == 1) return launch_tc<128, 6, 1, 3, 64, true>(a, st);
     if (ms == 2) return launch_tc<128, 4, 2, 2, 64, true>(a, st);
     return YK_EINVAL;

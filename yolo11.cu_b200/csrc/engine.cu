@@ -508,7 +508,7 @@ void Engine::autotune() {
   // halo patches with transposed tiles (3x3 stride-1 convs, Cin % 32 == 0)
   static const int combos[][3] = {{1, 32, 1}, {1, 32, 2}, {1, 32, 4}, {1, 64, 1}, {1, 64, 2},
                                   {1, 64, 4}, {1, 128, 1}, {1, 128, 2}, {1, 256, 1},
-                                  {3, 128, 1}, {3, 128, 2},
+                                  {3, 128, 1}, {3, 128, 2}, {3, 256, 2},
                                   {4, 64, 1}, {4, 64, 2}, {4, 128, 1}, {4, 128, 2},
                                   {5, 32, 1}, {5, 32, 2}, {5, 64, 1}};
   for (Op& op : ops) {
@@ -522,7 +522,7 @@ void Engine::autotune() {
       const int tile = cm[1];
       if (cm[0] == 4 && (!patch_ok || (tile == 128 && op.Cout <= 64))) continue;
       if (cm[0] == 5 && (!patch_ok || (tile == 64 && op.Cout <= 32))) continue;
-      if (cm[0] == 3 && !trans_ok) continue;
+      if (cm[0] == 3 && (!trans_ok || (tile == 256 && op.Cout <= 128))) continue;
       if (cm[0] == 1 && tile > 32 && tile / 2 >= op.Cout) continue;   // half the tile wasted
       if (tile == 32 && op.Cout > 64) continue;
       op.algo = cm[0];
