@@ -59,7 +59,8 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 bool pdl_enabled();
-bool patch_enabled();   // halo-patch 3x3 convs offered to the autotuner (YK_NO_PATCH=1: no)
+bool patch_enabled();
+bool bulk_store_enabled();   // epilogue bulk tensor stores (YK_NO_BULK_STORE=1: per-row stores)   // halo-patch 3x3 convs offered to the autotuner (YK_NO_PATCH=1: no)
 // Per host thread: -1 follows pdl_enabled(), 0 / 1 force plain / programmatic launches (the
 // engine captures its graphs both ways and keeps the faster).
 static thread_local int g_pdl_override = -1;
@@ -269,6 +270,85 @@ __device__ __forceinline__ __half2 bias_act2(float2 acc, float2 bias, int act) {
     v = ffma2(v, sg, make_float2(0.f, 0.f));
   }
   return __floats2half2_rn(v.x, v.y);
+}
+
+// ---------------- bulk tensor stores (shared -> global) ----------------
+__device__ __forceinline__ void tma_store_2d(const void* map, uint32_t src, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          (uint64_t)map),
+      "r"(src), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Epilogue of one warp's 32 accumulator rows (one row per lane: TMEM lane, output row
+// row0 + lane) of a BN-column tile, through a [32 rows][32 channels] staging block in
+// shared memory (64-byte rows, 64-byte swizzle; 2 KB, 512-byte aligned) and one bulk tensor
+// store per 32 channels: the global writes leave as whole rows of channels instead of a
+// 16-byte piece per row and instruction.  Rows past the tensor map (the M tail) and channels
+// past Cout are clipped by the store.  rrow: this lane's residual row or null.
+template <int BN>
+__device__ __forceinline__ void epi_rows_tma(uint32_t trow, int n0, int Cout, int row0,
+                                             const __half* rrow, const float* bias, int act,
+                                             uint32_t stg, const void* ymap, int lane) {
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    if (n0 + c0 >= Cout) break;   // uniform across the warp
+    uint32_t r[32];
+    tmem_ld16p(trow + c0, r);
+    if (BN > 16 && n0 + c0 + 16 < Cout) tmem_ld16p(trow + c0 + 16, r + 16);
+    tmem_ld_wait();
+    if (lane == 0) bulk_wait_read0();   // the previous store has read the staging block
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 4; h++) {
+      const int nn = n0 + c0 + 8 * h;
+      if (8 * h >= BN || nn >= Cout) break;
+      const float4 b0 = *(const float4*)(bias + nn);
+      const float4 b1 = *(const float4*)(bias + nn + 4);
+      const float2 bb[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
+                            make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
+      uint4 o;
+      __half2* oh = (__half2*)&o;
+      if (!rrow) {
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+          oh[q] = bias_act2(make_float2(__uint_as_float(r[8 * h + 2 * q]),
+                                        __uint_as_float(r[8 * h + 2 * q + 1])), bb[q], act);
+      } else {
+        const uint4 rv = *(const uint4*)(rrow + nn);
+        const __half2* rh = (const __half2*)&rv;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          float v0 = __uint_as_float(r[8 * h + 2 * q]) + bb[q].x;
+          float v1 = __uint_as_float(r[8 * h + 2 * q + 1]) + bb[q].y;
+          if (act == 1) { v0 = silu_fast(v0); v1 = silu_fast(v1); }
+          const float2 f = __half22float2(rh[q]);
+          oh[q] = __floats2half2_rn(v0 + f.x, v1 + f.y);
+        }
+      }
+      // 64-byte swizzle: 16-byte chunk h of row `lane` at chunk h ^ ((lane >> 1) & 3)
+      const uint32_t dst = stg + lane * 64 + ((h ^ ((lane >> 1) & 3)) << 4);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(o.x), "r"(o.y),
+                   "r"(o.z), "r"(o.w)
+                   : "memory");
+    }
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(ymap, stg, n0 + c0, row0);
+      bulk_commit();
+    }
+  }
 }
 
 // Epilogue of one accumulator row (this thread's TMEM lane) of a BN-column tile: output

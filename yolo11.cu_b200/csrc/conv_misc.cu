@@ -22,6 +22,14 @@ static bool dw_tiled_enabled() {
   return on;
 }
 
+bool bulk_store_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("YK_NO_BULK_STORE");
+    return !(e && *e && *e != '0');
+  }();
+  return on;
+}
+
 bool patch_enabled() {
   static const bool on = [] {
     const char* e = getenv("YK_NO_PATCH");

@@ -50,11 +50,12 @@ struct ConvArgs {
   int Ktot, M, nk, ntn, ntiles;
   int tmaA;          // A tiles: 0 cp.async gather, 1 TMA 2-D (1x1 s1 p0), 2 TMA im2col
   int ncb;           // TMA modes: CB-channel blocks per filter tap
+  int bulk_store;    // plain tiles: epilogue rows leave by bulk tensor stores (tmY)
 };
 
 constexpr int kProducers = 128;
 constexpr int kEpiGroup = 128;      // one epilogue group = 4 warps = all 128 sub-tile rows
-constexpr int kBiasSmem = 2048;     // bias floats cached in shared memory
+constexpr int kBiasSmem = 1024;     // bias floats cached in shared memory
 constexpr int kThreads = 416;      // halo-patch kernel: 13 warps
 constexpr int kTcThreads = 448;    // implicit GEMM: 14 warps (warp 13 = second MMA issuer)
 constexpr int kMmaWarp = 12;
@@ -70,7 +71,9 @@ struct TcCfg {
   static constexpr int kNacc = 512 / kTileCols >= 4 ? 4 : 512 / kTileCols;  // TMEM ring
   static constexpr int kTmemCols = kNacc * kTileCols;        // <= 512, power of two
   // transposed tiles: per epilogue warp a [32 pixels][32 channels] fp16 staging block
-  static constexpr int kStg = T ? 8 * 32 * 32 * 2 : 0;
+  // per epilogue warp a 2 KB staging block ([32 px][32 ch] transposed, or [32 rows][32 ch]
+  // for the bulk row stores), 512-byte aligned
+  static constexpr int kStg = 8 * 32 * 32 * 2 + 512;
   static constexpr size_t kSmem = (size_t)STAGES * kStage + 1024 + 256 + kBiasSmem * 4 + kStg;
   static_assert(kTmemCols <= 512, "TMEM budget");
   static_assert((size_t)STAGES * kStage + 1024 + 256 + kBiasSmem * 4 + kStg <= 232448,
@@ -115,7 +118,7 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
 template <int BN, int STAGES, int MT, int CB, int G, bool T>
 __global__ void __launch_bounds__(kTcThreads, 1)
 conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmA) {
+               const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmY) {
   using Cfg = TcCfg<BN, STAGES, MT, CB, T>;
   static_assert(!T || ((BN == 128 || BN == 256) && CB == 64),
                 "transposed tiles: 128 or 256 channels, 64-channel blocks");
@@ -143,7 +146,9 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
   volatile uint32_t* tslot_ptr = (volatile uint32_t*)(smem_raw + (tslot - raw));
   volatile int* abort_flag = (volatile int*)(smem_raw + (tslot - raw) + 8);
   float* bias_s = (float*)(smem_raw + (base - raw) + STAGES * Cfg::kStage + 256);
-  __half* stg_s = (__half*)(bias_s + kBiasSmem);   // transposed tiles only
+  const uint32_t stg_base =
+      (smem_u32(bias_s + kBiasSmem) + 511u) & ~511u;   // per-warp 2 KB staging blocks
+  __half* stg_s = (__half*)(smem_raw + (stg_base - raw));
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -356,11 +361,16 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
         const __half* rrow = a.res ? a.res + (size_t)(mok ? m : 0) * a.rs : nullptr;
         const uint32_t trow = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kTileCols +
                               mt * Cfg::kAccCols;
-        epi_row<BN>(trow, n0, a.Cout, mok, yrow, rrow, bias, a.act);
+        if (a.bulk_store)
+          epi_rows_tma<BN>(trow, n0, a.Cout, m0 + mt * 128 + sp * 32, mok ? rrow : nullptr,
+                           bias, a.act, stg_base + (warp - 4) * 2048, &tmY, lane);
+        else
+          epi_row<BN>(trow, n0, a.Cout, mok, yrow, rrow, bias, a.act);
       }
       tc_fence_before();
       mbar_arrive(tempty_bar(acc));
     }
+    if (lane == 0) bulk_wait0();
     if (lane == 0) YK_PROF_ADD(9, clock64() - t_role);
   } else if (lane == 0 && warp - kMmaWarp < kNMma) {
     // ---------------- MMA issuers (warp 12, and 13 for stacked plain tiles) ----------------
@@ -523,8 +533,14 @@ static int launch_tc(const ConvArgs& a, cudaStream_t st) {
     return YK_EUNSUP;
   if (a.tmaA == 2 && !encode_im2col(&tmA, a, CB))
     return YK_EUNSUP;
+  CUtensorMap tmY;
+  memset(&tmY, 0, sizeof tmY);
+  ConvArgs b = a;
+  // output [M][Cout] view with row stride ys: 32 channels x 32 rows per store, 64-byte swizzle
+  b.bulk_store = !T && ((uintptr_t)a.y & 15) == 0 && a.ys % 8 == 0 && bulk_store_enabled() &&
+                 encode_2d(&tmY, a.y, (uint64_t)a.Cout, (uint64_t)a.M, (uint64_t)a.ys * 2, 32, 32);
   launch_k(conv_tc_kernel<BN, STAGES, MT, CB, G, T>, grid, kTcThreads, Cfg::kSmem,
-           (cudaStream_t)st, a, tmB, tmA);
+           (cudaStream_t)st, b, tmB, tmA, tmY);
   note_launch();
   return check_launch("conv_tc");
 }
