@@ -249,6 +249,27 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   return r;
 }
 
+// Two mixed-precision FMAs on the halves of packed fp16 pairs: c0 += x.lo * w.lo and
+// c1 += x.hi * w.hi with fp32 accumulators (fp16 products are exact in fp32, so this rounds
+// like fmaf on converted inputs, without the conversions).
+__device__ __forceinline__ void fma2_f16f32(float& c0, float& c1, uint32_t x2, uint32_t w2) {
+  asm("{\n\t.reg .f16 xl, xh, wl, wh;\n\t"
+      "mov.b32 {xl, xh}, %2;\n\tmov.b32 {wl, wh}, %3;\n\t"
+      "fma.rn.f32.f16 %0, xl, wl, %0;\n\tfma.rn.f32.f16 %1, xh, wh, %1;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "r"(x2), "r"(w2));
+}
+
+// As fma2_f16f32, starting from (b0, b1) instead of the accumulators.
+__device__ __forceinline__ void fma2_f16f32_from(float& c0, float& c1, uint32_t x2, uint32_t w2,
+                                                 float b0, float b1) {
+  asm("{\n\t.reg .f16 xl, xh, wl, wh;\n\t"
+      "mov.b32 {xl, xh}, %2;\n\tmov.b32 {wl, wh}, %3;\n\t"
+      "fma.rn.f32.f16 %0, xl, wl, %4;\n\tfma.rn.f32.f16 %1, xh, wh, %5;\n\t}"
+      : "=f"(c0), "=f"(c1)
+      : "r"(x2), "r"(w2), "f"(b0), "f"(b1));
+}
+
 // SiLU with one special-function op: v * sigmoid(v), sigmoid(v) = 0.5 + 0.5 * tanh(v / 2)
 // (the hardware tanh approximation, relative error about 2^-11, below fp16 output rounding).
 __device__ __forceinline__ float silu_fast(float v) {

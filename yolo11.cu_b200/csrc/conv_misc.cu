@@ -346,12 +346,15 @@ __global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restric
 // of the channel-tile count, so the fp32 [9][64] filter is staged once), double-buffer the
 // windows: the next tile's loads are in flight while the current one is computed.  Thread =
 // 8 channels x 2 output rows x 4 output columns, so each loaded input row feeds two output
-// rows; packed fp32 pair FMAs, taps accumulated in (ky, kx) order like the other depthwise
+// rows; mixed-precision FMAs (fp16 inputs, fp32 accumulators), taps accumulated in (ky, kx) order like the other depthwise
 // kernels.
 constexpr int kDwTY = 8, kDwTX = 16, kDwCh = 64, kDwThreads = 128;
 constexpr int kDwIW = kDwTX + 2, kDwIH = kDwTY + 2;
 constexpr int kDwWin = kDwIH * kDwIW * kDwCh;   // halves per window buffer
-__global__ void __launch_bounds__(kDwThreads, 4) dwconv3t_kernel(DView x, DView y, DView r,
+#ifndef YK_DW_MINB
+#define YK_DW_MINB 4   // resident blocks per SM the register budget is sized for
+#endif
+__global__ void __launch_bounds__(kDwThreads, YK_DW_MINB) dwconv3t_kernel(DView x, DView y, DView r,
                                                                  const __half* __restrict__ w,
                                                                  const float* __restrict__ b,
                                                                  int act, int tiles_c,
@@ -360,14 +363,14 @@ __global__ void __launch_bounds__(kDwThreads, 4) dwconv3t_kernel(DView x, DView 
   pdl_wait();     // inputs come from the previous kernel
   pdl_trigger();
   extern __shared__ __align__(16) __half dw_smem[];   // [2][window] + fp32 [9][64] filter
-  float* wsm = (float*)(dw_smem + 2 * kDwWin);
+  __half* wsm = dw_smem + 2 * kDwWin;
   const int tid = threadIdx.x;
   const int tc = blockIdx.x % tiles_c;                  // fixed: gridDim.x % tiles_c == 0
   const int c0 = tc * kDwCh;
   const int cvalid = min(kDwCh, y.C - c0);
   for (int i = tid; i < 9 * kDwCh; i += kDwThreads) {
     const int t = i / kDwCh, c = i - t * kDwCh;
-    wsm[i] = c < cvalid ? __half2float(w[(size_t)(c0 + c) * 9 + t]) : 0.f;
+    wsm[i] = c < cvalid ? w[(size_t)(c0 + c) * 9 + t] : __float2half(0.f);
   }
   const int per_img = tiles_y * tiles_x * tiles_c;
   auto stage = [&](int t, __half* buf) {
@@ -408,39 +411,35 @@ __global__ void __launch_bounds__(kDwThreads, 4) dwconv3t_kernel(DView x, DView 
     const int ty = q / tiles_x, tx = q - ty * tiles_x;
     const int oy = ty * kDwTY + r0, ox0 = tx * kDwTX + xq;
     if (cok && oy < y.H) {
-      float2 acc[2][4][4];   // [output row][pixel][channel pair]
-#pragma unroll
-      for (int h = 0; h < 2; h++)
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-#pragma unroll
-          for (int e = 0; e < 4; e++) acc[h][j][e] = bias[e];
-      // input rows r0 .. r0+3 of the window; input row ir feeds output row h with ky = ir - h
+      float acc[2][4][8];   // [output row][pixel][channel]; tap (0, 0) starts from the bias
+      // input rows r0 .. r0+3 of the window; input row ir feeds output row h with ky = ir - h;
+      // fp16 inputs and weights go straight into mixed-precision FMAs
 #pragma unroll
       for (int ir = 0; ir < 4; ir++) {
         const __half* trow = cur + ((r0 + ir) * kDwIW + xq) * kDwCh + cg * 8;
-        float2 xf[6][4];
+        uint4 xr[6];
 #pragma unroll
-        for (int u = 0; u < 6; u++) {
-          const uint4 v = *(const uint4*)(trow + u * kDwCh);
-          const __half2* xh = (const __half2*)&v;
-#pragma unroll
-          for (int e = 0; e < 4; e++) xf[u][e] = __half22float2(xh[e]);
-        }
+        for (int u = 0; u < 6; u++) xr[u] = *(const uint4*)(trow + u * kDwCh);
 #pragma unroll
         for (int h = 0; h < 2; h++) {
           const int ky = ir - h;
           if (ky < 0 || ky > 2) continue;
 #pragma unroll
           for (int kx = 0; kx < 3; kx++) {
-            const float4 w0 = *(const float4*)(wsm + (ky * 3 + kx) * kDwCh + cg * 8);
-            const float4 w1 = *(const float4*)(wsm + (ky * 3 + kx) * kDwCh + cg * 8 + 4);
-            const float2 wv[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w),
-                                  make_float2(w1.x, w1.y), make_float2(w1.z, w1.w)};
+            const uint4 wv = *(const uint4*)(wsm + (ky * 3 + kx) * kDwCh + cg * 8);
+            const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-            for (int j = 0; j < 4; j++)
+            for (int j = 0; j < 4; j++) {
+              const uint32_t xx[4] = {xr[j + kx].x, xr[j + kx].y, xr[j + kx].z, xr[j + kx].w};
 #pragma unroll
-              for (int e = 0; e < 4; e++) acc[h][j][e] = ffma2(xf[j + kx][e], wv[e], acc[h][j][e]);
+              for (int e = 0; e < 4; e++) {
+                if (ky == 0 && kx == 0)
+                  fma2_f16f32_from(acc[h][j][2 * e], acc[h][j][2 * e + 1], xx[e], ww[e],
+                                   bias[e].x, bias[e].y);
+                else
+                  fma2_f16f32(acc[h][j][2 * e], acc[h][j][2 * e + 1], xx[e], ww[e]);
+              }
+            }
           }
         }
       }
@@ -463,7 +462,7 @@ __global__ void __launch_bounds__(kDwThreads, 4) dwconv3t_kernel(DView x, DView 
           __half2* oh = (__half2*)&o;
 #pragma unroll
           for (int e = 0; e < 4; e++) {
-            float a0 = acc[h][j][e].x, a1 = acc[h][j][e].y;
+            float a0 = acc[h][j][2 * e], a1 = acc[h][j][2 * e + 1];
             if (act == 1) { a0 = silu_fast(a0); a1 = silu_fast(a1); }
             oh[e] = __floats2half2_rn(a0 + rv[e].x, a1 + rv[e].y);
           }
@@ -791,9 +790,9 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
         if (nsm <= 0) nsm = 148;
       }
       // persistent grid, a multiple of the channel-tile count (each block keeps its filter)
-      long long grid = std::min<long long>(nt, (long long)nsm * 4);
+      long long grid = std::min<long long>(nt, (long long)nsm * YK_DW_MINB);
       grid = std::max<long long>(tcn, grid / tcn * tcn);
-      const size_t smem = 2 * (size_t)kDwWin * sizeof(__half) + 9 * kDwCh * sizeof(float);
+      const size_t smem = (2 * (size_t)kDwWin + 9 * kDwCh) * sizeof(__half);
       static bool attr = false;
       if (!attr) {
         cudaFuncSetAttribute(dwconv3t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
