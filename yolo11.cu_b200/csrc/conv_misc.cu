@@ -343,10 +343,11 @@ __global__ void dwconv_kernel(DView x, DView y, DView r, const __half* __restric
 // x 16 output columns; its 10 x 18 input window comes into shared memory by 16-byte cp.async
 // (zero outside the image), so every input element is read from L2 about 1.4 times instead
 // of once per tap.  Persistent blocks, each with a fixed channel tile (the grid is a multiple
-// of the channel-tile count, so the fp32 [9][64] filter is staged once), double-buffer the
+// of the channel-tile count, so the [9][64] fp16 filter is staged once), double-buffer the
 // windows: the next tile's loads are in flight while the current one is computed.  Thread =
 // 8 channels x 2 output rows x 4 output columns, so each loaded input row feeds two output
-// rows; mixed-precision FMAs (fp16 inputs, fp32 accumulators), taps accumulated in (ky, kx) order like the other depthwise
+// rows; mixed-precision FMAs (fp16 inputs, fp32 accumulators), taps accumulated in
+// (ky, kx) order like the other depthwise
 // kernels.
 constexpr int kDwTY = 8, kDwTX = 16, kDwCh = 64, kDwThreads = 128;
 constexpr int kDwIW = kDwTX + 2, kDwIH = kDwTY + 2;
