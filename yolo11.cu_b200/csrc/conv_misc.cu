@@ -215,13 +215,11 @@ __global__ void __launch_bounds__(128) conv_stem_mma_kernel(DView x, DView y,
       }
 #pragma unroll
       for (int f = 0; f < NF; f++) {
-        float v0 = acc[f][0] + bias2[f][0], v1 = acc[f][1] + bias2[f][1];
-        float v2 = acc[f][2] + bias2[f][0], v3 = acc[f][3] + bias2[f][1];
-        if (act == 1) {
-          v0 = silu_fast(v0); v1 = silu_fast(v1); v2 = silu_fast(v2); v3 = silu_fast(v3);
-        }
-        *(uint32_t*)(stg + g * kStgRow + 8 * f + 2 * t) = pack_half2(v0, v1);
-        *(uint32_t*)(stg + (g + 8) * kStgRow + 8 * f + 2 * t) = pack_half2(v2, v3);
+        const float2 bb = make_float2(bias2[f][0], bias2[f][1]);
+        const __half2 h01 = bias_act2(make_float2(acc[f][0], acc[f][1]), bb, act);
+        const __half2 h23 = bias_act2(make_float2(acc[f][2], acc[f][3]), bb, act);
+        *(__half2*)(stg + g * kStgRow + 8 * f + 2 * t) = h01;
+        *(__half2*)(stg + (g + 8) * kStgRow + 8 * f + 2 * t) = h23;
       }
       __syncwarp();
       for (int q = lane; q < 16 * NF; q += 32) {
