@@ -47,7 +47,8 @@ typedef struct {
                         // (3x3 stride 1 pad 1, Cin % 64 == 0; tile 64/128/256, msub 1/2),
                         // 3 implicit GEMM with transposed tiles (128 output channels x
                         // 128*msub pixels per MMA; Cin >= 64; msub 1/2; tile 256: two
-                        // 128-channel MMAs share the pixel operand, msub 2 only),
+                        // 128-channel MMAs share the pixel operand, msub 2 only; msub 4:
+                        // two 256-pixel MMAs share the weight operand),
                         // 4 halo patches with transposed tiles (as 2 but Cin % 32 == 0;
                         // tile = output channels per MMA, 64 or 128; msub 1/2),
                         // 5 halo patches with the 3 horizontal taps folded into the MMA's N

@@ -133,7 +133,7 @@ def test_conv_patch(lib, cuda, case, tile, msub):
 
 
 @pytest.mark.parametrize("case", [c for c in CONV_CASES if c[3] >= 64])
-@pytest.mark.parametrize("tile,msub", [(128, 1), (128, 2), (256, 2)])
+@pytest.mark.parametrize("tile,msub", [(128, 1), (128, 2), (128, 4), (256, 2)])
 def test_conv_transposed(lib, cuda, case, tile, msub):
     """Transposed tiles (algo 3): output channels on the MMA's M side, pixels on N."""
     from yolo11_cu_b200 import runtime as rt

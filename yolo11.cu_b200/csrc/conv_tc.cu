@@ -126,6 +126,11 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
   // operand bytes per FLOP of 128-channel tiles); one accumulator fills TMEM, and the two
   // epilogue groups drain its channel halves together
   constexpr bool kT2 = T && BN == 256;
+  // 512 transposed pixels (MT = 4): two N = 256 MMAs per K step share the weight operand;
+  // one accumulator fills TMEM, the two epilogue groups drain its pixel halves together
+  constexpr bool kT4 = T && MT == 4;
+  static_assert(!(kT2 && kT4), "one split at a time");
+  constexpr bool kSplit = kT2 || kT4;
   // Plain tiles with stacked sub-tiles have two MMA issuers (warps 12 and 13), each owning half
   // of the sub-tiles: a single thread issues a narrow MMA only every ~50-80 cycles, below the
   // tensor pipe's rate, and each issuer's commits stall only itself.
@@ -160,7 +165,7 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
     }
     for (int b = 0; b < Cfg::kNacc; b++) {
       mbar_init(tfull_bar(b), kNMma);
-      mbar_init(tempty_bar(b), kT2 ? 2 * kEpiGroup : kEpiGroup);
+      mbar_init(tempty_bar(b), kSplit ? 2 * kEpiGroup : kEpiGroup);
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -284,20 +289,20 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
     __half* stg = stg_s + (warp - 4) * 32 * 32;
     uint32_t li = 0;
     for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, li++) {
-      if (!kT2 && (int)(li & 1) != grp) continue;
+      if (!kSplit && (int)(li & 1) != grp) continue;
       const int acc = li % Cfg::kNacc;
       const uint32_t use = li / Cfg::kNacc;
       if (!mbar_wait(tfull_bar(acc), use & 1, 0x103)) { *abort_flag = 1; break; }
       tc_fence_after();
-      const int m0 = (t / a.ntn) * kTM;
+      const int m0 = (t / a.ntn) * kTM + (kT4 ? 256 * grp : 0);
       const int n0 = (t % a.ntn) * BN + (kT2 ? 128 * grp : 0);
       const int ch = n0 + sp * 32 + lane;
       const float bc = ch < a.Cout ? a.bias[ch] : 0.f;
       const uint32_t tcol = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kTileCols +
-                            (kT2 ? 256 * grp : 0);
+                            (kSplit ? 256 * grp : 0);
       const bool any_ch = n0 + sp * 32 < a.Cout;   // uniform
 #pragma unroll 1
-      for (int pc = 0; pc < kTM / 32 && any_ch; pc++) {
+      for (int pc = 0; pc < (kT4 ? 256 : kTM) / 32 && any_ch; pc++) {
         uint32_t r[32];
         tmem_ld16p(tcol + pc * 32, r);
         tmem_ld16p(tcol + pc * 32 + 16, r + 16);
@@ -393,7 +398,7 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
         constexpr uint32_t kABlk = 128 * CB * 2, kBBlk = BN * CB * 2;
         if constexpr (T) {
           // transposed: A = 128 weight rows (output channels), B = all MT*128 pixel rows
-          constexpr uint32_t idt = idesc_f16_m128(MT * 128);
+          constexpr uint32_t idt = idesc_f16_m128(kT4 ? 256 : MT * 128);
 #pragma unroll
           for (int kk = 0; kk < 4; kk++) {
             tc_mma_f16(d, swz_desc<128>(sB + kk * 32), swz_desc<128>(sA + kk * 32), idt,
@@ -401,6 +406,9 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
             if constexpr (kT2)   // channels 128-255: weight rows 128-255, columns 256-511
               tc_mma_f16(d + 256, swz_desc<128>(sB + 128 * 128 + kk * 32),
                          swz_desc<128>(sA + kk * 32), idt, (kb | kk) != 0);
+            if constexpr (kT4)   // pixels 256-511: pixel rows 256-511, columns 256-511
+              tc_mma_f16(d + 256, swz_desc<128>(sB + kk * 32),
+                         swz_desc<128>(sA + 2 * Cfg::kABytes + kk * 32), idt, (kb | kk) != 0);
           }
         } else if constexpr (CB == 8) {
           // 16-byte blocks, no swizzle: one K=16 step spans blocks 2i and 2i+1 (LBO apart)
@@ -613,7 +621,7 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   if (bn != 32 && bn != 64 && bn != 128 && bn != 256) return YK_EINVAL;
   int ms = p->msub ? p->msub : p->algo == 3 ? 2 : pick_msub(a.M, a.Cout, bn);
   if (bn == 256 && p->algo != 3) ms = 1;
-  if (bn == 128 && ms > 2) ms = 2;
+  if (bn == 128 && ms > 2 && p->algo != 3) ms = 2;
   if (ms != 1 && ms != 2 && ms != 4) return YK_EINVAL;
   a.ntn = (a.Cout + bn - 1) / bn;
   const long long nt = ((M + 128LL * ms - 1) / (128LL * ms)) * a.ntn;
@@ -638,6 +646,7 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   if (p->algo == 3) {   // transposed tiles: 128 output channels x 128*ms pixels
     if (cb != 64) return YK_EINVAL;
     if (bn == 256) return ms == 2 ? launch_tc<256, 3, 2, 1, 64, true>(a, st) : YK_EINVAL;
+    if (ms == 4) return launch_tc<128, 2, 4, 1, 64, true>(a, st);
     if (ms == 1) return launch_tc<128, 6, 1, 3, 64, true>(a, st);
     if (ms == 2) return launch_tc<128, 4, 2, 2, 64, true>(a, st);
     return YK_EINVAL;
