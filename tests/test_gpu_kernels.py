@@ -287,9 +287,12 @@ def _v(rt, t, coff=0, Cv=None):
     return rt.tview(t, coff, Cv)
 
 
-def test_maxpool_chain(lib, cuda):
+@pytest.mark.parametrize("shape", [(2, 20, 20, 32), (3, 20, 20, 256), (1, 13, 17, 128),
+                                   (1, 32, 32, 96), (1, 100, 100, 64)])
+def test_maxpool_chain(lib, cuda, shape):
+    """SPPF chain: shared-memory planes (small images) or the direct windows (large)."""
     from yolo11_cu_b200 import runtime as rt
-    x = torch.randn(2, 20, 20, 32, device=cuda).half()
+    x = torch.randn(*shape, device=cuda).half()
     ys = [torch.empty_like(x) for _ in range(3)]
     st = torch.cuda.current_stream().cuda_stream
     assert lib.yk_maxpool5x3(C.byref(_v(rt, x)), *[C.byref(_v(rt, y)) for y in ys], st) == 0

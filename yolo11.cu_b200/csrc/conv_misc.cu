@@ -632,6 +632,65 @@ __global__ void maxpool_kernel(DView x, DView y1, DView y2, DView y3, int nr, I 
   if (nr > 2) *(uint4*)(y3.p + (size_t)pix * y3.stride + c) = m3;
 }
 
+// SPPF chain y1 = pool5(x), y2 = pool5(y1), y3 = pool5(y2) for images small enough to keep
+// a channel block's whole plane in shared memory (the P5 level: 20x20 at 640).  Block = one
+// (image, CB-channel block): the plane comes in once, each 5x5 max is separable (max over
+// 5 columns, then over 5 rows, borders clipped like -inf padding) and runs shared-memory to
+// shared-memory, and the three results go out once each.  Max is exact in fp16, so this
+// equals the direct 5x5 / 9x9 / 13x13 windows of maxpool_kernel.
+template <int CB>
+__global__ void __launch_bounds__(256) pool5x3_plane_kernel(DView x, DView y1, DView y2,
+                                                            DView y3, int ncb) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
+  extern __shared__ __align__(16) uint4 pl_sm[];   // two planes [H*W][CB/8] chunks
+  constexpr int kG = CB / 8;
+  const int img = blockIdx.x / ncb, c0 = (blockIdx.x - img * ncb) * CB;
+  const int H = x.H, W = x.W, n = H * W * kG;
+  uint4* A = pl_sm;
+  uint4* Bp = pl_sm + n;
+  for (int i0 = threadIdx.x; i0 < n; i0 += 256 * 8) {   // all loads in flight, then stores
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = i0 + u * 256, px = i / kG, g = i - px * kG;
+      if (i < n) v[u] = *(const uint4*)(x.p + (size_t)(img * H * W + px) * x.stride + c0 + g * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+      if (i0 + u * 256 < n) A[i0 + u * 256] = v[u];
+  }
+  __syncthreads();
+  const DView* outs[3] = {&y1, &y2, &y3};
+#pragma unroll 1
+  for (int pass = 0; pass < 3; pass++) {
+    for (int i = threadIdx.x; i < n; i += 256) {   // max over 5 columns: A -> B
+      const int px = i / kG, g = i - px * kG;
+      const int yy = px / W, xx = px - yy * W;
+      uint4 m = A[i];
+      for (int dx = -2; dx <= 2; dx++) {
+        const int ix = xx + dx;
+        if (dx != 0 && ix >= 0 && ix < W) hmax8(m, A[(yy * W + ix) * kG + g]);
+      }
+      Bp[i] = m;
+    }
+    __syncthreads();
+    const DView& yo = *outs[pass];
+    for (int i = threadIdx.x; i < n; i += 256) {   // max over 5 rows: B -> A, and out
+      const int px = i / kG, g = i - px * kG;
+      const int yy = px / W, xx = px - yy * W;
+      uint4 m = Bp[i];
+      for (int dy = -2; dy <= 2; dy++) {
+        const int iy = yy + dy;
+        if (dy != 0 && iy >= 0 && iy < H) hmax8(m, Bp[(iy * W + xx) * kG + g]);
+      }
+      A[i] = m;
+      *(uint4*)(yo.p + (size_t)(img * H * W + px) * yo.stride + c0 + g * 8) = m;
+    }
+    __syncthreads();
+  }
+}
+
 // ---------------- data movement ----------------
 // mode 0: nearest 2x upsample (engine/engine.cu:697-708); mode 1: pixel shuffle r=2 from
 // quadrant blocks (engine/engine.cu:713-725); mode 2: channel-slice copy (727-732).
@@ -862,7 +921,25 @@ int yk_maxpool5x3(const YkView* x, const YkView* y1, const YkView* y2, const YkV
       !same_shape(x, y1) || !same_shape(x, y2) || !same_shape(x, y3))
     return YK_EINVAL;
   const long long total = (long long)x->batch * x->H * x->W * (x->C / 8);
-  if (total < (1LL << 31))
+  // whole planes in shared memory: two of H*W*CB halves within 200 KB
+  const size_t plane = (size_t)x->H * x->W * 2;
+  // 64-channel blocks only when 32-channel ones would not fill the GPU twice over
+  const bool many32 = (long long)x->batch * (x->C / 32) >= 2 * 148;
+  const int cbk = (x->C % 32 == 0 && 2 * plane * 32 <= 200 * 1024 && (many32 || x->C % 64))
+                      ? 32
+                  : (x->C % 64 == 0 && 2 * plane * 64 <= 200 * 1024) ? 64
+                  : (x->C % 32 == 0 && 2 * plane * 32 <= 200 * 1024) ? 32 : 0;
+  if (cbk && (long long)x->batch * (x->C / cbk) < (1LL << 31)) {
+    const int ncb = x->C / cbk;
+    const size_t smem = 2 * plane * cbk;
+    auto kern = cbk == 64 ? pool5x3_plane_kernel<64> : pool5x3_plane_kernel<32>;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+      return check_launch("pool5x3 attr");
+    launch_k(kern, (unsigned)(x->batch * ncb), 256, smem, (cudaStream_t)st, dview(*x),
+             dview(*y1), dview(*y2), dview(*y3), ncb);
+  } else if (total < (1LL << 31))
     launch_k(maxpool_kernel<unsigned>, nblk(total, 256), 256, 0, (cudaStream_t)st, 
         dview(*x), dview(*y1), dview(*y2), dview(*y3), 3, (unsigned)total);
   else

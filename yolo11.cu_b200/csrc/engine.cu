@@ -385,18 +385,23 @@ void Engine::allocate(const std::string& dir) {
 // one pass.  The unfused list stays available for per-op dumps.
 void Engine::plan() {
   ops.clear();
+  // the exporter may give one buffer slice several tensor ids
+  auto same_view = [&](int a, int b) {
+    return a == b || (a >= 0 && b >= 0 && tens[a].buf == tens[b].buf &&
+                      tens[a].coff == tens[b].coff && tens[a].C == tens[b].C);
+  };
   for (size_t i = 0; i < raw.size(); i++) {
     Op op = raw[i];
     if (opt.fuse && op.kind == CONV && i + 1 < raw.size()) {
       const Op& nx = raw[i + 1];
-      if (nx.kind == ADD && (nx.a == op.out || nx.b == op.out)) {
-        op.res = nx.a == op.out ? nx.b : nx.a;
+      if (nx.kind == ADD && (same_view(nx.a, op.out) || same_view(nx.b, op.out))) {
+        op.res = same_view(nx.a, op.out) ? nx.b : nx.a;
         op.out = nx.out;
         i++;
       }
     } else if (opt.fuse && op.kind == MAXPOOL5 && i + 2 < raw.size() &&
                raw[i + 1].kind == MAXPOOL5 && raw[i + 2].kind == MAXPOOL5 &&
-               raw[i + 1].a == op.out && raw[i + 2].a == raw[i + 1].out) {
+               same_view(raw[i + 1].a, op.out) && same_view(raw[i + 2].a, raw[i + 1].out)) {
       op.kind = POOLX3;
       op.y2 = raw[i + 1].out;
       op.y3 = raw[i + 2].out;
