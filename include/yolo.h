@@ -76,6 +76,9 @@ int yolo_write_tensor(void* h, int tensor, int B, const void* host);
 int yolo_profile(void* h, int B, int iters, float* ms, int cap);
 // Kind name of fused op i ("CONV", ...) and its tensor-core tile (0 if none).
 const char* yolo_op_desc(void* h, int op_index, int* tile);
+// Shape of fused op i: info[0..9] = Cin, Cout, k, s, groups, output H, output W, algo, msub,
+// has residual.  0, or -1 for a bad index.
+int yolo_op_shape(void* h, int op_index, int* info);
 
 #ifdef __cplusplus
 }

@@ -23,28 +23,40 @@
 
 namespace yk {
 
-// 21 warps: 0 producer, 4-19 epilogue (four groups of four), 20 MMA.  The kx sums make the
-// epilogue the long pole for small Cin, so each accumulator is drained by two groups, each
-// taking alternate 16-channel blocks.
+// 21 warps: 0 producer, 4-19 epilogue, 20 MMA.  The kx sums make the epilogue the long pole
+// for small Cin, so it has 16 warps: with four TMEM accumulators (when four tiles fit in 512
+// columns) each accumulator has its own four warps and four tiles drain at once; with two,
+// each is drained by eight warps taking alternate 16-channel blocks.  Residual rows are
+// copied to shared memory (cp.async) before the accumulator wait, hiding their latency
+// behind the MMAs.
 constexpr int kKxMma = 20;
 constexpr int kKxThreads = 32 * (kKxMma + 1);
 
 template <int BN, int MT, int CB>
 struct KxnCfg {
-  static constexpr int kWST = 2;                                  // window ring
   static constexpr int kRows = 8 * MT + 2;
   static constexpr int kRB = CB * 2;
   static constexpr int kWinTx = kRows * kPatchCols * kRB;
   static constexpr int kWin = (kWinTx + 1023) & ~1023;
   static constexpr int kB = 3 * BN * kRB;                         // one ky: rows (c, kx)
-  static constexpr int kBST = 3 * kWST;
   static constexpr int kSub = 3 * BN;                             // accumulator columns
   static constexpr int kTileCols = MT * kSub;
-  static constexpr int kNacc = 2;
+  // TMEM accumulator ring: four when they fit (so four tiles drain at once), else two
+  static constexpr int kNacc = 4 * kTileCols <= 512 ? 4 : 2;
+  // epilogue warps per sub-partition and tile: 16 epilogue warps = kNacc groups of 4 * kH,
+  // the kH warps of one sub-partition taking alternate 16-channel blocks
+  static constexpr int kH = 4 / kNacc;
+  // window ring: as deep as 200 KB allows (up to 6), so small tiles keep several TMA loads
+  // in flight; each slot holds a window and its three weight stages
+  static constexpr int kResSlot = MT * (BN / (16 * kH)) * 2 * 16;   // residual bytes per thread
+  static constexpr int kRes = 512 * kResSlot;                      // all epilogue threads
+  static constexpr int kWSTfit = (216 * 1024 - kRes) / (kWin + 3 * kB);
+  static constexpr int kWST = kWSTfit > 6 ? 6 : kWSTfit < 2 ? 2 : kWSTfit;
+  static constexpr int kBST = 3 * kWST;
   static constexpr int kTmemCols = kNacc * kTileCols <= 256 ? 256 : 512;
-  static constexpr int kBars = 256;
+  static constexpr int kBars = 512;
   static constexpr size_t kSmem =
-      (size_t)kWST * kWin + (size_t)kBST * kB + 1024 + kBars + kBiasSmem * 4;
+      (size_t)kWST * kWin + (size_t)kBST * kB + 1024 + kBars + kBiasSmem * 4 + kRes;
   static_assert(kNacc * kTileCols <= 512, "TMEM budget");
   static_assert(kSmem <= 232448, "smem budget");
   static_assert(3 * BN <= 256 && BN % 16 == 0, "N = 3 * BN");
@@ -72,13 +84,14 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
   volatile uint32_t* tslot_ptr = (volatile uint32_t*)(smem_raw + (tslot - raw));
   volatile int* abort_flag = (volatile int*)(smem_raw + (tslot - raw) + 8);
   float* bias_s = (float*)(smem_raw + (bar_base - raw) + Cfg::kBars);
+  const uint32_t res_base = bar_base + Cfg::kBars + kBiasSmem * 4;   // residual staging
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int s = 0; s < WST; s++) { mbar_init(wfull(s), 1); mbar_init(wempty(s), 1); }
     for (int s = 0; s < Cfg::kBST; s++) mbar_init(bfull(s), 1);
-    for (int b = 0; b < Cfg::kNacc; b++) { mbar_init(tfull(b), 1); mbar_init(tempty(b), 2 * kEpiGroup); }
+    for (int b = 0; b < Cfg::kNacc; b++) { mbar_init(tfull(b), 1); mbar_init(tempty(b), Cfg::kH * kEpiGroup); }
     *abort_flag = 0;
     mbar_fence_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmW) : "memory");
@@ -95,6 +108,9 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
   tc_fence_after();
   const uint32_t tmem = *tslot_ptr;
   const int per_img = a.nty * a.ntx;
+  // one weight block for the whole conv (Cin <= CB and Cout <= BN): loaded once into the
+  // first slot's stages and kept there
+  const bool wres = a.ncb == 1 && a.ntn == 1;
 
   if (warp == 0) {
     // ---------------- producer (one thread, all loads by TMA) ----------------
@@ -113,7 +129,7 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
           mbar_expect_tx(wfull(ws), Cfg::kWinTx);
           tma_load_4d(wbase + ws * Cfg::kWin, &tmX, wfull(ws), cb * CB, tx * kPatchUse - 1,
                       ty * 8 * MT - 1, img);
-          for (int ky = 0; ky < 3; ky++) {
+          for (int ky = 0; ky < 3 && !(wres && gw > 0); ky++) {
             const int bs = ws * 3 + ky;
             mbar_expect_tx(bfull(bs), Cfg::kB);
             tma_load_4d(bbase + bs * Cfg::kB, &tmW, bfull(bs), cb * CB, 0, ky, n0);
@@ -125,8 +141,9 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
   } else if (warp >= 4 && warp < kKxMma) {
     // ---------------- epilogue ----------------
     const int sp = warp & 3;
-    const int grp = (warp - 4) >> 3;          // accumulator parity this group pair drains
-    const int half = ((warp - 4) >> 2) & 1;   // which alternate 16-channel blocks
+    constexpr int kH = Cfg::kH;
+    const int grp = (warp - 4) / (4 * kH);    // the accumulator (tile index mod kNacc) it drains
+    const int half = ((warp - 4) >> 2) % kH;  // which alternate 16-channel blocks
     const int row = sp * 32 + lane;
     const int pr = row >> 4, pc = row & 15;
     const bool bias_cached = a.Cout <= kBiasSmem;
@@ -136,28 +153,53 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
     const float* bias = bias_cached ? bias_s : a.bias;
     uint32_t li = 0;
     for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, li++) {
-      if ((int)(li & 1) != grp) continue;
+      if ((int)(li % Cfg::kNacc) != grp) continue;
       const int acc = li % Cfg::kNacc;
       const uint32_t use = li / Cfg::kNacc;
-      if (!mbar_wait(tfull(acc), use & 1, 0x303)) { *abort_flag = 1; break; }
-      tc_fence_after();
       const int mtile = t / a.ntn, n0 = (t - mtile * a.ntn) * BN;
       const int img = mtile / per_img, r = mtile - img * per_img;
       const int ty = r / a.ntx, tx = r - ty * a.ntx;
       const int x = tx * kPatchUse + pc;
+      // residual rows fetched before the accumulator wait, so their latency hides behind
+      // the MMAs: [mt][channel block][8-channel half]
+      constexpr int kNcb = BN / (16 * kH);
+      const uint32_t rslot = res_base + (uint32_t)(tid - 128) * Cfg::kResSlot;
+      if (a.res) {
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++) {
+          const int y = ty * 8 * MT + mt * 8 + pr;
+          const bool mok = pc < kPatchUse && x < a.W && y < a.H;
+          const __half* rrow = a.res + (mok ? ((size_t)img * a.H + y) * a.W + x : 0) * a.rs;
+#pragma unroll
+          for (int cb = 0; cb < kNcb; cb++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              const int nn = n0 + 16 * half + 16 * kH * cb + 8 * h;
+              const bool ok = mok && nn < a.Cout;
+              cp_async16(rslot + (uint32_t)(((mt * kNcb + cb) * 2 + h) * 16),
+                         ok ? (const void*)(rrow + nn) : (const void*)a.res, ok ? 16u : 0u);
+            }
+        }
+        cp_async_commit();
+      }
+      if (!mbar_wait(tfull(acc), use & 1, 0x303)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      if (a.res) cp_async_wait<0>();
 #pragma unroll 1
       for (int mt = 0; mt < MT; mt++) {
         const int y = ty * 8 * MT + mt * 8 + pr;
         const bool mok = pc < kPatchUse && x < a.W && y < a.H;
         const size_t m = mok ? ((size_t)img * a.H + y) * a.W + x : 0;
         __half* yrow = a.y + m * a.ys;
-        const __half* rrow = a.res ? a.res + m * a.rs : nullptr;
+        const bool has_res = a.res != nullptr;
         const uint32_t trow = tmem + ((uint32_t)(sp * 32) << 16) + acc * Cfg::kTileCols +
                               mt * Cfg::kSub;
-#pragma unroll 1
-        for (int c0 = 16 * half; c0 < BN; c0 += 32) {   // 16 channels = 48 columns
+#pragma unroll
+        for (int cb = 0; cb < kNcb; cb++) {   // 16 channels = 48 columns
+          const int c0 = 16 * half + 16 * kH * cb;
           if (n0 + c0 >= a.Cout) break;           // uniform
           uint32_t rg[48];
+          __syncwarp();   // the loads below are warp-collective; stores before may diverge
           tmem_ld16p(trow + 3 * c0, rg);
           tmem_ld16p(trow + 3 * c0 + 16, rg + 16);
           tmem_ld16p(trow + 3 * c0 + 32, rg + 32);
@@ -180,13 +222,16 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
                                   make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
             uint4 o;
             __half2* oh = (__half2*)&o;
-            if (!rrow) {
+            if (!has_res) {
 #pragma unroll
               for (int q = 0; q < 4; q++)
                 oh[q] = bias_act2(make_float2(v[8 * h + 2 * q], v[8 * h + 2 * q + 1]), bb[q],
                                   a.act);
             } else {
-              const uint4 rv = *(const uint4*)(rrow + nn);
+              uint4 rv;
+              asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(rv.x), "=r"(rv.y), "=r"(rv.z), "=r"(rv.w)
+                           : "r"(rslot + (uint32_t)(((mt * kNcb + cb) * 2 + h) * 16)));
               const __half2* rh = (const __half2*)&rv;
 #pragma unroll
               for (int q = 0; q < 4; q++) {
@@ -222,8 +267,8 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
         const uint32_t win = wbase + ws * Cfg::kWin;
 #pragma unroll
         for (int ky = 0; ky < 3; ky++) {
-          const int bs = ws * 3 + ky;
-          if (!mbar_wait(bfull(bs), par, 0x306)) { ok = false; break; }
+          const int bs = wres ? ky : ws * 3 + ky;
+          if (!mbar_wait(bfull(bs), wres ? 0u : par, 0x306)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sb = bbase + bs * Cfg::kB;
 #pragma unroll

@@ -942,6 +942,16 @@ const char* yolo_op_desc(void* h, int op_index, int* tile) {
   return kKindNames[e->ops[op_index].kind];
 }
 
+int yolo_op_shape(void* h, int op_index, int* info) {
+  Engine* e = as_engine(h);
+  if (!e || !info || op_index < 0 || op_index >= (int)e->ops.size()) return -1;
+  const Op& o = e->ops[op_index];
+  const Buf& b = e->bufs[e->tens[o.out >= 0 ? o.out : o.a].buf];
+  const int v[10] = {o.Cin, o.Cout, o.k, o.s, o.g, b.H, b.W, o.algo, o.msub, o.res >= 0};
+  for (int i = 0; i < 10; i++) info[i] = v[i];
+  return 0;
+}
+
 int yolo_profile(void* h, int B, int iters, float* ms, int cap) {
   return guarded([&]() -> int {
     Engine* e = as_engine(h);

@@ -268,8 +268,13 @@ int main(int argc, char** argv) {
     for (int i = 0; i < top && i < n; i++) {
       int k = order[i], tile = 0;
       const char* kind = k == n - 1 ? "POST" : yolo_op_desc(h, k, &tile);
-      printf("op%03d %-9s tile=%-3d %8.1f us (%4.1f%%)\n", k, kind, tile, ms[k] * 1000.0,
-             100.0 * ms[k] / tot);
+      int si[10] = {0};
+      char shape[96] = "";
+      if (k < n - 1 && !strcmp(kind, "CONV") && yolo_op_shape(h, k, si) == 0)
+        snprintf(shape, sizeof shape, "  %d->%d k%ds%d g%d %dx%d algo%d ms%d%s", si[0], si[1],
+                 si[2], si[3], si[4], si[5], si[6], si[7], si[8], si[9] ? " +res" : "");
+      printf("op%03d %-9s tile=%-3d %8.1f us (%4.1f%%)%s\n", k, kind, tile, ms[k] * 1000.0,
+             100.0 * ms[k] / tot, shape);
     }
   }
   yolo_destroy(h);

@@ -97,6 +97,7 @@ _SIGS = {
     "yolo_write_tensor": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "yolo_profile": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _P(C.c_float), C.c_int]),
     "yolo_op_desc": (C.c_char_p, [C.c_void_p, C.c_int, _P(C.c_int)]),
+    "yolo_op_shape": (C.c_int, [C.c_void_p, C.c_int, _P(C.c_int)]),
 }
 
 _lib = None
