@@ -53,7 +53,10 @@ typedef struct {
                         // tile = output channels per MMA, 64 or 128; msub 1/2),
                         // 5 halo patches with the 3 horizontal taps folded into the MMA's N
                         // (3x3 stride 1 pad 1, Cin % 32 == 0; tile 32/64 output channels,
-                        // N = 3*tile; msub 1/2 for tile 32, 1 for 64)
+                        // N = 3*tile; msub 1/2 for tile 32, 1 for 64),
+                        // 6 CTA pairs: one M = 256 MMA over two SMs' shared memory, 256
+                        // output channels x 256 pixels per pair (Cin >= 64; tile, msub
+                        // ignored)
 } YkConv;
 
 // Convolution with bias, activation, optional residual (y = act(conv(x)+b) + res) written

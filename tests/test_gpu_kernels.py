@@ -158,6 +158,40 @@ def test_conv_transposed_residual(lib, cuda):
     assert rel(out, ref) < TOL
 
 
+PAIR_CASES = [c for c in CONV_CASES if c[3] >= 64] + [
+    (2, 40, 40, 128, 512, 1, 1, 0),
+    (1, 30, 30, 256, 384, 3, 2, 1),    # stride 2, Cout not a multiple of 256
+    (3, 17, 13, 64, 256, 3, 1, 1),     # ragged pixel tiles across images
+    (1, 9, 7, 512, 768, 1, 1, 0),      # fewer pixels than one pair tile
+]
+
+
+@pytest.mark.parametrize("case", PAIR_CASES)
+def test_conv_pair(lib, cuda, case):
+    """CTA pairs (algo 6): one M = 256 MMA over two SMs (cta_group::2)."""
+    from yolo11_cu_b200 import runtime as rt
+    B, H, W, Cin, Cout, k, s, p = case
+    g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000 + 17)
+    x = torch.randn(B, H, W, Cin + 16, generator=g).half().to(cuda)
+    w = (torch.randn(Cout, Cin, k, k, generator=g) / (Cin * k * k) ** 0.5)
+    b = torch.randn(Cout, generator=g) * 0.1
+    out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), k, s, p, act=1, xc=(8, None),
+                        yc=(8, 8), algo=6)
+    assert rel(out, ref) < TOL
+
+
+def test_conv_pair_residual(lib, cuda):
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(16)
+    x = torch.randn(2, 30, 30, 256, generator=g).half().to(cuda)
+    w = (torch.randn(256, 256, 1, 1, generator=g) / 16).to(cuda)
+    b = (torch.randn(256, generator=g) * 0.1).to(cuda)
+    res = torch.randn(2, 30, 30, 256, generator=g).half().to(cuda)
+    for _ in range(2):   # repeated launches reuse the cached occupancy / attributes
+        out, ref = run_conv(lib, rt, x, w, b, 1, 1, 0, act=1, res=res, algo=6)
+        assert rel(out, ref) < TOL
+
+
 @pytest.mark.parametrize("case", PATCH_CASES + [(2, 40, 40, 32, 32), (1, 19, 23, 96, 64),
                                                 (1, 160, 160, 32, 32)])
 @pytest.mark.parametrize("tile,msub", [(64, 1), (64, 2), (128, 1), (128, 2)])

@@ -587,6 +587,8 @@ int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv
 int conv_kxn(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, int bn,
              int ms, cudaStream_t st);
 
+int conv_pair(const ConvArgs& a, cudaStream_t st);
+
 int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p,
             cudaStream_t st) {
   if (p->algo == 5) {
@@ -601,7 +603,7 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     const int ms = p->msub ? p->msub : trans ? 2 : 1;
     return conv_patch(x, y, res, p, bn, ms, trans, st);
   }
-  if (p->algo < 0 || p->algo > 5) return YK_EINVAL;
+  if (p->algo < 0 || p->algo > 6) return YK_EINVAL;
   ConvArgs a;
   DView X = dview(*x), Y = dview(*y);
   a.x = X.p; a.H = x->H; a.W = x->W; a.xs = x->stride;
@@ -643,6 +645,10 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   }
   // (STAGES, G): a tcgen05.commit costs about as much issue time as ten MMAs, so stages are
   // released in groups of G with at least 16 MMAs per commit where shared memory allows
+  if (p->algo == 6) {   // CTA pairs: 256 output channels x 256 pixels
+    if (cb != 64 || !a.tmaA) return YK_EINVAL;
+    return conv_pair(a, st);
+  }
   if (p->algo == 3) {   // transposed tiles: 128 output channels x 128*ms pixels
     if (cb != 64) return YK_EINVAL;
     if (bn == 256) return ms == 2 ? launch_tc<256, 3, 2, 1, 64, true>(a, st) : YK_EINVAL;

@@ -510,17 +510,20 @@ void Engine::autotune() {
   CKE(cudaEventCreate(&e0));
   CKE(cudaEventCreate(&e1));
   // {algo, tile, msub}: implicit GEMM; implicit GEMM with transposed tiles (Cin >= 64);
-  // halo patches with transposed tiles (3x3 stride-1 convs, Cin % 32 == 0)
+  // halo patches with transposed tiles (3x3 stride-1 convs, Cin % 32 == 0); kx-folded halo
+  // patches; CTA pairs (Cin >= 64, input view on 16-byte rows for its TMA loads)
   static const int combos[][3] = {{1, 32, 1}, {1, 32, 2}, {1, 32, 4}, {1, 64, 1}, {1, 64, 2},
                                   {1, 64, 4}, {1, 128, 1}, {1, 128, 2}, {1, 256, 1},
                                   {3, 128, 1}, {3, 128, 2}, {3, 256, 2},
                                   {4, 64, 1}, {4, 64, 2}, {4, 128, 1}, {4, 128, 2},
-                                  {5, 32, 1}, {5, 32, 2}, {5, 64, 1}};
+                                  {5, 32, 1}, {5, 32, 2}, {5, 64, 1}, {6, 256, 2}};
   for (Op& op : ops) {
     if (op.kind != CONV || op.g != 1 || (op.Cin % 8 && !op.wpad)) continue;
     const bool patch_ok = !op.wpad && op.k == 3 && op.s == 1 && op.p == 1 && op.Cin % 32 == 0 &&
                           patch_enabled();
     const bool trans_ok = !op.wpad && op.Cin >= 64;
+    const YkView xin = view(op.a, maxB);
+    const bool pair_ok = trans_ok && xin.coff % 8 == 0 && xin.stride % 8 == 0;
     int best_t = 0, best_m = 0, best_a = 1;
     float tbest = 1e30f;
     for (const auto& cm : combos) {
@@ -528,6 +531,7 @@ void Engine::autotune() {
       if (cm[0] == 4 && (!patch_ok || (tile == 128 && op.Cout <= 64))) continue;
       if (cm[0] == 5 && (!patch_ok || (tile == 64 && op.Cout <= 32))) continue;
       if (cm[0] == 3 && (!trans_ok || (tile == 256 && op.Cout <= 128))) continue;
+      if (cm[0] == 6 && (!pair_ok || op.Cout <= 128)) continue;
       if (cm[0] == 1 && tile > 32 && tile / 2 >= op.Cout) continue;   // half the tile wasted
       if (tile == 32 && op.Cout > 64) continue;
       op.algo = cm[0];
@@ -554,7 +558,7 @@ void Engine::autotune() {
 std::string Engine::tuning_key() const {
   cudaDeviceProp pr;
   cudaGetDeviceProperties(&pr, device);
-  std::string k = "v2|" + std::string(pr.name) + "|B" + std::to_string(maxB);
+  std::string k = "v3|" + std::string(pr.name) + "|B" + std::to_string(maxB);
   for (const Op& op : ops)
     if (op.kind == CONV)
       k += "|" + std::to_string(op.Cin) + "," + std::to_string(op.Cout) + "," +

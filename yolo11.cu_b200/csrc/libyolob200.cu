@@ -2,6 +2,7 @@
 // device error word) then need no relocatable device code.
 #include "conv_misc.cu"
 #include "conv_tc.cu"
+#include "conv_pair.cu"
 #include "conv_patch.cu"
 #include "conv_kxn.cu"
 #include "attn.cu"
