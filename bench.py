@@ -36,7 +36,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) of the tcgen05 conv launches of one 32-frame yolo11m forward, from
 # one ncu capture of the current kernels, and the algorithmic bytes of the same convs (input,
 # weights, output, residual once each): profiles/dram_conv_yolo11m_bs32.md.
-CONV_DRAM_BYTES_PER_STEP = 7.489e9
+CONV_DRAM_BYTES_PER_STEP = 7.484e9
 CONV_ALG_BYTES_PER_STEP = 9.469e9
 
 
@@ -433,7 +433,8 @@ def run_ours(args):
                                        "104 tcgen05 conv launches of one 32-frame forward "
                                        "(profiles/dram_conv_yolo11m_bs32.md); algorithmic bytes "
                                        f"{CONV_ALG_BYTES_PER_STEP:.4g}",
-                     "kernel": "conv_tc_kernel + conv_patch_kernel + conv_kxn_kernel (tcgen05 convs), all launches "
+                     "kernel": "conv_tc_kernel + conv_patch_kernel + conv_kxn_kernel + conv_pair_kernel "
+                               "(tcgen05 convs), all launches "
                                "of one step",
                      "flops_per_step": flops, "conv_ms_per_step": conv_ms,
                      "conv_launches_per_step": conv_launches, "step_ms_profiled": total_ms,

@@ -214,12 +214,20 @@ conv_pair_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmW,
         tmem_ld16p(tcol + pc * 32, r);
         tmem_ld16p(tcol + pc * 32 + 16, r + 16);
         tmem_ld_wait();
+        // lanes 2j and 2j+1 (channels c, c+1) swap halves so that each writes one 32-bit
+        // (pixel, channel pair): even lanes pixel k, odd lanes pixel k+1, one full 128-byte
+        // shared-memory wavefront per store instead of two half-used ones
+        const bool odd = lane & 1;
+        uint32_t* stg32 = (uint32_t*)stg;
 #pragma unroll
         for (int k = 0; k < 32; k += 2) {
           const __half2 h = bias_act2(make_float2(__uint_as_float(r[k]), __uint_as_float(r[k + 1])),
                                       make_float2(bc, bc), a.act);
-          stg[k * 32 + lane] = __low2half(h);
-          stg[(k + 1) * 32 + lane] = __high2half(h);
+          const uint32_t own = *(const uint32_t*)&h;
+          const uint32_t other = __shfl_xor_sync(~0u, own, 1);
+          // even: (own.lo, other.lo) = pixel k, channels c, c+1; odd: (other.hi, own.hi)
+          const uint32_t v = odd ? __byte_perm(other, own, 0x7632) : __byte_perm(own, other, 0x5410);
+          stg32[((k + odd) * 32 + (lane & ~1)) >> 1] = v;
         }
         __syncwarp();
 #pragma unroll
