@@ -94,6 +94,20 @@ int yk_attn(const YkView* qkv, const YkView* y, int heads, int kd, int hd, yk_st
 int yk_letterbox(const uint8_t* bgr, int sh, int sw, const YkView* y, int slot,
                  float* scale_out, int* top_out, int* left_out, yk_stream_t st);
 
+// Classification head (task "classify").  Global average pool of x [B][H][W][C] into
+// y [B][1][1][C], fp32 sums (engine/engine.cu:735-744, k_gap); C % 8 == 0, 16-byte views.
+int yk_gap(const YkView* x, const YkView* y, yk_stream_t st);
+// Channel softmax of x [B][1][1][C] into y (not in place), fp32 max / exp sum
+// (engine/engine.cu:746-785, k_softmax_ch).
+int yk_softmax(const YkView* x, const YkView* y, yk_stream_t st);
+// Classify preprocessing of one BGR u8 HWC frame (device memory, sh x sw) into batch slot
+// `slot` of the S x S x 3 input view y: shortest edge resized to S with the antialiased
+// triangle filter, centre crop, RGB, /255 (torchvision Resize + CenterCrop + ToTensor;
+// engine/engine.cu:1000-1046, k_preprocess_cls + clsGeom).  geom_out (optional, 4 ints)
+// receives the resized height, width and the crop's top, left.
+int yk_preprocess_cls(const uint8_t* bgr, int sh, int sw, const YkView* y, int slot,
+                      int* geom_out, yk_stream_t st);
+
 // Detection head levels for decode / NMS / masks.
 typedef struct {
   YkView box;     // 64 channels: 4 sides x 16 DFL bins

@@ -23,7 +23,7 @@ typedef struct { float x, y, w, h, angle, score; int cls; } YoloObbDet;
 // engine/yolo.h:10-11 — load a model directory on the current device; buffers for up to
 // max_batch frames.  NULL on failure.
 void* yolo_create(const char* model_dir, int max_batch);
-// engine/yolo.h:12-16 — 0 detect, 1 obb, 2 classify, 3 segment (only 0 and 3 load here).
+// engine/yolo.h:12-16 — 0 detect, 1 obb, 2 classify, 3 segment (obb models do not load here).
 int yolo_task(void* h);
 // engine/yolo.h:17-18 — calibrated GPU latency (ms) of one batch-B graph launch.
 float yolo_exec_ms(void* h, int B);
@@ -39,8 +39,17 @@ void yolo_run_async(void* h, int B);
 void yolo_sync(void* h);
 // engine/yolo.h:29-30 — detections of a slot in original-image coordinates; returns count.
 int yolo_get(void* h, int slot, YoloDet* out, int cap);
+// engine/yolo.h:31-33 — classify models: resize the shortest edge to S (antialiased
+// triangle filter), centre crop, RGB /255 into slot `slot` (async on the engine stream).
+void yolo_preprocess_cls(void* h, const unsigned char* dev_bgr, int height, int width, int slot);
+// engine/yolo.h:34-35 — top-k class ids and probabilities of a slot after yolo_run, descending
+// (ties in class order); 0 for non-classify handles.  Returns the entries written.
+int yolo_get_cls(void* h, int slot, int* ids, float* probs, int k);
 // engine/yolo.h:36-38
 void yolo_slot_geom(void* h, int slot, float* scale, int* top, int* left);
+// engine/yolo.h:39-41 — oriented boxes.  No obb model loads in this engine (yolo_create
+// fails on DECODEOBB graphs with a clear error), so this always returns 0.
+int yolo_get_obb(void* h, int slot, YoloObbDet* out, int cap);
 // engine/yolo.h:42-43 — proto resolution (0/0 for detect models).
 void yolo_mask_dim(void* h, int* ph, int* pw);
 // engine/yolo.h:44-49 — binary {0,1} mask (ph*pw bytes) of detection `det`; 0 or -1.

@@ -147,6 +147,12 @@ def run_graph(g: Graph, x_hwc: np.ndarray, round_fp16: bool = True, inject=None,
             q_, k_, v_ = t.split([kd, kd, hd], dim=2)
             att = ((q_.transpose(-2, -1) @ k_) * (kd ** -0.5)).softmax(dim=-1)
             wr(out, (v_ @ att.transpose(-2, -1)).reshape(heads * hd, H, W))
+        elif kind == "GAP":             # export/export.py:501-502: mean over H, W
+            _, x, out = op
+            wr(out, rd(x).mean(dim=(1, 2), keepdim=True))
+        elif kind == "SOFTMAX":         # export/export.py:503-504: channel softmax of [C,1,1]
+            _, x, out = op
+            wr(out, rd(x).softmax(dim=0))
         elif kind in ("DECODE", "DECODESEG", "DECODEOBB", "MASKS"):
             outs.append(None)
             continue
@@ -194,6 +200,9 @@ def oracle_postproc():
         for n in ("oref_exp", "oref_sigmoid"):
             getattr(lib, n).restype = C.c_float
             getattr(lib, n).argtypes = [C.c_float]
+        lib.oref_preprocess_cls.restype = None
+        lib.oref_preprocess_cls.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                            C.c_void_p]
         lib.oref_f2h.restype = C.c_uint16
         lib.oref_f2h.argtypes = [C.c_float]
         _lib = lib
@@ -202,6 +211,16 @@ def oracle_postproc():
 
 def _p(a):
     return a.ctypes.data_as(C.c_void_p)
+
+
+def preprocess_cls(bgr: np.ndarray, S: int):
+    """Classify preprocessing (C oracle): ([S, S, 3] fp16 RGB, (rh, rw, top, left))."""
+    lib = oracle_postproc()
+    bgr = np.ascontiguousarray(bgr, np.uint8)
+    out = np.zeros((S, S, 3), np.uint16)
+    geom = np.zeros(4, np.int32)
+    lib.oref_preprocess_cls(_p(bgr), bgr.shape[0], bgr.shape[1], S, _p(out), _p(geom))
+    return out.view(np.float16), tuple(int(v) for v in geom)
 
 
 def letterbox(bgr: np.ndarray, S: int) -> np.ndarray:

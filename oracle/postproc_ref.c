@@ -4,6 +4,10 @@
  * checker; never by the engine.  Plain C, single thread, straight loops in the order the
  * reference kernels define:
  *   oref_letterbox  engine/engine.cu:968-998 (k_preprocess) + 1704-1713 (host geometry)
+ *   oref_preprocess_cls  engine/engine.cu:1000-1046 (k_preprocess_cls + clsGeom): shortest
+ *                   edge to S (long edge S*long/short truncated), centre crop with
+ *                   round-half-even offsets, per-axis triangle filter of support
+ *                   max(src/resized, 1), weights normalised by their sums, RGB /255
  *   oref_decode     engine/engine.cu:848-906 (k_decode): first-max class over nc logits,
  *                   sigmoid score, gate score >= conf, DFL softmax expectation, xyxy*stride
  *   oref_nms        engine/engine.cu:1051-1123 (k_nms) without its 1024-candidate cap:
@@ -182,5 +186,53 @@ void oref_mask(const uint16_t* coef, int nm, const uint16_t* proto, int pstride,
 /* exposed for the math tests */
 float oref_exp(float x) { return dm_exp(x); }
 float oref_sigmoid(float x) { return dm_sigmoid(x); }
+static float cls_tri(int i, float centre, float sup) {
+  float d = fabsf(DM_SUB(DM_ADD((float)i, 0.5f), centre));
+  float w = DM_SUB(1.f, DM_DIV(d, sup));
+  return w > 0.f ? w : 0.f;
+}
+
+/* out: S*S*3 fp16 (RGB), geom: {resized h, resized w, top, left} */
+void oref_preprocess_cls(const uint8_t* src, int sh, int sw, int S, uint16_t* out, int* geom) {
+  long rh, rw;
+  if (sw <= sh) { rw = S; rh = (long)S * sh / sw; }
+  else { rh = S; rw = (long)S * sw / sh; }
+  int dy = (int)rh - S, dx = (int)rw - S;
+  int top = dy / 2 + ((dy & 1) && ((dy / 2) & 1));
+  int left = dx / 2 + ((dx & 1) && ((dx / 2) & 1));
+  geom[0] = (int)rh; geom[1] = (int)rw; geom[2] = top; geom[3] = left;
+  float scy = DM_DIV((float)sh, (float)rh), scx = DM_DIV((float)sw, (float)rw);
+  float supy = scy > 1.f ? scy : 1.f, supx = scx > 1.f ? scx : 1.f;
+  for (int y = 0; y < S; y++)
+    for (int x = 0; x < S; x++) {
+      float cy = DM_MUL(DM_ADD((float)(y + top), 0.5f), scy);
+      float cx = DM_MUL(DM_ADD((float)(x + left), 0.5f), scx);
+      int y0 = (int)DM_ADD(DM_SUB(cy, supy), 0.5f), y1 = (int)DM_ADD(DM_ADD(cy, supy), 0.5f);
+      int x0 = (int)DM_ADD(DM_SUB(cx, supx), 0.5f), x1 = (int)DM_ADD(DM_ADD(cx, supx), 0.5f);
+      if (y0 < 0) y0 = 0;
+      if (x0 < 0) x0 = 0;
+      if (y1 > sh) y1 = sh;
+      if (x1 > sw) x1 = sw;
+      float wys = 0.f, wxs = 0.f, b = 0.f, g = 0.f, r = 0.f;
+      for (int i = y0; i < y1; i++) wys = DM_ADD(wys, cls_tri(i, cy, supy));
+      for (int j = x0; j < x1; j++) wxs = DM_ADD(wxs, cls_tri(j, cx, supx));
+      for (int i = y0; i < y1; i++) {
+        float wy = cls_tri(i, cy, supy);
+        for (int j = x0; j < x1; j++) {
+          float w = DM_MUL(wy, cls_tri(j, cx, supx));
+          const uint8_t* p = src + ((size_t)i * sw + j) * 3;
+          b = DM_ADD(b, DM_MUL(w, (float)p[0]));
+          g = DM_ADD(g, DM_MUL(w, (float)p[1]));
+          r = DM_ADD(r, DM_MUL(w, (float)p[2]));
+        }
+      }
+      float inv = DM_DIV(1.f, DM_MUL(DM_MUL(wys, wxs), 255.f));
+      uint16_t* o = out + ((size_t)y * S + x) * 3;
+      o[0] = dm_f2h(DM_MUL(r, inv));
+      o[1] = dm_f2h(DM_MUL(g, inv));
+      o[2] = dm_f2h(DM_MUL(b, inv));
+    }
+}
+
 uint16_t oref_f2h(float x) { return dm_f2h(x); }
 float oref_h2f(uint16_t h) { return dm_h2f(h); }

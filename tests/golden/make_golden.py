@@ -30,7 +30,8 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-CASES = [("yolo11n", 64), ("yolov8n", 64), ("yolo11n-seg", 64), ("yolo11n", 160)]
+CASES = [("yolo11n", 64), ("yolov8n", 64), ("yolo11n-seg", 64), ("yolo11n", 160),
+         ("yolo11n-cls", 224)]
 
 
 def sha256(path):

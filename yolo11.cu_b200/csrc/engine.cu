@@ -99,6 +99,8 @@ struct Engine {
   struct Level { int box, cls, coef, stride; };
   std::vector<Level> levels;
   int protoTen = -1, A = 0;
+  int probsTen = -1;              // classify: SOFTMAX output ([1,1,nc] standalone buffer)
+  __half* h_probs = nullptr;      // classify: pinned [maxB][nc] fp16 probabilities
   // post-processing state
   YkPost post{};
   uint8_t* dmasks = nullptr;
@@ -110,6 +112,7 @@ struct Engine {
   std::map<int, float> exec_ms;
   std::vector<SlotGeom> slots;
   bool seg() const { return task == "segment"; }
+  bool cls() const { return task == "classify"; }
 
   ~Engine() { release(); }
 
@@ -135,6 +138,8 @@ struct Engine {
     if (h_out) cudaFreeHost(h_out);
     if (h_cnt) cudaFreeHost(h_cnt);
     if (h_raw) cudaFreeHost(h_raw);
+    if (h_probs) cudaFreeHost(h_probs);
+    h_probs = nullptr;
     if (st) cudaStreamDestroy(st);
     dweights = nullptr; dstem = nullptr; dbias = nullptr; post = YkPost{}; dmasks = nullptr;
     h_out = nullptr; h_cnt = nullptr; h_raw = nullptr; st = nullptr;
@@ -236,8 +241,8 @@ void Engine::parse(const std::string& dir) {
 }
 
 void Engine::validate(const std::string& dir) {
-  if (task != "detect" && task != "segment")
-    throw Error("task '" + task + "' is not supported by this engine (detect, segment)");
+  if (task != "detect" && task != "segment" && task != "classify")
+    throw Error("task '" + task + "' is not supported by this engine (detect, segment, classify)");
   const Ten& t0 = tens[0];
   if (t0.coff != 0 || t0.C != 3 || bufs[t0.buf].C != 3 || bufs[t0.buf].H != bufs[t0.buf].W)
     throw Error("tensor 0 must be a standalone S x S x 3 input");
@@ -256,8 +261,17 @@ void Engine::validate(const std::string& dir) {
         if (op.woff < 0 || op.boff < 0 || op.woff % 8 || op.boff % 4) throw Error("bad weight offset");
         break;
       }
-      case GAP: case SOFTMAX: case DECODEOBB:
-        throw Error(std::string(kKindNames[op.kind]) + " (classify/obb) is not supported");
+      case GAP: case SOFTMAX: {
+        const Ten &x = tens[op.a], &y = tens[op.out];
+        const Buf &bx = bufs[x.buf], &by = bufs[y.buf];
+        if (!cls()) throw Error(std::string(kKindNames[op.kind]) + " needs task=classify");
+        if (x.C != y.C || by.H != 1 || by.W != 1 || (op.kind == SOFTMAX && (bx.H != 1 || bx.W != 1)))
+          throw Error(std::string(kKindNames[op.kind]) + " shape mismatch");
+        if (op.kind == SOFTMAX) probsTen = op.out;
+        break;
+      }
+      case DECODEOBB:
+        throw Error("DECODEOBB (obb) is not supported");
       case DECODE: case DECODESEG: {
         const Ten& c = tens[op.b];
         if (c.C % 8 || c.C < nc) throw Error("DECODE needs an 8-aligned cls view covering nc");
@@ -272,7 +286,17 @@ void Engine::validate(const std::string& dir) {
       default: break;
     }
   }
-  if (levels.empty() || levels.size() > 4) throw Error("graph needs 1..4 DECODE levels");
+  if (cls()) {
+    // the D2H copy reads [B][nc] contiguous: a standalone full-width [1,1,nc] buffer
+    if (probsTen < 0) throw Error("classify graph without SOFTMAX");
+    const Ten& t = tens[probsTen];
+    const Buf& b = bufs[t.buf];
+    if (t.coff || t.C != b.C || b.H != 1 || b.W != 1 || t.C != nc)
+      throw Error("probs tensor must be a standalone [1,1,nc] buffer");
+    if (!levels.empty()) throw Error("classify graph with DECODE ops");
+  } else if (levels.empty() || levels.size() > 4) {
+    throw Error("graph needs 1..4 DECODE levels");
+  }
   auto fsize = [&](const char* name) -> long {
     FILE* f = fopen((dir + "/" + name).c_str(), "rb");
     if (!f) throw Error(std::string("cannot open ") + dir + "/" + name);
@@ -374,6 +398,7 @@ void Engine::allocate(const std::string& dir) {
   CKE(cudaMallocHost(&h_out, (size_t)maxB * opt.max_det * 6 * sizeof(float)));
   CKE(cudaMallocHost(&h_cnt, maxB * sizeof(int)));
   CKE(cudaMallocHost(&h_raw, maxB * sizeof(int)));
+  if (cls()) CKE(cudaMallocHost(&h_probs, (size_t)maxB * nc * sizeof(__half)));
   memset(h_cnt, 0, maxB * sizeof(int));
   memset(h_raw, 0, maxB * sizeof(int));
   slots.assign(maxB, SlotGeom{});
@@ -471,12 +496,27 @@ void Engine::run_op(const Op& op, int B) {
       CKY(yk_attn(&q, &y, op.heads, op.kd, op.hd, (yk_stream_t)st));
       break;
     }
+    case GAP: {
+      YkView x = view(op.a, B), y = view(op.out, B);
+      CKY(yk_gap(&x, &y, (yk_stream_t)st));
+      break;
+    }
+    case SOFTMAX: {
+      YkView x = view(op.a, B), y = view(op.out, B);
+      CKY(yk_softmax(&x, &y, (yk_stream_t)st));
+      break;
+    }
     default:
       break;   // DECODE / DECODESEG / MASKS run in run_post
   }
 }
 
 void Engine::run_post(int B) {
+  if (cls()) {   // no decode / NMS: the probabilities go to the host
+    CKE(cudaMemcpyAsync(h_probs, bufs[tens[probsTen].buf].p, (size_t)B * nc * sizeof(__half),
+                        cudaMemcpyDeviceToHost, st));
+    return;
+  }
   std::vector<YkLevel> lv(levels.size());
   for (size_t i = 0; i < levels.size(); i++) {
     lv[i].box = view(levels[i].box, B);
@@ -753,7 +793,10 @@ void* yolo_create(const char* model_dir, int max_batch) {
 
 void yolo_destroy(void* h) { delete as_engine(h); }
 
-int yolo_task(void* h) { return h && as_engine(h)->seg() ? 3 : 0; }
+int yolo_task(void* h) {
+  if (!h) return 0;
+  return as_engine(h)->seg() ? 3 : as_engine(h)->cls() ? 2 : 0;
+}
 
 float yolo_exec_ms(void* h, int B) {
   return guarded([&]() -> float {
@@ -778,6 +821,45 @@ void yolo_preprocess(void* h, const unsigned char* dev_bgr, int height, int widt
                      (yk_stream_t)e->st));
     return 0;
   }, -1);
+}
+
+void yolo_preprocess_cls(void* h, const unsigned char* dev_bgr, int height, int width, int slot) {
+  guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || slot < 0 || slot >= e->maxB) throw Error("yolo_preprocess_cls: bad slot");
+    DeviceScope ds(e->device);
+    YkView in = e->view(0, e->maxB);
+    CKY(yk_preprocess_cls(dev_bgr, height, width, &in, slot, nullptr, (yk_stream_t)e->st));
+    return 0;
+  }, -1);
+}
+
+// Top-k of a slot's probabilities: descending, ties in class order (a value enters ahead of
+// the entries it strictly exceeds), as engine/engine.cu:1593-1605.
+int yolo_get_cls(void* h, int slot, int* ids, float* probs, int k) {
+  Engine* e = as_engine(h);
+  if (!e || !e->cls() || slot < 0 || slot >= e->maxB || k < 1 || !ids || !probs) return 0;
+  k = std::min(k, e->nc);
+  const __half* p = e->h_probs + (size_t)slot * e->nc;
+  for (int i = 0; i < k; i++) { ids[i] = -1; probs[i] = -1.f; }
+  for (int c = 0; c < e->nc; c++) {
+    const float v = __half2float(p[c]);
+    for (int i = 0; i < k; i++)
+      if (v > probs[i]) {
+        for (int j = k - 1; j > i; j--) { probs[j] = probs[j - 1]; ids[j] = ids[j - 1]; }
+        probs[i] = v;
+        ids[i] = c;
+        break;
+      }
+  }
+  return k;
+}
+
+// Oriented boxes: the engine loads no obb model (yolo_create rejects DECODEOBB graphs), so
+// there is never anything to return.
+int yolo_get_obb(void* h, int slot, YoloObbDet* out, int cap) {
+  (void)h; (void)slot; (void)out; (void)cap;
+  return 0;
 }
 
 void yolo_run_async(void* h, int B) {

@@ -7,4 +7,5 @@
 #include "conv_kxn.cu"
 #include "attn.cu"
 #include "post.cu"
+#include "cls.cu"
 #include "engine.cu"

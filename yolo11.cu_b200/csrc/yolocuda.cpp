@@ -97,6 +97,40 @@ static void print_dets(void* h, int slot, bool orig) {
            d[i].y1, d[i].x2, d[i].y2);
 }
 
+// classify models: top-5 of slot 0 with names from <dir>/names.txt (index if absent), and
+// the top-1 of every slot for the batch self-consistency check
+static void print_cls(void* h, const std::string& dir, int batch) {
+  std::vector<std::string> names;
+  if (FILE* f = fopen((dir + "/names.txt").c_str(), "r")) {
+    char line[256];
+    while (fgets(line, sizeof line, f)) {
+      std::string n = line;
+      while (!n.empty() && (n.back() == '\n' || n.back() == '\r')) n.pop_back();
+      names.push_back(n);
+    }
+    fclose(f);
+  }
+  int ids[5];
+  float probs[5];
+  if (batch > 1) {
+    printf("batch=%d per-image top1:", batch);
+    int c0 = -1;
+    bool same = true;
+    for (int b = 0; b < batch; b++) {
+      yolo_get_cls(h, b, ids, probs, 1);
+      printf(" %d", ids[0]);
+      if (b == 0) c0 = ids[0];
+      same &= ids[0] == c0;
+    }
+    printf("  %s\n", same ? "(consistent)" : "(MISMATCH!)");
+  }
+  const int n = yolo_get_cls(h, 0, ids, probs, 5);
+  printf("top5:\n");
+  for (int i = 0; i < n; i++)
+    printf("%4d %-24s %.4f\n", ids[i],
+           ids[i] >= 0 && ids[i] < (int)names.size() ? names[ids[i]].c_str() : "", probs[i]);
+}
+
 int main(int argc, char** argv) {
   std::string mode = argc > 1 ? argv[1] : "detect";
   std::string dir = "build/yolo11n";
@@ -183,6 +217,11 @@ int main(int argc, char** argv) {
   } else if (mode == "detect") {
     yolo_run(h, batch);
     if (*yolo_last_error()) { fprintf(stderr, "run: %s\n", yolo_last_error()); return 1; }
+    if (yolo_task(h) == 2) {
+      print_cls(h, dir, batch);
+      yolo_destroy(h);
+      return 0;
+    }
     if (batch > 1) {
       printf("batch=%d per-image kept:", batch);
       std::vector<YoloDet> d(100000);
@@ -237,7 +276,8 @@ int main(int argc, char** argv) {
       if (himg) {
         size_t fb = (size_t)sh * sw * 3;
         CK(cudaMemcpyAsync(dimg, himg, fb * batch, cudaMemcpyHostToDevice, st));
-        for (int b = 0; b < batch; b++) yolo_preprocess(h, dimg + b * fb, sh, sw, b);
+        for (int b = 0; b < batch; b++)
+          (yolo_task(h) == 2 ? yolo_preprocess_cls : yolo_preprocess)(h, dimg + b * fb, sh, sw, b);
       }
       yolo_run(h, batch);
       std::vector<YoloDet> d(300);
@@ -250,8 +290,11 @@ int main(int argc, char** argv) {
     mean /= lat.size();
     printf("%s (B=%d): mean %.3f ms  p50 %.3f ms  p99 %.3f ms  (%.1f frames/s at p50); "
            "graph exec %.3f ms\n",
-           mode == "pipeline" ? "end-to-end pipeline (H2D + preprocess + net + decode + NMS)"
-                              : "cuda graph (net + decode + NMS)",
+           mode == "pipeline"
+               ? (yolo_task(h) == 2 ? "end-to-end pipeline (H2D + preprocess + net + probs D2H)"
+                                    : "end-to-end pipeline (H2D + preprocess + net + decode + NMS)")
+               : (yolo_task(h) == 2 ? "cuda graph (net + softmax + probs D2H)"
+                                    : "cuda graph (net + decode + NMS)"),
            batch, mean, pct(lat, 0.5), pct(lat, 0.99), 1000.0 * batch / pct(lat, 0.5),
            yolo_exec_ms(h, batch));
     if (himg) { cudaFreeHost(himg); cudaFree(dimg); }

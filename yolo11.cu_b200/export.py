@@ -310,6 +310,23 @@ def build_graph(model: "ynn.DetectionModel", S: int) -> GraphBuilder:
         g.layer_out[i] = y
 
     det = net[-1]
+    if isinstance(det, ynn.Classify):
+        # reference export/export.py:389-397: conv -> GAP -> linear (a 1x1 CONV on the
+        # [1,1,1280] pooled tensor) -> channel SOFTMAX, each into a standalone buffer
+        h = g.conv(outs[nbody - 1], det.conv)
+        _, _, C = g.hwc(h)
+        gp = g.fresh(1, 1, C)
+        g.ops.append(("GAP", h, gp))
+        O, I = det.linear.weight.shape
+        logits = g.fresh(1, 1, O)
+        woff, boff = g._weights(det.linear.weight.detach().numpy().reshape(O, 1, 1, I),
+                                det.linear.bias.detach().numpy())
+        g.ops.append(("CONV", gp, logits, 1, 1, 0, 1, ACT_NONE, I, O, woff, boff))
+        probs = g.fresh(1, 1, O)
+        g.ops.append(("SOFTMAX", logits, probs))
+        g.layer_out[len(net) - 1] = probs
+        g.det_ref, g.seg_ref, g.probs = [], None, probs
+        return g
     assert torch.allclose(det.dfl.conv.weight.view(-1), torch.arange(16, dtype=torch.float32))
     seg = isinstance(det, ynn.Segment)
     feats = [outs[j] for j in det.f]
@@ -353,6 +370,18 @@ def letterbox(bgr: np.ndarray, S: int) -> np.ndarray:
     return out[:, :, ::-1].astype(np.float32) / 255.0
 
 
+def classify_input(bgr: np.ndarray, S: int) -> np.ndarray:
+    """torchvision classify preprocessing (ultralytics classify_transforms): PIL bilinear
+    (antialiased) resize of the shortest edge to S, center crop S x S, RGB /255 ->
+    float32 [S, S, 3]."""
+    from PIL import Image
+    import torchvision.transforms as T
+    rgb = np.ascontiguousarray(bgr[:, :, ::-1])
+    t = T.Compose([T.Resize(S, interpolation=T.InterpolationMode.BILINEAR), T.CenterCrop(S),
+                   T.ToTensor()])
+    return t(Image.fromarray(rgb)).permute(1, 2, 0).numpy()
+
+
 def export_model(name: str, out_dir: str, imgsz: int = 640, frame_hw=(1080, 810),
                  frame_seed: int = 0, model=None) -> GraphBuilder:
     """Write ``out_dir`` for the seeded model ``name`` at input size ``imgsz``."""
@@ -361,8 +390,10 @@ def export_model(name: str, out_dir: str, imgsz: int = 640, frame_hw=(1080, 810)
     model = ynn.build_model(name, imgsz=imgsz) if model is None else model
     g = build_graph(model, imgsz)
     os.makedirs(out_dir, exist_ok=True)
-    task = "segment" if isinstance(model.model[-1], ynn.Segment) else "detect"
-    nc = model.model[-1].nc
+    head = model.model[-1]
+    task = ("segment" if isinstance(head, ynn.Segment) else
+            "classify" if isinstance(head, ynn.Classify) else "detect")
+    nc = head.linear.out_features if task == "classify" else head.nc
     with open(os.path.join(out_dir, "model.graph"), "w") as f:
         f.write(g.graph_text(task, nc, imgsz))
     np.concatenate(g.w16).tofile(os.path.join(out_dir, "weights.f16"))
@@ -371,13 +402,20 @@ def export_model(name: str, out_dir: str, imgsz: int = 640, frame_hw=(1080, 810)
     bgr.tofile(os.path.join(out_dir, "bus_raw.u8"))
     with open(os.path.join(out_dir, "bus_raw.txt"), "w") as f:
         f.write(f"{bgr.shape[0]} {bgr.shape[1]}")
-    letterbox(bgr, imgsz).astype(np.float16).tofile(os.path.join(out_dir, "input.f16"))
+    x = classify_input(bgr, imgsz) if task == "classify" else letterbox(bgr, imgsz)
+    x.astype(np.float16).tofile(os.path.join(out_dir, "input.f16"))
+    if task == "classify":
+        with open(os.path.join(out_dir, "names.txt"), "w") as f:
+            f.write("\n".join(model.names[i] for i in range(nc)) + "\n")
     return g
 
 
 def ensure_model_dir(name: str, root: str, imgsz: int = 640, frame_hw=(1080, 810)) -> str:
-    """Return ``root/<name>[-S]``, exporting it first if ``model.graph`` is missing."""
-    d = os.path.join(root, name if imgsz == 640 else f"{name}-{imgsz}")
+    """Return ``root/<name>[-S]`` (S omitted at the model's default size: 640, or 224 for
+    classify), exporting it first if ``model.graph`` is missing."""
+    default = 224 if name.endswith("-cls") else 640
+    d = os.path.join(root, name if imgsz == default else f"{name}-{imgsz}")
     if not os.path.exists(os.path.join(d, "model.graph")):
         export_model(name, d, imgsz, frame_hw)
     return d
+

@@ -35,7 +35,7 @@ import torch.nn.functional as F
 
 __all__ = ["build_model", "MODEL_SCALES", "Conv", "DWConv", "Concat", "Bottleneck", "C2f",
            "C3", "C3k", "C3k2", "SPPF", "Attention", "PSABlock", "C2PSA", "DFL", "Proto",
-           "Detect", "Segment", "DetectionModel", "CLS_BIAS"]
+           "Detect", "Segment", "Classify", "DetectionModel", "CLS_BIAS"]
 
 # Constant bias of the final cls convs, per model: chosen once (frame 0 at 640) so that about
 # 3 % of the 8400 anchors pass conf 0.25, i.e. NMS sees a few hundred candidates per image.
@@ -312,6 +312,21 @@ class Segment(Detect):
         return (torch.cat([self._decode(x), mc], 1), p), (x, mc, p)
 
 
+class Classify(nn.Module):
+    """Classification head: 1x1 Conv to 1280 (+SiLU), global average pool, Linear, softmax."""
+
+    def __init__(self, c1, nc=1000):
+        super().__init__()
+        self.conv = Conv(c1, 1280, 1, 1)
+        self.pool = nn.AdaptiveAvgPool2d(1)
+        self.linear = nn.Linear(1280, nc)
+        self.nc = nc
+
+    def forward(self, x):
+        x = self.linear(self.pool(self.conv(x)).flatten(1))
+        return x.softmax(1), x       # (probs, logits), as the eval-mode head returns
+
+
 # yaml layer lists: (from, repeats, module, args)
 _YOLO11 = [
     (-1, 1, "Conv", [64, 3, 2]), (-1, 1, "Conv", [128, 3, 2]),
@@ -339,16 +354,23 @@ _YOLOV8 = [
 class DetectionModel(nn.Module):
     def __init__(self, name: str, nc: int = 80, imgsz: int = 640):
         super().__init__()
-        m = re.fullmatch(r"(yolo11|yolov8)([nsmlx])(-seg)?", name)
+        m = re.fullmatch(r"(yolo11|yolov8)([nsmlx])(-seg|-cls)?", name)
         if not m:
             raise ValueError(f"unknown model name {name!r} (expected yolo11n, yolov8m-seg, ...)")
-        family, scale, seg = m.group(1), m.group(2), bool(m.group(3))
+        family, scale = m.group(1), m.group(2)
+        seg, cls = m.group(3) == "-seg", m.group(3) == "-cls"
         depth, width, max_ch = MODEL_SCALES[family][scale]
-        self.family, self.scale_name, self.task = family, scale, "segment" if seg else "detect"
+        self.family, self.scale_name = family, scale
+        self.task = "segment" if seg else "classify" if cls else "detect"
+        if cls and nc == 80:
+            nc = 1000      # ImageNet head
         self.names = {i: f"class{i}" for i in range(nc)}
         self.args = {"imgsz": imgsz}
         layers, ch, save_ch = [], [3], []
-        for i, (f, n, mod, args) in enumerate(_YOLO11 if family == "yolo11" else _YOLOV8):
+        table = _YOLO11 if family == "yolo11" else _YOLOV8
+        if cls:   # the backbone without SPPF (yolo11: its C2PSA directly after layer 8)
+            table = table[:9] + ([(-1, 2, "C2PSA", [1024])] if family == "yolo11" else [])
+        for i, (f, n, mod, args) in enumerate(table):
             n = max(round(n * depth), 1) if n > 1 else n
             c1 = ch[f] if isinstance(f, int) else None
             if mod == "Conv":
@@ -381,6 +403,13 @@ class DetectionModel(nn.Module):
             if i == 0:
                 ch = []
             ch.append(c2)
+        if cls:
+            head = Classify(ch[-1], nc)
+            head.f, head.i = -1, len(layers)
+            layers.append(head)
+            self.model = nn.Sequential(*layers)
+            self.stride = torch.tensor([32.0])
+            return
         heads_from = [16, 19, 22] if family == "yolo11" else [15, 18, 21]
         hch = [ch[j] for j in heads_from]
         legacy = family == "yolov8"
@@ -412,7 +441,7 @@ def _init_weights(model: DetectionModel, seed: int, cls_bias: float, gain2: floa
     rng = np.random.Generator(np.random.PCG64(seed))
     head = model.model[-1]
     finals = {}
-    for i in range(head.nl):
+    for i in range(getattr(head, "nl", 0)):
         finals[id(head.cv2[i][-1])] = "box"
         finals[id(head.cv3[i][-1])] = "cls"
         if isinstance(head, Segment):
@@ -439,6 +468,10 @@ def _init_weights(model: DetectionModel, seed: int, cls_bias: float, gain2: floa
                 mod.weight.copy_(torch.from_numpy(normal((O, Ig, kh, kw), 1.0 / math.sqrt(Ig))))
                 b = np.full(O, cls_bias if finals[id(mod)] == "cls" else 0.0, np.float32)
                 mod.bias.copy_(torch.from_numpy(b))
+            elif isinstance(mod, nn.Linear):
+                O, I = mod.weight.shape
+                mod.weight.copy_(torch.from_numpy(normal((O, I), 4.0 / math.sqrt(I))))
+                mod.bias.copy_(torch.from_numpy(normal(O, 0.1)))
             elif isinstance(mod, nn.ConvTranspose2d):
                 Ci, Co, kh, kw = mod.weight.shape
                 mod.weight.copy_(torch.from_numpy(normal((Ci, Co, kh, kw), 1.0 / math.sqrt(Ci))))

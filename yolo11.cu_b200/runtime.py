@@ -40,6 +40,11 @@ class YoloDet(C.Structure):
                 ("score", C.c_float), ("cls", C.c_int)]
 
 
+class YoloObbDet(C.Structure):
+    _fields_ = [("x", C.c_float), ("y", C.c_float), ("w", C.c_float), ("h", C.c_float),
+                ("angle", C.c_float), ("score", C.c_float), ("cls", C.c_int)]
+
+
 class YoloOptions(C.Structure):
     _fields_ = [("device", C.c_int), ("conf", C.c_float), ("iou", C.c_float),
                 ("max_det", C.c_int), ("autotune", C.c_int), ("fuse", C.c_int)]
@@ -60,6 +65,10 @@ _SIGS = {
     "yk_letterbox": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _P(YkView), C.c_int,
                                _P(C.c_float), _P(C.c_int), _P(C.c_int), C.c_void_p]),
     "yk_post_workspace_bytes": (C.c_size_t, [C.c_int, C.c_int]),
+    "yk_gap": (C.c_int, [_P(YkView), _P(YkView), C.c_void_p]),
+    "yk_softmax": (C.c_int, [_P(YkView), _P(YkView), C.c_void_p]),
+    "yk_preprocess_cls": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _P(YkView), C.c_int,
+                                    _P(C.c_int), C.c_void_p]),
     "yk_decode": (C.c_int, [_P(YkLevel), C.c_int, C.c_int, C.c_int, C.c_float, _P(YkPost),
                             C.c_void_p]),
     "yk_nms": (C.c_int, [C.c_int, C.c_int, C.c_float, C.c_int, _P(YkPost), C.c_void_p]),
@@ -81,6 +90,9 @@ _SIGS = {
     "yolo_run_async": (None, [C.c_void_p, C.c_int]),
     "yolo_sync": (None, [C.c_void_p]),
     "yolo_get": (C.c_int, [C.c_void_p, C.c_int, _P(YoloDet), C.c_int]),
+    "yolo_preprocess_cls": (None, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]),
+    "yolo_get_cls": (C.c_int, [C.c_void_p, C.c_int, _P(C.c_int), _P(C.c_float), C.c_int]),
+    "yolo_get_obb": (C.c_int, [C.c_void_p, C.c_int, _P(YoloObbDet), C.c_int]),
     "yolo_slot_geom": (None, [C.c_void_p, C.c_int, _P(C.c_float), _P(C.c_int), _P(C.c_int)]),
     "yolo_mask_dim": (None, [C.c_void_p, _P(C.c_int), _P(C.c_int)]),
     "yolo_get_mask": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
@@ -169,6 +181,17 @@ class Engine:
 
     def preprocess(self, dev_bgr_ptr: int, h: int, w: int, slot: int):
         self.lib.yolo_preprocess(self.h, C.c_void_p(dev_bgr_ptr), h, w, slot)
+
+    def preprocess_cls(self, dev_bgr_ptr: int, h: int, w: int, slot: int):
+        self.lib.yolo_preprocess_cls(self.h, C.c_void_p(dev_bgr_ptr), h, w, slot)
+
+    def task(self) -> int:
+        return self.lib.yolo_task(self.h)
+
+    def get_cls(self, slot: int, k: int = 5):
+        ids, probs = (C.c_int * k)(), (C.c_float * k)()
+        n = self.lib.yolo_get_cls(self.h, slot, ids, probs, k)
+        return list(ids[:n]), list(probs[:n])
 
     def run(self, B: int):
         self.lib.yolo_run(self.h, B)
