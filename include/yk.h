@@ -116,6 +116,20 @@ typedef struct {
   int stride;     // 8, 16, 32
 } YkLevel;
 
+// Oriented boxes (task "obb").  Workspace bytes for batch x anchors.
+size_t yk_obb_workspace_bytes(int batch, int anchors);
+// Decode of every anchor: levels[i].coef is the ANGLE view (channel 0 real); cls views hold
+// nc logits zero-padded to a multiple of 8.  Records cx, cy, w, h (letterbox px), score,
+// cls, theta (engine/engine.cu:908-960, k_decode_obb).
+int yk_decode_obb(const YkLevel* levels, int nlevels, int batch, int nc, float conf, void* ws,
+                  yk_stream_t st);
+// Rotated NMS over ALL candidates (the reference keeps the first 2048): score order (ties by
+// anchor), same-class probiou >= iou drops the later box, dropped boxes still suppress
+// (ultralytics fast-NMS; engine/engine.cu:1160-1252).  outdets [batch][max_out][7] as the
+// decode records, outcnt / rawcnt per image (survivors / candidates).
+int yk_nms_obb(int batch, int anchors, float iou, int max_out, void* ws, float* outdets,
+               int* outcnt, int* rawcnt, yk_stream_t st);
+
 // Device workspace of the post-processing chain, sized by yk_post_workspace_bytes.
 typedef struct {
   void* ws;          // device scratch

@@ -23,7 +23,7 @@ typedef struct { float x, y, w, h, angle, score; int cls; } YoloObbDet;
 // engine/yolo.h:10-11 — load a model directory on the current device; buffers for up to
 // max_batch frames.  NULL on failure.
 void* yolo_create(const char* model_dir, int max_batch);
-// engine/yolo.h:12-16 — 0 detect, 1 obb, 2 classify, 3 segment (obb models do not load here).
+// engine/yolo.h:12-16 — 0 detect, 1 obb, 2 classify, 3 segment.
 int yolo_task(void* h);
 // engine/yolo.h:17-18 — calibrated GPU latency (ms) of one batch-B graph launch.
 float yolo_exec_ms(void* h, int B);
@@ -47,8 +47,9 @@ void yolo_preprocess_cls(void* h, const unsigned char* dev_bgr, int height, int 
 int yolo_get_cls(void* h, int slot, int* ids, float* probs, int k);
 // engine/yolo.h:36-38
 void yolo_slot_geom(void* h, int slot, float* scale, int* top, int* left);
-// engine/yolo.h:39-41 — oriented boxes.  No obb model loads in this engine (yolo_create
-// fails on DECODEOBB graphs with a clear error), so this always returns 0.
+// engine/yolo.h:39-41 — oriented boxes of a slot (obb handles): centre / size in original
+// image coordinates, angle in radians, no clipping; 0 for other handles (and yolo_get
+// returns 0 on obb handles).
 int yolo_get_obb(void* h, int slot, YoloObbDet* out, int cap);
 // engine/yolo.h:42-43 — proto resolution (0/0 for detect models).
 void yolo_mask_dim(void* h, int* ph, int* pw);

@@ -62,12 +62,12 @@ class Graph:
         return op[3] if op[0] == "ADD" else op[2]
 
     def levels(self):
-        """[(box tensor, cls tensor, coef tensor or None, stride)] in graph order."""
+        """[(box tensor, cls tensor, coef / angle tensor or None, stride)] in graph order."""
         out = []
         for op in self.ops:
             if op[0] == "DECODE":
                 out.append((op[1], op[2], None, op[3]))
-            elif op[0] == "DECODESEG":
+            elif op[0] in ("DECODESEG", "DECODEOBB"):   # third view: coefs / angle
                 out.append((op[1], op[2], op[3], op[4]))
         return out
 
@@ -200,6 +200,12 @@ def oracle_postproc():
         for n in ("oref_exp", "oref_sigmoid"):
             getattr(lib, n).restype = C.c_float
             getattr(lib, n).argtypes = [C.c_float]
+        lib.oref_decode_obb_level.restype = C.c_int
+        lib.oref_decode_obb_level.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                              C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                              C.c_int, C.c_int, C.c_float, C.c_int, C.c_void_p]
+        lib.oref_nms_obb.restype = C.c_int
+        lib.oref_nms_obb.argtypes = [C.c_void_p, C.c_int, C.c_float, C.c_int, C.c_void_p]
         lib.oref_preprocess_cls.restype = None
         lib.oref_preprocess_cls.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                             C.c_void_p]
@@ -230,6 +236,30 @@ def letterbox(bgr: np.ndarray, S: int) -> np.ndarray:
     out = np.zeros((S, S, 3), np.uint16)
     lib.oref_letterbox(_p(bgr), bgr.shape[0], bgr.shape[1], S, _p(out))
     return out.view(np.float16)
+
+
+def decode_obb(levels, nc: int, conf: float = 0.25):
+    """levels: [(box fp16 [H,W,64], cls fp16 [H,W,>=nc], angle fp16 [H,W,>=1], stride)] of
+    one image.  Returns [n, 8] float32 (cx cy w h score cls theta anchor), anchor order."""
+    lib = oracle_postproc()
+    recs, abase = [], 0
+    for box, cls, ang, st in levels:
+        box, cls, ang = (np.ascontiguousarray(t, np.float16) for t in (box, cls, ang))
+        H, W = box.shape[:2]
+        out = np.zeros((H * W, 8), np.float32)
+        n = lib.oref_decode_obb_level(_p(box), box.shape[2], _p(cls), cls.shape[2], _p(ang),
+                                      ang.shape[2], H, W, 0, nc, st, conf, abase, _p(out))
+        recs.append(out[:n])
+        abase += H * W
+    return np.concatenate(recs) if recs else np.zeros((0, 8), np.float32)
+
+
+def nms_obb(recs: np.ndarray, iou: float, max_out: int = 300) -> np.ndarray:
+    lib = oracle_postproc()
+    recs = np.ascontiguousarray(recs, np.float32)
+    out = np.zeros((max(len(recs), 1), 8), np.float32)
+    m = lib.oref_nms_obb(_p(recs), len(recs), iou, max_out, _p(out))
+    return out[:m]
 
 
 def decode(levels, nc: int, conf: float = 0.25):

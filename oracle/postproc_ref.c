@@ -4,6 +4,12 @@
  * checker; never by the engine.  Plain C, single thread, straight loops in the order the
  * reference kernels define:
  *   oref_letterbox  engine/engine.cu:968-998 (k_preprocess) + 1704-1713 (host geometry)
+ *   oref_decode_obb_level / oref_nms_obb  engine/engine.cu:908-960 (k_decode_obb) and
+ *                   1160-1252 (probiou, k_nms_obb): first-max class, sigmoid score >= conf,
+ *                   DFL sides, theta = (sigmoid(a) - 0.25) * pi, centre offset rotated by
+ *                   theta; NMS in score order (ties: anchor asc), candidate j dropped when
+ *                   any earlier candidate of its class (dropped or not) has probiou >= thr
+ *                   with it (ultralytics fast-NMS), every candidate considered
  *   oref_preprocess_cls  engine/engine.cu:1000-1046 (k_preprocess_cls + clsGeom): shortest
  *                   edge to S (long edge S*long/short truncated), centre crop with
  *                   round-half-even offsets, per-axis triangle filter of support
@@ -125,6 +131,84 @@ int oref_decode_level(const uint16_t* box, int bstride, const uint16_t* cls, int
       n++;
     }
   return n;
+}
+
+/* out: n x 8 records (cx cy w h score cls theta anchor) in anchor order */
+int oref_decode_obb_level(const uint16_t* box, int bstride, const uint16_t* cls, int cstride,
+                          const uint16_t* ang, int astride, int H, int W, int img, int nc,
+                          int stride, float conf, int abase, float* out) {
+  OView bv = {box, H, W, bstride}, cv = {cls, H, W, cstride}, av = {ang, H, W, astride};
+  int n = 0;
+  for (int y = 0; y < H; y++)
+    for (int x = 0; x < W; x++) {
+      const uint16_t* cp = opix(&cv, img, y, x);
+      float best = -INFINITY;
+      int bc = 0;
+      for (int c = 0; c < nc; c++) {
+        float f = dm_h2f(cp[c]);
+        if (f > best) { best = f; bc = c; }
+      }
+      float score = dm_sigmoid(best);
+      if (!(score >= conf)) continue;
+      const uint16_t* bp = opix(&bv, img, y, x);
+      float d[4];
+      for (int s = 0; s < 4; s++) {
+        float l[16];
+        for (int i = 0; i < 16; i++) l[i] = dm_h2f(bp[s * 16 + i]);
+        d[s] = dm_dfl16(l);
+      }
+      float th = DM_MUL(DM_SUB(dm_sigmoid(dm_h2f(opix(&av, img, y, x)[0])), 0.25f), 3.14159265358979f);
+      float sn, cs;
+      dm_sincos(th, &sn, &cs);
+      float xf = DM_MUL(DM_SUB(d[2], d[0]), 0.5f), yf = DM_MUL(DM_SUB(d[3], d[1]), 0.5f);
+      float st = (float)stride;
+      float* o = out + (size_t)n * 8;
+      o[0] = DM_MUL(DM_SUB(DM_ADD(DM_ADD((float)x, 0.5f), DM_MUL(xf, cs)), DM_MUL(yf, sn)), st);
+      o[1] = DM_MUL(DM_ADD(DM_ADD(DM_ADD((float)y, 0.5f), DM_MUL(xf, sn)), DM_MUL(yf, cs)), st);
+      o[2] = DM_MUL(DM_ADD(d[0], d[2]), st);
+      o[3] = DM_MUL(DM_ADD(d[1], d[3]), st);
+      o[4] = score;
+      o[5] = (float)bc;
+      o[6] = th;
+      o[7] = (float)(abase + y * W + x);
+      n++;
+    }
+  return n;
+}
+
+static const float* g_obb_recs;
+static int cmp_obb(const void* a, const void* b) {
+  const float* ra = g_obb_recs + (size_t)(*(const int*)a) * 8;
+  const float* rb = g_obb_recs + (size_t)(*(const int*)b) * 8;
+  if (ra[4] != rb[4]) return ra[4] > rb[4] ? -1 : 1;
+  return ra[7] < rb[7] ? -1 : ra[7] > rb[7];
+}
+
+/* recs: n x 8 (anchor order); out: up to max_out x 8 survivors in score order */
+int oref_nms_obb(const float* recs, int n, float thr, int max_out, float* out) {
+  int* order = (int*)malloc(sizeof(int) * (n > 0 ? n : 1));
+  float* cov = (float*)malloc(sizeof(float) * 3 * (n > 0 ? n : 1));
+  for (int i = 0; i < n; i++) order[i] = i;
+  g_obb_recs = recs;
+  qsort(order, n, sizeof(int), cmp_obb);
+  for (int i = 0; i < n; i++) {
+    const float* r = recs + (size_t)order[i] * 8;
+    dm_obb_cov(r[2], r[3], r[6], cov + 3 * i);
+  }
+  int m = 0;
+  for (int j = 0; j < n && m < max_out; j++) {
+    const float* b = recs + (size_t)order[j] * 8;
+    int dead = 0;
+    for (int i = 0; i < j && !dead; i++) {
+      const float* a = recs + (size_t)order[i] * 8;
+      if (a[5] != b[5]) continue;
+      if (dm_probiou(a[0], a[1], cov + 3 * i, b[0], b[1], cov + 3 * j) >= thr) dead = 1;
+    }
+    if (!dead) memcpy(out + (size_t)(m++) * 8, b, 8 * sizeof(float));
+  }
+  free(order);
+  free(cov);
+  return m;
 }
 
 static const float* g_sort_recs;

@@ -31,7 +31,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 CASES = [("yolo11n", 64), ("yolov8n", 64), ("yolo11n-seg", 64), ("yolo11n", 160),
-         ("yolo11n-cls", 224)]
+         ("yolo11n-cls", 224), ("yolo11n-obb", 128)]
 
 
 def sha256(path):

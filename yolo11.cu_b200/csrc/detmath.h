@@ -153,3 +153,109 @@ DM_HD float dm_area(float x1, float y1, float x2, float y2) {
 
 // Logit threshold equivalent of sigmoid(x) >= conf is NOT used: the gate is the sigmoid
 // itself (score = dm_sigmoid(best) >= conf), so host and device agree bit for bit.
+
+// ---------------- oriented boxes ----------------
+#if defined(__CUDA_ARCH__)
+#define DM_SQRT(a) __fsqrt_rn(a)
+#else
+#define DM_SQRT(a) sqrtf(a)
+#endif
+
+// sin and cos of x (|x| < 2^20): Cody-Waite reduction x = k*pi/2 + r, |r| <= pi/4 (pi/2 split
+// into a 12-bit high part and a low correction), Taylor polynomials of sin r (to r^13) and
+// cos r (to r^14) by Horner with fmaf (truncation < 2^-30 on |r| <= pi/4), then the quadrant
+// k mod 4 selects and signs the pair.
+DM_HD void dm_sincos(float x, float* s, float* c) {
+  const float two_over_pi = 0.636619772367581343f;
+  const float pio2_hi = 1.5703125f;                 // low 12 bits zero: k * hi is exact
+  const float pio2_lo = 4.83826792333275079e-4f;    // pi/2 - pio2_hi
+  float t = DM_MUL(x, two_over_pi);
+  int k = (int)(t + (t >= 0.f ? 0.5f : -0.5f));
+  float kf = (float)k;
+  float r = DM_FMA(-kf, pio2_hi, x);
+  r = DM_FMA(-kf, pio2_lo, r);
+  float r2 = DM_MUL(r, r);
+  float ps = 1.60590438368216146e-10f;               // 1/13!
+  ps = DM_FMA(ps, r2, -2.50521083854417188e-8f);     // -1/11!
+  ps = DM_FMA(ps, r2, 2.75573192239858907e-6f);      // 1/9!
+  ps = DM_FMA(ps, r2, -1.98412698412698413e-4f);     // -1/7!
+  ps = DM_FMA(ps, r2, 8.33333333333333333e-3f);      // 1/5!
+  ps = DM_FMA(ps, r2, -1.66666666666666667e-1f);     // -1/3!
+  float sr = DM_FMA(DM_MUL(ps, r2), r, r);
+  float pc = -1.14707455977297247e-11f;              // -1/14!
+  pc = DM_FMA(pc, r2, 2.08767569878680990e-9f);      // 1/12!
+  pc = DM_FMA(pc, r2, -2.75573192239858907e-7f);     // -1/10!
+  pc = DM_FMA(pc, r2, 2.48015873015873016e-5f);      // 1/8!
+  pc = DM_FMA(pc, r2, -1.38888888888888889e-3f);     // -1/6!
+  pc = DM_FMA(pc, r2, 4.16666666666666667e-2f);      // 1/4!
+  pc = DM_FMA(pc, r2, -0.5f);                        // -1/2!
+  float cr = DM_FMA(pc, r2, 1.0f);
+  switch (k & 3) {
+    case 0: *s = sr; *c = cr; break;
+    case 1: *s = cr; *c = -sr; break;
+    case 2: *s = -sr; *c = -cr; break;
+    default: *s = -cr; *c = sr; break;
+  }
+}
+
+// natural log of x > 0 (normal range): x = m * 2^e with m in [sqrt(1/2), sqrt(2)),
+// log m = 2 atanh(s), s = (m - 1) / (m + 1), |s| < 0.1716, by the odd series to s^15
+// (truncation < 2^-40); log x = e * ln2 (split hi / lo) + log m.  Returns -inf for 0 and NaN
+// for negative or NaN input; denormals are scaled up first.
+DM_HD float dm_log(float x) {
+  if (!(x > 0.f)) return x == 0.f ? dm_bits2f(0xff800000u) : dm_bits2f(0x7fc00000u);
+  if (x == dm_bits2f(0x7f800000u)) return x;
+  int e = 0;
+  if (x < 1.17549435e-38f) { x = DM_MUL(x, 16777216.f); e = -24; }   // 2^24
+  uint32_t u = dm_f2bits(x);
+  e += (int)((u >> 23) & 0xff) - 127;
+  float m = dm_bits2f((u & 0x7fffffu) | 0x3f800000u);   // [1, 2)
+  if (m > 1.41421356f) { m = DM_MUL(m, 0.5f); e += 1; }
+  float s = DM_DIV(DM_SUB(m, 1.f), DM_ADD(m, 1.f));
+  float s2 = DM_MUL(s, s);
+  float p = 6.66666666666666667e-2f;                  // 1/15
+  p = DM_FMA(p, s2, 7.69230769230769231e-2f);         // 1/13
+  p = DM_FMA(p, s2, 9.09090909090909091e-2f);         // 1/11
+  p = DM_FMA(p, s2, 1.11111111111111111e-1f);         // 1/9
+  p = DM_FMA(p, s2, 1.42857142857142857e-1f);         // 1/7
+  p = DM_FMA(p, s2, 2.0e-1f);                         // 1/5
+  p = DM_FMA(p, s2, 3.33333333333333333e-1f);         // 1/3
+  float lm = DM_MUL(2.f, DM_FMA(DM_MUL(p, s2), s, s));
+  const float ln2_hi = 0.693145751953125f, ln2_lo = 1.42860682030941723e-6f;
+  float ef = (float)e;
+  return DM_FMA(ef, ln2_hi, DM_FMA(ef, ln2_lo, lm));
+}
+
+// Covariance (a, b, c) of the Gaussian of an oriented box (w, h, theta): a = w^2/12,
+// b = h^2/12 rotated by theta (ultralytics _get_covariance_matrix).
+DM_HD void dm_obb_cov(float w, float h, float th, float* cov) {
+  float a = DM_DIV(DM_MUL(w, w), 12.f), b = DM_DIV(DM_MUL(h, h), 12.f);
+  float s, c;
+  dm_sincos(th, &s, &c);
+  float c2 = DM_MUL(c, c), s2 = DM_MUL(s, s);
+  cov[0] = DM_ADD(DM_MUL(a, c2), DM_MUL(b, s2));
+  cov[1] = DM_ADD(DM_MUL(a, s2), DM_MUL(b, c2));
+  cov[2] = DM_MUL(DM_MUL(DM_SUB(a, b), c), s);
+}
+
+// probiou of two oriented boxes from their centres and covariances (ultralytics
+// batch_probiou: Bhattacharyya distance of the two Gaussians, clamped to [eps, 100], then
+// 1 - sqrt(1 - exp(-bd) + eps); eps = 1e-7 in the same three places).
+DM_HD float dm_probiou(float x1, float y1, const float* c1, float x2, float y2, const float* c2) {
+  const float eps = 1e-7f;
+  float dx = DM_SUB(x1, x2), dy = DM_SUB(y1, y2);
+  float sa = DM_ADD(c1[0], c2[0]), sb = DM_ADD(c1[1], c2[1]), sc = DM_ADD(c1[2], c2[2]);
+  float disc = DM_SUB(DM_MUL(sa, sb), DM_MUL(sc, sc));
+  float den = DM_ADD(disc, eps);
+  float t1 = DM_DIV(DM_MUL(0.25f, DM_ADD(DM_MUL(DM_MUL(sa, dy), dy), DM_MUL(DM_MUL(sb, dx), dx))), den);
+  float t2 = DM_DIV(DM_MUL(0.5f, DM_MUL(DM_MUL(sc, -dx), dy)), den);
+  float d1 = DM_SUB(DM_MUL(c1[0], c1[1]), DM_MUL(c1[2], c1[2]));
+  float d2 = DM_SUB(DM_MUL(c2[0], c2[1]), DM_MUL(c2[2], c2[2]));
+  d1 = d1 > 0.f ? d1 : 0.f;
+  d2 = d2 > 0.f ? d2 : 0.f;
+  float t3 = DM_MUL(0.5f, dm_log(DM_ADD(DM_DIV(disc, DM_ADD(DM_MUL(4.f, DM_SQRT(DM_MUL(d1, d2))), eps)), eps)));
+  float bd = DM_ADD(DM_ADD(t1, t2), t3);
+  bd = bd > eps ? bd : eps;
+  bd = bd < 100.f ? bd : 100.f;
+  return DM_SUB(1.f, DM_SQRT(DM_ADD(DM_SUB(1.f, dm_exp(-bd)), eps)));
+}

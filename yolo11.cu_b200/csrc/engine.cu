@@ -113,6 +113,8 @@ struct Engine {
   std::vector<SlotGeom> slots;
   bool seg() const { return task == "segment"; }
   bool cls() const { return task == "classify"; }
+  bool obb() const { return task == "obb"; }
+  int rec() const { return obb() ? 7 : 6; }   // floats per survivor record
 
   ~Engine() { release(); }
 
@@ -241,8 +243,8 @@ void Engine::parse(const std::string& dir) {
 }
 
 void Engine::validate(const std::string& dir) {
-  if (task != "detect" && task != "segment" && task != "classify")
-    throw Error("task '" + task + "' is not supported by this engine (detect, segment, classify)");
+  if (task != "detect" && task != "segment" && task != "classify" && task != "obb")
+    throw Error("task '" + task + "' is not supported by this engine");
   const Ten& t0 = tens[0];
   if (t0.coff != 0 || t0.C != 3 || bufs[t0.buf].C != 3 || bufs[t0.buf].H != bufs[t0.buf].W)
     throw Error("tensor 0 must be a standalone S x S x 3 input");
@@ -270,8 +272,17 @@ void Engine::validate(const std::string& dir) {
         if (op.kind == SOFTMAX) probsTen = op.out;
         break;
       }
-      case DECODEOBB:
-        throw Error("DECODEOBB (obb) is not supported");
+      case DECODEOBB: {   // a = box view, b = cls view, out = angle view (channel 0 real)
+        if (!obb()) throw Error("DECODEOBB needs task=obb");
+        const Ten &c = tens[op.b], &an = tens[op.out];
+        if (c.C % 8 || c.C < nc || an.C % 8 || an.C < 1)
+          throw Error("DECODEOBB needs 8-aligned cls / angle views covering nc");
+        if (tens[op.a].C != 64) throw Error("DECODEOBB box view must have 64 channels");
+        levels.push_back({op.a, op.b, op.out, op.stride});
+        const Buf& bb = bufs[tens[op.a].buf];
+        A += bb.H * bb.W;
+        break;
+      }
       case DECODE: case DECODESEG: {
         const Ten& c = tens[op.b];
         if (c.C % 8 || c.C < nc) throw Error("DECODE needs an 8-aligned cls view covering nc");
@@ -383,9 +394,9 @@ void Engine::allocate(const std::string& dir) {
   CKE(cudaMemcpy(dweights, wf.data(), wf.size(), cudaMemcpyHostToDevice));
   CKE(cudaMalloc(&dbias, std::max<size_t>(bf.size(), 16)));
   CKE(cudaMemcpy(dbias, bf.data(), bf.size(), cudaMemcpyHostToDevice));
-  post.ws_bytes = yk_post_workspace_bytes(maxB, A);
+  post.ws_bytes = obb() ? yk_obb_workspace_bytes(maxB, A) : yk_post_workspace_bytes(maxB, A);
   CKE(cudaMalloc(&post.ws, post.ws_bytes));
-  CKE(cudaMalloc(&post.outdets, (size_t)maxB * opt.max_det * 6 * sizeof(float)));
+  CKE(cudaMalloc(&post.outdets, (size_t)maxB * opt.max_det * rec() * sizeof(float)));
   CKE(cudaMalloc(&post.outidx, (size_t)maxB * opt.max_det * sizeof(int)));
   CKE(cudaMalloc(&post.outcnt, maxB * sizeof(int)));
   CKE(cudaMalloc(&post.rawcnt, maxB * sizeof(int)));
@@ -395,7 +406,7 @@ void Engine::allocate(const std::string& dir) {
     const Buf& pb = bufs[tens[protoTen].buf];
     CKE(cudaMalloc(&dmasks, (size_t)maxB * opt.max_det * pb.H * pb.W));
   }
-  CKE(cudaMallocHost(&h_out, (size_t)maxB * opt.max_det * 6 * sizeof(float)));
+  CKE(cudaMallocHost(&h_out, (size_t)maxB * opt.max_det * rec() * sizeof(float)));
   CKE(cudaMallocHost(&h_cnt, maxB * sizeof(int)));
   CKE(cudaMallocHost(&h_raw, maxB * sizeof(int)));
   if (cls()) CKE(cudaMallocHost(&h_probs, (size_t)maxB * nc * sizeof(__half)));
@@ -432,7 +443,7 @@ void Engine::plan() {
       op.y3 = raw[i + 2].out;
       i += 2;
     }
-    if (op.kind == DECODE || op.kind == DECODESEG || op.kind == MASKS) continue;
+    if (op.kind == DECODE || op.kind == DECODESEG || op.kind == DECODEOBB || op.kind == MASKS) continue;
     ops.push_back(op);
   }
 }
@@ -525,8 +536,14 @@ void Engine::run_post(int B) {
     else memset(&lv[i].coef, 0, sizeof(YkView));
     lv[i].stride = levels[i].stride;
   }
-  CKY(yk_decode(lv.data(), (int)lv.size(), B, nc, opt.conf, &post, (yk_stream_t)st));
-  CKY(yk_nms(B, A, opt.iou, opt.max_det, &post, (yk_stream_t)st));
+  if (obb()) {
+    CKY(yk_decode_obb(lv.data(), (int)lv.size(), B, nc, opt.conf, post.ws, (yk_stream_t)st));
+    CKY(yk_nms_obb(B, A, opt.iou, opt.max_det, post.ws, post.outdets, post.outcnt, post.rawcnt,
+                   (yk_stream_t)st));
+  } else {
+    CKY(yk_decode(lv.data(), (int)lv.size(), B, nc, opt.conf, &post, (yk_stream_t)st));
+    CKY(yk_nms(B, A, opt.iou, opt.max_det, &post, (yk_stream_t)st));
+  }
   if (seg()) {
     YkView pr = view(protoTen, B);
     CKY(yk_masks(lv.data(), (int)lv.size(), &pr, S, S, opt.max_det, &post, dmasks,
@@ -534,7 +551,7 @@ void Engine::run_post(int B) {
   }
   CKE(cudaMemcpyAsync(h_raw, post.rawcnt, B * sizeof(int), cudaMemcpyDeviceToHost, st));
   CKE(cudaMemcpyAsync(h_cnt, post.outcnt, B * sizeof(int), cudaMemcpyDeviceToHost, st));
-  CKE(cudaMemcpyAsync(h_out, post.outdets, (size_t)B * opt.max_det * 6 * sizeof(float),
+  CKE(cudaMemcpyAsync(h_out, post.outdets, (size_t)B * opt.max_det * rec() * sizeof(float),
                       cudaMemcpyDeviceToHost, st));
 }
 
@@ -795,7 +812,7 @@ void yolo_destroy(void* h) { delete as_engine(h); }
 
 int yolo_task(void* h) {
   if (!h) return 0;
-  return as_engine(h)->seg() ? 3 : as_engine(h)->cls() ? 2 : 0;
+  return as_engine(h)->seg() ? 3 : as_engine(h)->cls() ? 2 : as_engine(h)->obb() ? 1 : 0;
 }
 
 float yolo_exec_ms(void* h, int B) {
@@ -855,11 +872,24 @@ int yolo_get_cls(void* h, int slot, int* ids, float* probs, int k) {
   return k;
 }
 
-// Oriented boxes: the engine loads no obb model (yolo_create rejects DECODEOBB graphs), so
-// there is never anything to return.
+// Oriented boxes of a slot in original-image coordinates: centre and size mapped back
+// through the letterbox, angle unchanged, no clipping (engine/engine.cu:1783-1794).
 int yolo_get_obb(void* h, int slot, YoloObbDet* out, int cap) {
-  (void)h; (void)slot; (void)out; (void)cap;
-  return 0;
+  Engine* e = as_engine(h);
+  if (!e || !e->obb() || slot < 0 || slot >= e->maxB || (!out && cap > 0)) return 0;
+  const SlotGeom& g = e->slots[slot];
+  const int n = std::min(e->h_cnt[slot], cap);
+  for (int i = 0; i < n; i++) {
+    const float* d = e->h_out + ((size_t)slot * e->opt.max_det + i) * 7;
+    out[i].x = (d[0] - g.left) / g.scale;
+    out[i].y = (d[1] - g.top) / g.scale;
+    out[i].w = d[2] / g.scale;
+    out[i].h = d[3] / g.scale;
+    out[i].angle = d[6];
+    out[i].score = d[4];
+    out[i].cls = (int)d[5];
+  }
+  return n;
 }
 
 void yolo_run_async(void* h, int B) {
@@ -890,7 +920,7 @@ void yolo_run(void* h, int B) {
 
 int yolo_get(void* h, int slot, YoloDet* out, int cap) {
   Engine* e = as_engine(h);
-  if (!e || slot < 0 || slot >= e->maxB || (!out && cap > 0)) return 0;
+  if (!e || e->obb() || slot < 0 || slot >= e->maxB || (!out && cap > 0)) return 0;
   const SlotGeom& g = e->slots[slot];
   const int n = std::min(e->h_cnt[slot], cap);
   for (int i = 0; i < n; i++) {
@@ -954,11 +984,12 @@ int yolo_run_op(void* h, int op_index, int B) {
       throw Error("yolo_run_op: bad arguments");
     DeviceScope ds(e->device);
     const Op& op = e->raw[op_index];
-    if (op.kind == DECODE || op.kind == DECODESEG || op.kind == MASKS) {
+    if (op.kind == DECODE || op.kind == DECODESEG || op.kind == DECODEOBB || op.kind == MASKS) {
       // the whole post chain runs once, at the last head op of the graph
       bool last = true;
       for (size_t j = op_index + 1; j < e->raw.size(); j++)
-        if (e->raw[j].kind == DECODE || e->raw[j].kind == DECODESEG || e->raw[j].kind == MASKS)
+        if (e->raw[j].kind == DECODE || e->raw[j].kind == DECODESEG ||
+            e->raw[j].kind == DECODEOBB || e->raw[j].kind == MASKS)
           last = false;
       if (last) e->run_post(B);
       CKE(cudaStreamSynchronize(e->st));

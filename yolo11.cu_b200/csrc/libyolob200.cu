@@ -8,4 +8,5 @@
 #include "attn.cu"
 #include "post.cu"
 #include "cls.cu"
+#include "obb.cu"
 #include "engine.cu"

@@ -222,6 +222,16 @@ int main(int argc, char** argv) {
       yolo_destroy(h);
       return 0;
     }
+    if (yolo_task(h) == 1) {   // oriented boxes, original image coordinates
+      std::vector<YoloObbDet> d(10000);
+      const int n = yolo_get_obb(h, 0, d.data(), (int)d.size());
+      printf("kept=%d (candidates %d)\n", n, yolo_raw_count(h, 0));
+      for (int i = 0; i < n; i++)
+        printf("cls=%2d score=%.4f obb=(%.1f, %.1f, %.1f, %.1f, %.3f rad)\n", d[i].cls, d[i].score,
+               d[i].x, d[i].y, d[i].w, d[i].h, d[i].angle);
+      yolo_destroy(h);
+      return 0;
+    }
     if (batch > 1) {
       printf("batch=%d per-image kept:", batch);
       std::vector<YoloDet> d(100000);

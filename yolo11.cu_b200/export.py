@@ -329,6 +329,7 @@ def build_graph(model: "ynn.DetectionModel", S: int) -> GraphBuilder:
         return g
     assert torch.allclose(det.dfl.conv.weight.view(-1), torch.arange(16, dtype=torch.float32))
     seg = isinstance(det, ynn.Segment)
+    obb = isinstance(det, ynn.OBB)
     feats = [outs[j] for j in det.f]
     strides = [int(s) for s in det.stride]
     g.det_ref, g.seg_ref = [], None
@@ -344,7 +345,12 @@ def build_graph(model: "ynn.DetectionModel", S: int) -> GraphBuilder:
         b = _chain(g, f, det.cv2[i])
         c = _chain(g, f, det.cv3[i][:2], pad8=True)
         c = g.conv_pad8(c, det.cv3[i][2], ncpad)
-        if seg:
+        if obb:   # angle branch: 3x3, 3x3, then the 1-channel final zero-padded to 8
+            a = _chain(g, f, det.cv4[i][:2])
+            a = g.conv_pad8(a, det.cv4[i][2], (det.ne + 7) // 8 * 8)
+            g.ops.append(("DECODEOBB", b, c, a, st))
+            g.det_ref.append((b, c, a))
+        elif seg:
             mc = _chain(g, f, det.cv4[i])
             g.ops.append(("DECODESEG", b, c, mc, st))
             g.seg_ref["cv4"].append(mc)
@@ -392,7 +398,8 @@ def export_model(name: str, out_dir: str, imgsz: int = 640, frame_hw=(1080, 810)
     os.makedirs(out_dir, exist_ok=True)
     head = model.model[-1]
     task = ("segment" if isinstance(head, ynn.Segment) else
-            "classify" if isinstance(head, ynn.Classify) else "detect")
+            "classify" if isinstance(head, ynn.Classify) else
+            "obb" if isinstance(head, ynn.OBB) else "detect")
     nc = head.linear.out_features if task == "classify" else head.nc
     with open(os.path.join(out_dir, "model.graph"), "w") as f:
         f.write(g.graph_text(task, nc, imgsz))
@@ -411,9 +418,9 @@ def export_model(name: str, out_dir: str, imgsz: int = 640, frame_hw=(1080, 810)
 
 
 def ensure_model_dir(name: str, root: str, imgsz: int = 640, frame_hw=(1080, 810)) -> str:
-    """Return ``root/<name>[-S]`` (S omitted at the model's default size: 640, or 224 for
-    classify), exporting it first if ``model.graph`` is missing."""
-    default = 224 if name.endswith("-cls") else 640
+    """Return ``root/<name>[-S]`` (S omitted at the model's default size: 640, 224 for
+    classify, 1024 for obb), exporting it first if ``model.graph`` is missing."""
+    default = 224 if name.endswith("-cls") else 1024 if name.endswith("-obb") else 640
     d = os.path.join(root, name if imgsz == default else f"{name}-{imgsz}")
     if not os.path.exists(os.path.join(d, "model.graph")):
         export_model(name, d, imgsz, frame_hw)

@@ -35,18 +35,20 @@ import torch.nn.functional as F
 
 __all__ = ["build_model", "MODEL_SCALES", "Conv", "DWConv", "Concat", "Bottleneck", "C2f",
            "C3", "C3k", "C3k2", "SPPF", "Attention", "PSABlock", "C2PSA", "DFL", "Proto",
-           "Detect", "Segment", "Classify", "DetectionModel", "CLS_BIAS"]
+           "Detect", "Segment", "OBB", "Classify", "DetectionModel", "CLS_BIAS"]
 
 # Constant bias of the final cls convs, per model: chosen once (frame 0 at 640) so that about
 # 3 % of the 8400 anchors pass conf 0.25, i.e. NMS sees a few hundred candidates per image.
 CLS_BIAS = {"yolo11n": -3.75, "yolo11s": -6.25, "yolo11m": -6.25, "yolo11l": -2.25,
             "yolo11x": -2.0, "yolov8n": -18.25, "yolov8s": -6.75, "yolov8m": -2.0,
-            "yolo11n-seg": -1.64, "yolo11m-seg": -8.5, "yolov8n-seg": -16.75}
+            "yolo11n-seg": -1.64, "yolo11m-seg": -8.5, "yolov8n-seg": -16.75,
+            "yolo11n-obb": -4.5}   # obb: frame 0 at 1024, ~4 % of 21504 anchors
 CLS_BIAS_DEFAULT = -3.0
 # Squared Kaiming gain of the Conv+BN weights, per model: 2 (He) unless the random net's
 # activations then grow or shrink geometrically with depth; chosen once so the deepest layer's
 # std on frame 0 stays O(1) (fp16 storage needs |x| far below 65504).
-KAIMING_GAIN2 = {"yolo11l": 1.4, "yolo11x": 1.4, "yolov8n": 2.4, "yolov8n-seg": 2.2}
+KAIMING_GAIN2 = {"yolo11l": 1.4, "yolo11x": 1.4, "yolov8n": 2.4, "yolov8n-seg": 2.2,
+                 "yolo11n-obb": 1.75}
 
 # (depth, width, max_channels) per published scale
 MODEL_SCALES = {
@@ -295,6 +297,37 @@ class Detect(nn.Module):
         return self._decode(x), x
 
 
+class OBB(Detect):
+    """Oriented-box head: Detect plus an angle branch (ne = 1 channel per anchor).
+
+    theta = (sigmoid(angle logit) - 0.25) * pi; the DFL side distances (l, t, r, b) give the
+    box size (l + r, t + b) along theta and the centre offset ((r - l) / 2, (b - t) / 2)
+    rotated by theta from the anchor point; all times the level stride."""
+
+    def __init__(self, nc=15, ne=1, ch=(), legacy=False):
+        super().__init__(nc, ch, legacy)
+        self.ne = ne
+        c4 = max(ch[0] // 4, self.ne)
+        self.cv4 = nn.ModuleList(nn.Sequential(Conv(x, c4, 3), Conv(c4, c4, 3),
+                                               nn.Conv2d(c4, self.ne, 1)) for x in ch)
+
+    def forward(self, x):
+        bs = x[0].shape[0]
+        ang = torch.cat([self.cv4[i](x[i]).view(bs, self.ne, -1) for i in range(self.nl)], 2)
+        ang = (ang.sigmoid() - 0.25) * math.pi
+        lv = self._levels(x)
+        shape = lv[0].shape
+        x_cat = torch.cat([xi.view(shape[0], self.no, -1) for xi in lv], 2)
+        anchors, strides = (t.transpose(0, 1) for t in _make_anchors(lv, self.stride))
+        box, cls = x_cat.split((self.reg_max * 4, self.nc), 1)
+        lt, rb = self.dfl(box).chunk(2, 1)
+        cos, sin = torch.cos(ang), torch.sin(ang)
+        xf, yf = ((rb - lt) / 2).split(1, dim=1)
+        xy = torch.cat([xf * cos - yf * sin, xf * sin + yf * cos], 1) + anchors.unsqueeze(0)
+        dbox = torch.cat([xy, lt + rb], 1) * strides
+        return torch.cat([dbox, cls.sigmoid(), ang], 1), (lv, ang)
+
+
 class Segment(Detect):
     def __init__(self, nc=80, nm=32, npr=256, ch=(), legacy=False):
         super().__init__(nc, ch, legacy)
@@ -354,16 +387,18 @@ _YOLOV8 = [
 class DetectionModel(nn.Module):
     def __init__(self, name: str, nc: int = 80, imgsz: int = 640):
         super().__init__()
-        m = re.fullmatch(r"(yolo11|yolov8)([nsmlx])(-seg|-cls)?", name)
+        m = re.fullmatch(r"(yolo11|yolov8)([nsmlx])(-seg|-cls|-obb)?", name)
         if not m:
             raise ValueError(f"unknown model name {name!r} (expected yolo11n, yolov8m-seg, ...)")
         family, scale = m.group(1), m.group(2)
-        seg, cls = m.group(3) == "-seg", m.group(3) == "-cls"
+        seg, cls, obb = m.group(3) == "-seg", m.group(3) == "-cls", m.group(3) == "-obb"
         depth, width, max_ch = MODEL_SCALES[family][scale]
         self.family, self.scale_name = family, scale
-        self.task = "segment" if seg else "classify" if cls else "detect"
+        self.task = "segment" if seg else "classify" if cls else "obb" if obb else "detect"
         if cls and nc == 80:
             nc = 1000      # ImageNet head
+        if obb and nc == 80:
+            nc = 15        # DOTA
         self.names = {i: f"class{i}" for i in range(nc)}
         self.args = {"imgsz": imgsz}
         layers, ch, save_ch = [], [3], []
@@ -416,6 +451,8 @@ class DetectionModel(nn.Module):
         if seg:
             npr = _ceil8(min(256, max_ch) * width)
             head = Segment(nc, 32, npr, hch, legacy=legacy)
+        elif obb:
+            head = OBB(nc, 1, hch, legacy=legacy)
         else:
             head = Detect(nc, hch, legacy=legacy)
         head.f, head.i = heads_from, len(layers)
@@ -444,7 +481,7 @@ def _init_weights(model: DetectionModel, seed: int, cls_bias: float, gain2: floa
     for i in range(getattr(head, "nl", 0)):
         finals[id(head.cv2[i][-1])] = "box"
         finals[id(head.cv3[i][-1])] = "cls"
-        if isinstance(head, Segment):
+        if isinstance(head, (Segment, OBB)):
             finals[id(head.cv4[i][-1])] = "coef"
 
     def normal(shape, std):

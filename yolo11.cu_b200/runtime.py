@@ -65,6 +65,11 @@ _SIGS = {
     "yk_letterbox": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _P(YkView), C.c_int,
                                _P(C.c_float), _P(C.c_int), _P(C.c_int), C.c_void_p]),
     "yk_post_workspace_bytes": (C.c_size_t, [C.c_int, C.c_int]),
+    "yk_obb_workspace_bytes": (C.c_size_t, [C.c_int, C.c_int]),
+    "yk_decode_obb": (C.c_int, [_P(YkLevel), C.c_int, C.c_int, C.c_int, C.c_float, C.c_void_p,
+                                C.c_void_p]),
+    "yk_nms_obb": (C.c_int, [C.c_int, C.c_int, C.c_float, C.c_int, C.c_void_p, C.c_void_p,
+                             C.c_void_p, C.c_void_p, C.c_void_p]),
     "yk_gap": (C.c_int, [_P(YkView), _P(YkView), C.c_void_p]),
     "yk_softmax": (C.c_int, [_P(YkView), _P(YkView), C.c_void_p]),
     "yk_preprocess_cls": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _P(YkView), C.c_int,
@@ -187,6 +192,12 @@ class Engine:
 
     def task(self) -> int:
         return self.lib.yolo_task(self.h)
+
+    def get_obb(self, slot: int, cap: int | None = None):
+        cap = self.max_det if cap is None else cap
+        arr = (YoloObbDet * cap)()
+        n = self.lib.yolo_get_obb(self.h, slot, arr, cap)
+        return [(d.x, d.y, d.w, d.h, d.angle, d.score, d.cls) for d in arr[:n]]
 
     def get_cls(self, slot: int, k: int = 5):
         ids, probs = (C.c_int * k)(), (C.c_float * k)()
