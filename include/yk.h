@@ -160,7 +160,7 @@ int yk_masks(const YkLevel* levels, int nlevels, const YkView* proto, int in_h, 
 // lives in one static 8 MiB device array inside the library instead of a YkPost workspace.
 // Same arguments and results as yk_decode + yk_nms; outputs as in YkPost ([batch][max_out][6],
 // [batch][max_out], [batch], [batch]).  Limit: batch * per-image scratch <= 8 MiB (about
-// 11 images of 8400 anchors at 640, 4 images at 1024); larger requests return YK_EINVAL with
+// 9 images of 8400 anchors at 640, 3 images at 1024); larger requests return YK_EINVAL with
 // the reason in yk_last_cuda_error.  The first call on each device looks up the array's
 // device address (cudaGetSymbolAddress), so make that first call before any stream capture.
 // All calls on a device share the one array and it keeps the last call's contents: calls

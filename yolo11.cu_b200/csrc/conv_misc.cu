@@ -929,10 +929,13 @@ int yk_maxpool5x3(const YkView* x, const YkView* y1, const YkView* y2, const YkV
                       ? 32
                   : (x->C % 64 == 0 && 2 * plane * 64 <= 200 * 1024) ? 64
                   : (x->C % 32 == 0 && 2 * plane * 32 <= 200 * 1024) ? 32 : 0;
-  if (cbk && (long long)x->batch * (x->C / cbk) < (1LL << 31)) {
-    const int ncb = x->C / cbk;
-    const size_t smem = 2 * plane * cbk;
-    auto kern = cbk == 64 ? pool5x3_plane_kernel<64> : pool5x3_plane_kernel<32>;
+  // a handful of planes (small batches): 8-channel planes, 4x-8x more blocks
+  const int cbp = cbk && (long long)x->batch * (x->C / 32) < 148 ? 8 : cbk;
+  if (cbp && (long long)x->batch * (x->C / cbp) < (1LL << 31)) {
+    const int ncb = x->C / cbp;
+    const size_t smem = 2 * plane * cbp;
+    auto kern = cbp == 64 ? pool5x3_plane_kernel<64>
+                : cbp == 32 ? pool5x3_plane_kernel<32> : pool5x3_plane_kernel<8>;
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)

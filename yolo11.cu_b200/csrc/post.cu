@@ -72,9 +72,10 @@ struct DevLevels {
 // more candidates than shared memory holds: anchor[A] u32, box[A] float4, skey[A] u32,
 // cls[A] u32, ord[3][A] u32, surv[A] u8; kept[A][5] f32 (kept boxes past the shared cache).
 struct WsLayout {
-  size_t rec, flag, anch, box, skey, cls, ord, surv, kept, per_img;
-  int A;
+  size_t rec, flag, anch, box, skey, cls, ord, surv, kept, bmask, per_img;
+  int A, bmask_words;
 };
+constexpr int kBitMax = 512;   // classes of 33..kBitMax candidates: bit-mask suppression
 static inline size_t al16(size_t v) { return (v + 15) & ~(size_t)15; }
 static inline WsLayout ws_layout(int A) {
   WsLayout L;
@@ -89,6 +90,9 @@ static inline WsLayout ws_layout(int A) {
   L.ord = o;  o = al16(o + (size_t)A * 12);
   L.surv = o; o = al16(o + (size_t)A);
   L.kept = o; o = al16(o + (size_t)A * 5 * 4);
+  // bit masks of the mid-size classes: up to 16 words per candidate, at most 128 KB
+  L.bmask_words = (int)std::min<size_t>((size_t)A * 16, 32768);
+  L.bmask = o; o = al16(o + (size_t)L.bmask_words * 4);
   L.per_img = o;
   return L;
 }
@@ -178,7 +182,7 @@ __global__ void __launch_bounds__(256) decode_kernel(DevLevels lv, int batch, in
 // Up to kNmsSmemCand candidates live in shared memory, more in the workspace.
 constexpr int kNmsThreads = 1024;
 constexpr int kNmsSmemCand = 4096;
-constexpr int kRankSortMax = 256;
+constexpr int kRankSortMax = 512;
 constexpr int kMaxClasses = 1024;
 constexpr int kKeptSmem = 32;          // kept boxes per class held in shared memory
 constexpr int kHistStride = 33;        // per-warp digit counters, [digit][warp] padded
@@ -297,6 +301,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   extern __shared__ __align__(16) uint8_t nsm[];
   __shared__ int wsum[32];
   __shared__ int segs[kMaxClasses + 1];
+  __shared__ int msegoff[kMaxClasses + 1];
   __shared__ int s_total;
   __shared__ unsigned s_bits[4];        // OR / AND of the score keys, OR / AND of the classes
   __shared__ float kept_s[32][kKeptSmem][5];
@@ -379,18 +384,29 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   const uint32_t* ordS;
   const uint32_t* ordC;
   if (n <= kRankSortMax) {
-    if (tid < n) {
-      const unsigned long long ks = ((unsigned long long)skey[tid] << 20) | (unsigned)tid;
-      const unsigned long long kc = ((unsigned long long)ccls[tid] << 52) | ks;
-      int rs = 0, rc = 0;
-      for (int j = 0; j < n; j++) {
+    // rank sort, four lanes per candidate up to 256 candidates, two up to 512 (each lane
+    // counts its share of the list; the shares are summed by shuffles)
+    const int sh = n <= 256 ? 2 : 1, lanes = 1 << sh;
+    const int me = tid >> sh, part = tid & (lanes - 1);
+    const bool has = me < n;
+    const int mi = has ? me : 0;
+    const unsigned long long ks = ((unsigned long long)skey[mi] << 20) | (unsigned)mi;
+    const unsigned long long kc = ((unsigned long long)ccls[mi] << 52) | ks;
+    int rs = 0, rc = 0;
+    if (has)
+      for (int j = part; j < n; j += lanes) {
         const unsigned long long js = ((unsigned long long)skey[j] << 20) | (unsigned)j;
         const unsigned long long jc = ((unsigned long long)ccls[j] << 52) | js;
         rs += js < ks;
         rc += jc < kc;
       }
-      ord1[rs] = (uint32_t)tid;
-      ord2[rc] = (uint32_t)tid;
+    for (int o = 1; o < lanes; o <<= 1) {
+      rs += __shfl_xor_sync(~0u, rs, o);
+      rc += __shfl_xor_sync(~0u, rc, o);
+    }
+    if (has && part == 0) {
+      ord1[rs] = (uint32_t)me;
+      ord2[rc] = (uint32_t)me;
     }
     __syncthreads();
     ordS = ord1;
@@ -436,12 +452,81 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   if (tid == 0) segs[nseg] = n;
   __syncthreads();
 
-  // 4. greedy suppression per class, one warp per class, 32 candidates per step; the first
-  // kKeptSmem kept boxes of the class live in shared memory, later ones in the workspace
+  // 4. per-class suppression in score order.  Classes of 33..kBitMax candidates whose bit
+  // masks fit the workspace region, with all candidates in shared memory, use bit masks: the whole block builds them (bit j of row
+  // i: dm_iou_gt(i, j) for a later j, the same test as the greedy path), then one warp per
+  // class walks the rows: a row not yet removed is kept and removes its mask.  The other
+  // classes run the greedy loop, one warp per class.  Both are exact greedy NMS, and both
+  // stop a class at max_out kept boxes: its later survivors could never reach the output.
+  int* moff = msegoff;                 // per class: first mask word, or -1 (greedy)
+  if (tid == 0) {
+    int off = 0;
+    for (int sg = 0; sg < nseg; sg++) {
+      const int m = segs[sg + 1] - segs[sg], words = (m + 31) >> 5;
+      // (only with the candidates in shared memory: from the workspace, the pair tests'
+      // loads cost more than the greedy loop saves)
+      const bool bit = in_smem && m > 32 && m <= kBitMax && off + m * words <= L.bmask_words;
+      moff[sg] = bit ? off : -1;
+      if (bit) off += m * words;
+    }
+    moff[nseg] = off;
+  }
+  __syncthreads();
+  uint32_t* bmask = (uint32_t*)(wimg + L.bmask);
+  {
+    // flattened over all mask words of all bit-mask classes
+    const int total = moff[nseg];
+    int sg = 0;
+    for (int t = tid; t < total; t += kNmsThreads) {
+      while (moff[sg] < 0 || (sg + 1 <= nseg && t >= moff[sg] + (segs[sg + 1] - segs[sg]) *
+                                                           ((segs[sg + 1] - segs[sg] + 31) >> 5)))
+        sg++;
+      const int s = segs[sg], m = segs[sg + 1] - s, words = (m + 31) >> 5;
+      const int li = t - moff[sg], i = li / words, w = li - i * words;
+      const float4 bi = box[ordC[s + i]];
+      const float ai = dm_area(bi.x, bi.y, bi.z, bi.w);
+      uint32_t bits = 0;
+      for (int k = 0; k < 32; k++) {
+        const int j = w * 32 + k;
+        if (j <= i || j >= m) continue;
+        const float4 bj = box[ordC[s + j]];
+        if (dm_iou_gt(bi.x, bi.y, bi.z, bi.w, ai, bj.x, bj.y, bj.z, bj.w, iou)) bits |= 1u << k;
+      }
+      bmask[t] = bits;
+    }
+  }
+  __syncthreads();
   for (int sg = warp; sg < nseg; sg += kNmsThreads >> 5) {
     const int s = segs[sg], e = segs[sg + 1];
+    if (moff[sg] >= 0) {
+      const int m = e - s, words = (m + 31) >> 5;
+      const uint32_t* rows = bmask + moff[sg];
+      uint32_t removed = 0;                 // lane w holds word w
+      int nk = 0;
+      for (int i0 = 0; i0 < m; i0 += 8) {
+        uint32_t r8[8];                     // eight rows' words in flight at once
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          r8[u] = i0 + u < m && lane < words ? rows[(size_t)(i0 + u) * words + lane] : 0u;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          const int i = i0 + u;
+          if (i >= m) break;                 // uniform
+          const uint32_t rw = __shfl_sync(~0u, removed, i >> 5);
+          const bool alive = !((rw >> (i & 31)) & 1u) && nk < max_out;
+          if (alive) removed |= r8[u];
+          if (lane == 0) surv[ordC[s + i]] = alive ? 1 : 0;
+          nk += alive;
+        }
+      }
+      continue;
+    }
     int nk = 0;
     for (int c0 = s; c0 < e; c0 += 32) {
+      if (nk >= max_out) {                  // the rest of the class cannot reach the output
+        for (int q = c0 + lane; q < e; q += 32) surv[ordC[q]] = 0;
+        break;
+      }
       const int i = c0 + lane;
       const bool valid = i < e;
       const uint32_t ci = valid ? ordC[i] : 0u;
