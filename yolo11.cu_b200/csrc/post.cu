@@ -483,12 +483,13 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
         sg++;
       const int s = segs[sg], m = segs[sg + 1] - s, words = (m + 31) >> 5;
       const int li = t - moff[sg], i = li / words, w = li - i * words;
+      uint32_t bits = 0;
+      if (w * 32 + 31 <= i) { bmask[t] = 0u; continue; }   // below the diagonal: no later j
       const float4 bi = box[ordC[s + i]];
       const float ai = dm_area(bi.x, bi.y, bi.z, bi.w);
-      uint32_t bits = 0;
-      for (int k = 0; k < 32; k++) {
+      for (int k = max(0, i + 1 - w * 32); k < 32; k++) {
         const int j = w * 32 + k;
-        if (j <= i || j >= m) continue;
+        if (j >= m) break;
         const float4 bj = box[ordC[s + j]];
         if (dm_iou_gt(bi.x, bi.y, bi.z, bi.w, ai, bj.x, bj.y, bj.z, bj.w, iou)) bits |= 1u << k;
       }
