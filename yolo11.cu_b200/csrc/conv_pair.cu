@@ -12,7 +12,7 @@
 // Roles (672 threads per CTA, one CTA per SM, clusters of two):
 //   warp 0     lane 0: TMA producer.  Both CTAs load their halves with the .cta_group::2
 //              form of the tensor copy, completing bytes on the LEADER's full barrier (the
-//              leader arms it with both halves' bytes).  No cluster multicast of loads.
+//              leader arms it with both halves' bytes).  Each CTA's loads fill only its own memory.
 //   warp 20    both CTAs: TMEM allocation (cta_group::2).  Leader lane 0: issues the MMAs,
 //              releases each stage group in both CTAs and hands finished accumulators to
 //              both CTAs' epilogues by tcgen05.commit to each CTA's barrier (two commits).
