@@ -41,9 +41,11 @@ static void usage() {
   printf("yolocuda - B200 (sm_100a) inference engine for YOLOv8 / YOLO11\n\n"
          "usage: yolocuda <mode> [model-dir] [iters] [--batch N] [--save-masks] [--iou X] [--conf X]\n\n"
          "modes:\n"
-         "  detect    one inference on the directory's input.f16, print detections\n"
-         "  bench     net + decode + NMS CUDA-graph latency (mean / p50 / p99)\n"
-         "  pipeline  end to end: H2D of the raw frame + letterbox + net + decode + NMS\n"
+         "  detect    one inference on the directory's input.f16, print detections (segment:\n"
+         "            --save-masks; obb: oriented boxes; classify: top-5 with names.txt)\n"
+         "  bench     net + post-processing CUDA-graph latency (mean / p50 / p99)\n"
+         "  pipeline  end to end: H2D of the raw frame + preprocessing (letterbox, or the\n"
+         "            classify resize + crop) + net + post-processing\n"
          "  profile   per-op device time of the planned op list\n"
          "  dump      per-op outputs (gpu/opNNN.bin) with reference resync for compare.py\n");
 }
