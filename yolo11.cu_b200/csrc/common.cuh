@@ -60,6 +60,7 @@ __device__ __forceinline__ void pdl_trigger() {
 }
 bool pdl_enabled();
 bool patch_enabled();
+bool streams_enabled();      // multi-stream graph capture candidate (YK_NO_STREAMS=1: no)
 bool bulk_store_enabled();   // epilogue bulk tensor stores (YK_NO_BULK_STORE=1: per-row stores)   // halo-patch 3x3 convs offered to the autotuner (YK_NO_PATCH=1: no)
 // Per host thread: -1 follows pdl_enabled(), 0 / 1 force plain / programmatic launches (the
 // engine captures its graphs both ways and keeps the faster).

@@ -30,6 +30,14 @@ bool bulk_store_enabled() {
   return on;
 }
 
+bool streams_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("YK_NO_STREAMS");
+    return !(e && *e && *e != '0');
+  }();
+  return on;
+}
+
 bool patch_enabled() {
   static const bool on = [] {
     const char* e = getenv("YK_NO_PATCH");

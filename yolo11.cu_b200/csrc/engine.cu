@@ -110,6 +110,8 @@ struct Engine {
   cudaStream_t st = nullptr;
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, float> exec_ms;
+  std::vector<cudaStream_t> side;  // extra streams of the multi-stream graph capture
+  std::vector<cudaEvent_t> opev;   // one event per planned op (capture-time ordering)
   std::vector<SlotGeom> slots;
   bool seg() const { return task == "segment"; }
   bool cls() const { return task == "classify"; }
@@ -124,6 +126,10 @@ struct Engine {
     cudaSetDevice(device);
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
     graphs.clear();
+    for (cudaStream_t s : side) cudaStreamDestroy(s);
+    side.clear();
+    for (cudaEvent_t e : opev) cudaEventDestroy(e);
+    opev.clear();
     for (auto& b : bufs)
       if (b.p) cudaFree(b.p), b.p = nullptr;
     if (dweights) cudaFree(dweights);
@@ -167,6 +173,7 @@ struct Engine {
   void run_op(const Op& op, int B);
   void run_post(int B);
   void forward(int B);
+  void forward_streams(int B);
   cudaGraphExec_t graph_for(int B);
 };
 
@@ -560,6 +567,97 @@ void Engine::forward(int B) {
   run_post(B);
 }
 
+// The same forward spread over several streams inside one capture, so the graph has the
+// op DAG instead of a chain: independent branches (the detection head's per-level box and
+// class chains, neck paths) run concurrently, which pays when each kernel fills only part
+// of the GPU (batch 1).  Op k depends on every earlier op whose written channel range
+// overlaps one it reads or writes, or that reads a range it writes (read-after-write,
+// write-after-write, write-after-read on buffer channel ranges).  Ops join the stream whose
+// last op they depend on, else a fresh stream (up to 8); cross-stream dependencies are
+// event waits.  The post-processing runs on the main stream after all streams join.
+void Engine::forward_streams(int B) {
+  constexpr int kMaxStreams = 8;
+  const int n = (int)ops.size();
+  while ((int)side.size() < kMaxStreams - 1) {
+    cudaStream_t s;
+    CKE(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    side.push_back(s);
+  }
+  while ((int)opev.size() < n + 1) {
+    cudaEvent_t e;
+    CKE(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    opev.push_back(e);
+  }
+  struct Reg { int buf, c0, c1; };
+  auto reg = [&](int t) { const Ten& v = tens[t]; return Reg{v.buf, v.coff, v.coff + v.C}; };
+  auto overlap = [](const Reg& a, const Reg& b) { return a.buf == b.buf && a.c0 < b.c1 && b.c0 < a.c1; };
+  std::vector<std::vector<Reg>> rd(n), wr(n);
+  for (int k = 0; k < n; k++) {
+    const Op& o = ops[k];
+    if (o.a >= 0) rd[k].push_back(reg(o.a));
+    if (o.kind == ADD && o.b >= 0) rd[k].push_back(reg(o.b));
+    if (o.res >= 0) rd[k].push_back(reg(o.res));
+    if (o.out >= 0) wr[k].push_back(reg(o.out));
+    if (o.y2 >= 0) wr[k].push_back(reg(o.y2));
+    if (o.y3 >= 0) wr[k].push_back(reg(o.y3));
+  }
+  auto any = [&](const std::vector<Reg>& x, const std::vector<Reg>& y) {
+    for (const Reg& a : x)
+      for (const Reg& b : y)
+        if (overlap(a, b)) return true;
+    return false;
+  };
+  std::vector<cudaStream_t> strm(kMaxStreams);
+  strm[0] = st;
+  for (int i = 1; i < kMaxStreams; i++) strm[i] = side[i - 1];
+  std::vector<int> tail(kMaxStreams, -1), on(n, 0);
+  int used = 1;
+  // fork: every stream starts after what the main stream holds so far
+  CKE(cudaEventRecord(opev[n], st));
+  for (int i = 1; i < kMaxStreams; i++) CKE(cudaStreamWaitEvent(strm[i], opev[n], 0));
+  const cudaStream_t main_st = st;
+  try {
+    for (int k = 0; k < n; k++) {
+      std::vector<int> deps;
+      for (int j = 0; j < k; j++)
+        if (any(wr[j], rd[k]) || any(wr[j], wr[k]) || any(rd[j], wr[k])) deps.push_back(j);
+      int s = -1;
+      for (int i = 0; i < used; i++)      // continue the chain of the latest dependency
+        if (tail[i] >= 0 && std::find(deps.begin(), deps.end(), tail[i]) != deps.end() &&
+            (s < 0 || tail[i] > tail[s]))
+          s = i;
+      if (s < 0) {
+        if (used < kMaxStreams) s = used++;
+        else {
+          s = 0;
+          for (int i = 1; i < used; i++)
+            if (tail[i] < tail[s]) s = i;
+        }
+      }
+      std::vector<int> latest(kMaxStreams, -1);   // latest dependency on each other stream
+      for (int j : deps)
+        if (on[j] != s) latest[on[j]] = std::max(latest[on[j]], j);
+      for (int i = 0; i < kMaxStreams; i++)
+        if (latest[i] >= 0) CKE(cudaStreamWaitEvent(strm[s], opev[latest[i]], 0));
+      st = strm[s];
+      run_op(ops[k], B);
+      st = main_st;
+      CKE(cudaEventRecord(opev[k], strm[s]));
+      on[k] = s;
+      tail[s] = k;
+    }
+  } catch (...) {
+    st = main_st;
+    throw;
+  }
+  // join every stream back into the main one, then decode / NMS / D2H there
+  for (int i = 1; i < kMaxStreams; i++) {
+    CKE(cudaEventRecord(opev[n], strm[i]));
+    CKE(cudaStreamWaitEvent(st, opev[n], 0));
+  }
+  run_post(B);
+}
+
 // Startup autotune (reference engine/engine.cu:1504-1533): time every tensor-core tile width
 // that fits the layer at the full batch and keep the fastest.
 void Engine::autotune() {
@@ -667,12 +765,13 @@ cudaGraphExec_t Engine::graph_for(int B) {
   // when that is enabled, once without; keep the faster.  Overlapping each kernel's set-up
   // with its predecessor's tail pays at small batches, where every kernel is a few
   // microseconds; at large batches the early-resident waiting CTAs can cost a little.
-  auto capture = [&](int pdl) {
+  auto capture = [&](int pdl, bool multi = false) {
     cudaGraph_t g;
     g_pdl_override = pdl;
     CKE(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     try {
-      forward(B);
+      if (multi) forward_streams(B);
+      else forward(B);
     } catch (...) {
       g_pdl_override = -1;
       cudaGraph_t dummy;
@@ -711,6 +810,25 @@ cudaGraphExec_t Engine::graph_for(int B) {
       float alt_ms = time10(alt), plain_ms = time10(best);
       alt_ms = std::min(alt_ms, time10(alt));
       best_ms = std::min(best_ms, plain_ms);
+      if (alt_ms < best_ms) {
+        std::swap(alt, best);
+        best_ms = alt_ms;
+      }
+    } catch (...) {
+      if (alt) cudaGraphExecDestroy(alt);
+      cudaEventDestroy(e0);
+      cudaEventDestroy(e1);
+      cudaGraphExecDestroy(best);
+      throw;
+    }
+    cudaGraphExecDestroy(alt);
+  }
+  if (streams_enabled()) {   // the op DAG over several streams; kept only if faster
+    cudaGraphExec_t alt = nullptr;
+    try {
+      alt = capture(pdl_enabled() ? 1 : 0, true);
+      float alt_ms = std::min(time10(alt), time10(alt)), cur_ms = time10(best);
+      best_ms = std::min(best_ms, cur_ms);
       if (alt_ms < best_ms) {
         std::swap(alt, best);
         best_ms = alt_ms;
