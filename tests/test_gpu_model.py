@@ -152,3 +152,33 @@ def test_detections_close_to_fp32_forward(lib, cuda):
         ua = (same[:, 2] - same[:, 0]) * (same[:, 3] - same[:, 1]) + (k[2] - k[0]) * (k[3] - k[1]) - inter
         hit += (inter / ua).max() > 0.8
     assert hit >= 0.9 * len(keep)
+
+
+def test_multistream_graph_matches(lib, cuda, pkg):
+    """The forward captured over several streams (the op dependency DAG) must give the same
+    bits as the single-stream graph: YK_STREAMS=force makes the engine keep it."""
+    from yolo11_cu_b200 import frames, runtime as rt
+    d = _model_dir("yolo11n")
+    bgr = frames.synthetic_bgr(1080, 810, seed=0)
+    dev = torch.from_numpy(bgr).to(cuda)
+    torch.cuda.synchronize()
+    res = {}
+    for mode in ("force", None):
+        if mode:
+            os.environ["YK_STREAMS"] = mode
+        try:
+            eng = rt.Engine(d, 2, iou=0.7, autotune=False)   # same kernels in both runs
+            for s in range(2):
+                eng.preprocess(dev.data_ptr(), 1080, 810, s)
+            eng.run(2)
+            eng._check()
+            res[mode] = ([eng.get(s) for s in range(2)],
+                         [eng.read(t, 2) for t in (g_ for lv in graph_ref.Graph(d).levels() for g_ in lv[:2])])
+            eng.close()
+        finally:
+            os.environ.pop("YK_STREAMS", None)
+    dets_f, heads_f = res["force"]
+    dets_s, heads_s = res[None]
+    assert dets_f == dets_s and len(dets_f[0]) > 0
+    for a, b in zip(heads_f, heads_s):
+        assert np.array_equal(a.view(np.uint16), b.view(np.uint16))

@@ -824,12 +824,15 @@ cudaGraphExec_t Engine::graph_for(int B) {
     cudaGraphExecDestroy(alt);
   }
   if (streams_enabled()) {   // the op DAG over several streams; kept only if faster
+    // (YK_STREAMS=force keeps it regardless: tests use it to check the DAG capture)
+    const char* fs = getenv("YK_STREAMS");
+    const bool force = fs && !strcmp(fs, "force");
     cudaGraphExec_t alt = nullptr;
     try {
       alt = capture(pdl_enabled() ? 1 : 0, true);
       float alt_ms = std::min(time10(alt), time10(alt)), cur_ms = time10(best);
       best_ms = std::min(best_ms, cur_ms);
-      if (alt_ms < best_ms) {
+      if (force || alt_ms < best_ms) {
         std::swap(alt, best);
         best_ms = alt_ms;
       }
