@@ -104,6 +104,11 @@ struct Engine {
   // post-processing state
   YkPost post{};
   uint8_t* dmasks = nullptr;
+  // results in one block, device and pinned host alike, so one copy per run fetches them:
+  // rawcnt[maxB] | outcnt[maxB] | (16-byte aligned) outdets[maxB][max_det][rec]
+  void* dres = nullptr;
+  void* hres = nullptr;
+  size_t res_hdr = 0;
   float* h_out = nullptr;
   int* h_cnt = nullptr;
   int* h_raw = nullptr;
@@ -138,14 +143,11 @@ struct Engine {
     dcols.clear();
     if (dbias) cudaFree(dbias);
     if (post.ws) cudaFree(post.ws);
-    if (post.outdets) cudaFree(post.outdets);
+    if (dres) cudaFree(dres);
     if (post.outidx) cudaFree(post.outidx);
-    if (post.outcnt) cudaFree(post.outcnt);
-    if (post.rawcnt) cudaFree(post.rawcnt);
     if (dmasks) cudaFree(dmasks);
-    if (h_out) cudaFreeHost(h_out);
-    if (h_cnt) cudaFreeHost(h_cnt);
-    if (h_raw) cudaFreeHost(h_raw);
+    if (hres) cudaFreeHost(hres);
+    dres = hres = nullptr;
     if (h_probs) cudaFreeHost(h_probs);
     h_probs = nullptr;
     if (st) cudaStreamDestroy(st);
@@ -403,19 +405,22 @@ void Engine::allocate(const std::string& dir) {
   CKE(cudaMemcpy(dbias, bf.data(), bf.size(), cudaMemcpyHostToDevice));
   post.ws_bytes = obb() ? yk_obb_workspace_bytes(maxB, A) : yk_post_workspace_bytes(maxB, A);
   CKE(cudaMalloc(&post.ws, post.ws_bytes));
-  CKE(cudaMalloc(&post.outdets, (size_t)maxB * opt.max_det * rec() * sizeof(float)));
+  res_hdr = ((size_t)2 * maxB * sizeof(int) + 15) & ~(size_t)15;
+  const size_t res_bytes = res_hdr + (size_t)maxB * opt.max_det * rec() * sizeof(float);
+  CKE(cudaMalloc(&dres, res_bytes));
+  CKE(cudaMemset(dres, 0, res_bytes));
+  post.rawcnt = (int*)dres;
+  post.outcnt = (int*)dres + maxB;
+  post.outdets = (float*)((char*)dres + res_hdr);
   CKE(cudaMalloc(&post.outidx, (size_t)maxB * opt.max_det * sizeof(int)));
-  CKE(cudaMalloc(&post.outcnt, maxB * sizeof(int)));
-  CKE(cudaMalloc(&post.rawcnt, maxB * sizeof(int)));
-  CKE(cudaMemset(post.outcnt, 0, maxB * sizeof(int)));
-  CKE(cudaMemset(post.rawcnt, 0, maxB * sizeof(int)));
   if (seg()) {
     const Buf& pb = bufs[tens[protoTen].buf];
     CKE(cudaMalloc(&dmasks, (size_t)maxB * opt.max_det * pb.H * pb.W));
   }
-  CKE(cudaMallocHost(&h_out, (size_t)maxB * opt.max_det * rec() * sizeof(float)));
-  CKE(cudaMallocHost(&h_cnt, maxB * sizeof(int)));
-  CKE(cudaMallocHost(&h_raw, maxB * sizeof(int)));
+  CKE(cudaMallocHost(&hres, res_bytes));
+  h_raw = (int*)hres;
+  h_cnt = (int*)hres + maxB;
+  h_out = (float*)((char*)hres + res_hdr);
   if (cls()) CKE(cudaMallocHost(&h_probs, (size_t)maxB * nc * sizeof(__half)));
   memset(h_cnt, 0, maxB * sizeof(int));
   memset(h_raw, 0, maxB * sizeof(int));
@@ -556,9 +561,8 @@ void Engine::run_post(int B) {
     CKY(yk_masks(lv.data(), (int)lv.size(), &pr, S, S, opt.max_det, &post, dmasks,
                  (yk_stream_t)st));
   }
-  CKE(cudaMemcpyAsync(h_raw, post.rawcnt, B * sizeof(int), cudaMemcpyDeviceToHost, st));
-  CKE(cudaMemcpyAsync(h_cnt, post.outcnt, B * sizeof(int), cudaMemcpyDeviceToHost, st));
-  CKE(cudaMemcpyAsync(h_out, post.outdets, (size_t)B * opt.max_det * rec() * sizeof(float),
+  // counts of all slots and the first B images' records: one copy
+  CKE(cudaMemcpyAsync(hres, dres, res_hdr + (size_t)B * opt.max_det * rec() * sizeof(float),
                       cudaMemcpyDeviceToHost, st));
 }
 
