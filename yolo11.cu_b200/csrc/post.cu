@@ -502,23 +502,33 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
     if (moff[sg] >= 0) {
       const int m = e - s, words = (m + 31) >> 5;
       const uint32_t* rows = bmask + moff[sg];
-      uint32_t removed = 0;                 // lane w holds word w
+      uint32_t removed = 0;                 // lane w holds word w of the removed set
       int nk = 0;
-      for (int i0 = 0; i0 < m; i0 += 8) {
-        uint32_t r8[8];                     // eight rows' words in flight at once
+      for (int i0 = 0; i0 < m; i0 += 16) {  // 16 rows: their own bits share word wq
+        const int wq = i0 >> 5, sh = i0 & 31;
+        uint32_t r16[16];                   // word `lane` of each of the 16 rows
 #pragma unroll
-        for (int u = 0; u < 8; u++)
-          r8[u] = i0 + u < m && lane < words ? rows[(size_t)(i0 + u) * words + lane] : 0u;
+        for (int u = 0; u < 16; u++)
+          r16[u] = i0 + u < m && lane < words ? rows[(size_t)(i0 + u) * words + lane] : 0u;
+        // the lane holding word wq decides the 16 rows in order from that word alone
+        uint32_t keep = 0;
+        if (lane == wq) {
+          uint32_t rem = removed;
+          int k = nk;
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-          const int i = i0 + u;
-          if (i >= m) break;                 // uniform
-          const uint32_t rw = __shfl_sync(~0u, removed, i >> 5);
-          const bool alive = !((rw >> (i & 31)) & 1u) && nk < max_out;
-          if (alive) removed |= r8[u];
-          if (lane == 0) surv[ordC[s + i]] = alive ? 1 : 0;
-          nk += alive;
+          for (int u = 0; u < 16; u++)
+            if (i0 + u < m && !((rem >> (sh + u)) & 1u) && k < max_out) {
+              keep |= 1u << u;
+              rem |= r16[u];
+              k++;
+            }
         }
+        keep = __shfl_sync(~0u, keep, wq);
+#pragma unroll
+        for (int u = 0; u < 16; u++)        // every lane removes the kept rows' words
+          if ((keep >> u) & 1u) removed |= r16[u];
+        if (lane < 16 && i0 + lane < m) surv[ordC[s + i0 + lane]] = (uint8_t)((keep >> lane) & 1u);
+        nk += __popc(keep);
       }
       continue;
     }
