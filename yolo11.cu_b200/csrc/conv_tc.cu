@@ -7,7 +7,7 @@
 // engine/engine.cu:270-358), so Cin = 8/16 layers waste nothing.  W is the OHWI weight
 // tensor, already [N][K] K-contiguous.
 //
-// Persistent, warp-specialised CTA (416 threads, one per SM); a CTA tile is MT stacked
+// Persistent, warp-specialised CTA (448 threads, one per SM); a CTA tile is MT stacked
 // 128-row sub-tiles x BN columns, taken round-robin:
 //   warps 0-3  producers, into a STAGES-deep ring of 128-byte-swizzled K-major tiles (BK=64):
 //              W tiles come by TMA (2-D tensor map over [Cout][K], zero fill past the edges,
@@ -16,7 +16,8 @@
 //              one 64-channel block of one filter tap); thinner A tiles are gathered in 16-byte
 //              cp.async chunks whose completion arrives on the stage's mbarrier in hardware
 //              (cp.async.mbarrier.arrive.noinc), so producers never stall on their own loads.
-//   warp 12    allocates TMEM and one lane issues tcgen05.mma (M=128, N=BN, K=16): per stage
+//   warp 12    allocates TMEM and one lane issues tcgen05.mma (M=128, N=BN, K=16; warp 13
+//              issues for half of the stacked sub-tiles of plain tiles): per stage
 //              four K steps x MT independent sub-tile accumulators (independent chains keep
 //              the tensor pipe busy when BN is small), then tcgen05.commit releases the stage;
 //              a finished tile's accumulators are handed to the epilogue.
