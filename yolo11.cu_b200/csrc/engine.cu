@@ -421,7 +421,10 @@ void Engine::allocate(const std::string& dir) {
   h_raw = (int*)hres;
   h_cnt = (int*)hres + maxB;
   h_out = (float*)((char*)hres + res_hdr);
-  if (cls()) CKE(cudaMallocHost(&h_probs, (size_t)maxB * nc * sizeof(__half)));
+  if (cls()) {
+    CKE(cudaMallocHost(&h_probs, (size_t)maxB * nc * sizeof(__half)));
+    memset(h_probs, 0, (size_t)maxB * nc * sizeof(__half));   // defined before the first run
+  }
   memset(h_cnt, 0, maxB * sizeof(int));
   memset(h_raw, 0, maxB * sizeof(int));
   slots.assign(maxB, SlotGeom{});
