@@ -197,7 +197,9 @@ def oracle_postproc():
         lib.oref_letterbox.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
         lib.oref_letterbox_geom.restype = None
         lib.oref_letterbox_geom.argtypes = [C.c_int, C.c_int, C.c_int] + [C.c_void_p] * 5
-        for n in ("oref_exp", "oref_sigmoid"):
+        lib.oref_probiou.restype = C.c_float
+        lib.oref_probiou.argtypes = [C.c_void_p, C.c_void_p]
+        for n in ("oref_exp", "oref_sigmoid", "oref_sin", "oref_cos", "oref_log"):
             getattr(lib, n).restype = C.c_float
             getattr(lib, n).argtypes = [C.c_float]
         lib.oref_decode_obb_level.restype = C.c_int

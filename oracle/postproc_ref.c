@@ -270,6 +270,15 @@ void oref_mask(const uint16_t* coef, int nm, const uint16_t* proto, int pstride,
 /* exposed for the math tests */
 float oref_exp(float x) { return dm_exp(x); }
 float oref_sigmoid(float x) { return dm_sigmoid(x); }
+float oref_sin(float x) { float s, c; dm_sincos(x, &s, &c); return s; }
+float oref_cos(float x) { float s, c; dm_sincos(x, &s, &c); return c; }
+float oref_log(float x) { return dm_log(x); }
+float oref_probiou(const float* a, const float* b) {   /* a, b: cx cy w h theta */
+  float ca[3], cb[3];
+  dm_obb_cov(a[2], a[3], a[4], ca);
+  dm_obb_cov(b[2], b[3], b[4], cb);
+  return dm_probiou(a[0], a[1], ca, b[0], b[1], cb);
+}
 static float cls_tri(int i, float centre, float sup) {
   float d = fabsf(DM_SUB(DM_ADD((float)i, 0.5f), centre));
   float w = DM_SUB(1.f, DM_DIV(d, sup));

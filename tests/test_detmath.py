@@ -35,3 +35,40 @@ def test_f2h_matches_numpy_rne():
     got = np.array([lib.oref_f2h(float(x)) for x in xs], np.uint16)
     want = xs.astype(np.float16).view(np.uint16)
     assert np.array_equal(got, want)
+
+
+def test_sincos_log_accuracy():
+    """dm_sincos on the decode's angle range and beyond, dm_log over the normal range: within
+    2 ulp (sin / cos: 2 ulp of 1 near zeros) of float64 libm."""
+    lib = graph_ref.oracle_postproc()
+    xs = np.linspace(-3.3, 3.3, 20001, dtype=np.float32)
+    s = np.array([lib.oref_sin(float(x)) for x in xs], np.float64)
+    c = np.array([lib.oref_cos(float(x)) for x in xs], np.float64)
+    tol = 2 * np.spacing(np.float32(1.0))
+    assert np.abs(s - np.sin(xs.astype(np.float64))).max() <= tol
+    assert np.abs(c - np.cos(xs.astype(np.float64))).max() <= tol
+    ys = np.exp(np.random.default_rng(2).uniform(-80, 80, 20000)).astype(np.float32)
+    ys = np.concatenate([ys, np.float32([1.0, 0.5, 2.0, 1e-30, 3e38])])
+    lg = np.array([lib.oref_log(float(y)) for y in ys], np.float64)
+    want = np.log(ys.astype(np.float64))
+    ulp = np.maximum(np.spacing(np.abs(want).astype(np.float32)).astype(np.float64), 1e-9)
+    assert (np.abs(lg - want) / ulp).max() <= 2.0
+    assert lib.oref_log(1.0) == 0.0
+
+
+def test_probiou_properties():
+    """probiou: 1 - O(sqrt(eps)) for identical boxes, symmetric, ~0 for far-apart boxes,
+    unchanged by a pi rotation of either box."""
+    import ctypes as C
+    lib = graph_ref.oracle_postproc()
+
+    def piou(a, b):
+        a, b = np.float32(a), np.float32(b)
+        return lib.oref_probiou(a.ctypes.data_as(C.c_void_p), b.ctypes.data_as(C.c_void_p))
+
+    a = [100, 100, 40, 20, 0.3]
+    assert piou(a, a) > 0.999
+    b = [110, 95, 30, 25, -0.4]
+    assert abs(piou(a, b) - piou(b, a)) < 1e-6
+    assert piou(a, [900, 900, 40, 20, 0.3]) < 1e-3
+    assert abs(piou(a, b) - piou([100, 100, 40, 20, 0.3 + np.pi], b)) < 1e-4
