@@ -182,3 +182,55 @@ def test_multistream_graph_matches(lib, cuda, pkg):
     assert dets_f == dets_s and len(dets_f[0]) > 0
     for a, b in zip(heads_f, heads_s):
         assert np.array_equal(a.view(np.uint16), b.view(np.uint16))
+
+
+def test_seg_masks_close_to_fp32_forward(lib, cuda, capsys):
+    """Per-instance mask IoU of the fused fp16 engine against the fp32 oracle forward of the
+    same input (yolo11n-seg 640): each fp32 survivor (first 40) is matched to the engine's
+    same-class box of highest IoU (> 0.9) and the two 160x160 masks compared.  Measured on a
+    B200: 30 of 30 matched, median 0.9992, minimum 0.991, 93 % at >= 0.995; the gate keeps
+    margin for autotuned kernel choices: median >= 0.995 and >= 80 % of instances at >= 0.995."""
+    from yolo11_cu_b200 import runtime as rt
+    d = _model_dir("yolo11n-seg")
+    g = graph_ref.Graph(d)
+    x = np.fromfile(os.path.join(d, "input.f16"), np.float16).reshape(g.S, g.S, 3)
+    bufs, _ = graph_ref.run_graph(g, x.astype(np.float32), round_fp16=False)
+    levels = g.levels()
+    heads = [(graph_ref.tensor_hwc(g, bufs, b_).astype(np.float16),
+              graph_ref.tensor_hwc(g, bufs, c_).astype(np.float16), st) for b_, c_, _, st in levels]
+    coefs = [graph_ref.tensor_hwc(g, bufs, cf).astype(np.float16) for _, _, cf, _ in levels]
+    proto = graph_ref.tensor_hwc(g, bufs, g.proto()).astype(np.float16)
+    keep = graph_ref.nms(graph_ref.decode(heads, g.nc), 0.45, 300)
+    Ws = [h[0].shape[1] for h in heads]
+    bases = np.cumsum([0] + [w * w for w in Ws])
+    eng = rt.Engine(d, 1)
+    eng.write(0, x)
+    eng.run(1)
+    dets = np.array(eng.get(0), np.float32)
+    ious = []
+    for k in keep[:40]:
+        same = np.nonzero(dets[:, 5] == k[5])[0]
+        if len(same) == 0:
+            continue
+        s_ = dets[same]
+        ix1 = np.maximum(s_[:, 0], k[0]); iy1 = np.maximum(s_[:, 1], k[1])
+        ix2 = np.minimum(s_[:, 2], k[2]); iy2 = np.minimum(s_[:, 3], k[3])
+        inter = np.clip(ix2 - ix1, 0, None) * np.clip(iy2 - iy1, 0, None)
+        ua = (s_[:, 2] - s_[:, 0]) * (s_[:, 3] - s_[:, 1]) + (k[2] - k[0]) * (k[3] - k[1]) - inter
+        j = int(np.argmax(inter / ua))
+        if (inter / ua)[j] <= 0.9:
+            continue
+        a = int(k[6])
+        li = int(np.searchsorted(bases, a, side="right") - 1)
+        y, xx = divmod(a - bases[li], Ws[li])
+        ref = graph_ref.mask(coefs[li][y, xx], proto, k, g.S).astype(bool)
+        got = eng.get_mask(0, int(same[j])).astype(bool)
+        union = (ref | got).sum()
+        ious.append(1.0 if union == 0 else (ref & got).sum() / union)
+    ious = np.array(ious)
+    with capsys.disabled():
+        print(f"\nseg mask IoU vs fp32: {len(ious)} matched of {min(40, len(keep))}, "
+              f"median {np.median(ious):.4f}, min {ious.min():.4f}, >= 0.995: {(ious >= 0.995).mean():.2f}")
+    assert len(ious) >= 0.8 * min(40, len(keep))
+    assert np.median(ious) >= 0.995
+    assert (ious >= 0.995).mean() >= 0.8
