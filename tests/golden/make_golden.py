@@ -12,7 +12,7 @@ random-init models, at small input sizes, and keeps:
     <model>-<S>/final.npy        the shim model's head output
 
 Needs the reference checkout (build container only):
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref <reference checkout>]
 """
 from __future__ import annotations
 
