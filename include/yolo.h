@@ -68,7 +68,14 @@ typedef struct {
 void yolo_default_options(YoloOptions* o);
 void* yolo_create_ex(const char* model_dir, int max_batch, const YoloOptions* opts);
 void yolo_destroy(void* h);
+// Message of the most recent failed call on this thread: every call that can fail clears it
+// on entry, so after a void call an empty string means success.
 const char* yolo_last_error(void);
+// JPEG front end (the reference server's nvJPEG decode, server/serve.cpp:84-102, as a
+// library call): decode host JPEG bytes on the GPU and preprocess them into slot `slot`
+// (letterbox, or the classify resize + crop on classify handles).  Returns when done (the
+// bytes may be freed); 0, or -1 (not a JPEG / decode failure; see yolo_last_error).
+int yolo_preprocess_jpeg(void* h, const unsigned char* jpeg, size_t nbytes, int slot);
 // Number of conf-passing candidates of a slot before NMS (reference h_rawcnt tripwire).
 int yolo_raw_count(void* h, int slot);
 // Run one op of the UNFUSED graph for B images (dump mode, engine/engine.cu:1843-1888);

@@ -51,7 +51,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
         if verbose:
             print("nvcc ->", LIB, flush=True)
         tmp = LIB + ".tmp"
-        _run([NVCC, *ARCH, *FLAGS, "-shared", os.path.join(CSRC, "libyolob200.cu"), "-o", tmp])
+        _run([NVCC, *ARCH, *FLAGS, "-shared", os.path.join(CSRC, "libyolob200.cu"), "-o", tmp,
+              "-lnvjpeg"])
         os.replace(tmp, LIB)
     if force or _stale(CLI, deps + [LIB]):
         if verbose:

@@ -7,6 +7,7 @@
 // is owned per handle and released by yolo_destroy, NMS output is exact (no 1024 cap),
 // and graphs are captured per batch size on first use.
 #include <cuda_runtime.h>
+#include <nvjpeg.h>
 
 #include <algorithm>
 #include <cmath>
@@ -115,6 +116,10 @@ struct Engine {
   cudaStream_t st = nullptr;
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, float> exec_ms;
+  nvjpegHandle_t jpeg = nullptr;   // JPEG front end (created on first use)
+  nvjpegJpegState_t jstate = nullptr;
+  std::vector<void*> jbuf;         // per slot: the decoded BGR frame
+  std::vector<size_t> jcap;
   std::vector<cudaStream_t> side;  // extra streams of the multi-stream graph capture
   std::vector<cudaEvent_t> opev;   // one event per planned op (capture-time ordering)
   std::vector<SlotGeom> slots;
@@ -133,6 +138,14 @@ struct Engine {
     graphs.clear();
     for (cudaStream_t s : side) cudaStreamDestroy(s);
     side.clear();
+    for (void* b : jbuf)
+      if (b) cudaFree(b);
+    jbuf.clear();
+    jcap.clear();
+    if (jstate) nvjpegJpegStateDestroy(jstate);
+    if (jpeg) nvjpegDestroy(jpeg);
+    jstate = nullptr;
+    jpeg = nullptr;
     for (cudaEvent_t e : opev) cudaEventDestroy(e);
     opev.clear();
     for (auto& b : bufs)
@@ -876,6 +889,7 @@ struct DeviceScope {   // makes the handle's device current for the duration of 
 
 template <class F>
 auto guarded(F&& f, decltype(f()) fail) -> decltype(f()) {
+  g_err.clear();   // the last error describes the most recent call on this thread
   try {
     return f();
   } catch (const std::exception& e) {
@@ -964,6 +978,57 @@ void yolo_preprocess(void* h, const unsigned char* dev_bgr, int height, int widt
     SlotGeom& g = e->slots[slot];
     CKY(yk_letterbox(dev_bgr, height, width, &in, slot, &g.scale, &g.top, &g.left,
                      (yk_stream_t)e->st));
+    return 0;
+  }, -1);
+}
+
+// JPEG front end (the reference server's decodeOne, server/serve.cpp:84-102): nvJPEG
+// decodes the host bytes to a device BGR frame (per-slot buffer), then the task's own
+// preprocessing (letterbox, or the classify resize + crop) fills the slot.  Synchronises the
+// engine stream before returning, so the bytes may be freed at once.
+int yolo_preprocess_jpeg(void* h, const unsigned char* bytes, size_t nbytes, int slot) {
+  return guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || slot < 0 || slot >= e->maxB || !bytes) throw Error("yolo_preprocess_jpeg: bad arguments");
+    if (nbytes < 4 || bytes[0] != 0xFF || bytes[1] != 0xD8) throw Error("yolo_preprocess_jpeg: not a JPEG");
+    DeviceScope ds(e->device);
+    auto ckj = [](nvjpegStatus_t r, const char* what) {
+      if (r != NVJPEG_STATUS_SUCCESS) throw Error(std::string(what) + " failed (nvjpeg " + std::to_string((int)r) + ")");
+    };
+    if (!e->jpeg) {
+      ckj(nvjpegCreateSimple(&e->jpeg), "nvjpegCreateSimple");
+      ckj(nvjpegJpegStateCreate(e->jpeg, &e->jstate), "nvjpegJpegStateCreate");
+      e->jbuf.assign(e->maxB, nullptr);
+      e->jcap.assign(e->maxB, 0);
+    }
+    int ncomp = 0, ws[NVJPEG_MAX_COMPONENT] = {}, hs[NVJPEG_MAX_COMPONENT] = {};
+    nvjpegChromaSubsampling_t sub;
+    ckj(nvjpegGetImageInfo(e->jpeg, bytes, nbytes, &ncomp, &sub, ws, hs), "nvjpegGetImageInfo");
+    const int w = ws[0], hgt = hs[0];
+    if (w < 1 || hgt < 1) throw Error("yolo_preprocess_jpeg: empty image");
+    const size_t need = (size_t)w * hgt * 3;
+    if (e->jcap[slot] < need) {
+      CKE(cudaStreamSynchronize(e->st));      // the old buffer may still be in use
+      if (e->jbuf[slot]) CKE(cudaFree(e->jbuf[slot]));
+      e->jbuf[slot] = nullptr;
+      e->jcap[slot] = 0;
+      CKE(cudaMalloc(&e->jbuf[slot], need));
+      e->jcap[slot] = need;
+    }
+    nvjpegImage_t out{};
+    out.channel[0] = (unsigned char*)e->jbuf[slot];
+    out.pitch[0] = (size_t)w * 3;
+    ckj(nvjpegDecode(e->jpeg, e->jstate, bytes, nbytes, NVJPEG_OUTPUT_BGRI, &out, e->st),
+        "nvjpegDecode");
+    YkView in = e->view(0, e->maxB);
+    const uint8_t* src = (const uint8_t*)e->jbuf[slot];
+    if (e->cls()) {
+      CKY(yk_preprocess_cls(src, hgt, w, &in, slot, nullptr, (yk_stream_t)e->st));
+    } else {
+      SlotGeom& g = e->slots[slot];
+      CKY(yk_letterbox(src, hgt, w, &in, slot, &g.scale, &g.top, &g.left, (yk_stream_t)e->st));
+    }
+    CKE(cudaStreamSynchronize(e->st));
     return 0;
   }, -1);
 }

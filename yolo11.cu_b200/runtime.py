@@ -96,6 +96,7 @@ _SIGS = {
     "yolo_sync": (None, [C.c_void_p]),
     "yolo_get": (C.c_int, [C.c_void_p, C.c_int, _P(YoloDet), C.c_int]),
     "yolo_preprocess_cls": (None, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]),
+    "yolo_preprocess_jpeg": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.c_int]),
     "yolo_get_cls": (C.c_int, [C.c_void_p, C.c_int, _P(C.c_int), _P(C.c_float), C.c_int]),
     "yolo_get_obb": (C.c_int, [C.c_void_p, C.c_int, _P(YoloObbDet), C.c_int]),
     "yolo_slot_geom": (None, [C.c_void_p, C.c_int, _P(C.c_float), _P(C.c_int), _P(C.c_int)]),
@@ -186,6 +187,9 @@ class Engine:
 
     def preprocess(self, dev_bgr_ptr: int, h: int, w: int, slot: int):
         self.lib.yolo_preprocess(self.h, C.c_void_p(dev_bgr_ptr), h, w, slot)
+
+    def preprocess_jpeg(self, data: bytes, slot: int) -> int:
+        return self.lib.yolo_preprocess_jpeg(self.h, data, len(data), slot)
 
     def preprocess_cls(self, dev_bgr_ptr: int, h: int, w: int, slot: int):
         self.lib.yolo_preprocess_cls(self.h, C.c_void_p(dev_bgr_ptr), h, w, slot)
