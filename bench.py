@@ -4,12 +4,16 @@ plus yolo11n batch-1 end-to-end latency (p50 / p99).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
 
-A step = one pass of the hot path over one batch: letterbox of 32 raw frames + net + DFL
-decode + NMS (+ D2H of the results), replayed as the engine's CUDA graph.  ``value`` times
-steps whose raw frames are already resident in HBM (CUDA events on the engine stream, max
-over ranks); ``e2e`` times the same steps through the public C ABI from pinned host memory,
-H2D copies of every step's frames and the D2H of its detections included (wall clock, max
-over ranks).  Ranks shard frames; nothing is exchanged but the timing scalars.
+A step = one pass of the hot path over one batch, replayed as ONE CUDA graph: letterbox of
+32 raw frames (one launch) + net + DFL decode + NMS + D2H of the detections
+(yolo_bind_frames / yolo_run_frames).  ``value`` times steps whose raw frames are already
+resident in HBM (CUDA events on the engine stream, max over ranks); ``e2e`` times the same
+steps through the public C ABI from pinned host memory, H2D copies of every step's frames
+(double-buffered on a copy stream) and the fetch of its detections included (wall clock, max
+over ranks).  Ranks shard frames; nothing is exchanged but the timing scalars.  Beside the
+headline, the line carries yolo11x 1024 (16 frames per GPU) and yolo11n-seg 640 (64 frames
+split over the GPUs) as ``extra_configs``, the yolo11n batch-1 end-to-end latency, and a
+parity check of slot 0 against the oracle (rank 0, after the timed regions).
 
 ``--impl reference`` times the reference's CPU implementation of the path: the reference has
 no CPU inference path of its own, so this is the repository's restatement of the reference
@@ -32,10 +36,13 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.join(ROOT, "yolo11.cu_b200")
 MODELS = os.path.join(ROOT, "models")
 MODEL, S, FRAME_HW, PER_GPU = "yolo11m", 640, (720, 1280), 32
+# further BASELINE configurations reported beside the headline: (model, imgsz, frame h x w,
+# frames per GPU; the seg batch of 64 is split over the GPUs)
+EXTRA = [("yolo11x", 1024, (1080, 1920), 16), ("yolo11n-seg", 640, (1080, 810), 64)]
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) of the tcgen05 conv launches of one 32-frame yolo11m forward, from
 # one ncu capture of the current kernels, and the algorithmic bytes of the same convs (input,
-# weights, output, residual once each): profiles/dram_conv_yolo11m_bs32.md.
+# weights, output, residual once each).
 CONV_DRAM_BYTES_PER_STEP = 7.484e9
 CONV_ALG_BYTES_PER_STEP = 9.469e9
 
@@ -91,6 +98,13 @@ class ClockSampler:
         self.gpu, self.samples, self._stop = gpu, [], threading.Event()
         self.sm_max, self.source = None, None
         self._nvml = None
+        self.smi_id = str(gpu)   # nvidia-smi selects by UUID when torch can tell it
+        try:
+            import torch
+            u = str(torch.cuda.get_device_properties(gpu).uuid)
+            self.smi_id = u if u.startswith("GPU-") else "GPU-" + u
+        except Exception:
+            pass
         try:
             import pynvml
             import torch
@@ -120,7 +134,7 @@ class ClockSampler:
         q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
-        out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + q,
+        out = subprocess.run(["nvidia-smi", "-i", self.smi_id, "--query-gpu=" + q,
                               "--format=csv,noheader,nounits"], capture_output=True, text=True,
                              timeout=5).stdout.strip()
         if out:
@@ -235,38 +249,43 @@ def run_reference(args):
 
 
 # ---------------- GPU arm ----------------
-def bench_latency_yolo11n(rt, pkg, dev, iters=200):
-    import numpy as np
+def tuned_engine(rt, d, B, dev):
+    """Engine with tiles from (or tuned into) the model directory's batch-B cache."""
+    os.environ["YOLO_TUNE_CACHE"] = os.path.join(d, f"tune_b{B}.txt")
+    try:
+        return rt.Engine(d, B, device=dev)
+    finally:
+        del os.environ["YOLO_TUNE_CACHE"]
+
+
+def bench_latency_yolo11n(rt, dev, iters=200):
+    """yolo11n 640 batch 1, end to end through the one-graph pipeline: one pinned 1080x810
+    frame, graph = H2D + letterbox + net + decode + NMS + D2H, then yolo_get (wall clock)."""
     import torch
     from yolo11_cu_b200 import export, frames
     d = export.ensure_model_dir("yolo11n", MODELS, 640)
-    os.environ["YOLO_TUNE_CACHE"] = os.path.join(d, "tune_b1.txt")
-    eng = rt.Engine(d, 1, device=dev)
-    del os.environ["YOLO_TUNE_CACHE"]
+    eng = tuned_engine(rt, d, 1, dev)
     hw = (1080, 810)
     host = torch.from_numpy(frames.synthetic_bgr(*hw, seed=0)).pin_memory()
-    dbuf = torch.empty_like(host, device=f"cuda:{dev}")
-    es = torch.cuda.ExternalStream(eng.stream, device=f"cuda:{dev}")
-    eng.exec_ms(1)
+    eng.bind_frames(0, host.data_ptr(), hw[0], hw[1], 1, True)
+    graph_ms = eng.frames_exec_ms(0, 1)
     lat = []
     for i in range(20 + iters):
         t0 = time.perf_counter()
-        with torch.cuda.stream(es):
-            dbuf.copy_(host, non_blocking=True)
-        eng.preprocess(dbuf.data_ptr(), hw[0], hw[1], 0)
-        eng.run(1)
+        eng.run_frames(0, 1)
         eng.get(0)
         t1 = time.perf_counter()
         if i >= 20:
             lat.append(1000 * (t1 - t0))
     eng._check()
-    torch.cuda.synchronize()
-    del host, dbuf          # blocks used on the engine stream are freed while it still exists
     lat.sort()
     out = {"p50_ms": lat[len(lat) // 2], "p99_ms": lat[int(0.99 * (len(lat) - 1))],
-           "graph_exec_ms": eng.exec_ms(1), "iters": iters,
-           "config": "yolo11n detect 640, batch 1, 1080x810 frame: H2D + letterbox + net + decode + NMS + D2H"}
+           "graph_exec_ms": graph_ms, "iters": iters,
+           "graph_kernels": eng.lib.yolo_graph_kernels(eng.h, 0, 1),
+           "config": "yolo11n detect 640, batch 1, 1080x810 frame: one CUDA graph of H2D + "
+                     "letterbox + net + decode + NMS + D2H, then yolo_get"}
     eng.close()
+    del host
     return out
 
 
@@ -274,8 +293,90 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
-def run_ours(args):
+def conv_roofline(lib, eng, d, B, clk, pk, pk_kind):
+    """Tensor-core conv roofline: algorithmic FLOPs of one batch-B forward over the device
+    time of its tcgen05 convs replayed as one graph (yolo_conv_exec_ms).  ``frac`` is taken
+    against the measured burst bf16 peak (the harder denominator); ``frac_sustained`` against
+    the measured sustained one, for runs whose clocks sat under the power cap."""
     import ctypes as C
+    nconv = C.c_int()
+    conv_ms = lib.yolo_conv_exec_ms(eng.h, B, C.byref(nconv))
+    flops = conv_flops(d, B)
+    achieved = flops / (conv_ms * 1e-3) / 1e12 if conv_ms > 0 else None
+    peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    sus = pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    return {"achieved": achieved, "peak": peak, "frac": (achieved / peak) if achieved else None,
+            "frac_sustained": (achieved / sus) if achieved else None,
+            "conv_ms_per_step": conv_ms, "conv_launches_per_step": nconv.value,
+            "flops_per_step": flops,
+            "peak_source": f"{pk_kind} bf16_tflops (burst); timed region median SM clock "
+                           f"{clk.get('sm_mhz')} of max {clk.get('sm_max_mhz')} MHz"}
+
+
+def parity_slot0(eng, d, bgr0, B):
+    """Slot 0 of the benched graph against the oracle (checker only, after the timed
+    regions): letterbox bit-exact, head tensors within 1.5 % of the fp32 forward of the same
+    input, and decode + NMS of the engine's own head logits bit-exact."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import graph_ref
+    g = graph_ref.Graph(d)
+    x = eng.read(0, 1)[0]
+    lb_ok = bool(np.array_equal(x.view(np.uint16), graph_ref.letterbox(bgr0, g.S).view(np.uint16)))
+    bufs, _ = graph_ref.run_graph(g, x.astype(np.float32), round_fp16=False)
+    worst, heads = 0.0, []
+    for bt, ct, _, st in g.levels():
+        hb, hc = eng.read(bt, 1)[0], eng.read(ct, 1)[0]
+        for t, got in ((bt, hb), (ct, hc)):
+            ref = graph_ref.tensor_hwc(g, bufs, t)
+            worst = max(worst, float(np.abs(got.astype(np.float32) - ref).max() / (np.abs(ref).max() + 1e-6)))
+        heads.append((hb, hc, st))
+    keep = graph_ref.nms(graph_ref.decode(heads, g.nc, 0.25), 0.45, 300)
+    dets = eng.get(0)
+    post_ok = len(dets) == len(keep) and bool(np.array_equal(
+        np.float32([q[4] for q in dets]).view(np.uint32), keep[:, 4].astype(np.float32).view(np.uint32)))
+    return {"ok": lb_ok and post_ok and worst <= 0.015, "letterbox_bitexact": lb_ok,
+            "head_rel_vs_fp32_max": worst, "post_bitexact": post_ok, "detections": len(dets),
+            "slot": 0}
+
+
+def bench_extra(rt, lib, name, S, frame_hw, per_gpu, local, world, rank, steps, pk, pk_kind):
+    """A further BASELINE configuration on this GPU: frames/s over `steps` replays of the
+    one-graph pipeline on device-resident frames (CUDA events, max over ranks) and its conv
+    roofline fraction."""
+    import numpy as np
+    import torch
+    from yolo11_cu_b200 import export, frames
+    d = export.ensure_model_dir(name, MODELS, S, frame_hw)
+    eng = tuned_engine(rt, d, per_gpu, local)
+    dev = torch.from_numpy(np.stack([frames.synthetic_bgr(*frame_hw, seed=1000 * rank + i)
+                                     for i in range(per_gpu)])).to(f"cuda:{local}")
+    eng.bind_frames(0, dev.data_ptr(), frame_hw[0], frame_hw[1], per_gpu, False)
+    eng.frames_exec_ms(0, per_gpu)
+    es = torch.cuda.ExternalStream(eng.stream, device=f"cuda:{local}")
+    for _ in range(3):
+        eng.run_frames_async(0, per_gpu)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record(es)
+        for _ in range(steps):
+            eng.run_frames_async(0, per_gpu)
+        e1.record(es)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    eng._check()
+    roof = conv_roofline(lib, eng, d, per_gpu, clk.summary(), pk, pk_kind)
+    eng.close()
+    del dev
+    return {"frames_per_s": per_gpu * world * steps / (ms / 1000), "ms_per_step": ms / steps,
+            "frames_per_gpu": per_gpu, "n_gpus": world, "steps": steps,
+            "conv_tflops": roof["achieved"], "conv_frac": roof["frac"],
+            "conv_peak_source": roof["peak_source"], "clocks": clk.summary()}
+
+
+def run_ours(args):
     import numpy as np
     import torch
     rank, world, local = dist_env()
@@ -288,48 +389,45 @@ def run_ours(args):
     if rank == 0:
         build.build()
         export.ensure_model_dir(MODEL, MODELS, S, FRAME_HW)
+        if not args.no_extra:
+            for name, S_, hw, _ in EXTRA:
+                export.ensure_model_dir(name, MODELS, S_, hw)
     barrier(world)
     d = export.ensure_model_dir(MODEL, MODELS, S, FRAME_HW)
     log('bench: engine create')
     lib = rt.load()
     B = PER_GPU
     lo, hi = shard(PER_GPU * world, world, rank)
-    os.environ["YOLO_TUNE_CACHE"] = os.path.join(d, f"tune_b{B}.txt")   # tiles tuned once per box
-    eng = rt.Engine(d, B, device=local)
-    del os.environ["YOLO_TUNE_CACHE"]
-    n0 = lib.yk_launch_count()
-    lib.yolo_exec_ms(eng.h, B)          # capture (counted launches) + calibrate the batch-B graph
-    graph_kernels = lib.yk_launch_count() - n0
-    launches_per_step = graph_kernels + B          # graph kernels + one letterbox per frame
+    eng = tuned_engine(rt, d, B, local)
 
     log('bench: frames')
-    hostf = torch.from_numpy(np.stack([frames.synthetic_bgr(*FRAME_HW, seed=i) for i in range(lo, hi)])).pin_memory()
+    bgr = np.stack([frames.synthetic_bgr(*FRAME_HW, seed=i) for i in range(lo, hi)])
+    hostf = torch.from_numpy(bgr).pin_memory()
     dev = f"cuda:{local}"
     dbuf = [torch.empty_like(hostf, device=dev) for _ in range(2)]
     dbuf[0].copy_(hostf)
     torch.cuda.synchronize()
+    for j in range(2):       # two device frame arrays, used alternately by the e2e loop
+        eng.bind_frames(j, dbuf[j].data_ptr(), FRAME_HW[0], FRAME_HW[1], B, False)
+    graph_ms = eng.frames_exec_ms(0, B)      # capture + calibrate the pipeline graph
+    eng.frames_exec_ms(1, B)
+    graph_kernels = lib.yolo_graph_kernels(eng.h, 0, B)
     es = torch.cuda.ExternalStream(eng.stream, device=dev)
-    fb = FRAME_HW[0] * FRAME_HW[1] * 3
-
-    def step_resident():
-        for s in range(B):
-            eng.preprocess(dbuf[0].data_ptr() + s * fb, FRAME_HW[0], FRAME_HW[1], s)
-        eng.run_async(B)
 
     for _ in range(args.warmup):
-        step_resident()
+        eng.run_frames_async(0, B)
     eng.sync()
     eng._check()
 
     log('bench: timed value')
-    # ---- value: frames resident in HBM, CUDA events on the engine stream ----
+    # ---- value: frames resident in HBM, one graph launch per step, CUDA events ----
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         e0.record(es)
         for _ in range(args.steps):
-            step_resident()
+            eng.run_frames_async(0, B)
         e1.record(es)
         torch.cuda.synchronize()
     dev_ms = e0.elapsed_time(e1)
@@ -338,7 +436,8 @@ def run_ours(args):
     eng._check()
 
     log('bench: e2e')
-    # ---- e2e: pinned host frames -> H2D (double-buffered) -> ABI -> D2H results ----
+    # ---- e2e: pinned host frames -> H2D (copy stream, double-buffered) -> pipeline graph
+    #      -> D2H of the detections inside the graph -> yolo_get_batch ----
     cs = torch.cuda.Stream(device=dev)
     copied = [torch.cuda.Event() for _ in range(2)]
     freed = [torch.cuda.Event() for _ in range(2)]
@@ -356,15 +455,12 @@ def run_ours(args):
         for i in range(k):
             j = i % 2
             es.wait_event(copied[j])
-            for s in range(B):
-                eng.preprocess(dbuf[j].data_ptr() + s * fb, FRAME_HW[0], FRAME_HW[1], s)
+            eng.run_frames_async(j, B)
             freed[j].record(es)
             if i + 1 < k:
                 issue_copy(i + 1)
-            eng.run_async(B)
             eng.sync()
-            for s in range(B):
-                eng.get(s)
+            eng.get_batch(B)
 
     e2e_steps(max(args.warmup, 1))
     barrier(world)
@@ -377,24 +473,27 @@ def run_ours(args):
     eng._check()
 
     log('bench: roofline')
-    # ---- roofline of the dominant kernel (tensor-core implicit-GEMM conv) ----
-    ms = (C.c_float * 4096)()
-    nprof = lib.yolo_profile(eng.h, B, 10, ms, 4096)
-    conv_ms, conv_launches, total_ms = 0.0, 0, 0.0
-    for k in range(nprof):
-        total_ms += ms[k]
-        tile = C.c_int()
-        desc = lib.yolo_op_desc(eng.h, k, C.byref(tile)) if k < nprof - 1 else b"POST"
-        if desc == b"CONV" and tile.value > 0:
-            conv_ms += ms[k]
-            conv_launches += 1
-    flops = conv_flops(d, B)
     pk, pk_kind = peaks()
-    achieved = flops / (conv_ms * 1e-3) / 1e12 if conv_ms > 0 else None
-    peak = pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    clocks = clk.summary()
+    roof = conv_roofline(lib, eng, d, B, clocks, pk, pk_kind)
+    parity = None
+    if rank == 0 and not args.no_cpu:
+        log('bench: parity (oracle check of slot 0)')
+        parity = parity_slot0(eng, d, bgr[0], B)
+    torch.cuda.synchronize()
+    h2d_bytes = int(hostf.numel())
+    del hostf, dbuf          # free the blocks used on the engine stream before closing it
+    eng.close()
 
+    extra = {}
+    if not args.no_extra:
+        for name, S_, hw, per in EXTRA:
+            log(f'bench: extra {name}')
+            per_gpu = per if name != "yolo11n-seg" else max(1, per // world)
+            extra[name] = bench_extra(rt, lib, name, S_, hw, per_gpu, local, world, rank,
+                                      args.extra_steps, pk, pk_kind)
     log('bench: latency')
-    lat = bench_latency_yolo11n(rt, pkg, local) if rank == 0 and not args.no_latency else None
+    lat = bench_latency_yolo11n(rt, local) if rank == 0 and not args.no_latency else None
     log('bench: cpu')
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -402,47 +501,47 @@ def run_ours(args):
         cpu = {"value": n / secs, "unit": "frames/s", "cores": thr, "kind": "port",
                "sample": f"{n} frames of the same workload (fp32 torch restatement of the reference "
                          f"interpreter + C decode/NMS), {secs:.1f} s"}
-    torch.cuda.synchronize()
-    h2d_bytes = int(hostf.numel())
-    del hostf, dbuf          # free the blocks used on the engine stream before closing it
-    eng.close()
     if rank != 0:
         return 0
     frames_total = PER_GPU * world * args.steps
     value = frames_total / (dev_ms_max / 1000)
     e2e = frames_total / t_e2e_max
     h2d = h2d_bytes * world
-    d2h = (B * 300 * 6 * 4 + 2 * B * 4) * world
+    d2h = (8 * B + B * 300 * 6 * 4) * world     # counts + records: one copy per step
     line = {
         "metric": "frames/s", "value": value, "unit": "frames/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded 1280x720 uint8 frames; seeded random-init BN-folded weights)",
-        "config": {"workload": f"{MODEL} detect {S}x{S}, {PER_GPU} frames per GPU per step "
-                               f"(letterbox + net + decode + NMS in one CUDA graph)",
+        "config": {"workload": f"{MODEL} detect {S}x{S}, {PER_GPU} frames per GPU per step: "
+                               f"one CUDA graph per step (letterbox of the {PER_GPU} frames in "
+                               f"one launch + net + decode + NMS + D2H of the detections)",
                    "model": MODEL, "imgsz": S, "frames_per_gpu": PER_GPU,
                    "global_batch": PER_GPU * world, "frame_hw": list(FRAME_HW),
                    "parallelism": f"dp{world} (batch shards, no collectives)",
                    "l2": "working set per step (activations ~GBs) far exceeds the 126 MB L2"},
         "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": (achieved / peak) if achieved else None,
+        "roofline": {"bound": "tensor", "achieved": roof["achieved"], "peak": roof["peak"],
+                     "unit": "TFLOP/s", "frac": roof["frac"],
+                     "frac_sustained": roof["frac_sustained"],
                      "traffic": CONV_DRAM_BYTES_PER_STEP,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over the "
-                                       "104 tcgen05 conv launches of one 32-frame forward "
-                                       "(profiles/dram_conv_yolo11m_bs32.md); algorithmic bytes "
-                                       f"{CONV_ALG_BYTES_PER_STEP:.4g}",
+                                       "tcgen05 conv launches of one 32-frame forward; "
+                                       f"algorithmic bytes {CONV_ALG_BYTES_PER_STEP:.4g}",
                      "kernel": "conv_tc_kernel + conv_patch_kernel + conv_kxn_kernel + conv_pair_kernel "
-                               "(tcgen05 convs), all launches "
-                               "of one step",
-                     "flops_per_step": flops, "conv_ms_per_step": conv_ms,
-                     "conv_launches_per_step": conv_launches, "step_ms_profiled": total_ms,
-                     "peak_source": f"{pk_kind} bf16_tflops_sustained"},
-        "gpu_launches": launches_per_step * args.steps,
-        "clocks": clk.summary(),
+                               "(tcgen05 convs) of one step, replayed as their own graph",
+                     "flops_per_step": roof["flops_per_step"],
+                     "conv_ms_per_step": roof["conv_ms_per_step"],
+                     "conv_launches_per_step": roof["conv_launches_per_step"],
+                     "graph_ms_per_step": graph_ms, "peak_source": roof["peak_source"]},
+        "gpu_launches": graph_kernels * args.steps,
+        "graph_kernels_per_step": graph_kernels,
+        "clocks": clocks,
+        "parity": parity,
         "cpu_baseline": cpu,
         "latency_yolo11n_bs1": lat,
+        "extra_configs": extra or None,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -457,6 +556,8 @@ def main():
     ap.add_argument("--no-latency", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-extra", action="store_true", help="skip the yolo11x-1024 / yolo11n-seg lines")
+    ap.add_argument("--extra-steps", type=int, default=10)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

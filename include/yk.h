@@ -93,6 +93,14 @@ int yk_attn(const YkView* qkv, const YkView* y, int heads, int kd, int hd, yk_st
 // and returned through the optional out pointers.  Kernel: engine/engine.cu:968-998.
 int yk_letterbox(const uint8_t* bgr, int sh, int sw, const YkView* y, int slot,
                  float* scale_out, int* top_out, int* left_out, yk_stream_t st);
+// The same for n equal-size frames in one launch: frame i (BGR u8 HWC, sh x sw, device
+// memory) starts at bgr + i * frame_stride bytes and fills slot slot0 + i.  All frames
+// share one geometry, returned as by yk_letterbox.  Replaces one k_preprocess launch per
+// frame (engine/engine.cu:1704-1713, serve.cpp's per-frame yolo_preprocess loop).
+// y->W <= 2048.
+int yk_letterbox_batch(const uint8_t* bgr, size_t frame_stride, int n, int sh, int sw,
+                       const YkView* y, int slot0, float* scale_out, int* top_out,
+                       int* left_out, yk_stream_t st);
 
 // Classification head (task "classify").  Global average pool of x [B][H][W][C] into
 // y [B][1][1][C], fp32 sums (engine/engine.cu:735-744, k_gap); C % 8 == 0, 16-byte views.
@@ -165,12 +173,21 @@ int yk_masks(const YkLevel* levels, int nlevels, const YkView* proto, int in_h, 
 // device address (cudaGetSymbolAddress), so make that first call before any stream capture.
 // All calls on a device share the one array and it keeps the last call's contents: calls
 // whose kernels overlap on the GPU (other streams, other threads) race and corrupt each other.
+// The looked-up address is kept for the life of the process: resetting a device
+// (cudaDeviceReset) while the library stays loaded is not supported by this entry point.
 int yk_decode_nms_static(const YkLevel* levels, int nlevels, int batch, int nc, float conf,
                          float iou, int max_out, float* outdets, int* outidx, int* outcnt,
                          int* rawcnt, yk_stream_t st);
 
 // Device error word (bounded-wait timeouts) of the current device; cleared by the call.
 int yk_fetch_device_error(void);
+// Test hook for the bounded-wait failure path (no counterpart in the reference, which has no
+// bounded waits): wait_ns sets the wait budget of every kernel on the current device (0 =
+// the default 2 s); withhold = 1 makes block 0 of the next tensor-core conv launches on the
+// TMA path skip its first stage load, so that block's MMA wait runs out, the device error
+// word is set and the kernel unwinds (no trap, no hang: the wait is bounded).  Synchronous;
+// call yk_test_inject(0, 0) to restore normal operation.
+int yk_test_inject(int withhold, unsigned long long wait_ns);
 const char* yk_last_cuda_error(void);
 // Number of kernels this library launched since load (all devices) — a host-side counter.
 long long yk_launch_count(void);

@@ -76,6 +76,32 @@ const char* yolo_last_error(void);
 // (letterbox, or the classify resize + crop on classify handles).  Returns when done (the
 // bytes may be freed); 0, or -1 (not a JPEG / decode failure; see yolo_last_error).
 int yolo_preprocess_jpeg(void* h, const unsigned char* jpeg, size_t nbytes, int slot);
+// One-graph pipeline (the reference CLI's `pipeline` graph, engine/engine.cu:1992-2004:
+// H2D + preprocess + forward captured together, generalised to a batch and to the API).
+// Bind `count` (<= max_batch) equal-size BGR u8 HWC frames, frame i at
+// frames + i * height * width * 3, as input array `id` (0..3).  host = 1: page-locked host
+// memory, copied to the device inside the graph; host = 0: device memory of the handle's
+// GPU.  The memory must stay valid while the binding is used; rebinding an id drops its
+// graphs.  0, or -1 (see yolo_last_error).
+int yolo_bind_frames(void* h, int id, const unsigned char* frames, int height, int width,
+                     int count, int host);
+// Replay binding id's pipeline graph for its first B frames into slots 0..B-1: [H2D] +
+// preprocessing of all B frames (one letterbox launch) + net + decode + NMS (+ masks) + the
+// D2H of the results.  The _async form returns after the launch (yolo_sync, then yolo_get);
+// the frames are read when the graph runs.  0, or -1.
+int yolo_run_frames_async(void* h, int id, int B);
+int yolo_run_frames(void* h, int id, int B);
+// Calibrated GPU time (ms) of one launch of binding id's batch-B pipeline graph.
+float yolo_frames_exec_ms(void* h, int id, int B);
+// Kernel nodes in the graph yolo_run (id = -1) or yolo_run_frames (id >= 0) replays for
+// batch B; 0 before that graph has been captured, -1 on bad arguments.
+int yolo_graph_kernels(void* h, int id, int B);
+// Device time (ms) of the tensor-core convolutions of one batch-B forward, captured alone as
+// one graph in the planned order and replayed; *nconv (optional) receives their count.
+float yolo_conv_exec_ms(void* h, int B, int* nconv);
+// Detections of slots 0..B-1 in one call: slot s's go to out + s * cap (at most cap each),
+// its count to counts[s].  Returns the total, or -1 (bad arguments / obb handle).
+int yolo_get_batch(void* h, int B, YoloDet* out, int cap, int* counts);
 // Number of conf-passing candidates of a slot before NMS (reference h_rawcnt tripwire).
 int yolo_raw_count(void* h, int slot);
 // Run one op of the UNFUSED graph for B images (dump mode, engine/engine.cu:1843-1888);

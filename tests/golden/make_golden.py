@@ -43,8 +43,11 @@ def sha256(path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("YOLO_REFERENCE_DIR"),
+                    help="reference checkout (default: $YOLO_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref <reference checkout> or set YOLO_REFERENCE_DIR")
     sys.path.insert(0, os.path.join(ROOT, "yolo11.cu_b200"))
     import cv2
     import frames  # noqa: E402  (the package's frame generator, imported by path)

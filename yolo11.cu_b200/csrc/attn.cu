@@ -132,12 +132,8 @@ __global__ void __launch_bounds__(128) attn_kernel(DView qkv, DView y, int N) {
 template <int KS>
 static int launch_attn(const YkView* qkv, const YkView* y, int heads, int N, size_t smem,
                        cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attn_kernel<32, 64, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         227 * 1024);
-    attr = true;
-  }
+  if (smem_attr(attn_kernel<32, 64, KS>, 227 * 1024) != cudaSuccess)
+    return check_launch("attn attr");
   dim3 grid((N + 128 / KS - 1) / (128 / KS), heads, qkv->batch);
   launch_k(attn_kernel<32, 64, KS>, grid, 128, smem, (cudaStream_t)st, dview(*qkv), dview(*y), N);
   note_launch();

@@ -39,12 +39,26 @@ static inline bool view_vec8(const YkView* v) {
 }
 
 void note_launch();                        // bumps the launch counter
+
+// Raise a kernel's dynamic shared-memory limit to at least `bytes` on the current device.
+// The attribute belongs to the device's context, so it is set once per (kernel, device);
+// the record is guarded by a mutex so handles on several host threads may launch at once.
+cudaError_t ensure_smem_attr(const void* kernel, int bytes);
+template <class K>
+static inline cudaError_t smem_attr(K* kernel, int bytes) {
+  return ensure_smem_attr((const void*)kernel, bytes);
+}
 int check_launch(const char* what);        // cudaGetLastError -> YK_OK / YK_ECUDA
 __device__ int g_device_error = 0;         // set by bounded waits that give up (one TU)
 
 // Bounded-wait budget: a wait that has not completed after this many nanoseconds of
 // %globaltimer gives up, sets g_device_error and lets the kernel unwind.
 constexpr unsigned long long kWaitNs = 2000000000ull;
+// The budget the kernels use (kWaitNs unless a test shortened it with yk_test_inject), and
+// the test-only withheld arrival: when set, block 0 of the tensor-core conv kernel's TMA
+// path skips its first stage load, so the MMA warp's wait on that stage runs out.
+__device__ unsigned long long g_wait_ns = kWaitNs;
+__device__ int g_test_withhold = 0;
 
 // ---------------- programmatic dependent launch ----------------
 // Every kernel is launched with programmatic stream serialisation, so the next kernel in
@@ -116,12 +130,13 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Returns false (and sets the device error word to `code`) if the phase did not complete
-// within kWaitNs.
+// within g_wait_ns (kWaitNs by default).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int code) {
   if (mbar_try(bar, parity)) return true;
-  unsigned long long t0 = globaltimer();
+  const unsigned long long t0 = globaltimer();
+  const unsigned long long lim = *(volatile unsigned long long*)&g_wait_ns;
   while (!mbar_try(bar, parity)) {
-    if (globaltimer() - t0 > kWaitNs) {
+    if (globaltimer() - t0 > lim) {
       atomicCAS(&g_device_error, 0, code);
       return false;
     }

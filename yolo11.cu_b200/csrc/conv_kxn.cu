@@ -326,14 +326,7 @@ static bool encode_kxn_w(CUtensorMap* m, const __half* w, int Cin, int Cout, int
 template <int BN, int MT, int CB>
 static int launch_kxn(const PatchArgs& a, const YkView* x, cudaStream_t st) {
   using Cfg = KxnCfg<BN, MT, CB>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(conv_kxn_kernel<BN, MT, CB>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)Cfg::kSmem) != cudaSuccess)
-      return check_launch("conv_kxn attr");
-    attr_set = true;
-  }
+  if (smem_attr(conv_kxn_kernel<BN, MT, CB>, (int)Cfg::kSmem) != cudaSuccess) return check_launch("conv_kxn attr");
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return YK_EUNSUP;

@@ -7,6 +7,10 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
 
 namespace yk {
@@ -55,6 +59,20 @@ bool pdl_enabled() {
 }
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;   // (kernel, device) -> bytes set
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = done[{kernel, dev}];
+  if (have >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) have = bytes;
+  return e;
+}
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) return YK_OK;
@@ -769,6 +787,15 @@ extern "C" {
 long long yk_launch_count(void) { return g_launches.load(); }
 const char* yk_last_cuda_error(void) { return g_cuda_err; }
 
+int yk_test_inject(int withhold, unsigned long long wait_ns) {
+  const unsigned long long w = wait_ns ? wait_ns : kWaitNs;
+  const int h = withhold ? 1 : 0;
+  if (cudaMemcpyToSymbol(g_wait_ns, &w, sizeof w) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_test_withhold, &h, sizeof h) != cudaSuccess)
+    return check_launch("yk_test_inject");
+  return YK_OK;
+}
+
 int yk_fetch_device_error(void) {
   int v = 0, z = 0;
   if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof v) != cudaSuccess) return YK_ECUDA;
@@ -819,9 +846,7 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
       default: break;
     }
     if (kern) {
-      if (smem > 48 * 1024 &&
-          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-              cudaSuccess)
+      if (smem > 48 * 1024 && smem_attr(kern, (int)smem) != cudaSuccess)
         return check_launch("conv_stem attr");
       launch_k(kern, grid, 128, smem, (cudaStream_t)st, dview(*x), dview(*y),
                (const __half*)p->weight, p->bias, p->s, p->p, p->act, pitch, vec, (int)rows);
@@ -859,12 +884,7 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
       long long grid = std::min<long long>(nt, (long long)nsm * YK_DW_MINB);
       grid = std::max<long long>(tcn, grid / tcn * tcn);
       const size_t smem = (2 * (size_t)kDwWin + 9 * kDwCh) * sizeof(__half);
-      static bool attr = false;
-      if (!attr) {
-        cudaFuncSetAttribute(dwconv3t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-        attr = true;
-      }
+      if (smem_attr(dwconv3t_kernel, (int)smem) != cudaSuccess) return check_launch("dwconv3t attr");
       launch_k(dwconv3t_kernel, (unsigned)grid, kDwThreads, smem, (cudaStream_t)st, dview(*x),
                dview(*y), r, (const __half*)p->weight, p->bias, p->act, tcn, txn, tyn, (int)nt);
       note_launch();
@@ -888,11 +908,7 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     }
     const size_t smem = (size_t)p->Cout * p->k * p->k * sizeof(__half);
     if (smem > 96 * 1024) return YK_EUNSUP;
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(dwconv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      attr = true;
-    }
+    if (smem_attr(dwconv_kernel, 96 * 1024) != cudaSuccess) return check_launch("dwconv attr");
     launch_k(dwconv_kernel, nblk(total, 256), 256, smem, (cudaStream_t)st, dview(*x), dview(*y), r,
                                                     (const __half*)p->weight, p->bias, p->k,
                                                     p->s, p->p, p->act, total);
@@ -944,9 +960,7 @@ int yk_maxpool5x3(const YkView* x, const YkView* y1, const YkView* y2, const YkV
     const size_t smem = 2 * plane * cbp;
     auto kern = cbp == 64 ? pool5x3_plane_kernel<64>
                 : cbp == 32 ? pool5x3_plane_kernel<32> : pool5x3_plane_kernel<8>;
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
+    if (smem > 48 * 1024 && smem_attr(kern, (int)smem) != cudaSuccess)
       return check_launch("pool5x3 attr");
     launch_k(kern, (unsigned)(x->batch * ncb), 256, smem, (cudaStream_t)st, dview(*x),
              dview(*y1), dview(*y2), dview(*y3), ncb);

@@ -299,14 +299,7 @@ conv_pair_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmW,
 template <int STAGES, int G>
 static int launch_pair(const ConvArgs& a, cudaStream_t st) {
   using Cfg = PairCfg<STAGES, G>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(conv_pair_kernel<STAGES, G>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)Cfg::kSmem) != cudaSuccess)
-      return check_launch("conv_pair attr");
-    attr_set = true;
-  }
+  if (smem_attr(conv_pair_kernel<STAGES, G>, (int)Cfg::kSmem) != cudaSuccess) return check_launch("conv_pair attr");
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return YK_EUNSUP;

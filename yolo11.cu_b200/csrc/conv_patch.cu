@@ -366,14 +366,7 @@ static bool encode_patch_x(CUtensorMap* m, const __half* x, int C, int W, int H,
 template <int BN, int MT, int BST, int WST, int G, bool T = false, int CB = 64>
 static int launch_patch(const PatchArgs& a, const YkView* x, cudaStream_t st) {
   using Cfg = PatchCfg<BN, MT, BST, WST, T, CB>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(conv_patch_kernel<BN, MT, BST, WST, G, T, CB>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)Cfg::kSmem) != cudaSuccess)
-      return check_launch("conv_patch attr");
-    attr_set = true;
-  }
+  if (smem_attr(conv_patch_kernel<BN, MT, BST, WST, G, T, CB>, (int)Cfg::kSmem) != cudaSuccess) return check_launch("conv_patch attr");
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return YK_EUNSUP;

@@ -195,6 +195,9 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
     const int batch = a.M / HWo;
     uint32_t g = 0;   // global stage counter across tiles
     const bool gather = !a.tmaA;
+    // test hook (yk_test_inject): withhold block 0's first stage (no expect-tx, no loads),
+    // so its MMA warp's bounded wait runs out and the abort path unwinds the CTA
+    const bool withhold = !gather && blockIdx.x == 0 && *(volatile int*)&g_test_withhold;
     for (int t = blockIdx.x; t < a.ntiles && !*abort_flag && (gather || tid == 0); t += gridDim.x) {
       const int m0 = (t / a.ntn) * kTM, n0 = (t % a.ntn) * BN;
       int w0[MT], h0[MT], i0[MT];      // im2col start of each sub-tile (input coords of its pixel 0)
@@ -236,7 +239,7 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
           break;
         }
         const uint32_t sA = base + s * Cfg::kStage, sB = sA + MT * Cfg::kABytes;
-        if (tid == 0) {
+        if (tid == 0 && !(withhold && g == 0)) {
           mbar_expect_tx(full_bar(s), Cfg::kBBytes + (gather ? 0 : MT * Cfg::kABytes));
           // stage kb holds K blocks q = kb*TPS + j (j < TPS), each CB channels of one tap;
           // blocks past the end read weights out of range (zeros), so they add nothing
@@ -528,14 +531,8 @@ static bool encode_im2col(CUtensorMap* m, const ConvArgs& a, int cb) {
 template <int BN, int STAGES, int MT, int G, int CB = 64, bool T = false>
 static int launch_tc(const ConvArgs& a, cudaStream_t st) {
   using Cfg = TcCfg<BN, STAGES, MT, CB, T>;
-  static bool attr_set = false;   // the attribute is per function, for all devices
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(conv_tc_kernel<BN, STAGES, MT, CB, G, T>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)Cfg::kSmem) != cudaSuccess)
-      return check_launch("conv_tc attr");
-    attr_set = true;
-  }
+  if (smem_attr(conv_tc_kernel<BN, STAGES, MT, CB, G, T>, (int)Cfg::kSmem) != cudaSuccess)
+    return check_launch("conv_tc attr");
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return YK_EUNSUP;

@@ -114,8 +114,23 @@ struct Engine {
   int* h_cnt = nullptr;
   int* h_raw = nullptr;
   cudaStream_t st = nullptr;
+  // graphs by key: the batch size B for the plain forward (input already in the slots), or
+  // frames_key(id, B) for the whole pipeline over frame binding `id`
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, float> exec_ms;
+  std::map<int, int> graph_kernels;   // kernel nodes of each kept graph
+  // Frame bindings: a fixed array of equal-size BGR u8 frames the pipeline graph reads.
+  // Host (page-locked) frames are copied into `stage` inside the graph.
+  struct Binding {
+    const uint8_t* frames = nullptr;
+    int h = 0, w = 0, count = 0;
+    bool host = false;
+    void* stage = nullptr;
+    size_t stage_bytes = 0;
+  };
+  static constexpr int kBindings = 4;
+  Binding binds[kBindings];
+  static int frames_key(int id, int B) { return ((id + 1) << 20) | B; }
   nvjpegHandle_t jpeg = nullptr;   // JPEG front end (created on first use)
   nvjpegJpegState_t jstate = nullptr;
   std::vector<void*> jbuf;         // per slot: the decoded BGR frame
@@ -136,6 +151,10 @@ struct Engine {
     cudaSetDevice(device);
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
     graphs.clear();
+    for (Binding& b : binds) {
+      if (b.stage) cudaFree(b.stage);
+      b = Binding{};
+    }
     for (cudaStream_t s : side) cudaStreamDestroy(s);
     side.clear();
     for (void* b : jbuf)
@@ -189,7 +208,12 @@ struct Engine {
   void run_post(int B);
   void forward(int B);
   void forward_streams(int B);
-  cudaGraphExec_t graph_for(int B);
+  void load_frames(int id, int B);
+  cudaGraphExec_t graph_for(int B, int bind = -1);
+  float conv_graph_ms(int B);
+  bool tc_conv(const Op& op) const {
+    return op.kind == CONV && op.g == 1 && (op.Cin % 8 == 0 || op.wpad);
+  }
 };
 
 void Engine::parse(const std::string& dir) {
@@ -778,18 +802,100 @@ void Engine::save_tuning(const char* path) const {
   fclose(f);
 }
 
-cudaGraphExec_t Engine::graph_for(int B) {
-  auto it = graphs.find(B);
+// Pipeline prologue of frame binding `id`: the H2D copy of B host frames (one copy of the
+// contiguous array) and the preprocessing of all B slots.  Detect / segment / obb models
+// letterbox every frame in one launch; classify models run their resize + crop per frame.
+void Engine::load_frames(int id, int B) {
+  const Binding& b = binds[id];
+  const size_t fb = (size_t)b.h * b.w * 3;
+  const uint8_t* src = b.frames;
+  if (b.host) {
+    CKE(cudaMemcpyAsync(b.stage, b.frames, fb * B, cudaMemcpyHostToDevice, st));
+    src = (const uint8_t*)b.stage;
+  }
+  YkView in = view(0, maxB);
+  if (cls()) {
+    for (int i = 0; i < B; i++)
+      CKY(yk_preprocess_cls(src + fb * i, b.h, b.w, &in, i, nullptr, (yk_stream_t)st));
+  } else {
+    CKY(yk_letterbox_batch(src, fb, B, b.h, b.w, &in, 0, nullptr, nullptr, nullptr,
+                           (yk_stream_t)st));
+  }
+}
+
+int count_kernel_nodes(cudaGraph_t g) {
+  size_t n = 0;
+  if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess) return -1;
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (n && cudaGraphGetNodes(g, nodes.data(), &n) != cudaSuccess) return -1;
+  int k = 0;
+  for (size_t i = 0; i < n; i++) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) k++;
+  }
+  return k;
+}
+
+// Device time of the tensor-core convs of one batch-B forward as they run inside a graph:
+// the planned op list's tcgen05 convs (the stem GEMM with its im2col) captured alone, in
+// order, on one stream, with programmatic dependent launch when enabled, and replayed
+// (3 warm-up + 10 timed launches, the better of two rounds).  The convs read what the last
+// forward left in their input buffers, so shapes and data are those of the real forward.
+float Engine::conv_graph_ms(int B) {
+  cudaGraph_t g;
+  g_pdl_override = pdl_enabled() ? 1 : 0;
+  CKE(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  try {
+    for (const Op& op : ops)
+      if (tc_conv(op)) run_op(op, B);
+  } catch (...) {
+    g_pdl_override = -1;
+    cudaGraph_t dummy;
+    cudaStreamEndCapture(st, &dummy);
+    if (dummy) cudaGraphDestroy(dummy);
+    throw;
+  }
+  g_pdl_override = -1;
+  CKE(cudaStreamEndCapture(st, &g));
+  cudaGraphExec_t ge;
+  const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  CKE(e);
+  cudaEvent_t e0, e1;
+  CKE(cudaEventCreate(&e0));
+  CKE(cudaEventCreate(&e1));
+  float best = 1e30f;
+  for (int round = 0; round < 2; round++) {
+    for (int i = 0; i < 3; i++) CKE(cudaGraphLaunch(ge, st));
+    CKE(cudaEventRecord(e0, st));
+    for (int i = 0; i < 10; i++) CKE(cudaGraphLaunch(ge, st));
+    CKE(cudaEventRecord(e1, st));
+    CKE(cudaEventSynchronize(e1));
+    float ms = 0;
+    CKE(cudaEventElapsedTime(&ms, e0, e1));
+    best = std::min(best, ms / 10.f);
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaGraphExecDestroy(ge);
+  return best;
+}
+
+cudaGraphExec_t Engine::graph_for(int B, int bind) {
+  const int key = bind >= 0 ? frames_key(bind, B) : B;
+  auto it = graphs.find(key);
   if (it != graphs.end()) return it->second;
   // Capture the forward once with programmatic dependent launch between the kernels and,
   // when that is enabled, once without; keep the faster.  Overlapping each kernel's set-up
   // with its predecessor's tail pays at small batches, where every kernel is a few
   // microseconds; at large batches the early-resident waiting CTAs can cost a little.
+  int kernels = 0, best_kernels = 0;
   auto capture = [&](int pdl, bool multi = false) {
     cudaGraph_t g;
     g_pdl_override = pdl;
     CKE(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     try {
+      if (bind >= 0) load_frames(bind, B);
       if (multi) forward_streams(B);
       else forward(B);
     } catch (...) {
@@ -801,6 +907,7 @@ cudaGraphExec_t Engine::graph_for(int B) {
     }
     g_pdl_override = -1;
     CKE(cudaStreamEndCapture(st, &g));
+    kernels = count_kernel_nodes(g);
     cudaGraphExec_t ge;
     const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
     cudaGraphDestroy(g);
@@ -822,6 +929,7 @@ cudaGraphExec_t Engine::graph_for(int B) {
     return ms / 10.f;
   };
   cudaGraphExec_t best = capture(0);
+  best_kernels = kernels;
   float best_ms = time10(best);
   if (pdl_enabled()) {
     cudaGraphExec_t alt = nullptr;
@@ -833,6 +941,7 @@ cudaGraphExec_t Engine::graph_for(int B) {
       if (alt_ms < best_ms) {
         std::swap(alt, best);
         best_ms = alt_ms;
+        best_kernels = kernels;
       }
     } catch (...) {
       if (alt) cudaGraphExecDestroy(alt);
@@ -855,6 +964,7 @@ cudaGraphExec_t Engine::graph_for(int B) {
       if (force || alt_ms < best_ms) {
         std::swap(alt, best);
         best_ms = alt_ms;
+        best_kernels = kernels;
       }
     } catch (...) {
       if (alt) cudaGraphExecDestroy(alt);
@@ -865,8 +975,9 @@ cudaGraphExec_t Engine::graph_for(int B) {
     }
     cudaGraphExecDestroy(alt);
   }
-  graphs[B] = best;
-  exec_ms[B] = best_ms;
+  graphs[key] = best;
+  exec_ms[key] = best_ms;
+  graph_kernels[key] = best_kernels;
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   return best;
@@ -1109,6 +1220,125 @@ void yolo_sync(void* h) {
 void yolo_run(void* h, int B) {
   yolo_run_async(h, B);
   yolo_sync(h);
+}
+
+int yolo_bind_frames(void* h, int id, const unsigned char* frames, int height, int width,
+                     int count, int host) {
+  return guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || id < 0 || id >= Engine::kBindings || !frames || height < 1 || width < 1 ||
+        count < 1 || count > e->maxB)
+      throw Error("yolo_bind_frames: bad arguments");
+    DeviceScope ds(e->device);
+    cudaPointerAttributes pa;
+    CKE(cudaPointerGetAttributes(&pa, frames));
+    if (host && pa.type != cudaMemoryTypeHost)
+      throw Error("yolo_bind_frames: host frames must be page-locked (cudaMallocHost / cudaHostRegister)");
+    if (!host && !((pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged) &&
+                   pa.device == e->device))
+      throw Error("yolo_bind_frames: frames are not device memory of the handle's GPU");
+    CKE(cudaStreamSynchronize(e->st));        // no graph of this binding is in flight
+    for (auto it = e->graphs.begin(); it != e->graphs.end();) {
+      if ((it->first >> 20) == id + 1) {
+        cudaGraphExecDestroy(it->second);
+        e->exec_ms.erase(it->first);
+        it = e->graphs.erase(it);
+      } else {
+        ++it;
+      }
+    }
+    Engine::Binding& b = e->binds[id];
+    const size_t need = host ? (size_t)height * width * 3 * count : 0;
+    if (b.stage_bytes < need) {
+      if (b.stage) CKE(cudaFree(b.stage));
+      b.stage = nullptr;
+      b.stage_bytes = 0;
+      CKE(cudaMalloc(&b.stage, need));
+      b.stage_bytes = need;
+    }
+    b.frames = frames;
+    b.h = height;
+    b.w = width;
+    b.count = count;
+    b.host = host != 0;
+    return 0;
+  }, -1);
+}
+
+int yolo_run_frames_async(void* h, int id, int B) {
+  return guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || id < 0 || id >= Engine::kBindings || !e->binds[id].frames || B < 1 ||
+        B > e->binds[id].count)
+      throw Error("yolo_run_frames: bad binding or batch");
+    DeviceScope ds(e->device);
+    const Engine::Binding& b = e->binds[id];
+    SlotGeom g;
+    if (!e->cls()) {   // the letterbox geometry (engine/engine.cu:1704-1713)
+      const Buf& ib = e->bufs[e->tens[0].buf];
+      g.scale = std::min((float)ib.H / b.h, (float)ib.W / b.w);
+      const int nh = (int)roundf(b.h * g.scale), nw = (int)roundf(b.w * g.scale);
+      g.top = (ib.H - nh) / 2;
+      g.left = (ib.W - nw) / 2;
+    }
+    CKE(cudaGraphLaunch(e->graph_for(B, id), e->st));
+    for (int i = 0; i < B; i++) e->slots[i] = g;
+    return 0;
+  }, -1);
+}
+
+int yolo_run_frames(void* h, int id, int B) {
+  if (yolo_run_frames_async(h, id, B) != 0) return -1;
+  yolo_sync(h);
+  return yolo_last_error()[0] ? -1 : 0;
+}
+
+float yolo_frames_exec_ms(void* h, int id, int B) {
+  return guarded([&]() -> float {
+    Engine* e = as_engine(h);
+    if (!e || id < 0 || id >= Engine::kBindings || !e->binds[id].frames || B < 1 ||
+        B > e->binds[id].count)
+      throw Error("yolo_frames_exec_ms: bad binding or batch");
+    DeviceScope ds(e->device);
+    e->graph_for(B, id);
+    return e->exec_ms[Engine::frames_key(id, B)];
+  }, -1.f);
+}
+
+int yolo_graph_kernels(void* h, int id, int B) {
+  return guarded([&]() -> int {
+    Engine* e = as_engine(h);
+    if (!e || id < -1 || id >= Engine::kBindings || B < 1 || B > e->maxB)
+      throw Error("yolo_graph_kernels: bad arguments");
+    const int key = id >= 0 ? Engine::frames_key(id, B) : B;
+    auto it = e->graph_kernels.find(key);
+    return it == e->graph_kernels.end() ? 0 : it->second;
+  }, -1);
+}
+
+float yolo_conv_exec_ms(void* h, int B, int* nconv) {
+  return guarded([&]() -> float {
+    Engine* e = as_engine(h);
+    if (!e || B < 1 || B > e->maxB) throw Error("yolo_conv_exec_ms: bad batch");
+    DeviceScope ds(e->device);
+    if (nconv) {
+      *nconv = 0;
+      for (const Op& op : e->ops) *nconv += e->tc_conv(op);
+    }
+    return e->conv_graph_ms(B);
+  }, -1.f);
+}
+
+int yolo_get_batch(void* h, int B, YoloDet* out, int cap, int* counts) {
+  Engine* e = as_engine(h);
+  if (!e || e->obb() || B < 1 || B > e->maxB || cap < 0 || (!out && cap > 0) || !counts)
+    return -1;
+  int total = 0;
+  for (int s = 0; s < B; s++) {
+    counts[s] = yolo_get(h, s, out ? out + (size_t)s * cap : nullptr, cap);
+    total += counts[s];
+  }
+  return total;
 }
 
 int yolo_get(void* h, int slot, YoloDet* out, int cap) {

@@ -14,47 +14,98 @@
 namespace yk {
 
 // ---------------- letterbox (engine/engine.cu:968-998) ----------------
-__global__ void letterbox_kernel(const uint8_t* __restrict__ src, int sh, int sw, __half* dst,
-                                 int dh, int dw, int dstride, float scale, int top, int left,
-                                 int nh, int nw) {
-  pdl_wait();     // inputs come from the previous kernel
+// One launch letterboxes a batch of equal-size frames: grid (row blocks, frames).  Each
+// thread owns 8 consecutive output columns of kLbRows rows; their horizontal sampling
+// (source byte offsets, weights, inside/outside) is computed once and reused on every row,
+// and the 8 pixels (24 fp16) leave as three 16-byte stores when the view is a dense
+// 3-channel image whose width is a multiple of 8 (else element stores).  Source bytes come
+// through the read-only cache: neighbouring threads read neighbouring bytes of the same two
+// source rows, so each row is fetched from DRAM about once.  The arithmetic is the
+// reference's formula in explicitly rounded fp32 (src = (dst - off + 0.5) / scale - 0.5,
+// bilinear weights, /255, pad 114), so the C oracle reproduces it bit for bit.
+constexpr int kLbRows = 8;
+
+template <bool kVec>
+__global__ void __launch_bounds__(256) letterbox_kernel(
+    const uint8_t* __restrict__ src, size_t src_frame, int sh, int sw, __half* dst,
+    size_t dst_frame, int dh, int dw, int dstride, float scale, int top, int left, int nh,
+    int nw) {
+  pdl_wait();     // the destination may still be read by the previous graph's kernels
   pdl_trigger();
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= dh * dw) return;
-  const int x = idx % dw, y = idx / dw;
-  float r, g, b;
-  if (y < top || y >= top + nh || x < left || x >= left + nw) {
-    r = g = b = 114.f;
-  } else {
-    const float fy = DM_SUB(DM_DIV(DM_ADD((float)(y - top), 0.5f), scale), 0.5f);
-    const float fx = DM_SUB(DM_DIV(DM_ADD((float)(x - left), 0.5f), scale), 0.5f);
-    int y0 = (int)floorf(fy), x0 = (int)floorf(fx);
-    const float wy = DM_SUB(fy, (float)y0), wx = DM_SUB(fx, (float)x0);
-    const int y1 = min(y0 + 1, sh - 1), x1 = min(x0 + 1, sw - 1);
-    y0 = max(y0, 0);
-    x0 = max(x0, 0);
-    const uint8_t* p00 = src + ((size_t)y0 * sw + x0) * 3;
-    const uint8_t* p01 = src + ((size_t)y0 * sw + x1) * 3;
-    const uint8_t* p10 = src + ((size_t)y1 * sw + x0) * 3;
-    const uint8_t* p11 = src + ((size_t)y1 * sw + x1) * 3;
-    const float w00 = DM_MUL(DM_SUB(1.f, wy), DM_SUB(1.f, wx));
-    const float w01 = DM_MUL(DM_SUB(1.f, wy), wx);
-    const float w10 = DM_MUL(wy, DM_SUB(1.f, wx));
-    const float w11 = DM_MUL(wy, wx);
-    float v[3];
+  const int xb = threadIdx.x * 8;
+  if (xb >= dw) return;
+  const uint8_t* img = src + (size_t)blockIdx.y * src_frame;
+  __half* out = dst + (size_t)blockIdx.y * dst_frame;
+  int o0[8], o1[8];
+  float wx[8];
+  unsigned inside = 0;
 #pragma unroll
-    for (int c = 0; c < 3; c++) {
-      float t = DM_MUL((float)p00[c], w00);
-      t = DM_ADD(t, DM_MUL((float)p01[c], w01));
-      t = DM_ADD(t, DM_MUL((float)p10[c], w10));
-      v[c] = DM_ADD(t, DM_MUL((float)p11[c], w11));
-    }
-    b = v[0]; g = v[1]; r = v[2];
+  for (int j = 0; j < 8; j++) {
+    const int x = xb + j;
+    const float fx = DM_SUB(DM_DIV(DM_ADD((float)(x - left), 0.5f), scale), 0.5f);
+    int x0 = (int)floorf(fx);
+    wx[j] = DM_SUB(fx, (float)x0);
+    const int x1 = min(x0 + 1, sw - 1);
+    x0 = max(x0, 0);
+    o0[j] = x0 * 3;
+    o1[j] = x1 * 3;
+    if (x < dw && x >= left && x < left + nw) inside |= 1u << j;
   }
-  __half* o = dst + (size_t)idx * dstride;
-  o[0] = __float2half_rn(DM_DIV(r, 255.f));   // RGB order
-  o[1] = __float2half_rn(DM_DIV(g, 255.f));
-  o[2] = __float2half_rn(DM_DIV(b, 255.f));
+  const __half pad = __float2half_rn(DM_DIV(114.f, 255.f));
+  const int y_end = min(dh, (int)(blockIdx.x + 1) * kLbRows);
+  for (int y = blockIdx.x * kLbRows; y < y_end; y++) {
+    __align__(16) __half px[24];
+    const bool row_in = y >= top && y < top + nh;
+    if (!row_in || !inside) {
+#pragma unroll
+      for (int i = 0; i < 24; i++) px[i] = pad;
+    } else {
+      const float fy = DM_SUB(DM_DIV(DM_ADD((float)(y - top), 0.5f), scale), 0.5f);
+      int y0 = (int)floorf(fy);
+      const float wy = DM_SUB(fy, (float)y0);
+      const int y1 = min(y0 + 1, sh - 1);
+      y0 = max(y0, 0);
+      const uint8_t* r0 = img + (size_t)y0 * sw * 3;
+      const uint8_t* r1 = img + (size_t)y1 * sw * 3;
+      const float wy1 = DM_SUB(1.f, wy);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        if (!((inside >> j) & 1u)) {
+          px[3 * j] = px[3 * j + 1] = px[3 * j + 2] = pad;
+          continue;
+        }
+        const float wx1 = DM_SUB(1.f, wx[j]);
+        const float w00 = DM_MUL(wy1, wx1), w01 = DM_MUL(wy1, wx[j]);
+        const float w10 = DM_MUL(wy, wx1), w11 = DM_MUL(wy, wx[j]);
+        float v[3];
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+          float t = DM_MUL((float)__ldg(r0 + o0[j] + c), w00);
+          t = DM_ADD(t, DM_MUL((float)__ldg(r0 + o1[j] + c), w01));
+          t = DM_ADD(t, DM_MUL((float)__ldg(r1 + o0[j] + c), w10));
+          v[c] = DM_ADD(t, DM_MUL((float)__ldg(r1 + o1[j] + c), w11));
+        }
+        // BGR in, RGB out
+        px[3 * j] = __float2half_rn(DM_DIV(v[2], 255.f));
+        px[3 * j + 1] = __float2half_rn(DM_DIV(v[1], 255.f));
+        px[3 * j + 2] = __float2half_rn(DM_DIV(v[0], 255.f));
+      }
+    }
+    if (kVec) {
+      int4* o = (int4*)(out + ((size_t)y * dw + xb) * 3);
+      const int4* p = (const int4*)px;
+      o[0] = p[0];
+      o[1] = p[1];
+      o[2] = p[2];
+    } else {
+      for (int j = 0; j < 8 && xb + j < dw; j++) {
+        __half* o = out + ((size_t)y * dw + xb + j) * dstride;
+        o[0] = px[3 * j];
+        o[1] = px[3 * j + 1];
+        o[2] = px[3 * j + 2];
+      }
+    }
+  }
 }
 
 // ---------------- decode (engine/engine.cu:848-906) ----------------
@@ -658,22 +709,38 @@ using namespace yk;
 
 extern "C" {
 
-int yk_letterbox(const uint8_t* bgr, int sh, int sw, const YkView* y, int slot,
-                 float* scale_out, int* top_out, int* left_out, yk_stream_t st) {
-  if (!bgr || sh < 1 || sw < 1 || !view_ok(y) || y->C != 3 || slot < 0 || slot >= y->batch)
+int yk_letterbox_batch(const uint8_t* bgr, size_t frame_stride, int n, int sh, int sw,
+                       const YkView* y, int slot0, float* scale_out, int* top_out,
+                       int* left_out, yk_stream_t st) {
+  if (!bgr || n < 1 || sh < 1 || sw < 1 || !view_ok(y) || y->C != 3 || slot0 < 0 ||
+      slot0 + n > y->batch || y->W > 2048 || (n > 1 && frame_stride < (size_t)sh * sw * 3))
     return YK_EINVAL;
+  // geometry as yolo_preprocess computes it (engine/engine.cu:1704-1713)
   const float scale = std::min((float)y->H / sh, (float)y->W / sw);
   const int nh = (int)roundf(sh * scale), nw = (int)roundf(sw * scale);
   const int top = (y->H - nh) / 2, left = (y->W - nw) / 2;
   if (scale_out) *scale_out = scale;
   if (top_out) *top_out = top;
   if (left_out) *left_out = left;
-  __half* dst = (__half*)y->ptr + y->coff + (size_t)slot * y->H * y->W * y->stride;
-  const int npx = y->H * y->W;
-  launch_k(letterbox_kernel, (npx + 255) / 256, 256, 0, (cudaStream_t)st, 
-      bgr, sh, sw, dst, y->H, y->W, y->stride, scale, top, left, nh, nw);
+  const size_t dframe = (size_t)y->H * y->W * y->stride;
+  __half* dst = (__half*)y->ptr + y->coff + (size_t)slot0 * dframe;
+  const bool vec = y->stride == 3 && y->coff == 0 && y->W % 8 == 0 &&
+                   ((uintptr_t)y->ptr & 15) == 0;
+  const int threads = ((y->W + 7) / 8 + 31) / 32 * 32;
+  const dim3 grid((y->H + kLbRows - 1) / kLbRows, n);
+  if (vec)
+    launch_k(letterbox_kernel<true>, grid, threads, 0, (cudaStream_t)st, bgr, frame_stride, sh,
+             sw, dst, dframe, y->H, y->W, y->stride, scale, top, left, nh, nw);
+  else
+    launch_k(letterbox_kernel<false>, grid, threads, 0, (cudaStream_t)st, bgr, frame_stride, sh,
+             sw, dst, dframe, y->H, y->W, y->stride, scale, top, left, nh, nw);
   note_launch();
   return check_launch("letterbox");
+}
+
+int yk_letterbox(const uint8_t* bgr, int sh, int sw, const YkView* y, int slot,
+                 float* scale_out, int* top_out, int* left_out, yk_stream_t st) {
+  return yk_letterbox_batch(bgr, 0, 1, sh, sw, y, slot, scale_out, top_out, left_out, st);
 }
 
 size_t yk_post_workspace_bytes(int batch, int anchors) {
@@ -713,12 +780,7 @@ int yk_nms(int batch, int anchors, float iou, int max_out, const YkPost* post, y
     return YK_EINVAL;
   WsLayout L = ws_layout(anchors);
   if (post->ws_bytes < (size_t)batch * L.per_img) return YK_EINVAL;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(nms_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kNmsDynSmem);
-    attr = true;
-  }
+  if (smem_attr(nms_kernel, (int)kNmsDynSmem) != cudaSuccess) return check_launch("nms attr");
   launch_k(nms_kernel, batch, kNmsThreads, kNmsDynSmem, (cudaStream_t)st, iou, max_out,
            (uint8_t*)post->ws, L, post->outdets, post->outidx, post->outcnt, post->rawcnt);
   note_launch();
@@ -782,7 +844,12 @@ extern "C" int yk_decode_nms_static(const YkLevel* levels, int nlevels, int batc
   static std::mutex mu;
   static void* addr[128] = {};
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return check_launch("static ws");
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("static ws");
+  if (dev < 0 || dev >= 128) {
+    snprintf(g_cuda_err, sizeof g_cuda_err,
+             "yk_decode_nms_static: device ordinal %d outside the 128 this entry point tracks", dev);
+    return YK_EUNSUP;
+  }
   void* ws = nullptr;
   {
     std::lock_guard<std::mutex> lk(mu);

@@ -1,7 +1,12 @@
 // yolocuda — command-line front end of the B200 engine, built on the yolo.h C ABI only.
 // Same modes and arguments as the reference CLI (engine/engine.cu:1638-1651, 1796-2096):
-//   yolocuda <detect|pipeline|bench|profile|dump> [model-dir] [iters] [--batch N] [--save-masks]
+//   yolocuda <detect|pipeline|bench|profile|dump> [model-dir] [iters] [--image path.jpg]
+//            [--batch N] [--save-masks]
 // Additions: `pipeline` and `bench` report p50/p99 besides the mean; --iou / --conf.
+// `pipeline` replays one CUDA graph per iteration (H2D of the raw frames + letterbox of the
+// batch + net + decode + NMS + D2H, yolo_bind_frames / yolo_run_frames).  --image decodes a
+// JPEG on the GPU (nvJPEG, yolo_preprocess_jpeg); the reference decodes any format with
+// stb_image on the host (engine/engine.cu:1630-1636, 1891-1897).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -39,10 +44,12 @@ static std::vector<char> slurp(const std::string& p) {
 
 static void usage() {
   printf("yolocuda - B200 (sm_100a) inference engine for YOLOv8 / YOLO11\n\n"
-         "usage: yolocuda <mode> [model-dir] [iters] [--batch N] [--save-masks] [--iou X] [--conf X]\n\n"
+         "usage: yolocuda <mode> [model-dir] [iters] [--image path.jpg] [--batch N] [--save-masks]\n"
+         "                [--iou X] [--conf X]\n\n"
          "modes:\n"
-         "  detect    one inference on the directory's input.f16, print detections (segment:\n"
-         "            --save-masks; obb: oriented boxes; classify: top-5 with names.txt)\n"
+         "  detect    one inference on the directory's input.f16 (or --image, a JPEG decoded on\n"
+         "            the GPU), print detections (segment: --save-masks; obb: oriented boxes;\n"
+         "            classify: top-5 with names.txt)\n"
          "  bench     net + post-processing CUDA-graph latency (mean / p50 / p99)\n"
          "  pipeline  end to end: H2D of the raw frame + preprocessing (letterbox, or the\n"
          "            classify resize + crop) + net + post-processing\n"
@@ -138,11 +145,13 @@ int main(int argc, char** argv) {
   std::string dir = "build/yolo11n";
   int iters = -1, batch = 1;
   bool save_masks = false;
+  std::string image;
   YoloOptions opt;
   yolo_default_options(&opt);
   for (int i = 2; i < argc; i++) {
     std::string a = argv[i];
     if (a == "--batch" && i + 1 < argc) batch = atoi(argv[++i]);
+    else if (a == "--image" && i + 1 < argc) image = argv[++i];
     else if (a == "--iou" && i + 1 < argc) opt.iou = (float)atof(argv[++i]);
     else if (a == "--conf" && i + 1 < argc) opt.conf = (float)atof(argv[++i]);
     else if (a == "--save-masks") save_masks = true;
@@ -163,6 +172,15 @@ int main(int argc, char** argv) {
     return 1;
   }
   if (load_input(h, dir, batch)) return 1;
+  if (!image.empty() && mode == "detect") {   // any JPEG: nvJPEG decode + preprocessing per slot
+    auto bytes = slurp(image);
+    if (bytes.empty()) { fprintf(stderr, "cannot read image %s\n", image.c_str()); return 1; }
+    for (int b = 0; b < batch; b++)
+      if (yolo_preprocess_jpeg(h, (const unsigned char*)bytes.data(), bytes.size(), b) != 0) {
+        fprintf(stderr, "image %s: %s\n", image.c_str(), yolo_last_error());
+        return 1;
+      }
+  }
 
   if (mode == "dump") {
     if (system(("mkdir -p " + dir + "/gpu").c_str()) != 0) return 1;
@@ -246,7 +264,7 @@ int main(int argc, char** argv) {
       }
       printf("  %s\n", same ? "(consistent)" : "(MISMATCH!)");
     }
-    print_dets(h, 0, false);
+    print_dets(h, 0, !image.empty());
     int ph, pw;
     yolo_mask_dim(h, &ph, &pw);
     if (save_masks && ph) {
@@ -268,10 +286,9 @@ int main(int argc, char** argv) {
     }
   } else if (mode == "pipeline" || mode == "bench") {
     const int it = iters > 0 ? iters : 300;
-    cudaStream_t st = yolo_stream(h);
-    unsigned char *himg = nullptr, *dimg = nullptr;
-    int sh = 0, sw = 0;
-    if (mode == "pipeline") {
+    unsigned char* himg = nullptr;
+    if (mode == "pipeline") {   // the exporter's raw frame, pinned, bound as the graph's input
+      int sh = 0, sw = 0;
       FILE* fd = fopen((dir + "/bus_raw.txt").c_str(), "r");
       if (!fd || fscanf(fd, "%d %d", &sh, &sw) != 2) { fprintf(stderr, "no bus_raw.txt\n"); return 1; }
       fclose(fd);
@@ -279,37 +296,40 @@ int main(int argc, char** argv) {
       if (raw.size() != (size_t)sh * sw * 3) { fprintf(stderr, "bad bus_raw.u8\n"); return 1; }
       CK(cudaMallocHost(&himg, raw.size() * batch));
       for (int b = 0; b < batch; b++) memcpy(himg + b * raw.size(), raw.data(), raw.size());
-      CK(cudaMalloc(&dimg, raw.size() * batch));
+      if (yolo_bind_frames(h, 0, himg, sh, sw, batch, 1) != 0) {
+        fprintf(stderr, "bind: %s\n", yolo_last_error());
+        return 1;
+      }
     }
-    yolo_exec_ms(h, batch);   // capture + calibrate
+    const float graph_ms = himg ? yolo_frames_exec_ms(h, 0, batch) : yolo_exec_ms(h, batch);
+    std::vector<YoloDet> d((size_t)300 * batch);
+    std::vector<int> counts(batch);
     std::vector<double> lat;
     for (int i = 0; i < 20 + it; i++) {
       auto t0 = std::chrono::steady_clock::now();
       if (himg) {
-        size_t fb = (size_t)sh * sw * 3;
-        CK(cudaMemcpyAsync(dimg, himg, fb * batch, cudaMemcpyHostToDevice, st));
-        for (int b = 0; b < batch; b++)
-          (yolo_task(h) == 2 ? yolo_preprocess_cls : yolo_preprocess)(h, dimg + b * fb, sh, sw, b);
+        if (yolo_run_frames(h, 0, batch) != 0) { fprintf(stderr, "run: %s\n", yolo_last_error()); return 1; }
+      } else {
+        yolo_run(h, batch);
       }
-      yolo_run(h, batch);
-      std::vector<YoloDet> d(300);
-      for (int b = 0; b < batch; b++) yolo_get(h, b, d.data(), 300);
+      if (yolo_task(h) != 1 && yolo_task(h) != 2) yolo_get_batch(h, batch, d.data(), 300, counts.data());
       auto t1 = std::chrono::steady_clock::now();
       if (i >= 20) lat.push_back(std::chrono::duration<double, std::milli>(t1 - t0).count());
     }
+    if (*yolo_last_error()) { fprintf(stderr, "run: %s\n", yolo_last_error()); return 1; }
     double mean = 0;
     for (double v : lat) mean += v;
     mean /= lat.size();
     printf("%s (B=%d): mean %.3f ms  p50 %.3f ms  p99 %.3f ms  (%.1f frames/s at p50); "
            "graph exec %.3f ms\n",
            mode == "pipeline"
-               ? (yolo_task(h) == 2 ? "end-to-end pipeline (H2D + preprocess + net + probs D2H)"
-                                    : "end-to-end pipeline (H2D + preprocess + net + decode + NMS)")
+               ? (yolo_task(h) == 2 ? "end-to-end pipeline graph (H2D + preprocess + net + probs D2H)"
+                                    : "end-to-end pipeline graph (H2D + letterbox + net + decode + NMS + D2H)")
                : (yolo_task(h) == 2 ? "cuda graph (net + softmax + probs D2H)"
                                     : "cuda graph (net + decode + NMS)"),
-           batch, mean, pct(lat, 0.5), pct(lat, 0.99), 1000.0 * batch / pct(lat, 0.5),
-           yolo_exec_ms(h, batch));
-    if (himg) { cudaFreeHost(himg); cudaFree(dimg); }
+           batch, mean, pct(lat, 0.5), pct(lat, 0.99), 1000.0 * batch / pct(lat, 0.5), graph_ms);
+    if (mode == "pipeline" && yolo_task(h) != 2) print_dets(h, 0, true);
+    if (himg) cudaFreeHost(himg);
   } else if (mode == "profile") {
     std::vector<float> ms(4096);
     int n = yolo_profile(h, batch, 50, ms.data(), (int)ms.size());

@@ -64,6 +64,9 @@ _SIGS = {
     "yk_attn": (C.c_int, [_P(YkView), _P(YkView), C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "yk_letterbox": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _P(YkView), C.c_int,
                                _P(C.c_float), _P(C.c_int), _P(C.c_int), C.c_void_p]),
+    "yk_letterbox_batch": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_int,
+                                     _P(YkView), C.c_int, _P(C.c_float), _P(C.c_int),
+                                     _P(C.c_int), C.c_void_p]),
     "yk_post_workspace_bytes": (C.c_size_t, [C.c_int, C.c_int]),
     "yk_obb_workspace_bytes": (C.c_size_t, [C.c_int, C.c_int]),
     "yk_decode_obb": (C.c_int, [_P(YkLevel), C.c_int, C.c_int, C.c_int, C.c_float, C.c_void_p,
@@ -83,6 +86,7 @@ _SIGS = {
                                        C.c_float, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_void_p]),
     "yk_fetch_device_error": (C.c_int, []),
+    "yk_test_inject": (C.c_int, [C.c_int, C.c_ulonglong]),
     "yk_last_cuda_error": (C.c_char_p, []),
     "yk_launch_count": (C.c_longlong, []),
     # engine ABI (include/yolo.h)
@@ -107,6 +111,14 @@ _SIGS = {
     "yolo_destroy": (None, [C.c_void_p]),
     "yolo_last_error": (C.c_char_p, []),
     "yolo_raw_count": (C.c_int, [C.c_void_p, C.c_int]),
+    "yolo_bind_frames": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                   C.c_int]),
+    "yolo_run_frames_async": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "yolo_run_frames": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "yolo_frames_exec_ms": (C.c_float, [C.c_void_p, C.c_int, C.c_int]),
+    "yolo_graph_kernels": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "yolo_conv_exec_ms": (C.c_float, [C.c_void_p, C.c_int, _P(C.c_int)]),
+    "yolo_get_batch": (C.c_int, [C.c_void_p, C.c_int, _P(YoloDet), C.c_int, _P(C.c_int)]),
     "yolo_run_op": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
     "yolo_num_ops": (C.c_int, [C.c_void_p]),
     "yolo_tensor_view": (C.c_int, [C.c_void_p, C.c_int, _P(C.c_void_p), _P(C.c_int),
@@ -207,6 +219,31 @@ class Engine:
         ids, probs = (C.c_int * k)(), (C.c_float * k)()
         n = self.lib.yolo_get_cls(self.h, slot, ids, probs, k)
         return list(ids[:n]), list(probs[:n])
+
+    def bind_frames(self, id: int, ptr: int, h: int, w: int, count: int, host: bool):
+        if self.lib.yolo_bind_frames(self.h, id, C.c_void_p(ptr), h, w, count, int(host)) != 0:
+            raise RuntimeError(self.lib.yolo_last_error().decode())
+
+    def run_frames_async(self, id: int, B: int):
+        if self.lib.yolo_run_frames_async(self.h, id, B) != 0:
+            raise RuntimeError(self.lib.yolo_last_error().decode())
+
+    def run_frames(self, id: int, B: int):
+        if self.lib.yolo_run_frames(self.h, id, B) != 0:
+            raise RuntimeError(self.lib.yolo_last_error().decode())
+
+    def frames_exec_ms(self, id: int, B: int) -> float:
+        return self.lib.yolo_frames_exec_ms(self.h, id, B)
+
+    def get_batch(self, B: int, cap: int | None = None):
+        """Detections of slots 0..B-1 (one C call): list of per-slot lists."""
+        cap = self.max_det if cap is None else cap
+        arr = (YoloDet * (cap * B))()
+        cnt = (C.c_int * B)()
+        if self.lib.yolo_get_batch(self.h, B, arr, cap, cnt) < 0:
+            raise RuntimeError("yolo_get_batch failed")
+        return [[(d.x1, d.y1, d.x2, d.y2, d.score, d.cls) for d in arr[s * cap:s * cap + cnt[s]]]
+                for s in range(B)]
 
     def run(self, B: int):
         self.lib.yolo_run(self.h, B)
