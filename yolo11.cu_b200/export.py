@@ -1,30 +1,36 @@
 """Model-directory writer: torch YOLO module -> flat primitive-op graph + fp16 OHWI weights.
 
-Produces the reference's on-disk model format, byte for byte the same as the reference
-exporter (``export/export.py``) given the same modules:
+Writes the on-disk model format the engine loads (the reference's format, parsed by
+``engine/engine.cu:88-141``):
 
-    model.graph   text graph (``YOLO11GRAPH 2`` / ``TASK`` header, ``B`` buffers, ``T`` views,
-                  op lines), parsed by the engine (reference parser ``engine/engine.cu:88-141``)
-    weights.f16   every conv weight, fp16, OHWI = [Cout][kh][kw][Cin/g]
-    bias.f32      every conv bias, fp32
+    model.graph   ``YOLO11GRAPH 2`` / ``TASK`` header, ``B`` buffers, ``T`` channel views,
+                  op lines
+    weights.f16   every conv weight, fp16, OHWI = [Cout][kh][kw][Cin/g], in CONV-op order
+    bias.f32      every conv bias, fp32, same order
     input.f16     letterboxed frame 0, NHWC fp16 (S x S x 3), RGB, /255
     bus_raw.u8 / bus_raw.txt   the raw BGR frame and its "h w" (CLI ``pipeline`` input)
 
-Graph semantics (reference ``export/export.py:319-441``):
-  * tensor 0 is the S x S x 3 input; every tensor is a (buffer, channel offset, C) view;
-  * concats are zero-copy: the concat buffer is allocated up front and each producer writes
-    its channel slice; a producer that feeds a second concat gets a COPYC;
-  * composite modules decompose into CONV / ADD / MAXPOOL5 / UPSAMPLE2 / COPYC / ATTN / PS2;
-  * the head emits DECODE (detect) or DECODESEG + a final MASKS op (segment);
-  * cls-branch widths are zero-padded to multiples of 8 (pad rows w=0, b=0).
+Design: two passes.
 
-The emission order (which fixes every buffer, view and op index, and so the per-op
-``opNNN`` numbering of the parity fixtures) follows the reference walker step for step.
+1. Lowering (``_Lowering``) walks the layer list and turns every module into *declarations*
+   (``Slab``: a buffer; ``Span``: a channel range of a slab) and *instructions* (``Instr``),
+   all held as Python objects; nothing is numbered and no weight is packed yet.  Each
+   composite module has one recipe below saying which slabs/spans it declares, in which
+   order, and which instructions it issues.  Concats are zero-copy: a concat's slab is
+   declared before the walk and every producer writes its span; a producer that feeds a
+   second concat (or the input, or another concat) is copied in with COPYC.
+2. Packing (``_Program.pack``) numbers slabs and spans in declaration order, lays weights
+   and biases out in CONV-instruction order, and renders the text.  A conv's weights are
+   zero-extended to the channel counts of the spans it reads and writes, which is how the
+   head's class / angle branches get their multiple-of-8 widths (pad rows w = 0, b = 0).
+
+The declaration and instruction order fixes every buffer, view and op index (and so the
+``opNNN`` numbering of the parity fixtures); it is the reference exporter's
+(``export/export.py:319-441``), which ``tests/test_oracle_golden.py`` checks byte for byte.
 """
 from __future__ import annotations
 
 import os
-from dataclasses import dataclass, field
 
 import numpy as np
 import torch
@@ -35,334 +41,357 @@ from . import nn as ynn
 ACT_NONE, ACT_SILU = 0, 1
 
 
-@dataclass
-class GraphBuilder:
-    bufs: list = field(default_factory=list)     # (H, W, Ctot)
-    tens: list = field(default_factory=list)     # (buf, coff, C)
-    ops: list = field(default_factory=list)      # tuples, first element = kind
-    w16: list = field(default_factory=list)
-    w32: list = field(default_factory=list)
-    b32: list = field(default_factory=list)
-    nw: int = 0
-    nb: int = 0
-    layer_out: dict = field(default_factory=dict)
+# ---------------- declarations and instructions ----------------
+class Slab:
+    """A buffer: H x W x C fp16 per image."""
+    __slots__ = ("H", "W", "C", "id")
 
-    # ---- buffers and views ----
-    def buffer(self, H, W, C):
-        self.bufs.append((H, W, C))
-        return len(self.bufs) - 1
+    def __init__(self, H, W, C):
+        self.H, self.W, self.C, self.id = H, W, C, None
 
-    def view(self, b, coff, C):
-        assert coff + C <= self.bufs[b][2]
-        self.tens.append((b, coff, C))
-        return len(self.tens) - 1
 
-    def fresh(self, H, W, C):
-        return self.view(self.buffer(H, W, C), 0, C)
+class Span:
+    """Channels [c0, c0 + C) of a slab."""
+    __slots__ = ("slab", "c0", "C", "id")
 
-    def hwc(self, t):
-        b, _, C = self.tens[t]
-        return self.bufs[b][0], self.bufs[b][1], C
+    def __init__(self, slab, c0, C):
+        if c0 < 0 or c0 + C > slab.C:
+            raise ValueError(f"span [{c0}, {c0 + C}) outside a {slab.C}-channel slab")
+        self.slab, self.c0, self.C, self.id = slab, c0, C, None
 
-    def _weights(self, w_ohwi, bias):
-        self.w32.append(np.ascontiguousarray(w_ohwi, np.float32).ravel())
-        w = np.ascontiguousarray(w_ohwi, np.float16).ravel()
-        b = np.ascontiguousarray(bias, np.float32).ravel()
-        offs = (self.nw, self.nb)
-        self.w16.append(w)
-        self.b32.append(b)
-        self.nw += w.size
-        self.nb += b.size
-        return offs
+    @property
+    def H(self):
+        return self.slab.H
 
-    # ---- op emitters ----
-    @staticmethod
-    def _unwrap(mod):
-        if isinstance(mod, ynn.Conv):
-            return mod.conv, (ACT_SILU if isinstance(mod.act, nn.SiLU) else ACT_NONE)
-        return mod, ACT_NONE
+    @property
+    def W(self):
+        return self.slab.W
 
-    def conv(self, x, mod, out=None, act=None):
-        cv, a = self._unwrap(mod)
-        a = a if act is None else act
+
+class Instr:
+    """One op line.  ``args`` mixes spans (rendered as their ids) and integers; a CONV also
+    carries its weight [O, kh, kw, I] (float32), bias [O] and how to extend them."""
+    __slots__ = ("kind", "args", "weight", "bias")
+
+    def __init__(self, kind, *args, weight=None, bias=None):
+        self.kind, self.args, self.weight, self.bias = kind, args, weight, bias
+
+
+class _Program:
+    def __init__(self):
+        self.decls = []        # Slab / Span objects in declaration order
+        self.instrs = []
+
+    # declarations
+    def slab(self, H, W, C):
+        s = Slab(H, W, C)
+        self.decls.append(s)
+        return s
+
+    def span(self, slab, c0, C):
+        v = Span(slab, c0, C)
+        self.decls.append(v)
+        return v
+
+    def new(self, H, W, C):
+        """A slab of its own, wholly viewed."""
+        return self.span(self.slab(H, W, C), 0, C)
+
+    def issue(self, kind, *args, **kw):
+        self.instrs.append(Instr(kind, *args, **kw))
+
+    # packing
+    def pack(self, task, nc, S):
+        nslab = nspan = 0
+        for d in self.decls:
+            if isinstance(d, Slab):
+                d.id, nslab = nslab, nslab + 1
+            else:
+                d.id, nspan = nspan, nspan + 1
+        wblobs, bblobs, lines = [], [], []
+        woff = boff = 0
+        for ins in self.instrs:
+            vals = [a.id if isinstance(a, Span) else int(a) for a in ins.args]
+            if ins.kind == "CONV":
+                w16 = np.ascontiguousarray(ins.weight, np.float16).ravel()
+                b32 = np.ascontiguousarray(ins.bias, np.float32).ravel()
+                vals += [woff, boff]
+                woff += w16.size
+                boff += b32.size
+                wblobs.append(w16)
+                bblobs.append(b32)
+            lines.append(" ".join([ins.kind] + [str(v) for v in vals]))
+        slabs = [d for d in self.decls if isinstance(d, Slab)]
+        spans = [d for d in self.decls if isinstance(d, Span)]
+        head = ["YOLO11GRAPH 2", f"TASK {task} {nc} {S}", f"{nslab} {nspan} {len(self.instrs)}"]
+        head += [f"B {s.H} {s.W} {s.C}" for s in slabs]
+        head += [f"T {v.slab.id} {v.c0} {v.C}" for v in spans]
+        text = "\n".join(head + lines) + "\n"
+        empty = np.zeros(0, np.float16)
+        return (text, np.concatenate(wblobs) if wblobs else empty,
+                np.concatenate(bblobs) if bblobs else np.zeros(0, np.float32))
+
+
+# ---------------- weights ----------------
+def _conv_parts(mod):
+    """(nn.Conv2d, activation code) of a ynn.Conv or a bare nn.Conv2d."""
+    if isinstance(mod, ynn.Conv):
+        return mod.conv, ACT_SILU if isinstance(mod.act, nn.SiLU) else ACT_NONE
+    return mod, ACT_NONE
+
+
+def _extend(w, b, o_to, i_to):
+    """Zero-extend OHWI weights to o_to output / i_to input channels, bias to o_to."""
+    O, kh, kw, I = w.shape
+    out = np.zeros((o_to, kh, kw, i_to), np.float32)
+    out[:O, :, :, :I] = w
+    bb = np.zeros(o_to, np.float32)
+    bb[:O] = b
+    return out, bb
+
+
+# ---------------- lowering ----------------
+def _round8(c):
+    return (c + 7) // 8 * 8
+
+
+class _Lowering:
+    def __init__(self, model, S):
+        self.p = _Program()
+        self.model, self.S = model, S
+
+    # -- primitive: one convolution from span `src` into `dst` (declared here if None) --
+    def conv(self, src, mod, dst=None, width=None):
+        cv, act = _conv_parts(mod)
         O, Ig, kh, kw = cv.weight.shape
-        k, s, p, g = kh, cv.stride[0], cv.padding[0], cv.groups
-        H, W, Cin = self.hwc(x)
-        assert kh == kw and Ig * g == Cin and (g == 1 or (g == Cin and O == Cin))
-        Ho, Wo = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
-        if out is None:
-            out = self.fresh(Ho, Wo, O)
-        assert self.hwc(out) == (Ho, Wo, O)
-        w = cv.weight.detach().permute(0, 2, 3, 1).contiguous().numpy()
+        if kh != kw:
+            raise ValueError("square kernels only")
+        k, s, pd, groups = kh, cv.stride[0], cv.padding[0], cv.groups
+        depthwise = groups > 1
+        if depthwise and not (groups == O and Ig == 1):
+            raise ValueError("grouped convs other than depthwise are not supported")
+        if not depthwise and Ig > src.C:
+            raise ValueError(f"conv wants {Ig} input channels, span has {src.C}")
+        Ho, Wo = (src.H + 2 * pd - k) // s + 1, (src.W + 2 * pd - k) // s + 1
+        if dst is None:
+            dst = self.p.new(Ho, Wo, width or O)
+        if (dst.H, dst.W) != (Ho, Wo) or dst.C < O:
+            raise ValueError("conv output span has the wrong shape")
+        w = cv.weight.detach().permute(0, 2, 3, 1).numpy()
         b = cv.bias.detach().numpy() if cv.bias is not None else np.zeros(O, np.float32)
-        woff, boff = self._weights(w, b)
-        self.ops.append(("CONV", x, out, k, s, p, g, a, Cin, O, woff, boff))
-        return out
+        w, b = _extend(w, b, dst.C, 1 if depthwise else src.C)
+        g_field = dst.C if depthwise else 1
+        self.p.issue("CONV", src, dst, k, s, pd, g_field, act, src.C, dst.C, weight=w, bias=b)
+        return dst
 
-    def conv_pad8(self, x, mod, cpad=None, act=None):
-        """Conv whose output (and dead input) channels are zero-padded to a multiple of 8."""
-        cv, a = self._unwrap(mod)
-        a = a if act is None else act
-        O, Ig, kh, kw = cv.weight.shape
-        cpad = (O + 7) // 8 * 8 if cpad is None else cpad
-        H, W, Cin = self.hwc(x)
-        dw = cv.groups > 1
-        if O == cpad and Ig * cv.groups == Cin:
-            return self.conv(x, mod, act=act)
-        k, s, p = kh, cv.stride[0], cv.padding[0]
-        Ho, Wo = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
-        out = self.fresh(Ho, Wo, cpad)
-        w = cv.weight.detach().permute(0, 2, 3, 1).contiguous().numpy()
-        if not dw and Ig < Cin:
-            w = np.concatenate([w, np.zeros((O, kh, kw, Cin - Ig), w.dtype)], 3)
-        w = np.concatenate([w, np.zeros((cpad - O, kh, kw, w.shape[3]), w.dtype)], 0)
-        b0 = cv.bias.detach().numpy() if cv.bias is not None else np.zeros(O, np.float32)
-        b = np.concatenate([b0, np.zeros(cpad - O, np.float32)])
-        woff, boff = self._weights(w, b)
-        self.ops.append(("CONV", x, out, k, s, p, cpad if dw else 1, a, cpad if dw else Cin,
-                         cpad, woff, boff))
-        return out
+    def convs(self, src, mods, pad8=False):
+        """A (nested) Sequential of convs, each into a span of its own."""
+        if isinstance(mods, nn.Sequential):
+            for m in mods:
+                src = self.convs(src, m, pad8)
+            return src
+        O = _conv_parts(mods)[0].out_channels
+        return self.conv(src, mods, width=_round8(O) if pad8 else None)
 
-    def op(self, *t):
-        self.ops.append(tuple(t))
-        return t[-1] if t[0] in ("MAXPOOL5", "UPSAMPLE2", "PS2", "COPYC") else None
-
-    def convT2(self, x, mod, out=None):
-        """ConvTranspose2d(k=2, s=2) = 1x1 CONV to 4C (quadrant q = 2*di+dj blocks) + PS2."""
-        H, W, Cin = self.hwc(x)
-        wt = mod.weight.detach()
-        C = wt.shape[1]
-        assert tuple(wt.shape) == (Cin, C, 2, 2) and mod.stride[0] == 2 and mod.padding[0] == 0
+    def conv_transpose2(self, src, mod):
+        """ConvTranspose2d(k=2, s=2) as a 1x1 CONV to 4C (quadrant q = 2*di + dj blocks of C
+        channels) followed by PS2."""
+        wt = mod.weight.detach()                   # [Cin, C, 2, 2]
+        Cin, C = wt.shape[0], wt.shape[1]
+        if tuple(wt.shape[2:]) != (2, 2) or mod.stride[0] != 2 or mod.padding[0] != 0 or Cin != src.C:
+            raise ValueError("only ConvTranspose2d(k=2, s=2, p=0) is supported")
+        quad = self.p.new(src.H, src.W, 4 * C)
         w = wt.permute(2, 3, 1, 0).reshape(4 * C, 1, 1, Cin).numpy()
         b = np.tile(mod.bias.detach().numpy(), 4)
-        woff, boff = self._weights(w, b)
-        up4 = self.fresh(H, W, 4 * C)
-        self.ops.append(("CONV", x, up4, 1, 1, 0, 1, ACT_NONE, Cin, 4 * C, woff, boff))
-        if out is None:
-            out = self.fresh(H * 2, W * 2, C)
-        self.ops.append(("PS2", up4, out))
+        self.p.issue("CONV", src, quad, 1, 1, 0, 1, ACT_NONE, Cin, 4 * C, weight=w, bias=b)
+        out = self.p.new(2 * src.H, 2 * src.W, C)
+        self.p.issue("PS2", quad, out)
         return out
 
-    # ---- serialisation ----
-    def graph_text(self, task, nc, S):
-        lines = ["YOLO11GRAPH 2", f"TASK {task} {nc} {S}",
-                 f"{len(self.bufs)} {len(self.tens)} {len(self.ops)}"]
-        lines += [f"B {H} {W} {C}" for (H, W, C) in self.bufs]
-        lines += [f"T {b} {o} {C}" for (b, o, C) in self.tens]
-        lines += [" ".join(str(v) for v in op) for op in self.ops]
-        return "\n".join(lines) + "\n"
+    # -- composite recipes --
+    def bottleneck(self, src, m, dst):
+        mid = self.conv(src, m.cv1)
+        self.conv(mid, m.cv2, dst)
+        if m.add:
+            self.p.issue("ADD", dst, src, dst)
 
+    def c3k(self, src, m, dst):
+        h = m.cv1.conv.out_channels
+        pair = self.p.slab(src.H, src.W, 2 * h)      # [ bottleneck chain | cv2 ]
+        run = self.conv(src, m.cv1)
+        blocks = list(m.m)
+        for i, blk in enumerate(blocks):
+            last = i == len(blocks) - 1
+            tgt = self.p.span(pair, 0, h) if last else self.p.new(src.H, src.W, h)
+            self.bottleneck(run, blk, tgt)
+            run = tgt
+        self.conv(src, m.cv2, self.p.span(pair, h, h))
+        self.conv(self.p.span(pair, 0, 2 * h), m.cv3, dst)
 
-# ---------------- composite modules ----------------
+    def c2f(self, src, m, dst):
+        c, n = m.c, len(m.m)
+        stack = self.p.slab(src.H, src.W, (2 + n) * c)   # [ cv1 (2c) | block 0 | block 1 ... ]
+        self.conv(src, m.cv1, self.p.span(stack, 0, 2 * c))
+        feed = self.p.span(stack, c, c)
+        for i, blk in enumerate(m.m):
+            tgt = self.p.span(stack, (2 + i) * c, c)
+            (self.c3k if isinstance(blk, ynn.C3k) else self.bottleneck)(feed, blk, tgt)
+            feed = tgt
+        return self.conv(self.p.span(stack, 0, (2 + n) * c), m.cv2, dst)
 
-def _bottleneck(g, x, m, out):
-    t = g.conv(x, m.cv1)
-    g.conv(t, m.cv2, out=out)
-    if m.add:
-        g.op("ADD", out, x, out)
-    return out
+    def sppf(self, src, m, dst):
+        h = m.cv1.conv.out_channels
+        pools = self.p.slab(src.H, src.W, 4 * h)         # [ cv1 | pool | pool^2 | pool^3 ]
+        self.conv(src, m.cv1, self.p.span(pools, 0, h))
+        for i in range(3):
+            self.p.issue("MAXPOOL5", self.p.span(pools, i * h, h), self.p.span(pools, (i + 1) * h, h))
+        return self.conv(self.p.span(pools, 0, 4 * h), m.cv2, dst)
 
+    def psa_block(self, x, blk):
+        """In place on span x: x += proj(attn(x) + pe(v)); x += ffn(x)."""
+        at = blk.attn
+        nh, kd, hd = at.num_heads, at.key_dim, at.head_dim
+        if nh * hd != x.C:
+            raise ValueError("attention heads do not tile the channels")
+        qkv = self.conv(x, at.qkv)                       # per head [q kd | k kd | v hd]
+        vslab = self.p.slab(x.H, x.W, x.C)
+        for h in range(nh):
+            self.p.issue("COPYC", self.p.span(qkv.slab, h * (2 * kd + hd) + 2 * kd, hd),
+                         self.p.span(vslab, h * hd, hd))
+        v = self.p.span(vslab, 0, x.C)
+        att = self.p.new(x.H, x.W, x.C)
+        self.p.issue("ATTN", qkv, att, nh, kd, hd)
+        pe = self.conv(v, at.pe)
+        self.p.issue("ADD", att, pe, att)
+        proj = self.conv(att, at.proj)
+        self.p.issue("ADD", x, proj, x)
+        f = self.conv(self.conv(x, blk.ffn[0]), blk.ffn[1])
+        self.p.issue("ADD", x, f, x)
 
-def _c3k(g, x, m, out):
-    H, W, _ = g.hwc(x)
-    c_ = m.cv1.conv.out_channels
-    cat = g.buffer(H, W, 2 * c_)
-    blocks = list(m.m)
-    cur = g.conv(x, m.cv1)
-    for j, bo in enumerate(blocks):
-        dst = g.view(cat, 0, c_) if j == len(blocks) - 1 else g.fresh(H, W, c_)
-        cur = _bottleneck(g, cur, bo, dst)
-    g.conv(x, m.cv2, out=g.view(cat, c_, c_))
-    g.conv(g.view(cat, 0, 2 * c_), m.cv3, out=out)
-    return out
+    def c2psa(self, src, m, dst):
+        c = m.c
+        halves = self.p.slab(src.H, src.W, 2 * c)        # [ passthrough | attention path ]
+        self.conv(src, m.cv1, self.p.span(halves, 0, 2 * c))
+        path = self.p.span(halves, c, c)
+        for blk in m.m:
+            self.psa_block(path, blk)
+        return self.conv(self.p.span(halves, 0, 2 * c), m.cv2, dst)
 
+    # -- whole network --
+    def run(self):
+        net, S = self.model.model, self.S
+        body = list(net)[:-1]
+        x0 = self.p.new(S, S, 3)
 
-def _c2f(g, x, m, out=None):
-    H, W, _ = g.hwc(x)
-    c, n = m.c, len(m.m)
-    cat = g.buffer(H, W, (2 + n) * c)
-    g.conv(x, m.cv1, out=g.view(cat, 0, 2 * c))
-    prev = g.view(cat, c, c)
-    for j, blk in enumerate(m.m):
-        dst = g.view(cat, (2 + j) * c, c)
-        (_c3k if isinstance(blk, ynn.C3k) else _bottleneck)(g, prev, blk, dst)
-        prev = dst
-    return g.conv(g.view(cat, 0, (2 + n) * c), m.cv2, out=out)
+        def srcs(i):
+            f = body[i].f
+            return [i - 1 if j == -1 else j for j in ([f] if isinstance(f, int) else f)]
 
-
-def _sppf(g, x, m, out=None):
-    H, W, _ = g.hwc(x)
-    c_ = m.cv1.conv.out_channels
-    cat = g.buffer(H, W, 4 * c_)
-    g.conv(x, m.cv1, out=g.view(cat, 0, c_))
-    for j in range(3):
-        g.op("MAXPOOL5", g.view(cat, j * c_, c_), g.view(cat, (j + 1) * c_, c_))
-    return g.conv(g.view(cat, 0, 4 * c_), m.cv2, out=out)
-
-
-def _psa(g, xio, blk):
-    H, W, C = g.hwc(xio)
-    at = blk.attn
-    heads, kd, hd = at.num_heads, at.key_dim, at.head_dim
-    assert heads * hd == C
-    qkv = g.conv(xio, at.qkv)
-    qb = g.tens[qkv][0]
-    per = 2 * kd + hd
-    vbuf = g.buffer(H, W, C)
-    for h in range(heads):
-        g.op("COPYC", g.view(qb, h * per + 2 * kd, hd), g.view(vbuf, h * hd, hd))
-    vt = g.view(vbuf, 0, C)
-    ao = g.fresh(H, W, C)
-    g.ops.append(("ATTN", qkv, ao, heads, kd, hd))
-    pe = g.conv(vt, at.pe)
-    g.op("ADD", ao, pe, ao)
-    pr = g.conv(ao, at.proj)
-    g.op("ADD", xio, pr, xio)
-    f1 = g.conv(xio, blk.ffn[0])
-    f2 = g.conv(f1, blk.ffn[1])
-    g.op("ADD", xio, f2, xio)
-
-
-def _c2psa(g, x, m, out=None):
-    H, W, _ = g.hwc(x)
-    c = m.c
-    cat = g.buffer(H, W, 2 * c)
-    g.conv(x, m.cv1, out=g.view(cat, 0, 2 * c))
-    b = g.view(cat, c, c)
-    for blk in m.m:
-        _psa(g, b, blk)
-    return g.conv(g.view(cat, 0, 2 * c), m.cv2, out=out)
-
-
-def _chain(g, x, mod, pad8=False):
-    """Flatten (nested) Sequentials of convs into CONV ops."""
-    if isinstance(mod, nn.Sequential):
-        for sub in mod:
-            x = _chain(g, x, sub, pad8)
-        return x
-    return g.conv_pad8(x, mod) if pad8 else g.conv(x, mod)
-
-
-def build_graph(model: "ynn.DetectionModel", S: int) -> GraphBuilder:
-    """Walk the model's layer list (following each layer's ``.f``) into a GraphBuilder."""
-    net = model.model
-    g = GraphBuilder()
-    x0 = g.fresh(S, S, 3)
-    nbody = len(net) - 1
-
-    def sources(i):
-        f = net[i].f
-        return [i - 1 if j == -1 else j for j in ([f] if isinstance(f, int) else f)]
-
-    # channel / spatial size of every body layer
-    ch, hw = {-1: 3}, {-1: S}
-    for i in range(nbody):
-        m, src = net[i], sources(i)
-        ih = hw[src[0]]
-        if isinstance(m, ynn.Conv):
-            cv = m.conv
-            ch[i] = cv.out_channels
-            hw[i] = (ih + 2 * cv.padding[0] - cv.kernel_size[0]) // cv.stride[0] + 1
-        elif isinstance(m, (ynn.C2f, ynn.SPPF, ynn.C2PSA)):
-            ch[i], hw[i] = m.cv2.conv.out_channels, ih
-        elif isinstance(m, nn.Upsample):
-            ch[i], hw[i] = ch[src[0]], ih * 2
-        elif isinstance(m, ynn.Concat):
-            ch[i], hw[i] = sum(ch[s] for s in src), ih
-        else:
-            raise RuntimeError(f"unsupported module {type(m).__name__} at layer {i}")
-
-    # concat buffers first; each producer writes its slice of the first concat it feeds
-    catbuf, feed, copies = {}, {}, {}
-    for i in range(nbody):
-        if not isinstance(net[i], ynn.Concat):
-            continue
-        catbuf[i] = g.buffer(hw[i], hw[i], ch[i])
-        off = 0
-        for s in sources(i):
-            if s in feed or s < 0 or isinstance(net[s], ynn.Concat):
-                copies.setdefault(i, []).append((s, off))
+        # output channels and side of every body layer
+        chans, side = {-1: 3}, {-1: S}
+        for i, m in enumerate(body):
+            ins = srcs(i)
+            hin = side[ins[0]]
+            if isinstance(m, ynn.Conv):
+                cv = m.conv
+                chans[i] = cv.out_channels
+                side[i] = (hin + 2 * cv.padding[0] - cv.kernel_size[0]) // cv.stride[0] + 1
+            elif isinstance(m, (ynn.C2f, ynn.SPPF, ynn.C2PSA)):
+                chans[i], side[i] = m.cv2.conv.out_channels, hin
+            elif isinstance(m, nn.Upsample):
+                chans[i], side[i] = chans[ins[0]], 2 * hin
+            elif isinstance(m, ynn.Concat):
+                chans[i], side[i] = sum(chans[j] for j in ins), hin
             else:
-                feed[s] = (catbuf[i], off, ch[s])
-            off += ch[s]
+                raise ValueError(f"no lowering for {type(m).__name__} (layer {i})")
 
-    outs = {-1: x0}
-    for i in range(nbody):
-        m, src = net[i], sources(i)
-        xin = outs[src[0]]
-        dst = g.view(*feed[i]) if i in feed else None
-        if isinstance(m, ynn.Conv):
-            y = g.conv(xin, m, out=dst)
-        elif isinstance(m, ynn.C2PSA):
-            y = _c2psa(g, xin, m, out=dst)
-        elif isinstance(m, ynn.SPPF):
-            y = _sppf(g, xin, m, out=dst)
-        elif isinstance(m, ynn.C2f):
-            y = _c2f(g, xin, m, out=dst)
-        elif isinstance(m, nn.Upsample):
-            assert float(m.scale_factor) == 2.0
-            y = g.op("UPSAMPLE2", xin, dst if dst is not None else g.fresh(hw[i], hw[i], ch[i]))
-        else:
-            for s, off in copies.get(i, []):
-                g.op("COPYC", outs[s], g.view(catbuf[i], off, ch[s]))
-            y = g.view(catbuf[i], 0, ch[i])
-        outs[i] = y
-        g.layer_out[i] = y
+        # concat slabs, declared before the walk; each producer is routed into the first
+        # concat that takes it, later consumers of it get a copy
+        cat_slab, route, copy_in = {}, {}, {}
+        for i, m in enumerate(body):
+            if not isinstance(m, ynn.Concat):
+                continue
+            cat_slab[i] = self.p.slab(side[i], side[i], chans[i])
+            c0 = 0
+            for j in srcs(i):
+                direct = j >= 0 and j not in route and not isinstance(body[j], ynn.Concat)
+                if direct:
+                    route[j] = (i, c0)
+                else:
+                    copy_in.setdefault(i, []).append((j, c0))
+                c0 += chans[j]
 
-    det = net[-1]
-    if isinstance(det, ynn.Classify):
-        # reference export/export.py:389-397: conv -> GAP -> linear (a 1x1 CONV on the
-        # [1,1,1280] pooled tensor) -> channel SOFTMAX, each into a standalone buffer
-        h = g.conv(outs[nbody - 1], det.conv)
-        _, _, C = g.hwc(h)
-        gp = g.fresh(1, 1, C)
-        g.ops.append(("GAP", h, gp))
-        O, I = det.linear.weight.shape
-        logits = g.fresh(1, 1, O)
-        woff, boff = g._weights(det.linear.weight.detach().numpy().reshape(O, 1, 1, I),
-                                det.linear.bias.detach().numpy())
-        g.ops.append(("CONV", gp, logits, 1, 1, 0, 1, ACT_NONE, I, O, woff, boff))
-        probs = g.fresh(1, 1, O)
-        g.ops.append(("SOFTMAX", logits, probs))
-        g.layer_out[len(net) - 1] = probs
-        g.det_ref, g.seg_ref, g.probs = [], None, probs
-        return g
-    assert torch.allclose(det.dfl.conv.weight.view(-1), torch.arange(16, dtype=torch.float32))
-    seg = isinstance(det, ynn.Segment)
-    obb = isinstance(det, ynn.OBB)
-    feats = [outs[j] for j in det.f]
-    strides = [int(s) for s in det.stride]
-    g.det_ref, g.seg_ref = [], None
-    if seg:
-        assert det.nm % 8 == 0
-        t = g.conv(feats[0], det.proto.cv1)
-        t = g.convT2(t, det.proto.upsample)
-        t = g.conv(t, det.proto.cv2)
-        proto = g.conv(t, det.proto.cv3)
-        g.seg_ref = {"proto": proto, "cv4": []}
-    ncpad = (det.nc + 7) // 8 * 8
-    for i, (f, st) in enumerate(zip(feats, strides)):
-        b = _chain(g, f, det.cv2[i])
-        c = _chain(g, f, det.cv3[i][:2], pad8=True)
-        c = g.conv_pad8(c, det.cv3[i][2], ncpad)
-        if obb:   # angle branch: 3x3, 3x3, then the 1-channel final zero-padded to 8
-            a = _chain(g, f, det.cv4[i][:2])
-            a = g.conv_pad8(a, det.cv4[i][2], (det.ne + 7) // 8 * 8)
-            g.ops.append(("DECODEOBB", b, c, a, st))
-            g.det_ref.append((b, c, a))
-        elif seg:
-            mc = _chain(g, f, det.cv4[i])
-            g.ops.append(("DECODESEG", b, c, mc, st))
-            g.seg_ref["cv4"].append(mc)
-            g.det_ref.append((b, c, mc))
-        else:
-            g.ops.append(("DECODE", b, c, st))
-            g.det_ref.append((b, c))
-    if seg:
-        g.ops.append(("MASKS", proto))
-    return g
+        out = {-1: x0}
+        for i, m in enumerate(body):
+            src = out[srcs(i)[0]]
+            dst = None
+            if i in route:
+                ci, c0 = route[i]
+                dst = self.p.span(cat_slab[ci], c0, chans[i])
+            if isinstance(m, ynn.Conv):
+                y = self.conv(src, m, dst)
+            elif isinstance(m, ynn.C2PSA):
+                y = self.c2psa(src, m, dst)
+            elif isinstance(m, ynn.SPPF):
+                y = self.sppf(src, m, dst)
+            elif isinstance(m, ynn.C2f):
+                y = self.c2f(src, m, dst)
+            elif isinstance(m, nn.Upsample):
+                if float(m.scale_factor) != 2.0:
+                    raise ValueError("only 2x upsampling is supported")
+                y = dst if dst is not None else self.p.new(side[i], side[i], chans[i])
+                self.p.issue("UPSAMPLE2", src, y)
+            else:                                        # Concat
+                for j, c0 in copy_in.get(i, []):
+                    self.p.issue("COPYC", out[j], self.p.span(cat_slab[i], c0, chans[j]))
+                y = self.p.span(cat_slab[i], 0, chans[i])
+            out[i] = y
+        self.head(net[-1], out, len(body))
+        return self.p
+
+    def head(self, det, out, nbody):
+        if isinstance(det, ynn.Classify):
+            # conv -> GAP -> linear (a 1x1 CONV on the [1, 1, C] pooled tensor) -> channel
+            # softmax, each into a slab of its own (export/export.py:389-397)
+            feat = self.conv(out[nbody - 1], det.conv)
+            pooled = self.p.new(1, 1, feat.C)
+            self.p.issue("GAP", feat, pooled)
+            O, I = det.linear.weight.shape
+            logits = self.p.new(1, 1, O)
+            self.p.issue("CONV", pooled, logits, 1, 1, 0, 1, ACT_NONE, I, O,
+                         weight=det.linear.weight.detach().numpy().reshape(O, 1, 1, I),
+                         bias=det.linear.bias.detach().numpy())
+            self.p.issue("SOFTMAX", logits, self.p.new(1, 1, O))
+            return
+        if not torch.allclose(det.dfl.conv.weight.view(-1), torch.arange(16, dtype=torch.float32)):
+            raise ValueError("the DFL conv must be arange(16)")
+        seg, obb = isinstance(det, ynn.Segment), isinstance(det, ynn.OBB)
+        feats = [out[j] for j in det.f]
+        proto = None
+        if seg:
+            if det.nm % 8:
+                raise ValueError("mask coefficients must be a multiple of 8")
+            pr = det.proto
+            proto = self.conv(self.conv(self.conv_transpose2(self.conv(feats[0], pr.cv1),
+                                                             pr.upsample), pr.cv2), pr.cv3)
+        for i, (f, st) in enumerate(zip(feats, det.stride)):
+            st = int(st)
+            box = self.convs(f, det.cv2[i])
+            cls = self.convs(f, det.cv3[i][:2], pad8=True)
+            cls = self.conv(cls, det.cv3[i][2], width=_round8(det.nc))
+            if obb:        # angle branch, the 1-channel final padded to 8
+                ang = self.convs(f, det.cv4[i][:2])
+                ang = self.conv(ang, det.cv4[i][2], width=_round8(det.ne))
+                self.p.issue("DECODEOBB", box, cls, ang, st)
+            elif seg:
+                self.p.issue("DECODESEG", box, cls, self.convs(f, det.cv4[i]), st)
+            else:
+                self.p.issue("DECODE", box, cls, st)
+        if seg:
+            self.p.issue("MASKS", proto)
 
 
+# ---------------- inputs and the directory ----------------
 def letterbox(bgr: np.ndarray, S: int) -> np.ndarray:
     """cv2 INTER_LINEAR letterbox (pad 114) -> RGB float32 [S, S, 3] in [0, 1]."""
     import cv2
@@ -388,23 +417,29 @@ def classify_input(bgr: np.ndarray, S: int) -> np.ndarray:
     return t(Image.fromarray(rgb)).permute(1, 2, 0).numpy()
 
 
+def lower(model: "ynn.DetectionModel", S: int) -> _Program:
+    """The model's graph program at input size S (declarations + instructions, unnumbered)."""
+    return _Lowering(model, S).run()
+
+
 def export_model(name: str, out_dir: str, imgsz: int = 640, frame_hw=(1080, 810),
-                 frame_seed: int = 0, model=None) -> GraphBuilder:
+                 frame_seed: int = 0, model=None) -> None:
     """Write ``out_dir`` for the seeded model ``name`` at input size ``imgsz``."""
     from .frames import synthetic_bgr
-    assert imgsz % 32 == 0
+    if imgsz % 32:
+        raise ValueError("imgsz must be a multiple of 32")
     model = ynn.build_model(name, imgsz=imgsz) if model is None else model
-    g = build_graph(model, imgsz)
-    os.makedirs(out_dir, exist_ok=True)
     head = model.model[-1]
     task = ("segment" if isinstance(head, ynn.Segment) else
             "classify" if isinstance(head, ynn.Classify) else
             "obb" if isinstance(head, ynn.OBB) else "detect")
     nc = head.linear.out_features if task == "classify" else head.nc
+    text, w16, b32 = lower(model, imgsz).pack(task, nc, imgsz)
+    os.makedirs(out_dir, exist_ok=True)
     with open(os.path.join(out_dir, "model.graph"), "w") as f:
-        f.write(g.graph_text(task, nc, imgsz))
-    np.concatenate(g.w16).tofile(os.path.join(out_dir, "weights.f16"))
-    np.concatenate(g.b32).tofile(os.path.join(out_dir, "bias.f32"))
+        f.write(text)
+    w16.tofile(os.path.join(out_dir, "weights.f16"))
+    b32.tofile(os.path.join(out_dir, "bias.f32"))
     bgr = synthetic_bgr(*frame_hw, seed=frame_seed)
     bgr.tofile(os.path.join(out_dir, "bus_raw.u8"))
     with open(os.path.join(out_dir, "bus_raw.txt"), "w") as f:
@@ -414,7 +449,6 @@ def export_model(name: str, out_dir: str, imgsz: int = 640, frame_hw=(1080, 810)
     if task == "classify":
         with open(os.path.join(out_dir, "names.txt"), "w") as f:
             f.write("\n".join(model.names[i] for i in range(nc)) + "\n")
-    return g
 
 
 def ensure_model_dir(name: str, root: str, imgsz: int = 640, frame_hw=(1080, 810)) -> str:
@@ -425,4 +459,3 @@ def ensure_model_dir(name: str, root: str, imgsz: int = 640, frame_hw=(1080, 810
     if not os.path.exists(os.path.join(d, "model.graph")):
         export_model(name, d, imgsz, frame_hw)
     return d
-
