@@ -270,6 +270,15 @@ void oref_mask(const uint16_t* coef, int nm, const uint16_t* proto, int pstride,
 /* exposed for the math tests */
 float oref_exp(float x) { return dm_exp(x); }
 float oref_sigmoid(float x) { return dm_sigmoid(x); }
+/* Mismatches of dm_div255(v) against v / 255 over the binary32 bit patterns lo..hi (step). */
+long oref_div255_check(unsigned lo, unsigned hi, unsigned step) {
+  long bad = 0;
+  for (unsigned long long u = lo; u <= hi; u += step) {
+    const float v = dm_bits2f((unsigned)u);
+    if (dm_f2bits(dm_div255(v)) != dm_f2bits(DM_DIV(v, 255.0f))) bad++;
+  }
+  return bad;
+}
 float oref_sin(float x) { float s, c; dm_sincos(x, &s, &c); return s; }
 float oref_cos(float x) { float s, c; dm_sincos(x, &s, &c); return c; }
 float oref_log(float x) { return dm_log(x); }

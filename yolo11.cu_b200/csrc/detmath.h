@@ -83,6 +83,18 @@ DM_HD float dm_exp(float x) {
 }
 
 // 1 / (1 + e^-x)
+// v / 255 correctly rounded without a division: q = RN(v * RN(1/255)), then one Markstein
+// correction step, q' = RN(q + RN(v - q * 255) * RN(1/255)) with both steps as single-rounding
+// FMAs (P. Markstein, "Computation of elementary functions on the IBM RISC System/6000
+// processor", IBM J. Res. Dev. 34(1), 1990).  Checked exhaustively against v / 255 for every
+// binary32 v in [0, 256] (the letterbox's range: bilinear sums of bytes).
+DM_HD float dm_div255(float v) {
+  const float inv = 0.0039215688593685627f;   // RN(1/255) = 0x1.010102p-8
+  const float q = DM_MUL(v, inv);
+  const float r = DM_FMA(-q, 255.0f, v);
+  return DM_FMA(r, inv, q);
+}
+
 DM_HD float dm_sigmoid(float x) { return DM_DIV(1.0f, DM_ADD(1.0f, dm_exp(-x))); }
 
 // fp16 bits -> fp32 (exact)

@@ -14,98 +14,125 @@
 namespace yk {
 
 // ---------------- letterbox (engine/engine.cu:968-998) ----------------
-// One launch letterboxes a batch of equal-size frames: grid (row blocks, frames).  Each
-// thread owns 8 consecutive output columns of kLbRows rows; their horizontal sampling
-// (source byte offsets, weights, inside/outside) is computed once and reused on every row,
-// and the 8 pixels (24 fp16) leave as three 16-byte stores when the view is a dense
+// One launch letterboxes a batch of equal-size frames: grid (row blocks, frames), `rows`
+// output rows per block (chosen on the host so the grid fills the GPU: 1 row per block for
+// a single frame, 8 for a batch).  Each thread owns 8 consecutive output columns: their
+// horizontal sampling (source byte offsets, weights, inside / outside) is computed once and
+// reused on every row; rows go two at a time so both rows' source loads are in flight
+// together; the 8 pixels (24 fp16) leave as three 16-byte stores when the view is a dense
 // 3-channel image whose width is a multiple of 8 (else element stores).  Source bytes come
-// through the read-only cache: neighbouring threads read neighbouring bytes of the same two
+// through the read-only cache: neighbouring threads read neighbouring bytes of the same
 // source rows, so each row is fetched from DRAM about once.  The arithmetic is the
 // reference's formula in explicitly rounded fp32 (src = (dst - off + 0.5) / scale - 0.5,
-// bilinear weights, /255, pad 114), so the C oracle reproduces it bit for bit.
-constexpr int kLbRows = 8;
+// bilinear weights, /255, pad 114); /255 is dm_div255 (bit-identical to the division), so the
+// C oracle reproduces every value bit for bit.
+struct LbCols {
+  int o0[8], o1[8];
+  float wx[8];
+  unsigned inside;
+};
+
+template <bool kVec>
+__device__ __forceinline__ void letterbox_row(const uint8_t* __restrict__ img, int sh, int sw,
+                                              __half* out, int dh, int dw, int dstride,
+                                              float scale, int top, int nh, int y, int xb,
+                                              const LbCols& cs, __half pad) {
+  __align__(16) __half px[24];
+  if (y < top || y >= top + nh || !cs.inside) {
+#pragma unroll
+    for (int i = 0; i < 24; i++) px[i] = pad;
+  } else {
+    const float fy = DM_SUB(DM_DIV(DM_ADD((float)(y - top), 0.5f), scale), 0.5f);
+    int y0 = (int)floorf(fy);
+    const float wy = DM_SUB(fy, (float)y0);
+    const int y1 = min(y0 + 1, sh - 1);
+    y0 = max(y0, 0);
+    const uint8_t* r0 = img + (size_t)y0 * sw * 3;
+    const uint8_t* r1 = img + (size_t)y1 * sw * 3;
+    const float wy1 = DM_SUB(1.f, wy);
+    uint8_t p[8][12];                 // all 96 source bytes first: the loads overlap
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+      for (int c = 0; c < 3; c++) {
+        p[j][c] = __ldg(r0 + cs.o0[j] + c);
+        p[j][3 + c] = __ldg(r0 + cs.o1[j] + c);
+        p[j][6 + c] = __ldg(r1 + cs.o0[j] + c);
+        p[j][9 + c] = __ldg(r1 + cs.o1[j] + c);
+      }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      if (!((cs.inside >> j) & 1u)) {
+        px[3 * j] = px[3 * j + 1] = px[3 * j + 2] = pad;
+        continue;
+      }
+      const float wx1 = DM_SUB(1.f, cs.wx[j]);
+      const float w00 = DM_MUL(wy1, wx1), w01 = DM_MUL(wy1, cs.wx[j]);
+      const float w10 = DM_MUL(wy, wx1), w11 = DM_MUL(wy, cs.wx[j]);
+      float v[3];
+#pragma unroll
+      for (int c = 0; c < 3; c++) {
+        float t = DM_MUL((float)p[j][c], w00);
+        t = DM_ADD(t, DM_MUL((float)p[j][3 + c], w01));
+        t = DM_ADD(t, DM_MUL((float)p[j][6 + c], w10));
+        v[c] = DM_ADD(t, DM_MUL((float)p[j][9 + c], w11));
+      }
+      // BGR in, RGB out
+      px[3 * j] = __float2half_rn(dm_div255(v[2]));
+      px[3 * j + 1] = __float2half_rn(dm_div255(v[1]));
+      px[3 * j + 2] = __float2half_rn(dm_div255(v[0]));
+    }
+  }
+  if (kVec) {
+    int4* o = (int4*)(out + ((size_t)y * dw + xb) * 3);
+    const int4* q = (const int4*)px;
+    o[0] = q[0];
+    o[1] = q[1];
+    o[2] = q[2];
+  } else {
+    for (int j = 0; j < 8 && xb + j < dw; j++) {
+      __half* o = out + ((size_t)y * dw + xb + j) * dstride;
+      o[0] = px[3 * j];
+      o[1] = px[3 * j + 1];
+      o[2] = px[3 * j + 2];
+    }
+  }
+}
 
 template <bool kVec>
 __global__ void __launch_bounds__(256) letterbox_kernel(
     const uint8_t* __restrict__ src, size_t src_frame, int sh, int sw, __half* dst,
     size_t dst_frame, int dh, int dw, int dstride, float scale, int top, int left, int nh,
-    int nw) {
+    int nw, int rows) {
   pdl_wait();     // the destination may still be read by the previous graph's kernels
   pdl_trigger();
   const int xb = threadIdx.x * 8;
   if (xb >= dw) return;
   const uint8_t* img = src + (size_t)blockIdx.y * src_frame;
   __half* out = dst + (size_t)blockIdx.y * dst_frame;
-  int o0[8], o1[8];
-  float wx[8];
-  unsigned inside = 0;
+  LbCols cs;
+  cs.inside = 0;
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const int x = xb + j;
     const float fx = DM_SUB(DM_DIV(DM_ADD((float)(x - left), 0.5f), scale), 0.5f);
     int x0 = (int)floorf(fx);
-    wx[j] = DM_SUB(fx, (float)x0);
+    cs.wx[j] = DM_SUB(fx, (float)x0);
     const int x1 = min(x0 + 1, sw - 1);
     x0 = max(x0, 0);
-    o0[j] = x0 * 3;
-    o1[j] = x1 * 3;
-    if (x < dw && x >= left && x < left + nw) inside |= 1u << j;
+    cs.o0[j] = x0 * 3;
+    cs.o1[j] = x1 * 3;
+    if (x < dw && x >= left && x < left + nw) cs.inside |= 1u << j;
   }
-  const __half pad = __float2half_rn(DM_DIV(114.f, 255.f));
-  const int y_end = min(dh, (int)(blockIdx.x + 1) * kLbRows);
-  for (int y = blockIdx.x * kLbRows; y < y_end; y++) {
-    __align__(16) __half px[24];
-    const bool row_in = y >= top && y < top + nh;
-    if (!row_in || !inside) {
-#pragma unroll
-      for (int i = 0; i < 24; i++) px[i] = pad;
-    } else {
-      const float fy = DM_SUB(DM_DIV(DM_ADD((float)(y - top), 0.5f), scale), 0.5f);
-      int y0 = (int)floorf(fy);
-      const float wy = DM_SUB(fy, (float)y0);
-      const int y1 = min(y0 + 1, sh - 1);
-      y0 = max(y0, 0);
-      const uint8_t* r0 = img + (size_t)y0 * sw * 3;
-      const uint8_t* r1 = img + (size_t)y1 * sw * 3;
-      const float wy1 = DM_SUB(1.f, wy);
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        if (!((inside >> j) & 1u)) {
-          px[3 * j] = px[3 * j + 1] = px[3 * j + 2] = pad;
-          continue;
-        }
-        const float wx1 = DM_SUB(1.f, wx[j]);
-        const float w00 = DM_MUL(wy1, wx1), w01 = DM_MUL(wy1, wx[j]);
-        const float w10 = DM_MUL(wy, wx1), w11 = DM_MUL(wy, wx[j]);
-        float v[3];
-#pragma unroll
-        for (int c = 0; c < 3; c++) {
-          float t = DM_MUL((float)__ldg(r0 + o0[j] + c), w00);
-          t = DM_ADD(t, DM_MUL((float)__ldg(r0 + o1[j] + c), w01));
-          t = DM_ADD(t, DM_MUL((float)__ldg(r1 + o0[j] + c), w10));
-          v[c] = DM_ADD(t, DM_MUL((float)__ldg(r1 + o1[j] + c), w11));
-        }
-        // BGR in, RGB out
-        px[3 * j] = __float2half_rn(DM_DIV(v[2], 255.f));
-        px[3 * j + 1] = __float2half_rn(DM_DIV(v[1], 255.f));
-        px[3 * j + 2] = __float2half_rn(DM_DIV(v[0], 255.f));
-      }
-    }
-    if (kVec) {
-      int4* o = (int4*)(out + ((size_t)y * dw + xb) * 3);
-      const int4* p = (const int4*)px;
-      o[0] = p[0];
-      o[1] = p[1];
-      o[2] = p[2];
-    } else {
-      for (int j = 0; j < 8 && xb + j < dw; j++) {
-        __half* o = out + ((size_t)y * dw + xb + j) * dstride;
-        o[0] = px[3 * j];
-        o[1] = px[3 * j + 1];
-        o[2] = px[3 * j + 2];
-      }
-    }
+  const __half pad = __float2half_rn(dm_div255(114.f));
+  const int y_beg = blockIdx.x * rows, y_end = min(dh, y_beg + rows);
+  int y = y_beg;
+  for (; y + 1 < y_end; y += 2) {
+    letterbox_row<kVec>(img, sh, sw, out, dh, dw, dstride, scale, top, nh, y, xb, cs, pad);
+    letterbox_row<kVec>(img, sh, sw, out, dh, dw, dstride, scale, top, nh, y + 1, xb, cs, pad);
   }
+  if (y < y_end)
+    letterbox_row<kVec>(img, sh, sw, out, dh, dw, dstride, scale, top, nh, y, xb, cs, pad);
 }
 
 // ---------------- decode (engine/engine.cu:848-906) ----------------
@@ -727,13 +754,15 @@ int yk_letterbox_batch(const uint8_t* bgr, size_t frame_stride, int n, int sh, i
   const bool vec = y->stride == 3 && y->coff == 0 && y->W % 8 == 0 &&
                    ((uintptr_t)y->ptr & 15) == 0;
   const int threads = ((y->W + 7) / 8 + 31) / 32 * 32;
-  const dim3 grid((y->H + kLbRows - 1) / kLbRows, n);
+  // rows per block: enough blocks for about eight per SM, at most 8 rows each
+  const int rows = std::max(1, std::min(8, (int)((long long)y->H * n / (148 * 8))));
+  const dim3 grid((y->H + rows - 1) / rows, n);
   if (vec)
     launch_k(letterbox_kernel<true>, grid, threads, 0, (cudaStream_t)st, bgr, frame_stride, sh,
-             sw, dst, dframe, y->H, y->W, y->stride, scale, top, left, nh, nw);
+             sw, dst, dframe, y->H, y->W, y->stride, scale, top, left, nh, nw, rows);
   else
     launch_k(letterbox_kernel<false>, grid, threads, 0, (cudaStream_t)st, bgr, frame_stride, sh,
-             sw, dst, dframe, y->H, y->W, y->stride, scale, top, left, nh, nw);
+             sw, dst, dframe, y->H, y->W, y->stride, scale, top, left, nh, nw, rows);
   note_launch();
   return check_launch("letterbox");
 }
