@@ -97,7 +97,7 @@ int yk_letterbox(const uint8_t* bgr, int sh, int sw, const YkView* y, int slot,
 // memory) starts at bgr + i * frame_stride bytes and fills slot slot0 + i.  All frames
 // share one geometry, returned as by yk_letterbox.  Replaces one k_preprocess launch per
 // frame (engine/engine.cu:1704-1713, serve.cpp's per-frame yolo_preprocess loop).
-// y->W <= 2048.
+// Source rows up to about 34,000 pixels wide (YK_EUNSUP beyond).
 int yk_letterbox_batch(const uint8_t* bgr, size_t frame_stride, int n, int sh, int sw,
                        const YkView* y, int slot0, float* scale_out, int* top_out,
                        int* left_out, yk_stream_t st);

@@ -34,21 +34,30 @@ def test_letterbox_bitexact(lib, cuda, pkg, hw, S):
     assert torch.all(out[0] == 0)
 
 
-@pytest.mark.parametrize("hw,S,n,stride", [((720, 1280), 640, 5, 3), ((1080, 1920), 1024, 3, 3),
-                                           ((1080, 810), 640, 2, 3), ((333, 517), 640, 3, 3),
-                                           ((60, 100), 640, 2, 3), ((720, 1280), 640, 2, 8),
-                                           ((1, 1), 64, 1, 3)])
-def test_letterbox_batch_bitexact(lib, cuda, pkg, hw, S, n, stride):
+@pytest.mark.parametrize("hw,S,n,stride,off", [((720, 1280), 640, 5, 3, 0),
+                                               ((1080, 1920), 1024, 3, 3, 0),
+                                               ((1080, 810), 640, 2, 3, 0),
+                                               ((333, 517), 640, 3, 3, 5),
+                                               ((60, 100), 640, 2, 3, 0),
+                                               ((720, 1280), 640, 2, 8, 0),
+                                               ((1, 1), 64, 1, 3, 0), ((2, 3), 64, 2, 3, 9),
+                                               ((5, 7), 640, 3, 3, 1)])
+def test_letterbox_batch_bitexact(lib, cuda, pkg, hw, S, n, stride, off):
     """One launch over n equal-size frames into slots 1..n: every slot equals the oracle's
-    letterbox of its own frame, the untouched slot stays zero.  stride 8 exercises the
-    element-store path (view channels 0..2 of an 8-channel buffer)."""
+    letterbox of its own frame, the untouched slot stays zero.  stride 8 writes channels 0..2
+    of an 8-channel buffer; off > 0 starts the frames off any 16-byte boundary with `off`
+    bytes between them (rows then straddle the kernel's 16-byte staging words)."""
     from yolo11_cu_b200 import frames, runtime as rt
     bgrs = [frames.synthetic_bgr(*hw, seed=10 + i) for i in range(n)]
-    d = torch.from_numpy(np.stack(bgrs)).to(cuda)
+    fb = hw[0] * hw[1] * 3
+    flat = np.zeros(off + n * (fb + off), np.uint8)
+    for i, b in enumerate(bgrs):
+        flat[off + i * (fb + off):off + i * (fb + off) + fb] = b.ravel()
+    d = torch.from_numpy(flat).to(cuda)
     out = torch.zeros(n + 1, S, S, stride, dtype=torch.half, device=cuda)
     sc, top, left = C.c_float(), C.c_int(), C.c_int()
     v = rt.tview(out, 0, 3)
-    r = lib.yk_letterbox_batch(C.c_void_p(d.data_ptr()), hw[0] * hw[1] * 3, n, hw[0], hw[1],
+    r = lib.yk_letterbox_batch(C.c_void_p(d.data_ptr() + off), fb + off, n, hw[0], hw[1],
                                C.byref(v), 1, C.byref(sc), C.byref(top), C.byref(left),
                                torch.cuda.current_stream().cuda_stream)
     assert r == 0
@@ -64,7 +73,7 @@ def test_letterbox_batch_bitexact(lib, cuda, pkg, hw, S, n, stride):
     s_ = min(np.float32(S) / np.float32(hw[0]), np.float32(S) / np.float32(hw[1]))
     assert sc.value == np.float32(s_)
     # slot range past the view's batch is rejected without a launch
-    assert lib.yk_letterbox_batch(C.c_void_p(d.data_ptr()), hw[0] * hw[1] * 3, n, hw[0], hw[1],
+    assert lib.yk_letterbox_batch(C.c_void_p(d.data_ptr() + off), fb + off, n, hw[0], hw[1],
                                   C.byref(v), 2, None, None, None,
                                   torch.cuda.current_stream().cuda_stream) == -1
 

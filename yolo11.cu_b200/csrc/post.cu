@@ -15,124 +15,103 @@ namespace yk {
 
 // ---------------- letterbox (engine/engine.cu:968-998) ----------------
 // One launch letterboxes a batch of equal-size frames: grid (row blocks, frames), `rows`
-// output rows per block (chosen on the host so the grid fills the GPU: 1 row per block for
-// a single frame, 8 for a batch).  Each thread owns 8 consecutive output columns: their
-// horizontal sampling (source byte offsets, weights, inside / outside) is computed once and
-// reused on every row; rows go two at a time so both rows' source loads are in flight
-// together; the 8 pixels (24 fp16) leave as three 16-byte stores when the view is a dense
-// 3-channel image whose width is a multiple of 8 (else element stores).  Source bytes come
-// through the read-only cache: neighbouring threads read neighbouring bytes of the same
-// source rows, so each row is fetched from DRAM about once.  The arithmetic is the
-// reference's formula in explicitly rounded fp32 (src = (dst - off + 0.5) / scale - 0.5,
-// bilinear weights, /255, pad 114); /255 is dm_div255 (bit-identical to the division), so the
-// C oracle reproduces every value bit for bit.
-struct LbCols {
-  int o0[8], o1[8];
-  float wx[8];
-  unsigned inside;
-};
+// output rows per block (1 for a single frame, up to 4 for a batch, so the grid fills the
+// GPU).  The block first copies the two source rows each of its output rows samples into
+// shared memory with coalesced 16-byte loads (rows outside the image band are skipped), then
+// every thread computes whole output pixels, consecutive lanes on consecutive pixels, so the
+// shared-memory byte reads of a warp fall on neighbouring bytes and its fp16 stores on one
+// contiguous span.  The arithmetic is the reference's formula in explicitly rounded fp32
+// (src = (dst - off + 0.5) / scale - 0.5, bilinear weights, /255, pad 114); /255 is
+// dm_div255 (bit-identical to the division), so the C oracle reproduces every value.
+constexpr int kLbMaxRows = 4;
 
-template <bool kVec>
-__device__ __forceinline__ void letterbox_row(const uint8_t* __restrict__ img, int sh, int sw,
-                                              __half* out, int dh, int dw, int dstride,
-                                              float scale, int top, int nh, int y, int xb,
-                                              const LbCols& cs, __half pad) {
-  __align__(16) __half px[24];
-  if (y < top || y >= top + nh || !cs.inside) {
-#pragma unroll
-    for (int i = 0; i < 24; i++) px[i] = pad;
-  } else {
-    const float fy = DM_SUB(DM_DIV(DM_ADD((float)(y - top), 0.5f), scale), 0.5f);
-    int y0 = (int)floorf(fy);
-    const float wy = DM_SUB(fy, (float)y0);
-    const int y1 = min(y0 + 1, sh - 1);
-    y0 = max(y0, 0);
-    const uint8_t* r0 = img + (size_t)y0 * sw * 3;
-    const uint8_t* r1 = img + (size_t)y1 * sw * 3;
-    const float wy1 = DM_SUB(1.f, wy);
-    uint8_t p[8][12];                 // all 96 source bytes first: the loads overlap
-#pragma unroll
-    for (int j = 0; j < 8; j++)
-#pragma unroll
-      for (int c = 0; c < 3; c++) {
-        p[j][c] = __ldg(r0 + cs.o0[j] + c);
-        p[j][3 + c] = __ldg(r0 + cs.o1[j] + c);
-        p[j][6 + c] = __ldg(r1 + cs.o0[j] + c);
-        p[j][9 + c] = __ldg(r1 + cs.o1[j] + c);
-      }
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      if (!((cs.inside >> j) & 1u)) {
-        px[3 * j] = px[3 * j + 1] = px[3 * j + 2] = pad;
-        continue;
-      }
-      const float wx1 = DM_SUB(1.f, cs.wx[j]);
-      const float w00 = DM_MUL(wy1, wx1), w01 = DM_MUL(wy1, cs.wx[j]);
-      const float w10 = DM_MUL(wy, wx1), w11 = DM_MUL(wy, cs.wx[j]);
-      float v[3];
-#pragma unroll
-      for (int c = 0; c < 3; c++) {
-        float t = DM_MUL((float)p[j][c], w00);
-        t = DM_ADD(t, DM_MUL((float)p[j][3 + c], w01));
-        t = DM_ADD(t, DM_MUL((float)p[j][6 + c], w10));
-        v[c] = DM_ADD(t, DM_MUL((float)p[j][9 + c], w11));
-      }
-      // BGR in, RGB out
-      px[3 * j] = __float2half_rn(dm_div255(v[2]));
-      px[3 * j + 1] = __float2half_rn(dm_div255(v[1]));
-      px[3 * j + 2] = __float2half_rn(dm_div255(v[0]));
-    }
-  }
-  if (kVec) {
-    int4* o = (int4*)(out + ((size_t)y * dw + xb) * 3);
-    const int4* q = (const int4*)px;
-    o[0] = q[0];
-    o[1] = q[1];
-    o[2] = q[2];
-  } else {
-    for (int j = 0; j < 8 && xb + j < dw; j++) {
-      __half* o = out + ((size_t)y * dw + xb + j) * dstride;
-      o[0] = px[3 * j];
-      o[1] = px[3 * j + 1];
-      o[2] = px[3 * j + 2];
-    }
-  }
+__device__ __forceinline__ int lb_src_row(int y, int top, float scale, int sh, int which) {
+  const float fy = DM_SUB(DM_DIV(DM_ADD((float)(y - top), 0.5f), scale), 0.5f);
+  const int y0 = (int)floorf(fy);
+  return which ? min(y0 + 1, sh - 1) : max(y0, 0);
 }
 
-template <bool kVec>
 __global__ void __launch_bounds__(256) letterbox_kernel(
     const uint8_t* __restrict__ src, size_t src_frame, int sh, int sw, __half* dst,
     size_t dst_frame, int dh, int dw, int dstride, float scale, int top, int left, int nh,
-    int nw, int rows) {
+    int nw, int rows, int pitch) {
+  extern __shared__ __align__(16) uint8_t lb_rows[];   // [2 * rows][pitch]
   pdl_wait();     // the destination may still be read by the previous graph's kernels
   pdl_trigger();
-  const int xb = threadIdx.x * 8;
-  if (xb >= dw) return;
   const uint8_t* img = src + (size_t)blockIdx.y * src_frame;
   __half* out = dst + (size_t)blockIdx.y * dst_frame;
-  LbCols cs;
-  cs.inside = 0;
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const int x = xb + j;
-    const float fx = DM_SUB(DM_DIV(DM_ADD((float)(x - left), 0.5f), scale), 0.5f);
-    int x0 = (int)floorf(fx);
-    cs.wx[j] = DM_SUB(fx, (float)x0);
-    const int x1 = min(x0 + 1, sw - 1);
-    x0 = max(x0, 0);
-    cs.o0[j] = x0 * 3;
-    cs.o1[j] = x1 * 3;
-    if (x < dw && x >= left && x < left + nw) cs.inside |= 1u << j;
+  const int y_beg = blockIdx.x * rows, nrow = min(rows, dh - y_beg);
+  const int rb = sw * 3;
+  // stage: slot 2r / 2r + 1 hold the upper / lower source row of output row y_beg + r; a
+  // slot starts at the 16-byte boundary at or below its row, `shift` bytes before it
+  for (int slot = threadIdx.y; slot < 2 * nrow; slot += blockDim.y) {
+    const int y = y_beg + (slot >> 1);
+    if (y < top || y >= top + nh) continue;
+    const uint8_t* row = img + (size_t)lb_src_row(y, top, scale, sh, slot & 1) * rb;
+    const uintptr_t a0 = (uintptr_t)row & ~(uintptr_t)15, end = (uintptr_t)row + rb;
+    uint8_t* s = lb_rows + slot * pitch;
+    const int nvec = (int)((end - a0) >> 4);           // whole 16-byte words inside the row
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+      const uintptr_t p = a0 + ((uintptr_t)i << 4);
+      if (p < (uintptr_t)row) {                          // head word: the row's bytes only
+        for (int k = (int)((uintptr_t)row - p); k < 16; k++) s[i * 16 + k] = __ldg((const uint8_t*)p + k);
+      } else {
+        *(uint4*)(s + i * 16) = __ldg((const uint4*)p);
+      }
+    }
+    // bytes past the last whole word (all of a row shorter than one word), never before it
+    const uintptr_t t0 = max(a0 + ((uintptr_t)nvec << 4), (uintptr_t)row);
+    for (uintptr_t p = t0 + threadIdx.x; p < end; p += blockDim.x)
+      s[p - a0] = __ldg((const uint8_t*)p);
   }
+  __syncthreads();
   const __half pad = __float2half_rn(dm_div255(114.f));
-  const int y_beg = blockIdx.x * rows, y_end = min(dh, y_beg + rows);
-  int y = y_beg;
-  for (; y + 1 < y_end; y += 2) {
-    letterbox_row<kVec>(img, sh, sw, out, dh, dw, dstride, scale, top, nh, y, xb, cs, pad);
-    letterbox_row<kVec>(img, sh, sw, out, dh, dw, dstride, scale, top, nh, y + 1, xb, cs, pad);
+  const int tid = threadIdx.y * blockDim.x + threadIdx.x, nthr = blockDim.x * blockDim.y;
+  for (int r = 0; r < nrow; r++) {
+    const int y = y_beg + r;
+    __half* orow = out + (size_t)y * dw * dstride;
+    const bool row_in = y >= top && y < top + nh;
+    float wy = 0.f;
+    int sh0 = 0, sh1 = 0;
+    if (row_in) {
+      const float fy = DM_SUB(DM_DIV(DM_ADD((float)(y - top), 0.5f), scale), 0.5f);
+      wy = DM_SUB(fy, floorf(fy));
+      sh0 = (int)((uintptr_t)(img + (size_t)lb_src_row(y, top, scale, sh, 0) * rb) & 15);
+      sh1 = (int)((uintptr_t)(img + (size_t)lb_src_row(y, top, scale, sh, 1) * rb) & 15);
+    }
+    const uint8_t* s0 = lb_rows + (2 * r) * pitch + sh0;
+    const uint8_t* s1 = lb_rows + (2 * r + 1) * pitch + sh1;
+    const float wy1 = DM_SUB(1.f, wy);
+    for (int x = tid; x < dw; x += nthr) {
+      __half o0 = pad, o1 = pad, o2 = pad;
+      if (row_in && x >= left && x < left + nw) {
+        const float fx = DM_SUB(DM_DIV(DM_ADD((float)(x - left), 0.5f), scale), 0.5f);
+        int x0 = (int)floorf(fx);
+        const float wx = DM_SUB(fx, (float)x0);
+        const int x1 = min(x0 + 1, sw - 1) * 3;
+        x0 = max(x0, 0) * 3;
+        const float wx1 = DM_SUB(1.f, wx);
+        const float w00 = DM_MUL(wy1, wx1), w01 = DM_MUL(wy1, wx);
+        const float w10 = DM_MUL(wy, wx1), w11 = DM_MUL(wy, wx);
+        float v[3];
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+          float t = DM_MUL((float)s0[x0 + c], w00);
+          t = DM_ADD(t, DM_MUL((float)s0[x1 + c], w01));
+          t = DM_ADD(t, DM_MUL((float)s1[x0 + c], w10));
+          v[c] = DM_ADD(t, DM_MUL((float)s1[x1 + c], w11));
+        }
+        // BGR in, RGB out
+        o0 = __float2half_rn(dm_div255(v[2]));
+        o1 = __float2half_rn(dm_div255(v[1]));
+        o2 = __float2half_rn(dm_div255(v[0]));
+      }
+      __half* o = orow + (size_t)x * dstride;
+      o[0] = o0;
+      o[1] = o1;
+      o[2] = o2;
+    }
   }
-  if (y < y_end)
-    letterbox_row<kVec>(img, sh, sw, out, dh, dw, dstride, scale, top, nh, y, xb, cs, pad);
 }
 
 // ---------------- decode (engine/engine.cu:848-906) ----------------
@@ -537,28 +516,36 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   // classes run the greedy loop, one warp per class.  Both are exact greedy NMS, and both
   // stop a class at max_out kept boxes: its later survivors could never reach the output.
   int* moff = msegoff;                 // per class: first mask word, or -1 (greedy)
-  if (tid == 0) {
-    int off = 0;
-    for (int sg = 0; sg < nseg; sg++) {
-      const int m = segs[sg + 1] - segs[sg], words = (m + 31) >> 5;
+  // Up to kRankSortMax candidates the radix histogram area is unused: the masks live there
+  // (8448 words >= 512 x 16), else in the workspace.  Offsets by a block scan over the
+  // classes; a class takes the bit-mask path if it is mid-size and its words still fit.
+  const bool mask_smem = n <= kRankSortMax;
+  uint32_t* bmask = mask_smem ? hist : (uint32_t*)(wimg + L.bmask);
+  const int mask_cap = mask_smem ? 256 * kHistStride : L.bmask_words;
+  {
+    int need = 0;
+    if (tid < nseg) {
+      const int m = segs[tid + 1] - segs[tid], words = (m + 31) >> 5;
       // (only with the candidates in shared memory: from the workspace, the pair tests'
       // loads cost more than the greedy loop saves)
-      const bool bit = in_smem && m > 32 && m <= kBitMax && off + m * words <= L.bmask_words;
-      moff[sg] = bit ? off : -1;
-      if (bit) off += m * words;
+      if (in_smem && m > 32 && m <= kBitMax) need = m * words;
     }
-    moff[nseg] = off;
+    int total;
+    const int off = block_scan(need, wsum, &total);
+    if (tid < nseg) moff[tid] = need && off + need <= mask_cap ? off : -1;
+    if (tid == 0) moff[nseg] = min(total, mask_cap);
+    __syncthreads();
   }
-  __syncthreads();
-  uint32_t* bmask = (uint32_t*)(wimg + L.bmask);
   {
-    // flattened over all mask words of all bit-mask classes
+    // flattened over all mask words of all bit-mask classes (class sg owns words
+    // [moff[sg], moff[sg] + m * words); classes past the capacity have moff = -1)
     const int total = moff[nseg];
     int sg = 0;
     for (int t = tid; t < total; t += kNmsThreads) {
-      while (moff[sg] < 0 || (sg + 1 <= nseg && t >= moff[sg] + (segs[sg + 1] - segs[sg]) *
-                                                           ((segs[sg + 1] - segs[sg] + 31) >> 5)))
+      while (sg < nseg && (moff[sg] < 0 || t >= moff[sg] + (segs[sg + 1] - segs[sg]) *
+                                                        ((segs[sg + 1] - segs[sg] + 31) >> 5)))
         sg++;
+      if (sg >= nseg || t < moff[sg]) continue;   // a gap left by a class that did not fit
       const int s = segs[sg], m = segs[sg + 1] - s, words = (m + 31) >> 5;
       const int li = t - moff[sg], i = li / words, w = li - i * words;
       uint32_t bits = 0;
@@ -740,7 +727,7 @@ int yk_letterbox_batch(const uint8_t* bgr, size_t frame_stride, int n, int sh, i
                        const YkView* y, int slot0, float* scale_out, int* top_out,
                        int* left_out, yk_stream_t st) {
   if (!bgr || n < 1 || sh < 1 || sw < 1 || !view_ok(y) || y->C != 3 || slot0 < 0 ||
-      slot0 + n > y->batch || y->W > 2048 || (n > 1 && frame_stride < (size_t)sh * sw * 3))
+      slot0 + n > y->batch || (n > 1 && frame_stride < (size_t)sh * sw * 3))
     return YK_EINVAL;
   // geometry as yolo_preprocess computes it (engine/engine.cu:1704-1713)
   const float scale = std::min((float)y->H / sh, (float)y->W / sw);
@@ -751,18 +738,16 @@ int yk_letterbox_batch(const uint8_t* bgr, size_t frame_stride, int n, int sh, i
   if (left_out) *left_out = left;
   const size_t dframe = (size_t)y->H * y->W * y->stride;
   __half* dst = (__half*)y->ptr + y->coff + (size_t)slot0 * dframe;
-  const bool vec = y->stride == 3 && y->coff == 0 && y->W % 8 == 0 &&
-                   ((uintptr_t)y->ptr & 15) == 0;
-  const int threads = ((y->W + 7) / 8 + 31) / 32 * 32;
-  // rows per block: enough blocks for about eight per SM, at most 8 rows each
-  const int rows = std::max(1, std::min(8, (int)((long long)y->H * n / (148 * 8))));
-  const dim3 grid((y->H + rows - 1) / rows, n);
-  if (vec)
-    launch_k(letterbox_kernel<true>, grid, threads, 0, (cudaStream_t)st, bgr, frame_stride, sh,
-             sw, dst, dframe, y->H, y->W, y->stride, scale, top, left, nh, nw, rows);
-  else
-    launch_k(letterbox_kernel<false>, grid, threads, 0, (cudaStream_t)st, bgr, frame_stride, sh,
-             sw, dst, dframe, y->H, y->W, y->stride, scale, top, left, nh, nw, rows);
+  // rows per block: about eight blocks per SM, at most kLbMaxRows rows each
+  const int rows = std::max(1, std::min(kLbMaxRows, (int)((long long)y->H * n / (148 * 8))));
+  const int pitch = (sw * 3 + 16 + 15) & ~15;          // a row plus its alignment shift
+  const size_t smem = (size_t)2 * rows * pitch;
+  if (smem > 200 * 1024) return YK_EUNSUP;             // source rows wider than ~34k pixels
+  if (smem > 48 * 1024 && smem_attr(letterbox_kernel, (int)smem) != cudaSuccess)
+    return check_launch("letterbox attr");
+  const dim3 grid((y->H + rows - 1) / rows, n), block(64, 4);
+  launch_k(letterbox_kernel, grid, block, smem, (cudaStream_t)st, bgr, frame_stride, sh, sw,
+           dst, dframe, y->H, y->W, y->stride, scale, top, left, nh, nw, rows, pitch);
   note_launch();
   return check_launch("letterbox");
 }
