@@ -211,6 +211,8 @@ def oracle_postproc():
         lib.oref_preprocess_cls.restype = None
         lib.oref_preprocess_cls.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                             C.c_void_p]
+        lib.oref_quot_gt.restype = None
+        lib.oref_quot_gt.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
         lib.oref_div255_check.restype = C.c_long
         lib.oref_div255_check.argtypes = [C.c_uint, C.c_uint, C.c_uint]
         lib.oref_f2h.restype = C.c_uint16

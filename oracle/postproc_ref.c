@@ -270,6 +270,10 @@ void oref_mask(const uint16_t* coef, int nm, const uint16_t* proto, int pstride,
 /* exposed for the math tests */
 float oref_exp(float x) { return dm_exp(x); }
 float oref_sigmoid(float x) { return dm_sigmoid(x); }
+/* dm_quot_gt over arrays: out[i] = (RN(a[i] / b[i]) > t[i]) by the division-free test. */
+void oref_quot_gt(const float* a, const float* b, const float* t, int n, int* out) {
+  for (int i = 0; i < n; i++) out[i] = dm_quot_gt(a[i], b[i], t[i]);
+}
 /* Mismatches of dm_div255(v) against v / 255 over the binary32 bit patterns lo..hi (step). */
 long oref_div255_check(unsigned lo, unsigned hi, unsigned step) {
   long bad = 0;

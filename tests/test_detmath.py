@@ -122,3 +122,29 @@ def test_div255_is_the_division():
     assert lib.oref_div255_check(0, bits(256.0), 5) == 0
     for lo, hi in ((0.0, 2e-39), (0.999, 1.001), (254.0, 256.0)):
         assert lib.oref_div255_check(bits(lo), bits(hi), 1) == 0
+
+
+def test_quot_gt_matches_division():
+    """dm_quot_gt(a, b, t) (the division-free IoU threshold test of NMS) equals
+    RN(a / b) > t: random quotients near and far from random thresholds and next to the
+    midpoint between t and its successor, where the rounding decides."""
+    lib = graph_ref.oracle_postproc()
+    rng = np.random.default_rng(7)
+    n = 400000
+    t = rng.uniform(0, 1, n).astype(np.float32)
+    t[:1000] = np.float32(0.7)
+    t[1000:2000] = np.float32(0.45)
+    t[2000:2100] = 0.0
+    b = (rng.uniform(1, 1e5, n)).astype(np.float32)
+    near = (t.astype(np.float64) * b * (1 + rng.uniform(-1e-6, 1e-6, n))).astype(np.float32)
+    far = (b * rng.uniform(0, 1, n)).astype(np.float32)
+    tp = (t.view(np.uint32) + 1).view(np.float32)
+    mid = ((t.astype(np.float64) + tp) / 2 * b).astype(np.float32)   # near the midpoint
+    for a in (near, far, mid, np.nextafter(mid, np.float32(np.inf)), np.nextafter(mid, np.float32(0))):
+        a = np.ascontiguousarray(a, np.float32)
+        got = np.zeros(n, np.int32)
+        lib.oref_quot_gt(a.ctypes.data, b.ctypes.data, t.ctypes.data, n, got.ctypes.data)
+        want = (a / b) > t
+        assert np.array_equal(got.astype(bool), want)
+    # an exact tie a / b == m cannot occur: m = t + ulp(t)/2 has a 25-bit odd significand,
+    # so m * b needs more than the 24 bits a float a holds

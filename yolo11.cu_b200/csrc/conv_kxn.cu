@@ -57,6 +57,11 @@ struct KxnCfg {
   static constexpr int kBars = 512;
   static constexpr size_t kSmem =
       (size_t)kWST * kWin + (size_t)kBST * kB + 1024 + kBars + kBiasSmem * 4 + kRes;
+  // TMA epilogue: per epilogue warp and (sub-tile, channel block) one staging box of
+  // 2 rows x kPatchUse positions x 16 channels (residual in, then the output in place)
+  static constexpr int kEpiBox = 2 * 14 * 16 * 2;      // bytes one box moves
+  static constexpr int kEpiStride = 1024;              // boxes on 128-byte boundaries
+  static_assert(kRes >= 16 * MT * (BN / (16 * kH)) * kEpiStride, "TMA epilogue staging");
   static_assert(kNacc * kTileCols <= 512, "TMEM budget");
   static_assert(kSmem <= 232448, "smem budget");
   static_assert(3 * BN <= 256 && BN % 16 == 0, "N = 3 * BN");
@@ -65,7 +70,8 @@ struct KxnCfg {
 template <int BN, int MT, int CB>
 __global__ void __launch_bounds__(kKxThreads, 1)
 conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
-                const __grid_constant__ CUtensorMap tmX) {
+                const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmY,
+                const __grid_constant__ CUtensorMap tmR) {
   using Cfg = KxnCfg<BN, MT, CB>;
   constexpr int kRB = Cfg::kRB, WST = Cfg::kWST;
   extern __shared__ uint8_t smem_raw[];
@@ -80,7 +86,8 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
   auto tfull = [&](int b) { return bar_base + 8u * (2 * WST + Cfg::kBST + b); };
   auto tempty = [&](int b) { return bar_base + 8u * (2 * WST + Cfg::kBST + Cfg::kNacc + b); };
   const uint32_t tslot = bar_base + 8u * (2 * WST + Cfg::kBST + 2 * Cfg::kNacc);
-  static_assert(8 * (2 * WST + Cfg::kBST + 2 * Cfg::kNacc) + 16 <= Cfg::kBars, "barrier area");
+  static_assert(8 * (2 * WST + Cfg::kBST + 2 * Cfg::kNacc) + 16 + 8 * 16 <= Cfg::kBars, "barrier area");
+  auto rbar = [&](int e) { return tslot + 16u + 8u * e; };   // epilogue warp e's residual boxes
   volatile uint32_t* tslot_ptr = (volatile uint32_t*)(smem_raw + (tslot - raw));
   volatile int* abort_flag = (volatile int*)(smem_raw + (tslot - raw) + 8);
   float* bias_s = (float*)(smem_raw + (bar_base - raw) + Cfg::kBars);
@@ -92,10 +99,15 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
     for (int s = 0; s < WST; s++) { mbar_init(wfull(s), 1); mbar_init(wempty(s), 1); }
     for (int s = 0; s < Cfg::kBST; s++) mbar_init(bfull(s), 1);
     for (int b = 0; b < Cfg::kNacc; b++) { mbar_init(tfull(b), 1); mbar_init(tempty(b), Cfg::kH * kEpiGroup); }
+    for (int e = 0; e < 16; e++) mbar_init(rbar(e), 1);
     *abort_flag = 0;
     mbar_fence_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmW) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmX) : "memory");
+    if (a.tma_epi) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmY) : "memory");
+      if (a.res) asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmR) : "memory");
+    }
   }
   pdl_wait();
   pdl_trigger();
@@ -151,7 +163,9 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
       for (int i = tid - 128; i < a.Cout; i += 512) bias_s[i] = a.bias[i];
     asm volatile("bar.sync 1, 512;" ::: "memory");
     const float* bias = bias_cached ? bias_s : a.bias;
-    uint32_t li = 0;
+    const int e = warp - 4;                                  // epilogue warp index
+    const uint32_t ebuf = res_base + (uint32_t)(e * MT * (BN / (16 * kH)) * Cfg::kEpiStride);
+    uint32_t li = 0, ruse = 0;
     for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, li++) {
       if ((int)(li % Cfg::kNacc) != grp) continue;
       const int acc = li % Cfg::kNacc;
@@ -160,11 +174,32 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
       const int img = mtile / per_img, r = mtile - img * per_img;
       const int ty = r / a.ntx, tx = r - ty * a.ntx;
       const int x = tx * kPatchUse + pc;
-      // residual rows fetched before the accumulator wait, so their latency hides behind
-      // the MMAs: [mt][channel block][8-channel half]
       constexpr int kNcb = BN / (16 * kH);
-      const uint32_t rslot = res_base + (uint32_t)(tid - 128) * Cfg::kResSlot;
-      if (a.res) {
+      const int y_box = ty * 8 * MT + 2 * sp;        // first image row of this warp's box
+      if (a.tma_epi) {
+        // residual boxes before the accumulator wait, so their latency hides behind the
+        // MMAs; the staging boxes are free once this warp's earlier stores have read them
+        if (lane == 0) {
+          bulk_wait_read0();
+          if (a.res) {
+            int nbox = 0;
+            for (int cb = 0; cb < kNcb; cb++) nbox += n0 + 16 * half + 16 * kH * cb < a.Cout;
+            mbar_expect_tx(rbar(e), (uint32_t)(MT * nbox * Cfg::kEpiBox));
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+              for (int cb = 0; cb < kNcb; cb++) {
+                const int c0 = 16 * half + 16 * kH * cb;
+                if (n0 + c0 < a.Cout)
+                  tma_load_4d(ebuf + (uint32_t)((mt * kNcb + cb) * Cfg::kEpiStride), &tmR, rbar(e),
+                              n0 + c0, tx * kPatchUse, y_box + mt * 8, img);
+              }
+          }
+        }
+        __syncwarp();
+      } else if (a.res) {
+        // residual rows by cp.async: [mt][channel block][8-channel half]
+        const uint32_t rslot = res_base + (uint32_t)(tid - 128) * Cfg::kResSlot;
 #pragma unroll
         for (int mt = 0; mt < MT; mt++) {
           const int y = ty * 8 * MT + mt * 8 + pr;
@@ -184,7 +219,18 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
       }
       if (!mbar_wait(tfull(acc), use & 1, 0x303)) { *abort_flag = 1; break; }
       tc_fence_after();
-      if (a.res) cp_async_wait<0>();
+#ifdef YK_KXN_DIAG_NOEPI   // diagnostic builds only: drain the accumulator without reading it
+      if (a.tma_epi && a.res) { mbar_wait(rbar(e), ruse & 1, 0x307); ruse++; }
+      tc_fence_before();
+      mbar_arrive(tempty(acc));
+      continue;
+#endif
+      if (a.tma_epi && a.res) {
+        if (!mbar_wait(rbar(e), ruse & 1, 0x307)) { *abort_flag = 1; break; }
+        ruse++;
+      } else if (a.res) {
+        cp_async_wait<0>();
+      }
 #pragma unroll 1
       for (int mt = 0; mt < MT; mt++) {
         const int y = ty * 8 * MT + mt * 8 + pr;
@@ -211,43 +257,69 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
             const float p2 = __shfl_down_sync(~0u, __uint_as_float(rg[3 * j + 2]), 2);
             v[j] = (__uint_as_float(rg[3 * j]) + p1) + p2;
           }
-          if (!mok) continue;
+          // box position of this lane (2 rows x kPatchUse positions x 16 channels, 32 bytes
+          // per position); the halo lanes (pc >= kPatchUse) have none
+          const uint32_t box = ebuf + (uint32_t)((mt * kNcb + cb) * Cfg::kEpiStride);
+          const uint32_t bpos = box + (uint32_t)(((lane >> 4) * kPatchUse + pc) * 32);
+          if (a.tma_epi ? pc < kPatchUse : mok) {
 #pragma unroll
-          for (int h = 0; h < 2; h++) {
-            const int nn = n0 + c0 + 8 * h;
-            if (nn >= a.Cout) break;
-            const float4 b0 = *(const float4*)(bias + nn);
-            const float4 b1 = *(const float4*)(bias + nn + 4);
-            const float2 bb[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
-                                  make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
-            uint4 o;
-            __half2* oh = (__half2*)&o;
-            if (!has_res) {
+            for (int h = 0; h < 2; h++) {
+              const int nn = n0 + c0 + 8 * h;
+              uint4 o = make_uint4(0u, 0u, 0u, 0u);
+              __half2* oh = (__half2*)&o;
+              if (nn < a.Cout) {
+                const float4 b0 = *(const float4*)(bias + nn);
+                const float4 b1 = *(const float4*)(bias + nn + 4);
+                const float2 bb[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
+                                      make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
+                if (!has_res) {
 #pragma unroll
-              for (int q = 0; q < 4; q++)
-                oh[q] = bias_act2(make_float2(v[8 * h + 2 * q], v[8 * h + 2 * q + 1]), bb[q],
-                                  a.act);
-            } else {
-              uint4 rv;
-              asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                           : "=r"(rv.x), "=r"(rv.y), "=r"(rv.z), "=r"(rv.w)
-                           : "r"(rslot + (uint32_t)(((mt * kNcb + cb) * 2 + h) * 16)));
-              const __half2* rh = (const __half2*)&rv;
+                  for (int q = 0; q < 4; q++)
+                    oh[q] = bias_act2(make_float2(v[8 * h + 2 * q], v[8 * h + 2 * q + 1]), bb[q],
+                                      a.act);
+                } else {
+                  const uint32_t raddr =
+                      a.tma_epi ? bpos + 16u * h
+                                : res_base + (uint32_t)(tid - 128) * Cfg::kResSlot +
+                                      (uint32_t)(((mt * kNcb + cb) * 2 + h) * 16);
+                  uint4 rv;
+                  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                               : "=r"(rv.x), "=r"(rv.y), "=r"(rv.z), "=r"(rv.w)
+                               : "r"(raddr));
+                  const __half2* rh = (const __half2*)&rv;
 #pragma unroll
-              for (int q = 0; q < 4; q++) {
-                float v0 = v[8 * h + 2 * q] + bb[q].x, v1 = v[8 * h + 2 * q + 1] + bb[q].y;
-                if (a.act == 1) { v0 = silu_fast(v0); v1 = silu_fast(v1); }
-                const float2 f = __half22float2(rh[q]);
-                oh[q] = __floats2half2_rn(v0 + f.x, v1 + f.y);
+                  for (int q = 0; q < 4; q++) {
+                    float v0 = v[8 * h + 2 * q] + bb[q].x, v1 = v[8 * h + 2 * q + 1] + bb[q].y;
+                    if (a.act == 1) { v0 = silu_fast(v0); v1 = silu_fast(v1); }
+                    const float2 f = __half22float2(rh[q]);
+                    oh[q] = __floats2half2_rn(v0 + f.x, v1 + f.y);
+                  }
+                }
+              } else if (!a.tma_epi) {
+                break;
               }
+              if (a.tma_epi)
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(bpos + 16u * h),
+                             "r"(o.x), "r"(o.y), "r"(o.z), "r"(o.w)
+                             : "memory");
+              else
+                *(uint4*)(yrow + nn) = o;
             }
-            *(uint4*)(yrow + nn) = o;
+          }
+          if (a.tma_epi) {   // the box leaves by one bulk tensor store (clipped at the edges)
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_4d(&tmY, box, n0 + c0, tx * kPatchUse, y_box + mt * 8, img);
+              bulk_commit();
+            }
           }
         }
       }
       tc_fence_before();
       mbar_arrive(tempty(acc));
     }
+    if (a.tma_epi && lane == 0) bulk_wait0();   // every store has completed before exit
   } else if (warp == kKxMma && lane == 0) {
     // ---------------- MMA issuer ----------------
     constexpr uint32_t idesc = idesc_f16_m128(3 * BN);
@@ -278,8 +350,10 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
               // A: the window shifted by ky patch rows (the swizzle follows the absolute
               // shared-memory address, so whole-row shifts need no descriptor base offset)
               const uint32_t sa = win + (uint32_t)((mt * 8 + ky) * kPatchCols * kRB + kk * 32);
+#ifndef YK_KXN_DIAG_NOMMA   // diagnostic builds only: skip the MMAs, keep the pipeline
               tc_mma_f16(d + mt * Cfg::kSub, swz_desc<kRB>(sa), swz_desc<kRB>(sb + kk * 32),
                          idesc, (cb | ky | kk) != 0);
+#endif
             }
         }
         if (ok) tc_commit(wempty(ws));
@@ -323,6 +397,35 @@ static bool encode_kxn_w(CUtensorMap* m, const __half* w, int Cin, int Cout, int
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 4-D map {c, x, y, image} over an output / residual view (c = the view's channels, element
+// stride `stride`): box {16 channels, kPatchUse positions, 2 rows, 1} = one epilogue warp's
+// share of a tile, no swizzle.
+static bool encode_epi_box(CUtensorMap* m, const __half* p, int C, int W, int H, int N,
+                           int stride) {
+  static PFN_cuTensorMapEncodeTiled encode = nullptr;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+              cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return false;
+      encode = (PFN_cuTensorMapEncodeTiled)fn;
+    }
+  }
+  const cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N};
+  const cuuint64_t strides[3] = {(cuuint64_t)stride * 2, (cuuint64_t)W * stride * 2,
+                                 (cuuint64_t)H * W * stride * 2};
+  const cuuint32_t box[4] = {16, (cuuint32_t)kPatchUse, 2, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(p), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int MT, int CB>
 static int launch_kxn(const PatchArgs& a, const YkView* x, cudaStream_t st) {
   using Cfg = KxnCfg<BN, MT, CB>;
@@ -332,11 +435,16 @@ static int launch_kxn(const PatchArgs& a, const YkView* x, cudaStream_t st) {
   if (dev < 0 || dev >= 64) return YK_EUNSUP;
   if (!g_num_sms[dev]) cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
   const int grid = a.ntiles < g_num_sms[dev] ? a.ntiles : g_num_sms[dev];
-  CUtensorMap tmW, tmX;
+  CUtensorMap tmW, tmX, tmY = {}, tmR = {};
   if (!encode_kxn_w(&tmW, a.w, a.Cin, a.Cout, BN, CB)) return YK_EUNSUP;
   if (!encode_patch_x(&tmX, a.x, a.Cin, a.W, a.H, x->batch, x->stride, Cfg::kRows, CB))
     return YK_EUNSUP;
-  launch_k(conv_kxn_kernel<BN, MT, CB>, grid, kKxThreads, Cfg::kSmem, st, a, tmW, tmX);
+  PatchArgs b = a;
+  if (b.tma_epi &&
+      !(encode_epi_box(&tmY, b.y, b.Cout, b.W, b.H, x->batch, b.ys) &&
+        (!b.res || encode_epi_box(&tmR, b.res, b.Cout, b.W, b.H, x->batch, b.rs))))
+    b.tma_epi = 0;
+  launch_k(conv_kxn_kernel<BN, MT, CB>, grid, kKxThreads, Cfg::kSmem, st, b, tmW, tmX, tmY, tmR);
   note_launch();
   return check_launch("conv_kxn");
 }
@@ -351,7 +459,7 @@ int conv_kxn(const YkView* x, const YkView* y, const YkView* res, const YkConv* 
       ((uintptr_t)p->weight & 15))
     return YK_EUNSUP;
   if (y->H != x->H || y->W != x->W) return YK_EINVAL;
-  PatchArgs a;
+  PatchArgs a{};
   DView X = dview(*x), Y = dview(*y);
   a.x = X.p; a.H = x->H; a.W = x->W;
   a.y = Y.p; a.ys = y->stride;
@@ -366,6 +474,13 @@ int conv_kxn(const YkView* x, const YkView* y, const YkView* res, const YkConv* 
   const long long nt = (long long)y->batch * a.nty * a.ntx * a.ntn;
   if (nt > 0x7fffffffLL) return YK_EUNSUP;
   a.ntiles = (int)nt;
+  // outputs (and residual) by 4-D TMA boxes when the views are 16-byte rows
+  static const bool direct = [] {
+    const char* e = getenv("YK_KXN_DIRECT_EPI");
+    return e && *e && *e != '0';
+  }();
+  a.tma_epi = !direct && ((uintptr_t)a.y & 15) == 0 && a.ys % 8 == 0 &&
+              (!a.res || (((uintptr_t)a.res & 15) == 0 && a.rs % 8 == 0));
   switch (bn * 1000 + ms * 100 + cbw) {
     case 32132: return launch_kxn<32, 1, 32>(a, x, st);
     case 32232: return launch_kxn<32, 2, 32>(a, x, st);

@@ -32,6 +32,7 @@ struct PatchArgs {
   int ncb;          // 64-channel blocks of Cin
   int nty, ntx;     // patch tiles per image (rows of 8*MT, columns of 14)
   int ntn, ntiles;
+  int tma_epi;      // kx-folded kernel: residual in / output out by 4-D TMA boxes (0 = direct)
 };
 
 constexpr int kPatchCols = 16;     // positions per patch row (row pitch)
@@ -68,6 +69,16 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
       "l"((uint64_t)map), "r"(bar), "r"(c), "r"(x), "r"(y), "r"(n)
+      : "memory");
+}
+// 4-D tiled bulk store shared -> global (coordinates: channel, x, y, image; the store clips
+// elements past the tensor map's extents).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c, int x,
+                                             int y, int n) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          (uint64_t)map),
+      "r"(src), "r"(c), "r"(x), "r"(y), "r"(n)
       : "memory");
 }
 
@@ -392,7 +403,7 @@ int conv_patch(const YkView* x, const YkView* y, const YkView* res, const YkConv
       ((uintptr_t)x->ptr & 15) || x->stride % 8 || (x->coff % 8))
     return YK_EUNSUP;
   if (y->H != x->H || y->W != x->W) return YK_EINVAL;
-  PatchArgs a;
+  PatchArgs a{};
   DView X = dview(*x), Y = dview(*y);
   a.x = X.p; a.H = x->H; a.W = x->W;
   a.y = Y.p; a.ys = y->stride;

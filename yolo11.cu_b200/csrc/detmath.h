@@ -145,6 +145,18 @@ DM_HD float dm_dfl16(const float* l) {
 
 // IoU > thr test of two xyxy boxes with the reference's formula
 // (inter / (area_a + area_b - inter), union must be > 0).
+// RN(a / b) > t for b > 0, 0 <= t < FLT_MAX, without a division: with t+ the next float
+// above t and m = (t + t+) / 2 their midpoint, RN(q) > t holds exactly when q > m, or q == m
+// and round-to-nearest-even takes m up to t+ (t+ has an even significand).  m has at most 25
+// significant bits and b 24, so m * b is exact in binary64 and the test on a > m * b is exact.
+DM_HD int dm_quot_gt(float a, float b, float t) {
+  const float tp = dm_bits2f(dm_f2bits(t) + 1u);
+  const double m = 0.5 * ((double)t + (double)tp);
+  const double mb = m * (double)b;
+  const double ad = (double)a;
+  return ad > mb || (ad == mb && (dm_f2bits(tp) & 1u) == 0u);
+}
+
 DM_HD int dm_iou_gt(float ax1, float ay1, float ax2, float ay2, float aarea,
                     float bx1, float by1, float bx2, float by2, float thr) {
   float xx1 = ax1 > bx1 ? ax1 : bx1, yy1 = ay1 > by1 ? ay1 : by1;
@@ -156,7 +168,9 @@ DM_HD int dm_iou_gt(float ax1, float ay1, float ax2, float ay2, float aarea,
   if (inter == 0.f && thr >= 0.f) return 0;   // 0 / ua is 0, or ua > 0 fails: never > thr
   float barea = DM_MUL(DM_SUB(bx2, bx1), DM_SUB(by2, by1));
   float ua = DM_SUB(DM_ADD(aarea, barea), inter);
-  return ua > 0.f && DM_DIV(inter, ua) > thr;
+  if (!(ua > 0.f)) return 0;
+  if (!(thr >= 0.f) || !(thr < 3.0e38f)) return DM_DIV(inter, ua) > thr;
+  return dm_quot_gt(inter, ua, thr);
 }
 
 DM_HD float dm_area(float x1, float y1, float x2, float y2) {

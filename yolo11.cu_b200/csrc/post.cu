@@ -238,6 +238,16 @@ __global__ void __launch_bounds__(256) decode_kernel(DevLevels lv, int batch, in
 //   4. survivors in score order, the first max_out written out.
 // Up to kNmsSmemCand candidates live in shared memory, more in the workspace.
 constexpr int kNmsThreads = 1024;
+// Diagnostic builds (-DYK_NMS_PROF) record %globaltimer at each phase boundary of image 0.
+#ifdef YK_NMS_PROF
+__device__ unsigned long long g_nms_prof[8];
+#define NMS_MARK(i) do { if (blockIdx.x == 0 && threadIdx.x == 0) g_nms_prof[i] = globaltimer(); } while (0)
+extern "C" int yk_nms_prof(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, g_nms_prof, sizeof g_nms_prof) == cudaSuccess ? 0 : -1;
+}
+#else
+#define NMS_MARK(i) ((void)0)
+#endif
 constexpr int kNmsSmemCand = 4096;
 constexpr int kRankSortMax = 512;
 constexpr int kMaxClasses = 1024;
@@ -364,6 +374,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   __shared__ float kept_s[32][kKeptSmem][5];
   const int img = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int A = L.A;
+  NMS_MARK(0);
   uint8_t* wimg = ws + (size_t)img * L.per_img;
   const float* rec = (const float*)(wimg + L.rec);
   const int* flag = (const int*)(wimg + L.flag);
@@ -436,6 +447,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
     atomicOr(&s_bits[2], cor); atomicAnd(&s_bits[3], cand_);
   }
   __syncthreads();
+  NMS_MARK(1);
 
   // 2. score order (ordS) and class order (ordC), both stable on the anchor order
   const uint32_t* ordS;
@@ -450,13 +462,23 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
     const unsigned long long ks = ((unsigned long long)skey[mi] << 20) | (unsigned)mi;
     const unsigned long long kc = ((unsigned long long)ccls[mi] << 52) | ks;
     int rs = 0, rc = 0;
-    if (has)
-      for (int j = part; j < n; j += lanes) {
+    if (has) {
+      // four candidates per step: their shared-memory loads are independent and overlap
+      auto cmp = [&](int j) {
         const unsigned long long js = ((unsigned long long)skey[j] << 20) | (unsigned)j;
         const unsigned long long jc = ((unsigned long long)ccls[j] << 52) | js;
         rs += js < ks;
         rc += jc < kc;
+      };
+      int j = part;
+      for (; j + 3 * lanes < n; j += 4 * lanes) {
+        cmp(j);
+        cmp(j + lanes);
+        cmp(j + 2 * lanes);
+        cmp(j + 3 * lanes);
       }
+      for (; j < n; j += lanes) cmp(j);
+    }
     for (int o = 1; o < lanes; o <<= 1) {
       rs += __shfl_xor_sync(~0u, rs, o);
       rc += __shfl_xor_sync(~0u, rc, o);
@@ -491,6 +513,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
     ordC = bufs[ccur];
   }
 
+  NMS_MARK(2);
   // 3. class segments of the class order
   {
     int nseg_running = 0;
@@ -508,6 +531,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   const int nseg = s_total;
   if (tid == 0) segs[nseg] = n;
   __syncthreads();
+  NMS_MARK(3);
 
   // 4. per-class suppression in score order.  Classes of 33..kBitMax candidates whose bit
   // masks fit the workspace region, with all candidates in shared memory, use bit masks: the whole block builds them (bit j of row
@@ -535,30 +559,30 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
     if (tid < nseg) moff[tid] = need && off + need <= mask_cap ? off : -1;
     if (tid == 0) moff[nseg] = min(total, mask_cap);
     __syncthreads();
+  NMS_MARK(4);
   }
   {
-    // flattened over all mask words of all bit-mask classes (class sg owns words
-    // [moff[sg], moff[sg] + m * words); classes past the capacity have moff = -1)
-    const int total = moff[nseg];
-    int sg = 0;
-    for (int t = tid; t < total; t += kNmsThreads) {
-      while (sg < nseg && (moff[sg] < 0 || t >= moff[sg] + (segs[sg + 1] - segs[sg]) *
-                                                        ((segs[sg + 1] - segs[sg] + 31) >> 5)))
-        sg++;
-      if (sg >= nseg || t < moff[sg]) continue;   // a gap left by a class that did not fit
+    // one warp per row of a bit-mask class: lane k tests the pair (i, j = 32 w + k) and a
+    // ballot gives word w of row i (bit k: candidate j is suppressed by candidate i);
+    // words below the diagonal are zero
+    for (int sg = 0; sg < nseg; sg++) {
+      if (moff[sg] < 0) continue;                         // uniform across the block
       const int s = segs[sg], m = segs[sg + 1] - s, words = (m + 31) >> 5;
-      const int li = t - moff[sg], i = li / words, w = li - i * words;
-      uint32_t bits = 0;
-      if (w * 32 + 31 <= i) { bmask[t] = 0u; continue; }   // below the diagonal: no later j
-      const float4 bi = box[ordC[s + i]];
-      const float ai = dm_area(bi.x, bi.y, bi.z, bi.w);
-      for (int k = max(0, i + 1 - w * 32); k < 32; k++) {
-        const int j = w * 32 + k;
-        if (j >= m) break;
-        const float4 bj = box[ordC[s + j]];
-        if (dm_iou_gt(bi.x, bi.y, bi.z, bi.w, ai, bj.x, bj.y, bj.z, bj.w, iou)) bits |= 1u << k;
+      uint32_t* rows = bmask + moff[sg];
+      for (int i = warp; i < m; i += kNmsThreads >> 5) {
+        const float4 bi = box[ordC[s + i]];
+        const float ai = dm_area(bi.x, bi.y, bi.z, bi.w);
+        for (int w = 0; w < words; w++) {
+          const int j = w * 32 + lane;
+          bool sup = false;
+          if (j > i && j < m) {
+            const float4 bj = box[ordC[s + j]];
+            sup = dm_iou_gt(bi.x, bi.y, bi.z, bi.w, ai, bj.x, bj.y, bj.z, bj.w, iou);
+          }
+          const unsigned bits = __ballot_sync(~0u, sup);
+          if (lane == 0) rows[(size_t)i * words + w] = bits;
+        }
       }
-      bmask[t] = bits;
     }
   }
   __syncthreads();
@@ -640,6 +664,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
     }
   }
   __syncthreads();
+  NMS_MARK(6);
 
   // 5. survivors in score order, the first max_out kept
   int base = 0;
@@ -663,6 +688,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
     outcnt[img] = min(base, max_out);
     rawcnt[img] = n;
   }
+  NMS_MARK(7);
 }
 
 // ---------------- masks (engine/engine.cu:1129-1158) ----------------
