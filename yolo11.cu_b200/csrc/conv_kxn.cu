@@ -32,7 +32,7 @@ namespace yk {
 constexpr int kKxMma = 20;
 constexpr int kKxThreads = 32 * (kKxMma + 1);
 
-template <int BN, int MT, int CB>
+template <int BN, int MT, int CB, bool WR = false>
 struct KxnCfg {
   static constexpr int kRows = 8 * MT + 2;
   static constexpr int kRB = CB * 2;
@@ -46,13 +46,15 @@ struct KxnCfg {
   // epilogue warps per sub-partition and tile: 16 epilogue warps = kNacc groups of 4 * kH,
   // the kH warps of one sub-partition taking alternate 16-channel blocks
   static constexpr int kH = 4 / kNacc;
-  // window ring: as deep as 200 KB allows (up to 6), so small tiles keep several TMA loads
-  // in flight; each slot holds a window and its three weight stages
+  // window ring: as deep as 216 KB allows (up to 6), so small tiles keep several TMA loads
+  // in flight; each slot holds a window and its three weight stages, or, with WR (the whole
+  // filter is one block, loaded once and kept), the three stages exist once
   static constexpr int kResSlot = MT * (BN / (16 * kH)) * 2 * 16;   // residual bytes per thread
   static constexpr int kRes = 512 * kResSlot;                      // all epilogue threads
-  static constexpr int kWSTfit = (216 * 1024 - kRes) / (kWin + 3 * kB);
+  static constexpr int kWSTfit =
+      WR ? (216 * 1024 - kRes - 3 * kB) / kWin : (216 * 1024 - kRes) / (kWin + 3 * kB);
   static constexpr int kWST = kWSTfit > 6 ? 6 : kWSTfit < 2 ? 2 : kWSTfit;
-  static constexpr int kBST = 3 * kWST;
+  static constexpr int kBST = WR ? 3 : 3 * kWST;
   static constexpr int kTmemCols = kNacc * kTileCols <= 256 ? 256 : 512;
   static constexpr int kBars = 512;
   static constexpr size_t kSmem =
@@ -67,12 +69,12 @@ struct KxnCfg {
   static_assert(3 * BN <= 256 && BN % 16 == 0, "N = 3 * BN");
 };
 
-template <int BN, int MT, int CB>
+template <int BN, int MT, int CB, bool WR>
 __global__ void __launch_bounds__(kKxThreads, 1)
 conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
                 const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmY,
                 const __grid_constant__ CUtensorMap tmR) {
-  using Cfg = KxnCfg<BN, MT, CB>;
+  using Cfg = KxnCfg<BN, MT, CB, WR>;
   constexpr int kRB = Cfg::kRB, WST = Cfg::kWST;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -426,10 +428,11 @@ static bool encode_epi_box(CUtensorMap* m, const __half* p, int C, int W, int H,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int MT, int CB>
+template <int BN, int MT, int CB, bool WR = false>
 static int launch_kxn(const PatchArgs& a, const YkView* x, cudaStream_t st) {
-  using Cfg = KxnCfg<BN, MT, CB>;
-  if (smem_attr(conv_kxn_kernel<BN, MT, CB>, (int)Cfg::kSmem) != cudaSuccess) return check_launch("conv_kxn attr");
+  if (!WR && a.ncb == 1 && a.ntn == 1) return launch_kxn<BN, MT, CB, true>(a, x, st);
+  using Cfg = KxnCfg<BN, MT, CB, WR>;
+  if (smem_attr(conv_kxn_kernel<BN, MT, CB, WR>, (int)Cfg::kSmem) != cudaSuccess) return check_launch("conv_kxn attr");
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return YK_EUNSUP;
@@ -444,7 +447,7 @@ static int launch_kxn(const PatchArgs& a, const YkView* x, cudaStream_t st) {
       !(encode_epi_box(&tmY, b.y, b.Cout, b.W, b.H, x->batch, b.ys) &&
         (!b.res || encode_epi_box(&tmR, b.res, b.Cout, b.W, b.H, x->batch, b.rs))))
     b.tma_epi = 0;
-  launch_k(conv_kxn_kernel<BN, MT, CB>, grid, kKxThreads, Cfg::kSmem, st, b, tmW, tmX, tmY, tmR);
+  launch_k(conv_kxn_kernel<BN, MT, CB, WR>, grid, kKxThreads, Cfg::kSmem, st, b, tmW, tmX, tmY, tmR);
   note_launch();
   return check_launch("conv_kxn");
 }

@@ -453,39 +453,52 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   const uint32_t* ordS;
   const uint32_t* ordC;
   if (n <= kRankSortMax) {
-    // rank sort, four lanes per candidate up to 256 candidates, two up to 512 (each lane
-    // counts its share of the list; the shares are summed by shuffles)
-    const int sh = n <= 256 ? 2 : 1, lanes = 1 << sh;
-    const int me = tid >> sh, part = tid & (lanes - 1);
-    const bool has = me < n;
-    const int mi = has ? me : 0;
-    const unsigned long long ks = ((unsigned long long)skey[mi] << 20) | (unsigned)mi;
-    const unsigned long long kc = ((unsigned long long)ccls[mi] << 52) | ks;
-    int rs = 0, rc = 0;
-    if (has) {
-      // four candidates per step: their shared-memory loads are independent and overlap
-      auto cmp = [&](int j) {
-        const unsigned long long js = ((unsigned long long)skey[j] << 20) | (unsigned)j;
-        const unsigned long long jc = ((unsigned long long)ccls[j] << 52) | js;
-        rs += js < ks;
-        rc += jc < kc;
-      };
-      int j = part;
-      for (; j + 3 * lanes < n; j += 4 * lanes) {
-        cmp(j);
-        cmp(j + lanes);
-        cmp(j + 2 * lanes);
-        cmp(j + 3 * lanes);
+    // bitonic sort of the unique 64-bit keys (score key, index) and (class, score key,
+    // index) in the radix histogram area, unused on this path: threads 0-511 sort the first,
+    // 512-1023 the second, one compare-exchange each per stage; padding keys sort last
+    unsigned long long* kS = (unsigned long long*)hist;
+    unsigned long long* kC = kS + kRankSortMax;
+    int P = 2;
+    while (P < n) P <<= 1;
+    for (int i = tid; i < P; i += kNmsThreads) {
+      if (i < n) {
+        const unsigned long long ks = ((unsigned long long)skey[i] << 20) | (unsigned)i;
+        kS[i] = ks;
+        kC[i] = ((unsigned long long)ccls[i] << 52) | ks;
+      } else {
+        kS[i] = kC[i] = ~0ull;
       }
-      for (; j < n; j += lanes) cmp(j);
     }
-    for (int o = 1; o < lanes; o <<= 1) {
-      rs += __shfl_xor_sync(~0u, rs, o);
-      rc += __shfl_xor_sync(~0u, rc, o);
+    __syncthreads();
+    // element p of each array lives in thread p's register; partner distances j >= 32 go
+    // through shared memory (one barrier per stage), j < 32 by warp shuffles
+    unsigned long long* arr = tid < kRankSortMax ? kS : kC;
+    const int p = tid & (kRankSortMax - 1);
+    const bool live = p < P;
+    unsigned long long key = live ? arr[p] : ~0ull;
+    for (int k = 2; k <= P; k <<= 1) {
+      for (int j = k >> 1; j >= 32; j >>= 1) {
+        __syncthreads();
+        if (live) arr[p] = key;
+        __syncthreads();
+        if (live) {
+          const unsigned long long o = arr[p ^ j];
+          const bool lower = (p & j) == 0, up = (p & k) == 0;
+          key = (lower == up) ? (key < o ? key : o) : (key > o ? key : o);
+        }
+      }
+      for (int j = min(k >> 1, 16); j > 0; j >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(~0u, key, j);
+        const bool lower = (p & j) == 0, up = (p & k) == 0;
+        key = (lower == up) ? (key < o ? key : o) : (key > o ? key : o);
+      }
     }
-    if (has && part == 0) {
-      ord1[rs] = (uint32_t)me;
-      ord2[rc] = (uint32_t)me;
+    __syncthreads();
+    if (live) arr[p] = key;
+    __syncthreads();
+    for (int i = tid; i < n; i += kNmsThreads) {
+      ord1[i] = (uint32_t)(kS[i] & 0xFFFFFu);
+      ord2[i] = (uint32_t)(kC[i] & 0xFFFFFu);
     }
     __syncthreads();
     ordS = ord1;
@@ -569,23 +582,37 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
       if (moff[sg] < 0) continue;                         // uniform across the block
       const int s = segs[sg], m = segs[sg + 1] - s, words = (m + 31) >> 5;
       uint32_t* rows = bmask + moff[sg];
-      for (int i = warp; i < m; i += kNmsThreads >> 5) {
-        const float4 bi = box[ordC[s + i]];
-        const float ai = dm_area(bi.x, bi.y, bi.z, bi.w);
-        for (int w = 0; w < words; w++) {
-          const int j = w * 32 + lane;
-          bool sup = false;
-          if (j > i && j < m) {
-            const float4 bj = box[ordC[s + j]];
-            sup = dm_iou_gt(bi.x, bi.y, bi.z, bi.w, ai, bj.x, bj.y, bj.z, bj.w, iou);
-          }
-          const unsigned bits = __ballot_sync(~0u, sup);
-          if (lane == 0) rows[(size_t)i * words + w] = bits;
+      // four rows per warp at a time: four independent chains of loads and tests
+      for (int i0 = warp * 4; i0 < m; i0 += (kNmsThreads >> 5) * 4) {
+        float4 bi[4];
+        float ai[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          bi[u] = box[ordC[s + min(i0 + u, m - 1)]];
+          ai[u] = dm_area(bi[u].x, bi[u].y, bi[u].z, bi[u].w);
         }
+        for (int w = i0 >> 5; w < words; w++) {      // words left of the diagonal are zero
+          const int j = w * 32 + lane;
+          const float4 bj = box[ordC[s + min(j, m - 1)]];
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int i = i0 + u;
+            const bool sup = i < m && j > i && j < m &&
+                             dm_iou_gt(bi[u].x, bi[u].y, bi[u].z, bi[u].w, ai[u], bj.x, bj.y,
+                                       bj.z, bj.w, iou);
+            const unsigned bits = __ballot_sync(~0u, sup);
+            if (lane == 0 && i < m) rows[(size_t)i * words + w] = bits;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+          if (lane == 0 && i0 + u < m)
+            for (int w = 0; w < (i0 >> 5); w++) rows[(size_t)(i0 + u) * words + w] = 0u;
       }
     }
   }
   __syncthreads();
+  NMS_MARK(5);
   for (int sg = warp; sg < nseg; sg += kNmsThreads >> 5) {
     const int s = segs[sg], e = segs[sg + 1];
     if (moff[sg] >= 0) {
