@@ -316,6 +316,10 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
         // shared-memory wavefront per store instead of two half-used ones
         const bool odd = lane & 1;
         uint32_t* stg32 = (uint32_t*)stg;
+        if (a.bulk_store) {   // the previous chunk's store has read the staging block
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+        }
 #pragma unroll
         for (int k = 0; k < 32; k += 2) {
           const __half2 h = bias_act2(make_float2(__uint_as_float(r[k]), __uint_as_float(r[k + 1])),
@@ -327,6 +331,15 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
           stg32[((k + odd) * 32 + (lane & ~1)) >> 1] = v;
         }
         __syncwarp();
+        if (a.bulk_store) {   // no residual: the block leaves by one bulk tensor store
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmY, smem_u32(stg), n0 + sp * 32, m0 + pc * 32);
+            bulk_commit();
+          }
+          continue;
+        }
 #pragma unroll
         for (int i = 0; i < 4; i++) {
           const int q = lane + 32 * i, px = q >> 2, cc = q & 3;
@@ -351,6 +364,7 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
       tc_fence_before();
       mbar_arrive(tempty_bar(acc));
     }
+    if (a.bulk_store && lane == 0) bulk_wait0();
     if (lane == 0) YK_PROF_ADD(9, clock64() - t_role);
   } else if (warp < kMmaWarp) {
     // ---------------- epilogue ----------------
@@ -474,7 +488,7 @@ static CUtensorMapSwizzle swizzle_of(int cb) {
 // 2-D fp16 tensor map with a 64-element (128-byte) inner box and the 128-byte swizzle that
 // matches the UMMA K-major layout; out-of-range elements read as zero.
 static bool encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
-                      uint64_t row_bytes, uint32_t box_outer, int cb) {
+                      uint64_t row_bytes, uint32_t box_outer, int cb, bool swizzle = true) {
   static PFN_cuTensorMapEncodeTiled encode = nullptr;
   static std::mutex mu;
   {
@@ -493,7 +507,8 @@ static bool encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t
   const cuuint32_t box[2] = {(cuuint32_t)cb, box_outer};
   const cuuint32_t estr[2] = {1, 1};
   return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
-                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_of(cb),
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                swizzle ? swizzle_of(cb) : CU_TENSOR_MAP_SWIZZLE_NONE,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -550,9 +565,13 @@ static int launch_tc(const ConvArgs& a, cudaStream_t st) {
   CUtensorMap tmY;
   memset(&tmY, 0, sizeof tmY);
   ConvArgs b = a;
-  // output [M][Cout] view with row stride ys: 32 channels x 32 rows per store, 64-byte swizzle
-  b.bulk_store = !T && ((uintptr_t)a.y & 15) == 0 && a.ys % 8 == 0 && bulk_store_enabled() &&
-                 encode_2d(&tmY, a.y, (uint64_t)a.Cout, (uint64_t)a.M, (uint64_t)a.ys * 2, 32, 32);
+  // output [M][Cout] view with row stride ys: 32 channels x 32 rows per store (plain tiles:
+  // 64-byte swizzle; transposed tiles without a residual: the unswizzled [32 px][32 ch]
+  // staging block)
+  b.bulk_store = (!T || !a.res) && ((uintptr_t)a.y & 15) == 0 && a.ys % 8 == 0 &&
+                 bulk_store_enabled() &&
+                 encode_2d(&tmY, a.y, (uint64_t)a.Cout, (uint64_t)a.M, (uint64_t)a.ys * 2, 32, 32,
+                           !T);
   launch_k(conv_tc_kernel<BN, STAGES, MT, CB, G, T>, grid, kTcThreads, Cfg::kSmem,
            (cudaStream_t)st, b, tmB, tmA, tmY);
   note_launch();
