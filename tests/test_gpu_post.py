@@ -151,6 +151,24 @@ def test_decode_nms_bitexact(lib, cuda, S, B, cls_bias, iou, max_out):
         assert np.array_equal(od[img, :n].view(np.uint32), keep[:, :6].view(np.uint32))
 
 
+@pytest.mark.parametrize("nc,bias,iou", [(1, -2.9, 0.7), (2, -2.3, 0.7), (4, -2.0, 0.45),
+                                          (8, -1.2, 0.7), (3, -2.9, 0.3)])
+def test_nms_few_classes_bitexact(lib, cuda, nc, bias, iou):
+    """Few classes of tens to hundreds of candidates each: the greedy path (classes up to
+    128) and the bit-mask path (129..512, masks in shared memory below 512 candidates and
+    in the workspace above) must both give the oracle's survivors bit for bit."""
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(100 + nc)
+    sizes, box, cls = _levels(640, 1, g, bias, nc=8)   # 8 channels (16-byte rows), nc used
+    od, oi, oc, rc, _ = _run_gpu_post(lib, rt, cuda, sizes, box, cls, 1, iou, 300, nc=nc)
+    recs, keep = _oracle(sizes, box, cls, 0, iou, 300, nc=nc)
+    assert rc[0] == len(recs) > 0
+    assert oc[0] == len(keep)
+    n = len(keep)
+    assert np.array_equal(oi[0, :n], keep[:, 6].astype(np.int32))
+    assert np.array_equal(od[0, :n].view(np.uint32), keep[:, :6].view(np.uint32))
+
+
 @pytest.mark.parametrize("S,nc,bias", [(320, 600, 1.0), (640, 304, -1.0)])
 def test_decode_nms_many_classes(lib, cuda, S, nc, bias):
     """More than 256 classes: the class order takes two radix digits."""

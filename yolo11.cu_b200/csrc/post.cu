@@ -132,7 +132,11 @@ struct WsLayout {
   size_t rec, flag, anch, box, skey, cls, ord, surv, kept, bmask, per_img;
   int A, bmask_words;
 };
-constexpr int kBitMax = 512;   // classes of 33..kBitMax candidates: bit-mask suppression
+constexpr int kBitMax = 512;   // classes of kBitMin+1..kBitMax candidates: bit-mask suppression
+// Below that the greedy loop is cheaper: real detections suppress heavily, and its cost
+// follows the kept boxes, while the masks cost every pair (yolo11n, 268 candidates in four
+// classes, 16 kept: 24 us of masks and scan against a few us of greedy).
+constexpr int kBitMin = 128;
 static inline size_t al16(size_t v) { return (v + 15) & ~(size_t)15; }
 static inline WsLayout ws_layout(int A) {
   WsLayout L;
@@ -546,7 +550,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   __syncthreads();
   NMS_MARK(3);
 
-  // 4. per-class suppression in score order.  Classes of 33..kBitMax candidates whose bit
+  // 4. per-class suppression in score order.  Classes of kBitMin+1..kBitMax candidates whose bit
   // masks fit the workspace region, with all candidates in shared memory, use bit masks: the whole block builds them (bit j of row
   // i: dm_iou_gt(i, j) for a later j, the same test as the greedy path), then one warp per
   // class walks the rows: a row not yet removed is kept and removes its mask.  The other
@@ -565,7 +569,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
       const int m = segs[tid + 1] - segs[tid], words = (m + 31) >> 5;
       // (only with the candidates in shared memory: from the workspace, the pair tests'
       // loads cost more than the greedy loop saves)
-      if (in_smem && m > 32 && m <= kBitMax) need = m * words;
+      if (in_smem && m > kBitMin && m <= kBitMax) need = m * words;
     }
     int total;
     const int off = block_scan(need, wsum, &total);
