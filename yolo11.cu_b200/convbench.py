@@ -1,7 +1,7 @@
 """Time one convolution shape through the kernel ABI (yk_conv), for tuning and profiling.
 
     python yolo11.cu_b200/convbench.py B,H,W,Cin,Cout,k,s [--algo A --tile T --msub M]
-                                       [--iters N] [--res] [--dw]
+                                       [--iters N] [--res] [--dw] [--act 0|1]
 
 Allocates NHWC fp16 input / output (and residual) with torch on cuda:0, runs the conv
 `--warmup` times, then times `--iters` launches with CUDA events (inputs larger than L2 for
@@ -43,6 +43,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--res", action="store_true", help="fused residual add")
     ap.add_argument("--dw", action="store_true", help="depthwise (groups = Cin = Cout)")
+    ap.add_argument("--act", type=int, default=1, help="1 SiLU (default), 0 identity")
     a = ap.parse_args(argv)
     B, H, W, Cin, Cout, k, s = (int(v) for v in a.shape.split(","))
     rt = _runtime()
@@ -57,7 +58,8 @@ def main(argv=None):
     b = (torch.randn(Cout, generator=g) * 0.1).float().to(dev)
     y = torch.empty(B, Ho, Wo, Cout, dtype=torch.half, device=dev)
     r = torch.randn(B, Ho, Wo, Cout, generator=g).half().to(dev) if a.res else None
-    prm = rt.YkConv(w.data_ptr(), b.data_ptr(), k, s, p, groups, 1, Cin, Cout, a.tile, a.msub, a.algo)
+    prm = rt.YkConv(w.data_ptr(), b.data_ptr(), k, s, p, groups, a.act, Cin, Cout, a.tile, a.msub,
+                    a.algo)
     xv, yv = rt.tview(x), rt.tview(y)
     rv = rt.tview(r) if r is not None else None
     st = torch.cuda.current_stream()

@@ -832,7 +832,10 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
       cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
       if (nsm <= 0) nsm = 148;
     }
-    const unsigned grid = (unsigned)std::min<long long>(rows, (long long)nsm * 4);
+#ifndef YK_STEM_BPS
+#define YK_STEM_BPS 5   // persistent blocks per SM (96 registers x 128 threads: five fit)
+#endif
+    const unsigned grid = (unsigned)std::min<long long>(rows, (long long)nsm * YK_STEM_BPS);
     const int vec = x->stride == 3 && (x->W * 3) % 8 == 0 &&
                     (((uintptr_t)x->ptr + (size_t)x->coff * 2) & 15) == 0;
     void (*kern)(DView, DView, const __half*, const float*, int, int, int, int, int, int) = nullptr;

@@ -298,6 +298,11 @@ conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmB,
       const uint32_t use = li / Cfg::kNacc;
       if (!mbar_wait(tfull_bar(acc), use & 1, 0x103)) { *abort_flag = 1; break; }
       tc_fence_after();
+#ifdef YK_TC_DIAG_NOEPI   // diagnostic builds only: drain the accumulator without reading it
+      tc_fence_before();
+      mbar_arrive(tempty_bar(acc));
+      continue;
+#endif
       const int m0 = (t / a.ntn) * kTM + (kT4 ? 256 * grp : 0);
       const int n0 = (t % a.ntn) * BN + (kT2 ? 128 * grp : 0);
       const int ch = n0 + sp * 32 + lane;
