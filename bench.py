@@ -9,8 +9,8 @@ A step = one pass of the hot path over one batch, replayed as ONE CUDA graph: le
 (yolo_bind_frames / yolo_run_frames).  ``value`` times steps whose raw frames are already
 resident in HBM (CUDA events on the engine stream, max over ranks); ``e2e`` times the same
 steps through the public C ABI from pinned host memory, H2D copies of every step's frames
-(double-buffered on a copy stream) and the fetch of its detections included (wall clock, max
-over ranks).  Ranks shard frames; nothing is exchanged but the timing scalars.  Beside the
+(double-buffered on a copy stream) and the fetch of its detections (yolo_get_frames, while
+the next step's graph runs) included (wall clock, max over ranks).  Ranks shard frames; nothing is exchanged but the timing scalars.  Beside the
 headline, the line carries yolo11x 1024 (16 frames per GPU) and yolo11n-seg 640 (64 frames
 split over the GPUs) as ``extra_configs``, the yolo11n batch-1 end-to-end latency, and a
 parity check of slot 0 against the oracle (rank 0, after the timed regions).
@@ -437,7 +437,7 @@ def run_ours(args):
 
     log('bench: e2e')
     # ---- e2e: pinned host frames -> H2D (copy stream, double-buffered) -> pipeline graph
-    #      -> D2H of the detections inside the graph -> yolo_get_batch ----
+    #      -> D2H of the detections inside the graph -> yolo_get_frames ----
     cs = torch.cuda.Stream(device=dev)
     copied = [torch.cuda.Event() for _ in range(2)]
     freed = [torch.cuda.Event() for _ in range(2)]
@@ -450,17 +450,27 @@ def run_ours(args):
             dbuf[j].copy_(hostf, non_blocking=True)
             copied[j].record(cs)
 
+    done = [torch.cuda.Event() for _ in range(2)]
+
     def e2e_steps(k):
+        # step i+1's graph is queued before step i's detections are read: each binding's
+        # results have their own pinned block (yolo_get_frames), so the GPU never waits on
+        # the host between steps
         issue_copy(0)
         for i in range(k):
             j = i % 2
             es.wait_event(copied[j])
             eng.run_frames_async(j, B)
             freed[j].record(es)
+            done[j].record(es)
             if i + 1 < k:
                 issue_copy(i + 1)
-            eng.sync()
-            eng.get_batch(B)
+            if i > 0:
+                done[(i - 1) % 2].synchronize()
+                eng.get_frames((i - 1) % 2, B)
+        done[(k - 1) % 2].synchronize()
+        eng.get_frames((k - 1) % 2, B)
+        eng._check()
 
     e2e_steps(max(args.warmup, 1))
     barrier(world)

@@ -99,6 +99,13 @@ int yolo_graph_kernels(void* h, int id, int B);
 // Device time (ms) of the tensor-core convolutions of one batch-B forward, captured alone as
 // one graph in the planned order and replayed; *nconv (optional) receives their count.
 float yolo_conv_exec_ms(void* h, int B, int* nconv);
+// Detections of slots 0..B-1 of binding id's most recent completed run, from the binding's
+// own pinned result block (each binding's graphs copy their results there, and yolo_get
+// reads the block of the most recently launched run).  A caller with two bindings can
+// therefore launch the next batch before reading this one: results of binding id stay
+// valid until binding id runs again.  Wait for the run first (yolo_sync, or an event on
+// yolo_stream after the launch).  Detect / segment handles; returns the total or -1.
+int yolo_get_frames(void* h, int id, int B, YoloDet* out, int cap, int* counts);
 // Detections of slots 0..B-1 in one call: slot s's go to out + s * cap (at most cap each),
 // its count to counts[s].  Returns the total, or -1 (bad arguments / obb handle).
 int yolo_get_batch(void* h, int B, YoloDet* out, int cap, int* counts);

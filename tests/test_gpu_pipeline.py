@@ -76,3 +76,30 @@ def test_pipeline_rejects_bad_bindings(lib, cuda, pkg):
         eng.run_frames(2, 2)                                      # past the bound count
     eng.run_frames(2, 1)
     eng.close()
+
+
+def test_two_bindings_in_flight(lib, cuda, pkg):
+    """Two bound frame arrays launched back to back without a sync in between: each
+    binding's results stay in its own pinned block (yolo_get_frames), equal to running each
+    alone, and yolo_get reads the most recently launched run."""
+    from yolo11_cu_b200 import frames, runtime as rt
+    d = _model("yolo11n")
+    hw, B = (720, 1280), 3
+    a = torch.from_numpy(np.stack([frames.synthetic_bgr(*hw, seed=60 + i) for i in range(B)])).to(cuda)
+    b = torch.from_numpy(np.stack([frames.synthetic_bgr(*hw, seed=70 + i) for i in range(B)])).to(cuda)
+    torch.cuda.synchronize()
+    eng = rt.Engine(d, B, autotune=False)
+    eng.bind_frames(0, a.data_ptr(), hw[0], hw[1], B, False)
+    eng.bind_frames(1, b.data_ptr(), hw[0], hw[1], B, False)
+    eng.run_frames(0, B)
+    want_a = eng.get_batch(B)
+    eng.run_frames(1, B)
+    want_b = eng.get_batch(B)
+    assert want_a != want_b and len(want_a[0]) > 0
+    eng.run_frames_async(0, B)
+    eng.run_frames_async(1, B)
+    eng.sync()
+    assert eng.get_frames(0, B) == want_a
+    assert eng.get_frames(1, B) == want_b
+    assert eng.get_batch(B) == want_b            # the most recent launch
+    eng.close()

@@ -109,6 +109,8 @@ struct Engine {
   // rawcnt[maxB] | outcnt[maxB] | (16-byte aligned) outdets[maxB][max_det][rec]
   void* dres = nullptr;
   void* hres = nullptr;
+  void* hres_dst = nullptr;       // D2H target of run_post: hres, or a binding's own block
+  size_t res_bytes = 0;
   size_t res_hdr = 0;
   float* h_out = nullptr;
   int* h_cnt = nullptr;
@@ -127,6 +129,8 @@ struct Engine {
     bool host = false;
     void* stage = nullptr;
     size_t stage_bytes = 0;
+    void* hres = nullptr;         // pinned result block of this binding's graphs
+    SlotGeom geom;                // letterbox geometry of its frames (all equal-size)
   };
   static constexpr int kBindings = 4;
   Binding binds[kBindings];
@@ -138,6 +142,12 @@ struct Engine {
   std::vector<cudaStream_t> side;  // extra streams of the multi-stream graph capture
   std::vector<cudaEvent_t> opev;   // one event per planned op (capture-time ordering)
   std::vector<SlotGeom> slots;
+  // point the result getters (yolo_get & co.) at a pinned result block
+  void use_results(void* block) {
+    h_raw = (int*)block;
+    h_cnt = (int*)block + maxB;
+    h_out = (float*)((char*)block + res_hdr);
+  }
   bool seg() const { return task == "segment"; }
   bool cls() const { return task == "classify"; }
   bool obb() const { return task == "obb"; }
@@ -153,6 +163,7 @@ struct Engine {
     graphs.clear();
     for (Binding& b : binds) {
       if (b.stage) cudaFree(b.stage);
+      if (b.hres) cudaFreeHost(b.hres);
       b = Binding{};
     }
     for (cudaStream_t s : side) cudaStreamDestroy(s);
@@ -443,7 +454,7 @@ void Engine::allocate(const std::string& dir) {
   post.ws_bytes = obb() ? yk_obb_workspace_bytes(maxB, A) : yk_post_workspace_bytes(maxB, A);
   CKE(cudaMalloc(&post.ws, post.ws_bytes));
   res_hdr = ((size_t)2 * maxB * sizeof(int) + 15) & ~(size_t)15;
-  const size_t res_bytes = res_hdr + (size_t)maxB * opt.max_det * rec() * sizeof(float);
+  res_bytes = res_hdr + (size_t)maxB * opt.max_det * rec() * sizeof(float);
   CKE(cudaMalloc(&dres, res_bytes));
   CKE(cudaMemset(dres, 0, res_bytes));
   post.rawcnt = (int*)dres;
@@ -455,6 +466,7 @@ void Engine::allocate(const std::string& dir) {
     CKE(cudaMalloc(&dmasks, (size_t)maxB * opt.max_det * pb.H * pb.W));
   }
   CKE(cudaMallocHost(&hres, res_bytes));
+  hres_dst = hres;
   h_raw = (int*)hres;
   h_cnt = (int*)hres + maxB;
   h_out = (float*)((char*)hres + res_hdr);
@@ -602,7 +614,7 @@ void Engine::run_post(int B) {
                  (yk_stream_t)st));
   }
   // counts of all slots and the first B images' records: one copy
-  CKE(cudaMemcpyAsync(hres, dres, res_hdr + (size_t)B * opt.max_det * rec() * sizeof(float),
+  CKE(cudaMemcpyAsync(hres_dst, dres, res_hdr + (size_t)B * opt.max_det * rec() * sizeof(float),
                       cudaMemcpyDeviceToHost, st));
 }
 
@@ -894,11 +906,13 @@ cudaGraphExec_t Engine::graph_for(int B, int bind) {
     cudaGraph_t g;
     g_pdl_override = pdl;
     CKE(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    hres_dst = bind >= 0 && binds[bind].hres ? binds[bind].hres : hres;
     try {
       if (bind >= 0) load_frames(bind, B);
       if (multi) forward_streams(B);
       else forward(B);
     } catch (...) {
+      hres_dst = hres;
       g_pdl_override = -1;
       cudaGraph_t dummy;
       cudaStreamEndCapture(st, &dummy);
@@ -906,6 +920,7 @@ cudaGraphExec_t Engine::graph_for(int B, int bind) {
       throw;
     }
     g_pdl_override = -1;
+    hres_dst = hres;
     CKE(cudaStreamEndCapture(st, &g));
     kernels = count_kernel_nodes(g);
     cudaGraphExec_t ge;
@@ -1202,6 +1217,7 @@ void yolo_run_async(void* h, int B) {
     if (!e || B < 1 || B > e->maxB) throw Error("yolo_run: bad batch");
     DeviceScope ds(e->device);
     CKE(cudaGraphLaunch(e->graph_for(B), e->st));
+    e->use_results(e->hres);
     return 0;
   }, -1);
 }
@@ -1256,6 +1272,10 @@ int yolo_bind_frames(void* h, int id, const unsigned char* frames, int height, i
       CKE(cudaMalloc(&b.stage, need));
       b.stage_bytes = need;
     }
+    if (!b.hres) {
+      CKE(cudaMallocHost(&b.hres, e->res_bytes));
+      memset(b.hres, 0, e->res_bytes);
+    }
     b.frames = frames;
     b.h = height;
     b.w = width;
@@ -1282,7 +1302,11 @@ int yolo_run_frames_async(void* h, int id, int B) {
       g.left = (ib.W - nw) / 2;
     }
     CKE(cudaGraphLaunch(e->graph_for(B, id), e->st));
+    Engine::Binding& bb = e->binds[id];
+    bb.geom = g;
     for (int i = 0; i < B; i++) e->slots[i] = g;
+    // yolo_get & co. read the most recently launched run's results: this binding's block
+    e->use_results(bb.hres);
     return 0;
   }, -1);
 }
@@ -1327,6 +1351,33 @@ float yolo_conv_exec_ms(void* h, int B, int* nconv) {
     }
     return e->conv_graph_ms(B);
   }, -1.f);
+}
+
+int yolo_get_frames(void* h, int id, int B, YoloDet* out, int cap, int* counts) {
+  Engine* e = as_engine(h);
+  if (!e || e->obb() || e->cls() || id < 0 || id >= Engine::kBindings || !e->binds[id].hres ||
+      B < 1 || B > e->binds[id].count || cap < 0 || (!out && cap > 0) || !counts)
+    return -1;
+  const Engine::Binding& b = e->binds[id];
+  const int* cnt = (const int*)b.hres + e->maxB;
+  const float* recs = (const float*)((const char*)b.hres + e->res_hdr);
+  int total = 0;
+  for (int s = 0; s < B; s++) {
+    const int n = std::min(cnt[s], cap);
+    for (int i = 0; i < n; i++) {
+      const float* d = recs + ((size_t)s * e->opt.max_det + i) * 6;
+      YoloDet& o = out[(size_t)s * cap + i];
+      o.x1 = (d[0] - b.geom.left) / b.geom.scale;
+      o.y1 = (d[1] - b.geom.top) / b.geom.scale;
+      o.x2 = (d[2] - b.geom.left) / b.geom.scale;
+      o.y2 = (d[3] - b.geom.top) / b.geom.scale;
+      o.score = d[4];
+      o.cls = (int)d[5];
+    }
+    counts[s] = n;
+    total += n;
+  }
+  return total;
 }
 
 int yolo_get_batch(void* h, int B, YoloDet* out, int cap, int* counts) {
@@ -1414,7 +1465,10 @@ int yolo_run_op(void* h, int op_index, int B) {
         if (e->raw[j].kind == DECODE || e->raw[j].kind == DECODESEG ||
             e->raw[j].kind == DECODEOBB || e->raw[j].kind == MASKS)
           last = false;
-      if (last) e->run_post(B);
+      if (last) {
+        e->run_post(B);
+        e->use_results(e->hres);
+      }
       CKE(cudaStreamSynchronize(e->st));
       return 1;
     }

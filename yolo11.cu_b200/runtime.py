@@ -118,6 +118,8 @@ _SIGS = {
     "yolo_frames_exec_ms": (C.c_float, [C.c_void_p, C.c_int, C.c_int]),
     "yolo_graph_kernels": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
     "yolo_conv_exec_ms": (C.c_float, [C.c_void_p, C.c_int, _P(C.c_int)]),
+    "yolo_get_frames": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _P(YoloDet), C.c_int,
+                                  _P(C.c_int)]),
     "yolo_get_batch": (C.c_int, [C.c_void_p, C.c_int, _P(YoloDet), C.c_int, _P(C.c_int)]),
     "yolo_run_op": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
     "yolo_num_ops": (C.c_int, [C.c_void_p]),
@@ -234,6 +236,16 @@ class Engine:
 
     def frames_exec_ms(self, id: int, B: int) -> float:
         return self.lib.yolo_frames_exec_ms(self.h, id, B)
+
+    def get_frames(self, id: int, B: int, cap: int | None = None):
+        """Detections of slots 0..B-1 from binding id's most recent run (one C call)."""
+        cap = self.max_det if cap is None else cap
+        arr = (YoloDet * (cap * B))()
+        cnt = (C.c_int * B)()
+        if self.lib.yolo_get_frames(self.h, id, B, arr, cap, cnt) < 0:
+            raise RuntimeError("yolo_get_frames failed")
+        return [[(d.x1, d.y1, d.x2, d.y2, d.score, d.cls) for d in arr[s * cap:s * cap + cnt[s]]]
+                for s in range(B)]
 
     def get_batch(self, B: int, cap: int | None = None):
         """Detections of slots 0..B-1 (one C call): list of per-slot lists."""
