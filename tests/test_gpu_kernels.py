@@ -220,10 +220,13 @@ def test_conv_patch_transposed_residual(lib, cuda):
 
 
 @pytest.mark.parametrize("case", PATCH_CASES + [(2, 40, 40, 32, 32), (1, 19, 23, 96, 64),
-                                                (1, 160, 160, 32, 32), (1, 33, 30, 32, 48)])
+                                                (1, 160, 160, 32, 32), (1, 33, 30, 32, 48),
+                                                (2, 64, 64, 48, 48), (1, 37, 29, 16, 32),
+                                                (1, 21, 50, 80, 48)])
 @pytest.mark.parametrize("tile,msub", [(32, 1), (32, 2), (64, 1)])
 def test_conv_kx_folded(lib, cuda, case, tile, msub):
-    """Halo patches with the horizontal taps folded into N (algo 5)."""
+    """Halo patches with the horizontal taps folded into N (algo 5); Cin 48 / 16 / 80 take
+    16-channel blocks."""
     from yolo11_cu_b200 import runtime as rt
     B, H, W, Cin, Cout = case
     g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000 + 13)
@@ -232,6 +235,19 @@ def test_conv_kx_folded(lib, cuda, case, tile, msub):
     b = torch.randn(Cout, generator=g) * 0.1
     out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), 3, 1, 1, act=1, tile=tile,
                         msub=msub, xc=(8, None), yc=(8, 8), algo=5)
+    assert rel(out, ref) < TOL
+
+
+@pytest.mark.parametrize("C", [48, 16])
+def test_conv_kx_folded_16ch_residual(lib, cuda, C):
+    """16-channel blocks with a fused residual, as yolo11x's 48-channel bottlenecks."""
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(C)
+    x = torch.randn(2, 45, 70, C, generator=g).half().to(cuda)
+    w = (torch.randn(C, C, 3, 3, generator=g) / (C * 9) ** 0.5).to(cuda)
+    b = (torch.randn(C, generator=g) * 0.1).to(cuda)
+    res = torch.randn(2, 45, 70, C, generator=g).half().to(cuda)
+    out, ref = run_conv(lib, rt, x, w, b, 3, 1, 1, act=1, res=res, tile=64, msub=1, algo=5)
     assert rel(out, ref) < TOL
 
 

@@ -452,11 +452,12 @@ static int launch_kxn(const PatchArgs& a, const YkView* x, cudaStream_t st) {
   return check_launch("conv_kxn");
 }
 
-// 3x3 stride-1 pad-1 conv with kx folded into N; Cin % 32 == 0, 16-byte aligned view.
+// 3x3 stride-1 pad-1 conv with kx folded into N; Cin % 16 == 0 (64-, 32- or 16-channel
+// blocks, swizzle matched to the block), 16-byte aligned view.
 // bn (output channels per tile) in {32, 64}, ms (stacked 8x16 sub-tiles) in {1, 2} (bn 32).
 int conv_kxn(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, int bn,
              int ms, cudaStream_t st) {
-  const int cbw = p->Cin % 64 == 0 ? 64 : p->Cin % 32 == 0 ? 32 : 0;
+  const int cbw = p->Cin % 64 == 0 ? 64 : p->Cin % 32 == 0 ? 32 : p->Cin % 16 == 0 ? 16 : 0;
   if (p->k != 3 || p->s != 1 || p->p != 1 || p->groups != 1 || !cbw ||
       ((uintptr_t)x->ptr & 15) || x->stride % 8 || (x->coff % 8) ||
       ((uintptr_t)p->weight & 15))
@@ -491,6 +492,9 @@ int conv_kxn(const YkView* x, const YkView* y, const YkView* res, const YkConv* 
     case 32164: return launch_kxn<32, 1, 64>(a, x, st);
     case 32264: return launch_kxn<32, 2, 64>(a, x, st);
     case 64164: return launch_kxn<64, 1, 64>(a, x, st);
+    case 32116: return launch_kxn<32, 1, 16>(a, x, st);
+    case 32216: return launch_kxn<32, 2, 16>(a, x, st);
+    case 64116: return launch_kxn<64, 1, 16>(a, x, st);
     default: return YK_EINVAL;
   }
 }

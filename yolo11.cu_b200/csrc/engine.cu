@@ -732,6 +732,9 @@ void Engine::autotune() {
     if (op.kind != CONV || op.g != 1 || (op.Cin % 8 && !op.wpad)) continue;
     const bool patch_ok = !op.wpad && op.k == 3 && op.s == 1 && op.p == 1 && op.Cin % 32 == 0 &&
                           patch_enabled();
+    // the kx-folded kernel also takes 16-channel blocks (e.g. the 48-channel bottlenecks)
+    const bool kxn_ok = !op.wpad && op.k == 3 && op.s == 1 && op.p == 1 && op.Cin % 16 == 0 &&
+                        patch_enabled();
     const bool trans_ok = !op.wpad && op.Cin >= 64;
     const YkView xin = view(op.a, maxB);
     const bool pair_ok = trans_ok && xin.coff % 8 == 0 && xin.stride % 8 == 0;
@@ -740,7 +743,7 @@ void Engine::autotune() {
     for (const auto& cm : combos) {
       const int tile = cm[1];
       if (cm[0] == 4 && (!patch_ok || (tile == 128 && op.Cout <= 64))) continue;
-      if (cm[0] == 5 && (!patch_ok || (tile == 64 && op.Cout <= 32))) continue;
+      if (cm[0] == 5 && (!kxn_ok || (tile == 64 && op.Cout <= 32))) continue;
       if (cm[0] == 3 && (!trans_ok || (tile == 256 && op.Cout <= 128))) continue;
       if (cm[0] == 6 && (!pair_ok || op.Cout <= 128)) continue;
       if (cm[0] == 1 && tile > 32 && tile / 2 >= op.Cout) continue;   // half the tile wasted
