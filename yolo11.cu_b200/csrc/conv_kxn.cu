@@ -453,11 +453,18 @@ static int launch_kxn(const PatchArgs& a, const YkView* x, cudaStream_t st) {
 }
 
 // 3x3 stride-1 pad-1 conv with kx folded into N; Cin % 16 == 0 (64-, 32- or 16-channel
-// blocks, swizzle matched to the block), 16-byte aligned view.
+// blocks, swizzle matched to the block, the last block zero-filled past Cin), 16-byte
+// aligned view.
 // bn (output channels per tile) in {32, 64}, ms (stacked 8x16 sub-tiles) in {1, 2} (bn 32).
 int conv_kxn(const YkView* x, const YkView* y, const YkView* res, const YkConv* p, int bn,
              int ms, cudaStream_t st) {
-  const int cbw = p->Cin % 64 == 0 ? 64 : p->Cin % 32 == 0 ? 32 : p->Cin % 16 == 0 ? 16 : 0;
+  // channel block: the widest of 64 / 32 / 16 that pads Cin by at most a third (the tensor
+  // maps' channel extent stays Cin, so the padding channels load as zeros from both the
+  // activations and the weights and add nothing): 48 -> one 64-block, 80 -> three 32-blocks
+  int cbw = 0;
+  if (p->Cin % 16 == 0)
+    for (int c : {64, 32, 16})
+      if ((p->Cin + c - 1) / c * c * 3 <= p->Cin * 4) { cbw = c; break; }
   if (p->k != 3 || p->s != 1 || p->p != 1 || p->groups != 1 || !cbw ||
       ((uintptr_t)x->ptr & 15) || x->stride % 8 || (x->coff % 8) ||
       ((uintptr_t)p->weight & 15))
@@ -471,7 +478,7 @@ int conv_kxn(const YkView* x, const YkView* y, const YkView* res, const YkConv* 
   a.rs = res ? res->stride : 0;
   a.w = (const __half*)p->weight; a.bias = p->bias;
   a.Cin = p->Cin; a.Cout = p->Cout; a.act = p->act;
-  a.ncb = p->Cin / cbw;
+  a.ncb = (p->Cin + cbw - 1) / cbw;
   a.nty = (x->H + 8 * ms - 1) / (8 * ms);
   a.ntx = (x->W + kPatchUse - 1) / kPatchUse;
   a.ntn = (p->Cout + bn - 1) / bn;
