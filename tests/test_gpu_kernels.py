@@ -222,11 +222,11 @@ def test_conv_patch_transposed_residual(lib, cuda):
 @pytest.mark.parametrize("case", PATCH_CASES + [(2, 40, 40, 32, 32), (1, 19, 23, 96, 64),
                                                 (1, 160, 160, 32, 32), (1, 33, 30, 32, 48),
                                                 (2, 64, 64, 48, 48), (1, 37, 29, 16, 32),
-                                                (1, 21, 50, 80, 48)])
+                                                (1, 21, 50, 80, 48), (2, 40, 33, 8, 16)])
 @pytest.mark.parametrize("tile,msub", [(32, 1), (32, 2), (64, 1)])
 def test_conv_kx_folded(lib, cuda, case, tile, msub):
     """Halo patches with the horizontal taps folded into N (algo 5); Cin 48 / 16 / 80 take
-    16-channel blocks."""
+    16-channel blocks, Cin 8 one zero-filled 16-channel block."""
     from yolo11_cu_b200 import runtime as rt
     B, H, W, Cin, Cout = case
     g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000 + 13)
@@ -433,3 +433,18 @@ def test_im2col_thin(lib, cuda, k, s, p):
             patch = xp[:, :, ky:ky + s * (Ho - 1) + 1:s, kx:kx + s * (Wo - 1) + 1:s]
             ref[..., (ky * k + kx) * Cin:(ky * k + kx + 1) * Cin] = patch.permute(0, 2, 3, 1)
     assert torch.equal(col.float(), ref)
+
+
+@pytest.mark.parametrize("Cin,Cout,tile,msub", [(48, 64, 64, 2), (48, 64, 32, 4), (24, 40, 32, 1),
+                                               (40, 96, 128, 1), (48, 256, 256, 1)])
+def test_conv_1x1_padded_channel_block(lib, cuda, Cin, Cout, tile, msub):
+    """1x1 convs whose Cin is no 8/16/32-channel block: one wider block whose channels past
+    Cin the tensor maps zero-fill (48 -> 64, 24 -> 32, 40 -> three 16-channel blocks)."""
+    from yolo11_cu_b200 import runtime as rt
+    g = torch.Generator().manual_seed(Cin * 7 + Cout)
+    x = torch.randn(2, 37, 41, Cin + 16, generator=g).half().to(cuda)
+    w = (torch.randn(Cout, Cin, 1, 1, generator=g) / Cin ** 0.5)
+    b = torch.randn(Cout, generator=g) * 0.1
+    out, ref = run_conv(lib, rt, x, w.to(cuda), b.to(cuda), 1, 1, 0, act=1, tile=tile,
+                        msub=msub, xc=(8, None), yc=(8, 8), algo=1)
+    assert rel(out, ref) < TOL

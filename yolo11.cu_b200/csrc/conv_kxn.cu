@@ -452,7 +452,7 @@ static int launch_kxn(const PatchArgs& a, const YkView* x, cudaStream_t st) {
   return check_launch("conv_kxn");
 }
 
-// 3x3 stride-1 pad-1 conv with kx folded into N; Cin % 16 == 0 (64-, 32- or 16-channel
+// 3x3 stride-1 pad-1 conv with kx folded into N; Cin % 8 == 0 (64-, 32- or 16-channel
 // blocks, swizzle matched to the block, the last block zero-filled past Cin), 16-byte
 // aligned view.
 // bn (output channels per tile) in {32, 64}, ms (stacked 8x16 sub-tiles) in {1, 2} (bn 32).
@@ -462,9 +462,11 @@ int conv_kxn(const YkView* x, const YkView* y, const YkView* res, const YkConv* 
   // maps' channel extent stays Cin, so the padding channels load as zeros from both the
   // activations and the weights and add nothing): 48 -> one 64-block, 80 -> three 32-blocks
   int cbw = 0;
-  if (p->Cin % 16 == 0)
+  if (p->Cin % 8 == 0) {
     for (int c : {64, 32, 16})
       if ((p->Cin + c - 1) / c * c * 3 <= p->Cin * 4) { cbw = c; break; }
+    if (!cbw) cbw = 16;   // thin inputs (8 channels): one zero-filled 16-channel block
+  }
   if (p->k != 3 || p->s != 1 || p->p != 1 || p->groups != 1 || !cbw ||
       ((uintptr_t)x->ptr & 15) || x->stride % 8 || (x->coff % 8) ||
       ((uintptr_t)p->weight & 15))

@@ -662,8 +662,15 @@ int conv_tc(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
   // A by TMA when the view allows it: CB = 64-channel blocks (128-byte rows) for Cin >= 64,
   // 32 / 16 / 8-channel blocks (64 / 32-byte swizzled rows, 16-byte unswizzled core matrices)
   // for Cin = 32 / 16 / 8
-  const int cb = p->Cin >= 64 ? 64
-                 : ((p->Cin == 32 || p->Cin == 16 || p->Cin == 8) && bn <= 64) ? p->Cin : 0;
+  // (1x1 convs with other Cin below 64: the widest block padding Cin by at most a third,
+  // e.g. 48 -> 64;
+  // the A tensor map's channel extent stays Cin, so the padding channels load as zeros and
+  // whatever weights the B box reads for them add nothing)
+  int cb = p->Cin >= 64 ? 64
+           : ((p->Cin == 32 || p->Cin == 16 || p->Cin == 8) && bn <= 64) ? p->Cin : 0;
+  if (!cb && p->Cin % 8 == 0 && p->k == 1 && p->s == 1 && p->p == 0)   // tiled 2-D maps only
+    for (int c : {64, 32, 16, 8})
+      if ((c == 64 || bn <= 64) && (p->Cin + c - 1) / c * c * 3 <= p->Cin * 4) { cb = c; break; }
   const bool tma_ok = cb && ((uintptr_t)a.x & 15) == 0 && (a.xs % 8) == 0;
   a.tmaA = 0;
   a.ncb = cb ? (p->Cin + cb - 1) / cb : 0;

@@ -732,8 +732,9 @@ void Engine::autotune() {
     if (op.kind != CONV || op.g != 1 || (op.Cin % 8 && !op.wpad)) continue;
     const bool patch_ok = !op.wpad && op.k == 3 && op.s == 1 && op.p == 1 && op.Cin % 32 == 0 &&
                           patch_enabled();
-    // the kx-folded kernel also takes 16-channel blocks (e.g. the 48-channel bottlenecks)
-    const bool kxn_ok = !op.wpad && op.k == 3 && op.s == 1 && op.p == 1 && op.Cin % 16 == 0 &&
+    // the kx-folded kernel also takes 16-channel blocks (the 48-channel bottlenecks) and
+    // zero-filled ones (8-channel inputs)
+    const bool kxn_ok = !op.wpad && op.k == 3 && op.s == 1 && op.p == 1 && op.Cin % 8 == 0 &&
                         patch_enabled();
     const bool trans_ok = !op.wpad && op.Cin >= 64;
     const YkView xin = view(op.a, maxB);
