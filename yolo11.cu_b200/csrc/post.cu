@@ -729,6 +729,74 @@ struct DevCoefs {
   int n;
 };
 
+// Masks by pixel tiles (nm == NM): one block per (image, 256-pixel tile of the proto plane).
+// Each thread holds its pixel's NM proto values in registers, so the proto is read once per
+// image instead of once per survivor; survivors go through in chunks whose coefficients and
+// crop boxes are staged in shared memory.  Per (pixel, survivor) the arithmetic is
+// masks_kernel's (crop test, then the dot product in channel order), so results are equal.
+constexpr int kMaskTile = 256, kMaskChunk = 128;
+template <int NM>
+__global__ void __launch_bounds__(kMaskTile) masks_tile_kernel(
+    DevCoefs cf, DView proto, float rx, float ry, int max_out, const float* __restrict__ outdets,
+    const int* __restrict__ outidx, const int* __restrict__ outcnt, uint8_t* __restrict__ masks) {
+  pdl_wait();     // inputs come from the previous kernel
+  pdl_trigger();
+  __shared__ float co[kMaskChunk][NM + 1];
+  __shared__ float4 bx[kMaskChunk];
+  const int img = blockIdx.y, n = outcnt[img];
+  if (n == 0) return;
+  const int Ph = proto.H, Pw = proto.W, p = blockIdx.x * kMaskTile + threadIdx.x;
+  const bool live = p < Ph * Pw;
+  const int px = live ? p % Pw : 0, py = live ? p / Pw : 0;
+  float pv[NM];
+  {
+    const __half* pp = proto.p + proto.pix(img, py, px);
+#pragma unroll
+    for (int c = 0; c < NM; c += 8) {
+      const uint4 v = live ? *(const uint4*)(pp + c) : make_uint4(0u, 0u, 0u, 0u);
+      const __half* h = (const __half*)&v;
+#pragma unroll
+      for (int j = 0; j < 8; j++) pv[c + j] = __half2float(h[j]);
+    }
+  }
+  const float fx = (float)px, fy = (float)py;
+  for (int d0 = 0; d0 < n; d0 += kMaskChunk) {
+    const int nd = min(kMaskChunk, n - d0);
+    __syncthreads();   // the previous chunk is done with the staging
+    for (int i = threadIdx.x; i < nd * (NM / 8); i += kMaskTile) {
+      const int dd = i / (NM / 8), c8 = (i - dd * (NM / 8)) * 8;
+      const int a = outidx[(size_t)img * max_out + d0 + dd];
+      int li = 0;
+      while (li + 1 < cf.n && a >= cf.abase[li + 1]) li++;
+      const int rem = a - cf.abase[li];
+      const int y = rem / cf.W[li], x = rem - y * cf.W[li];
+      const uint4 v = *(const uint4*)(cf.coef[li].p + cf.coef[li].pix(img, y, x) + c8);
+      const __half* h = (const __half*)&v;
+#pragma unroll
+      for (int j = 0; j < 8; j++) co[dd][c8 + j] = __half2float(h[j]);
+    }
+    for (int dd = threadIdx.x; dd < nd; dd += kMaskTile) {
+      const float* det = outdets + ((size_t)img * max_out + d0 + dd) * 6;
+      bx[dd] = make_float4(DM_MUL(det[0], rx), DM_MUL(det[1], ry), DM_MUL(det[2], rx),
+                           DM_MUL(det[3], ry));
+    }
+    __syncthreads();
+    if (!live) continue;
+    uint8_t* out = masks + ((size_t)img * max_out + d0) * Ph * Pw + p;
+    for (int dd = 0; dd < nd; dd++) {
+      const float4 b = bx[dd];
+      uint8_t m = 0;
+      if (fx >= b.x && fx < b.z && fy >= b.y && fy < b.w) {
+        float acc = 0.f;
+#pragma unroll
+        for (int c = 0; c < NM; c++) acc = DM_FMA(co[dd][c], pv[c], acc);
+        m = acc > 0.f;
+      }
+      out[(size_t)dd * Ph * Pw] = m;
+    }
+  }
+}
+
 __global__ void masks_kernel(DevCoefs cf, DView proto, int nm, float rx, float ry, int max_out,
                              const float* __restrict__ outdets, const int* __restrict__ outidx,
                              const int* __restrict__ outcnt, uint8_t* __restrict__ masks) {
@@ -874,6 +942,16 @@ int yk_masks(const YkLevel* levels, int nlevels, const YkView* proto, int in_h, 
     A += levels[i].coef.H * levels[i].coef.W;
   }
   cf.n = nlevels;
+  bool tiles = proto->C == 32;
+  for (int i = 0; i < nlevels; i++) tiles = tiles && view_vec8(&levels[i].coef);
+  if (tiles) {   // pixel tiles, proto in registers (the 32-coefficient heads)
+    const dim3 grid((proto->H * proto->W + kMaskTile - 1) / kMaskTile, proto->batch);
+    launch_k(masks_tile_kernel<32>, grid, kMaskTile, 0, (cudaStream_t)st, cf, dview(*proto),
+             (float)proto->W / in_w, (float)proto->H / in_h, max_out, post->outdets,
+             post->outidx, post->outcnt, masks);
+    note_launch();
+    return check_launch("masks");
+  }
   dim3 grid(max_out, proto->batch);
   launch_k(masks_kernel, grid, 256, 0, (cudaStream_t)st, 
       cf, dview(*proto), proto->C, (float)proto->W / in_w, (float)proto->H / in_h, max_out,
