@@ -188,6 +188,10 @@ int yk_fetch_device_error(void);
 // word is set and the kernel unwinds (no trap, no hang: the wait is bounded).  Synchronous;
 // call yk_test_inject(0, 0) to restore normal operation.
 int yk_test_inject(int withhold, unsigned long long wait_ns);
+// Test hook: CTAs per image of the NMS launch (thread-block cluster size 1, 2, 4 or 8; 0
+// restores the default, the largest power of two up to 8 with batch x size <= the SM count).
+// Results do not depend on it; tests compare every size bit for bit.
+int yk_test_nms_cluster(int size);
 const char* yk_last_cuda_error(void);
 // Number of kernels this library launched since load (all devices) — a host-side counter.
 long long yk_launch_count(void);

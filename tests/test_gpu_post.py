@@ -231,3 +231,31 @@ def test_masks_bitexact(lib, cuda):
             y, x = divmod(a - bases[li], Ws[li])
             ref = graph_ref.mask(coef[li][img, y, x].numpy(), proto[img].numpy(), od[img, d], S)
             assert np.array_equal(masks[img, d], ref), (img, d)
+
+
+@pytest.mark.parametrize("csize", [1, 2, 4, 8])
+def test_nms_cluster_sizes_bitexact(lib, cuda, csize):
+    """The NMS launch spreads an image over a cluster of 1-8 CTAs (redundant sort in each
+    CTA with the candidates in shared memory, CTA 0 alone with them in the workspace; mask
+    rows and classes shared out).  Every size must give the oracle's survivors bit for bit:
+    one class with bit-mask rows in shared memory, few classes with rows in the workspace,
+    80 classes, and 8400 candidates in the workspace, over batches of 1 and 3."""
+    from yolo11_cu_b200 import runtime as rt
+    cases = [(1, -2.9, 0.7, 1, 8), (4, -2.0, 0.45, 1, 8), (80, -4.0, 0.45, 3, 80),
+             (80, -3.0, 0.7, 1, 80), (80, 6.0, 0.45, 1, 80)]
+    assert lib.yk_test_nms_cluster(csize) == 0
+    try:
+        for nc, bias, iou, B, ch in cases:
+            g = torch.Generator().manual_seed(500 + nc + B)
+            sizes, box, cls = _levels(640, B, g, bias, nc=ch)
+            od, oi, oc, rc, _ = _run_gpu_post(lib, rt, cuda, sizes, box, cls, B, iou, 300, nc=nc)
+            for img in range(B):
+                recs, keep = _oracle(sizes, box, cls, img, iou, 300, nc=nc)
+                assert rc[img] == len(recs) > 0, (nc, bias, img)
+                assert oc[img] == len(keep), (nc, bias, img)
+                n = len(keep)
+                assert np.array_equal(oi[img, :n], keep[:, 6].astype(np.int32)), (nc, bias, img)
+                assert np.array_equal(od[img, :n].view(np.uint32), keep[:, :6].view(np.uint32))
+    finally:
+        lib.yk_test_nms_cluster(0)
+    assert lib.yk_test_nms_cluster(3) == -1

@@ -73,9 +73,9 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 bool pdl_enabled();
-bool patch_enabled();
+bool patch_enabled();         // halo-patch 3x3 convs offered to the autotuner (YK_NO_PATCH=1: no)
 bool streams_enabled();      // multi-stream graph capture candidate (YK_NO_STREAMS=1: no)
-bool bulk_store_enabled();   // epilogue bulk tensor stores (YK_NO_BULK_STORE=1: per-row stores)   // halo-patch 3x3 convs offered to the autotuner (YK_NO_PATCH=1: no)
+bool bulk_store_enabled();   // epilogue bulk tensor stores (YK_NO_BULK_STORE=1: per-row stores)
 // Per host thread: -1 follows pdl_enabled(), 0 / 1 force plain / programmatic launches (the
 // engine captures its graphs both ways and keeps the faster).
 static thread_local int g_pdl_override = -1;
@@ -95,6 +95,57 @@ static inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 blo
   cfg.attrs = at;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// launch_k with thread-block clusters of `cluster` CTAs along x (1: a plain launch)
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_kc(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                                    size_t smem, int cluster, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed =
+      g_pdl_override >= 0 ? g_pdl_override : pdl_enabled() ? 1 : 0;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = (unsigned)cluster;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = cluster > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// ---- thread-block cluster primitives (distributed shared memory) ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster: shared-memory writes (local or remote) and global
+// writes before it are visible to every thread of the cluster after it.
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local, uint32_t rank) {
+  uint32_t o;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(o) : "r"(local), "r"(rank));
+  return o;
+}
+__device__ __forceinline__ void st_cluster_u8(uint32_t a, uint32_t v) {
+  asm volatile("st.shared::cluster.u8 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_u32(uint32_t a, uint32_t v) {
+  asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ unsigned long long globaltimer() {

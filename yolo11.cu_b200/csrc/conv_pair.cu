@@ -40,21 +40,6 @@ struct PairCfg {
   static_assert(STAGES % G == 0 && STAGES / G >= 2, "stage groups");
 };
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-               ::: "memory");
-}
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
@@ -143,7 +128,7 @@ conv_pair_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmW,
   }
   tc_fence_before();
   __syncwarp();
-  cluster_sync_all();   // barriers initialised and TMEM allocated in both CTAs
+  cluster_barrier();   // barriers initialised and TMEM allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem = *tslot_ptr;
   const int HWo = a.Ho * a.Wo;
@@ -172,7 +157,7 @@ conv_pair_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmW,
             break;
           }
           const uint32_t sW = base + s * Cfg::kStage, sP = sW + Cfg::kHalf;
-          const uint32_t fb = map_rank(full_bar(s), 0);
+          const uint32_t fb = cluster_map(full_bar(s), 0);
           if (rank == 0) mbar_expect_tx(full_bar(s), 2 * Cfg::kStage);
           if (a.tmaA == 2) {
             const int tap = kb / a.ncb, cbi = kb - tap * a.ncb;
@@ -193,7 +178,7 @@ conv_pair_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmW,
     // 32-pixel chunks
     const int sp = warp & 3, grp = (warp - 4) >> 3, half = ((warp - 4) >> 2) & 1;
     __half* stg = stg_s + (warp - 4) * 32 * 32;
-    const uint32_t tempty_leader0 = map_rank(tempty_bar(0), 0);
+    const uint32_t tempty_leader0 = cluster_map(tempty_bar(0), 0);
     uint32_t li = 0;
     for (int t = pair; t < a.ntiles; t += npairs, li++) {
       if ((int)(li & 1) != grp) continue;
@@ -278,17 +263,17 @@ conv_pair_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmW,
                       (kb | kk) != 0);
         if (s % G == G - 1) {
           tc_commit_pair(empty_bar(s / G));
-          tc_commit_pair(map_rank(empty_bar(s / G), 1));
+          tc_commit_pair(cluster_map(empty_bar(s / G), 1));
         }
       }
       if (!ok) { *abort_flag = 1; break; }
       tc_commit_pair(tfull_bar(acc));
-      tc_commit_pair(map_rank(tfull_bar(acc), 1));
+      tc_commit_pair(cluster_map(tfull_bar(acc), 1));
     }
   }
   tc_fence_before();
   __syncwarp();
-  cluster_sync_all();   // no remote arrivals or MMAs into the other CTA remain
+  cluster_barrier();   // no remote arrivals or MMAs into the other CTA remain
   if (warp == kPairMma) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512)

@@ -6,6 +6,7 @@
 // (the reference appends candidates with atomicAdd and truncates NMS input at 1024 in that
 // order, engine/engine.cu:890, 1064).
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -137,6 +138,12 @@ constexpr int kBitMax = 512;   // classes of kBitMin+1..kBitMax candidates: bit-
 // follows the kept boxes, while the masks cost every pair (yolo11n, 268 candidates in four
 // classes, 16 kept: 24 us of masks and scan against a few us of greedy).
 constexpr int kBitMin = 128;
+// With a cluster of 4 or more CTAs per image the rows are built by 128+ warps, so smaller
+// classes pay for masks too.
+#ifndef YK_NMS_BITMIN_CLUSTER
+#define YK_NMS_BITMIN_CLUSTER 32
+#endif
+constexpr int kBitMinCluster = YK_NMS_BITMIN_CLUSTER;
 static inline size_t al16(size_t v) { return (v + 15) & ~(size_t)15; }
 static inline WsLayout ws_layout(int A) {
   WsLayout L;
@@ -241,6 +248,12 @@ __global__ void __launch_bounds__(256) decode_kernel(DevLevels lv, int batch, in
 //   3. greedy suppression per class, one warp per class, 32 candidates per step;
 //   4. survivors in score order, the first max_out written out.
 // Up to kNmsSmemCand candidates live in shared memory, more in the workspace.
+// An image may own a cluster of `csize` CTAs (distributed shared memory): with the
+// candidates in shared memory every CTA runs steps 1-2 on its own copy (the same work, the
+// same result), otherwise CTA 0 alone sorts in the workspace; step 3 is shared out, the bit-mask rows
+// over all warps of the cluster and the classes round-robin over the CTAs (class s to CTA
+// s mod csize), the survivor flags going to CTA 0, which alone runs step 4.  A batch that
+// leaves SMs idle (batch 1: one SM of 148) thus spreads its pair tests over up to 8 SMs.
 constexpr int kNmsThreads = 1024;
 // Diagnostic builds (-DYK_NMS_PROF) record %globaltimer at each phase boundary of image 0.
 #ifdef YK_NMS_PROF
@@ -366,7 +379,7 @@ __device__ __forceinline__ unsigned warp_and(unsigned v) {
 
 __global__ void __launch_bounds__(kNmsThreads, 1)
 nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int* outidx,
-           int* outcnt, int* rawcnt) {
+           int* outcnt, int* rawcnt, int csize) {
   pdl_wait();     // inputs come from the previous kernel
   pdl_trigger();
   extern __shared__ __align__(16) uint8_t nsm[];
@@ -376,7 +389,9 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   __shared__ int s_total;
   __shared__ unsigned s_bits[4];        // OR / AND of the score keys, OR / AND of the classes
   __shared__ float kept_s[32][kKeptSmem][5];
-  const int img = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ int s_ordc;                // workspace sort: which ord buffer holds the class order
+  const int rank = csize > 1 ? (int)cluster_rank() : 0;
+  const int img = blockIdx.x / csize, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int A = L.A;
   NMS_MARK(0);
   uint8_t* wimg = ws + (size_t)img * L.per_img;
@@ -414,6 +429,11 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   uint32_t* ord1 = ord + cap;
   uint32_t* ord2 = ord + 2 * cap;
 
+  // workspace mode: CTA 0 alone gathers and sorts (the arrays are the cluster's)
+  const bool active = in_smem || rank == 0;
+  const uint32_t* ordS = ord1;
+  const uint32_t* ordC = ord2;
+  if (active) {
   // 1b. gather the candidates in anchor order
   unsigned kor = 0, kand = ~0u, cor = 0, cand_ = ~0u;
   for (int q0 = 0; q0 < per; q0 += 32) {
@@ -438,7 +458,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
       box[pos] = make_float4(r[0], r[1], r[2], r[3]);
       skey[pos] = sk;
       ccls[pos] = c;
-      canch[pos] = (uint32_t)a;
+      if (rank == 0) canch[pos] = (uint32_t)a;
       ord0[pos] = (uint32_t)pos;
       surv[pos] = 0;
       kor |= sk; kand &= sk; cor |= c; cand_ &= c;
@@ -454,8 +474,6 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
   NMS_MARK(1);
 
   // 2. score order (ordS) and class order (ordC), both stable on the anchor order
-  const uint32_t* ordS;
-  const uint32_t* ordC;
   if (n <= kRankSortMax) {
     // bitonic sort of the unique 64-bit keys (score key, index) and (class, score key,
     // index) in the radix histogram area, unused on this path: threads 0-511 sort the first,
@@ -542,19 +560,38 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
       if (st && p < kMaxClasses) segs[p] = i;
       nseg_running += t;
     }
-    if (tid == 0) s_total = min(nseg_running, kMaxClasses);
+    if (tid == 0) {
+      s_total = min(nseg_running, kMaxClasses);
+      s_ordc = (int)((ordC - ord) / cap);
+    }
     __syncthreads();
+  }
+  }   // active
+  if (csize > 1) {
+    cluster_barrier();   // every CTA is past its sort: shared memory may be written remotely
+    if (!active) {       // workspace mode: CTA 0's class segments and class order
+      if (tid == 0) {
+        s_total = (int)ld_cluster_u32(cluster_map(smem_u32(&s_total), 0));
+        s_ordc = (int)ld_cluster_u32(cluster_map(smem_u32(&s_ordc), 0));
+      }
+      __syncthreads();
+      for (int i = tid; i < s_total; i += kNmsThreads)
+        segs[i] = (int)ld_cluster_u32(cluster_map(smem_u32(&segs[i]), 0));
+      ordC = ord + (size_t)s_ordc * cap;
+      __syncthreads();
+    }
   }
   const int nseg = s_total;
   if (tid == 0) segs[nseg] = n;
   __syncthreads();
   NMS_MARK(3);
 
-  // 4. per-class suppression in score order.  Classes of kBitMin+1..kBitMax candidates whose bit
-  // masks fit the workspace region, with all candidates in shared memory, use bit masks: the whole block builds them (bit j of row
-  // i: dm_iou_gt(i, j) for a later j, the same test as the greedy path), then one warp per
-  // class walks the rows: a row not yet removed is kept and removes its mask.  The other
-  // classes run the greedy loop, one warp per class.  Both are exact greedy NMS, and both
+  // 4. per-class suppression in score order.  Classes of kBitMin+1..kBitMax candidates
+  // (kBitMinCluster+1.. with 4 or more CTAs per image) whose bit masks fit, with all
+  // candidates in shared memory, use bit masks: every warp of the cluster builds them (bit j
+  // of row i: dm_iou_gt(i, j) for a later j, the same test as the greedy path), then one
+  // warp per class walks the rows: a row not yet removed is kept and removes its mask.  The
+  // other classes run the greedy loop, one warp per class.  Both are exact greedy NMS, and both
   // stop a class at max_out kept boxes: its later survivors could never reach the output.
   int* moff = msegoff;                 // per class: first mask word, or -1 (greedy)
   // Up to kRankSortMax candidates the radix histogram area is unused: the masks live there
@@ -569,7 +606,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
       const int m = segs[tid + 1] - segs[tid], words = (m + 31) >> 5;
       // (only with the candidates in shared memory: from the workspace, the pair tests'
       // loads cost more than the greedy loop saves)
-      if (in_smem && m > kBitMin && m <= kBitMax) need = m * words;
+      if (in_smem && m > (csize >= 4 ? kBitMinCluster : kBitMin) && m <= kBitMax) need = m * words;
     }
     int total;
     const int off = block_scan(need, wsum, &total);
@@ -578,16 +615,32 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
     __syncthreads();
   NMS_MARK(4);
   }
+  // a class's bit-mask rows go to the CTA that scans them (class s: CTA s mod csize)
+  auto put_row = [&](uint32_t* rows, size_t idx, uint32_t v, int owner) {
+    if (csize > 1 && mask_smem) st_cluster_u32(cluster_map(smem_u32(rows + idx), (uint32_t)owner), v);
+    else rows[idx] = v;
+  };
   {
     // one warp per row of a bit-mask class: lane k tests the pair (i, j = 32 w + k) and a
     // ballot gives word w of row i (bit k: candidate j is suppressed by candidate i);
-    // words below the diagonal are zero
+    // words below the diagonal are zero.  The rows are shared out over every warp of the
+    // cluster.
+    // Work units are (four rows, one word): four independent chains of loads and tests per
+    // warp, and enough units that a single class spreads over every warp of the cluster.
+    // Units are dealt round-robin over the cluster's warps across all classes.
+    const int gwarp = rank * (kNmsThreads >> 5) + warp, nwarps = csize * (kNmsThreads >> 5);
+    int ubase = 0;
     for (int sg = 0; sg < nseg; sg++) {
-      if (moff[sg] < 0) continue;                         // uniform across the block
+      if (moff[sg] < 0) continue;                         // uniform across the cluster
       const int s = segs[sg], m = segs[sg + 1] - s, words = (m + 31) >> 5;
+      const int owner = sg % csize, units = ((m + 3) >> 2) * words;
       uint32_t* rows = bmask + moff[sg];
-      // four rows per warp at a time: four independent chains of loads and tests
-      for (int i0 = warp * 4; i0 < m; i0 += (kNmsThreads >> 5) * 4) {
+      for (int un = (gwarp - ubase % nwarps + nwarps) % nwarps; un < units; un += nwarps) {
+        const int i0 = (un / words) * 4, w = un - (un / words) * words;
+        if (w < (i0 >> 5)) {                              // left of the diagonal: zero
+          if (lane < 4 && i0 + lane < m) put_row(rows, (size_t)(i0 + lane) * words + w, 0u, owner);
+          continue;
+        }
         float4 bi[4];
         float ai[4];
 #pragma unroll
@@ -595,29 +648,32 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
           bi[u] = box[ordC[s + min(i0 + u, m - 1)]];
           ai[u] = dm_area(bi[u].x, bi[u].y, bi[u].z, bi[u].w);
         }
-        for (int w = i0 >> 5; w < words; w++) {      // words left of the diagonal are zero
-          const int j = w * 32 + lane;
-          const float4 bj = box[ordC[s + min(j, m - 1)]];
+        const int j = w * 32 + lane;
+        const float4 bj = box[ordC[s + min(j, m - 1)]];
 #pragma unroll
-          for (int u = 0; u < 4; u++) {
-            const int i = i0 + u;
-            const bool sup = i < m && j > i && j < m &&
-                             dm_iou_gt(bi[u].x, bi[u].y, bi[u].z, bi[u].w, ai[u], bj.x, bj.y,
-                                       bj.z, bj.w, iou);
-            const unsigned bits = __ballot_sync(~0u, sup);
-            if (lane == 0 && i < m) rows[(size_t)i * words + w] = bits;
-          }
+        for (int u = 0; u < 4; u++) {
+          const int i = i0 + u;
+          const bool sup = i < m && j > i && j < m &&
+                           dm_iou_gt(bi[u].x, bi[u].y, bi[u].z, bi[u].w, ai[u], bj.x, bj.y,
+                                     bj.z, bj.w, iou);
+          const unsigned bits = __ballot_sync(~0u, sup);
+          if (lane == 0 && i < m) put_row(rows, (size_t)i * words + w, bits, owner);
         }
-#pragma unroll
-        for (int u = 0; u < 4; u++)
-          if (lane == 0 && i0 + u < m)
-            for (int w = 0; w < (i0 >> 5); w++) rows[(size_t)(i0 + u) * words + w] = 0u;
       }
+      ubase += units;
     }
   }
-  __syncthreads();
+  if (csize > 1) cluster_barrier();   // the rows are complete in their owners' memory
+  else __syncthreads();
   NMS_MARK(5);
-  for (int sg = warp; sg < nseg; sg += kNmsThreads >> 5) {
+  // survivor flags live in CTA 0 (shared memory) or the workspace
+  const bool surv_remote = csize > 1 && in_smem;
+  const uint32_t surv0 = surv_remote ? cluster_map(smem_u32(surv), 0) : 0u;
+  auto put_surv = [&](uint32_t ci, uint32_t v) {
+    if (surv_remote) st_cluster_u8(surv0 + ci, v);
+    else surv[ci] = (uint8_t)v;
+  };
+  for (int sg = rank + csize * warp; sg < nseg; sg += csize * (kNmsThreads >> 5)) {
     const int s = segs[sg], e = segs[sg + 1];
     if (moff[sg] >= 0) {
       const int m = e - s, words = (m + 31) >> 5;
@@ -647,7 +703,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
 #pragma unroll
         for (int u = 0; u < 16; u++)        // every lane removes the kept rows' words
           if ((keep >> u) & 1u) removed |= r16[u];
-        if (lane < 16 && i0 + lane < m) surv[ordC[s + i0 + lane]] = (uint8_t)((keep >> lane) & 1u);
+        if (lane < 16 && i0 + lane < m) put_surv(ordC[s + i0 + lane], (keep >> lane) & 1u);
         nk += __popc(keep);
       }
       continue;
@@ -655,7 +711,7 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
     int nk = 0;
     for (int c0 = s; c0 < e; c0 += 32) {
       if (nk >= max_out) {                  // the rest of the class cannot reach the output
-        for (int q = c0 + lane; q < e; q += 32) surv[ordC[q]] = 0;
+        for (int q = c0 + lane; q < e; q += 32) put_surv(ordC[q], 0u);
         break;
       }
       const int i = c0 + lane;
@@ -689,12 +745,14 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
         float* kb = t < kKeptSmem ? kept_s[warp][t] : kept + (size_t)(s + t) * 5;
         kb[0] = x1; kb[1] = y1; kb[2] = x2; kb[3] = y2; kb[4] = ar;
       }
-      if (valid) surv[ci] = alive ? 1 : 0;
+      if (valid) put_surv(ci, alive ? 1u : 0u);
       nk += __popc(m);
       __syncwarp();
     }
   }
-  __syncthreads();
+  if (csize > 1) cluster_barrier();   // every survivor flag is in CTA 0
+  else __syncthreads();
+  if (rank != 0) return;
   NMS_MARK(6);
 
   // 5. survivors in score order, the first max_out kept
@@ -913,6 +971,54 @@ int yk_decode(const YkLevel* levels, int nlevels, int batch, int nc, float conf,
   return check_launch("decode");
 }
 
+// CTAs per image: the largest power of two up to 8 that keeps batch x size within the SMs,
+// capped by what the device can co-schedule (cudaOccupancyMaxActiveClusters, once per
+// device); yk_test_nms_cluster forces a size (0: this rule).
+static std::atomic<int> g_nms_cluster_force{0};
+static int nms_cluster(int batch) {
+  static std::mutex mu;
+  static int fit[128], sms[128];   // per device: largest size that schedules (0: not probed)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 1;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!fit[dev]) {
+      cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+      fit[dev] = 1;
+      for (int c = 8; c > 1; c >>= 1) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(c);
+        cfg.blockDim = dim3(kNmsThreads);
+        cfg.dynamicSmemBytes = kNmsDynSmem;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)c;
+        at[0].val.clusterDim.y = at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, nms_kernel, &cfg) == cudaSuccess && n >= 1) {
+          fit[dev] = c;
+          break;
+        }
+        cudaGetLastError();   // an unsupported size is not an error of the next launch
+      }
+    }
+  }
+  const int force = g_nms_cluster_force.load();
+  int c = 1;
+  if (force > 0) c = force;
+  else
+    while (c < 8 && (long long)batch * c * 2 <= sms[dev]) c <<= 1;
+  return c < fit[dev] ? c : fit[dev];
+}
+
+extern "C" int yk_test_nms_cluster(int size) {
+  if (size != 0 && size != 1 && size != 2 && size != 4 && size != 8) return YK_EINVAL;
+  g_nms_cluster_force.store(size);
+  return YK_OK;
+}
+
 int yk_nms(int batch, int anchors, float iou, int max_out, const YkPost* post, yk_stream_t st) {
   if (batch < 1 || anchors < 1 || anchors >= (1 << 20) || max_out < 1 || !post || !post->ws ||
       !post->outdets || !post->outidx || !post->outcnt || !post->rawcnt)
@@ -920,8 +1026,10 @@ int yk_nms(int batch, int anchors, float iou, int max_out, const YkPost* post, y
   WsLayout L = ws_layout(anchors);
   if (post->ws_bytes < (size_t)batch * L.per_img) return YK_EINVAL;
   if (smem_attr(nms_kernel, (int)kNmsDynSmem) != cudaSuccess) return check_launch("nms attr");
-  launch_k(nms_kernel, batch, kNmsThreads, kNmsDynSmem, (cudaStream_t)st, iou, max_out,
-           (uint8_t*)post->ws, L, post->outdets, post->outidx, post->outcnt, post->rawcnt);
+  const int cs = nms_cluster(batch);
+  launch_kc(nms_kernel, batch * cs, kNmsThreads, kNmsDynSmem, cs, (cudaStream_t)st, iou,
+            max_out, (uint8_t*)post->ws, L, post->outdets, post->outidx, post->outcnt,
+            post->rawcnt, cs);
   note_launch();
   return check_launch("nms");
 }

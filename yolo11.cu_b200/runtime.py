@@ -87,6 +87,7 @@ _SIGS = {
                                        C.c_void_p, C.c_void_p]),
     "yk_fetch_device_error": (C.c_int, []),
     "yk_test_inject": (C.c_int, [C.c_int, C.c_ulonglong]),
+    "yk_test_nms_cluster": (C.c_int, [C.c_int]),
     "yk_last_cuda_error": (C.c_char_p, []),
     "yk_launch_count": (C.c_longlong, []),
     # engine ABI (include/yolo.h)
