@@ -680,31 +680,56 @@ nms_kernel(float iou, int max_out, uint8_t* ws, WsLayout L, float* outdets, int*
       const uint32_t* rows = bmask + moff[sg];
       uint32_t removed = 0;                 // lane w holds word w of the removed set
       int nk = 0;
-      for (int i0 = 0; i0 < m; i0 += 16) {  // 16 rows: their own bits share word wq
-        const int wq = i0 >> 5, sh = i0 & 31;
-        uint32_t r16[16];                   // word `lane` of each of the 16 rows
-#pragma unroll
-        for (int u = 0; u < 16; u++)
-          r16[u] = i0 + u < m && lane < words ? rows[(size_t)(i0 + u) * words + lane] : 0u;
-        // the lane holding word wq decides the 16 rows in order from that word alone
-        uint32_t keep = 0;
-        if (lane == wq) {
-          uint32_t rem = removed;
+      for (int i0 = 0; i0 < m; i0 += 32) {  // 32 rows: their own bits share word wq
+        const int wq = i0 >> 5;
+        const uint32_t valid = m - i0 >= 32 ? ~0u : (1u << (m - i0)) - 1u;
+        uint32_t cand = ~__shfl_sync(~0u, removed, wq) & valid;   // rows not yet removed
+        if (__popc(cand) <= 8) {
+          // few rows left (the usual case: detections suppress heavily): take the first,
+          // drop what it removes (its diagonal word, held by lane u), repeat
+          const uint32_t diag = i0 + lane < m ? rows[(size_t)(i0 + lane) * words + wq] : 0u;
+          uint32_t keep = 0;
           int k = nk;
+          while (cand && k < max_out) {
+            const int u = __ffs(cand) - 1;
+            keep |= 1u << u;
+            k++;
+            cand &= ~(1u << u) & ~__shfl_sync(~0u, diag, u);
+          }
+          if (lane < words)                 // every lane adds its word of the kept rows
+            for (uint32_t km = keep; km; km &= km - 1)
+              removed |= rows[(size_t)(i0 + __ffs(km) - 1) * words + lane];
+          if (i0 + lane < m) put_surv(ordC[s + i0 + lane], (keep >> lane) & 1u);
+          nk = k;
+          continue;
+        }
+        // many rows left: 16 rows at a time, every lane loading its word of each row and
+        // the lane holding word wq deciding the 16 rows in order from its words alone
+        for (int h = i0; h < i0 + 32 && h < m; h += 16) {
+          const int sh = h & 31;
+          uint32_t r16[16];
 #pragma unroll
           for (int u = 0; u < 16; u++)
-            if (i0 + u < m && !((rem >> (sh + u)) & 1u) && k < max_out) {
-              keep |= 1u << u;
-              rem |= r16[u];
-              k++;
-            }
-        }
-        keep = __shfl_sync(~0u, keep, wq);
+            r16[u] = h + u < m && lane < words ? rows[(size_t)(h + u) * words + lane] : 0u;
+          uint32_t keep = 0;
+          if (lane == wq) {
+            uint32_t rem = removed;
+            int k = nk;
 #pragma unroll
-        for (int u = 0; u < 16; u++)        // every lane removes the kept rows' words
-          if ((keep >> u) & 1u) removed |= r16[u];
-        if (lane < 16 && i0 + lane < m) put_surv(ordC[s + i0 + lane], (keep >> lane) & 1u);
-        nk += __popc(keep);
+            for (int u = 0; u < 16; u++)
+              if (h + u < m && !((rem >> (sh + u)) & 1u) && k < max_out) {
+                keep |= 1u << u;
+                rem |= r16[u];
+                k++;
+              }
+          }
+          keep = __shfl_sync(~0u, keep, wq);
+#pragma unroll
+          for (int u = 0; u < 16; u++)      // every lane removes the kept rows' words
+            if ((keep >> u) & 1u) removed |= r16[u];
+          if (lane < 16 && h + lane < m) put_surv(ordC[s + h + lane], (keep >> lane) & 1u);
+          nk += __popc(keep);
+        }
       }
       continue;
     }
