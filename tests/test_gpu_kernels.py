@@ -222,11 +222,15 @@ def test_conv_patch_transposed_residual(lib, cuda):
 @pytest.mark.parametrize("case", PATCH_CASES + [(2, 40, 40, 32, 32), (1, 19, 23, 96, 64),
                                                 (1, 160, 160, 32, 32), (1, 33, 30, 32, 48),
                                                 (2, 64, 64, 48, 48), (1, 37, 29, 16, 32),
-                                                (1, 21, 50, 80, 48), (2, 40, 33, 8, 16)])
+                                                (1, 21, 50, 80, 48), (2, 40, 33, 8, 16),
+                                                (2, 40, 40, 128, 128), (4, 64, 64, 128, 128),
+                                                (1, 20, 20, 64, 192)])
 @pytest.mark.parametrize("tile,msub", [(32, 1), (32, 2), (64, 1)])
 def test_conv_kx_folded(lib, cuda, case, tile, msub):
     """Halo patches with the horizontal taps folded into N (algo 5); Cin 48 / 16 / 80 take
-    16-channel blocks, Cin 8 one zero-filled 16-channel block."""
+    16-channel blocks, Cin 8 one zero-filled 16-channel block; filters of one or two
+    channel blocks stay in shared memory, also with several output-channel tiles (each CTA
+    keeps one: 128 -> 128 over 2 or 4 tiles, 64 -> 192 over 3 or 6, more tiles than SMs)."""
     from yolo11_cu_b200 import runtime as rt
     B, H, W, Cin, Cout = case
     g = torch.Generator(device="cpu").manual_seed(hash(case) % 1000 + 13)
@@ -251,13 +255,14 @@ def test_conv_kx_folded_16ch_residual(lib, cuda, C):
     assert rel(out, ref) < TOL
 
 
-def test_conv_kx_folded_residual(lib, cuda):
+@pytest.mark.parametrize("C", [64, 128])
+def test_conv_kx_folded_residual(lib, cuda, C):
     from yolo11_cu_b200 import runtime as rt
     g = torch.Generator().manual_seed(9)
-    x = torch.randn(2, 30, 30, 64, generator=g).half().to(cuda)
-    w = (torch.randn(64, 64, 3, 3, generator=g) / 24).to(cuda)
-    b = (torch.randn(64, generator=g) * 0.1).to(cuda)
-    res = torch.randn(2, 30, 30, 64, generator=g).half().to(cuda)
+    x = torch.randn(2, 30, 30, C, generator=g).half().to(cuda)
+    w = (torch.randn(C, C, 3, 3, generator=g) / (C * 9) ** 0.5).to(cuda)
+    b = (torch.randn(C, generator=g) * 0.1).to(cuda)
+    res = torch.randn(2, 30, 30, C, generator=g).half().to(cuda)
     out, ref = run_conv(lib, rt, x, w, b, 3, 1, 1, act=1, res=res, tile=64, msub=1, algo=5)
     assert rel(out, ref) < TOL
 

@@ -32,7 +32,7 @@ namespace yk {
 constexpr int kKxMma = 20;
 constexpr int kKxThreads = 32 * (kKxMma + 1);
 
-template <int BN, int MT, int CB, bool WR = false>
+template <int BN, int MT, int CB, int WR = 0>
 struct KxnCfg {
   static constexpr int kRows = 8 * MT + 2;
   static constexpr int kRB = CB * 2;
@@ -47,14 +47,15 @@ struct KxnCfg {
   // the kH warps of one sub-partition taking alternate 16-channel blocks
   static constexpr int kH = 4 / kNacc;
   // window ring: as deep as 216 KB allows (up to 6), so small tiles keep several TMA loads
-  // in flight; each slot holds a window and its three weight stages, or, with WR (the whole
-  // filter is one block, loaded once and kept), the three stages exist once
+  // in flight; each slot holds a window and its three weight stages, or, with WR > 0 (the
+  // CTA's filter slice is WR channel blocks, loaded once and kept), the 3 * WR weight stages
+  // exist once and the slots hold windows only
   static constexpr int kResSlot = MT * (BN / (16 * kH)) * 2 * 16;   // residual bytes per thread
   static constexpr int kRes = 512 * kResSlot;                      // all epilogue threads
   static constexpr int kWSTfit =
-      WR ? (216 * 1024 - kRes - 3 * kB) / kWin : (216 * 1024 - kRes) / (kWin + 3 * kB);
+      WR ? (216 * 1024 - kRes - 3 * WR * kB) / kWin : (216 * 1024 - kRes) / (kWin + 3 * kB);
   static constexpr int kWST = kWSTfit > 6 ? 6 : kWSTfit < 2 ? 2 : kWSTfit;
-  static constexpr int kBST = WR ? 3 : 3 * kWST;
+  static constexpr int kBST = WR ? 3 * WR : 3 * kWST;
   static constexpr int kTmemCols = kNacc * kTileCols <= 256 ? 256 : 512;
   static constexpr int kBars = 512;
   static constexpr size_t kSmem =
@@ -65,16 +66,18 @@ struct KxnCfg {
   static constexpr int kEpiStride = 1024;              // boxes on 128-byte boundaries
   static_assert(kRes >= 16 * MT * (BN / (16 * kH)) * kEpiStride, "TMA epilogue staging");
   static_assert(kNacc * kTileCols <= 512, "TMEM budget");
-  static_assert(kSmem <= 232448, "smem budget");
+  // resident weights need a window ring of two slots besides them
+  static constexpr bool kFits = kSmem <= 232448 && (WR == 0 || kWSTfit >= 2);
   static_assert(3 * BN <= 256 && BN % 16 == 0, "N = 3 * BN");
 };
 
-template <int BN, int MT, int CB, bool WR>
+template <int BN, int MT, int CB, int WR>
 __global__ void __launch_bounds__(kKxThreads, 1)
 conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
                 const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmY,
                 const __grid_constant__ CUtensorMap tmR) {
   using Cfg = KxnCfg<BN, MT, CB, WR>;
+  static_assert(Cfg::kFits, "smem budget");
   constexpr int kRB = Cfg::kRB, WST = Cfg::kWST;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -122,9 +125,10 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
   tc_fence_after();
   const uint32_t tmem = *tslot_ptr;
   const int per_img = a.nty * a.ntx;
-  // one weight block for the whole conv (Cin <= CB and Cout <= BN): loaded once into the
-  // first slot's stages and kept there
-  const bool wres = a.ncb == 1 && a.ntn == 1;
+  // resident weights (WR = a.ncb channel blocks; the grid is a multiple of a.ntn, so every
+  // tile of this CTA has the same output channels): stage 3 * cb + ky, loaded with the
+  // first tile's blocks and kept
+  constexpr bool wres = WR > 0;
 
   if (warp == 0) {
     // ---------------- producer (one thread, all loads by TMA) ----------------
@@ -143,8 +147,8 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
           mbar_expect_tx(wfull(ws), Cfg::kWinTx);
           tma_load_4d(wbase + ws * Cfg::kWin, &tmX, wfull(ws), cb * CB, tx * kPatchUse - 1,
                       ty * 8 * MT - 1, img);
-          for (int ky = 0; ky < 3 && !(wres && gw > 0); ky++) {
-            const int bs = ws * 3 + ky;
+          for (int ky = 0; ky < 3 && !(wres && gw >= (uint32_t)WR); ky++) {
+            const int bs = (wres ? cb : ws) * 3 + ky;
             mbar_expect_tx(bfull(bs), Cfg::kB);
             tma_load_4d(bbase + bs * Cfg::kB, &tmW, bfull(bs), cb * CB, 0, ky, n0);
           }
@@ -341,7 +345,7 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
         const uint32_t win = wbase + ws * Cfg::kWin;
 #pragma unroll
         for (int ky = 0; ky < 3; ky++) {
-          const int bs = wres ? ky : ws * 3 + ky;
+          const int bs = (wres ? cb : ws) * 3 + ky;
           if (!mbar_wait(bfull(bs), wres ? 0u : par, 0x306)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sb = bbase + bs * Cfg::kB;
@@ -428,16 +432,21 @@ static bool encode_epi_box(CUtensorMap* m, const __half* p, int C, int W, int H,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int MT, int CB, bool WR = false>
+template <int BN, int MT, int CB, int WR = 0>
 static int launch_kxn(const PatchArgs& a, const YkView* x, cudaStream_t st) {
-  if (!WR && a.ncb == 1 && a.ntn == 1) return launch_kxn<BN, MT, CB, true>(a, x, st);
+  if constexpr (WR == 0) {
+    // the CTA's whole filter slice stays in shared memory when it fits beside two windows
+    if (a.ncb == 1 && KxnCfg<BN, MT, CB, 1>::kFits) return launch_kxn<BN, MT, CB, 1>(a, x, st);
+    if (a.ncb == 2 && KxnCfg<BN, MT, CB, 2>::kFits) return launch_kxn<BN, MT, CB, 2>(a, x, st);
+  }
   using Cfg = KxnCfg<BN, MT, CB, WR>;
   if (smem_attr(conv_kxn_kernel<BN, MT, CB, WR>, (int)Cfg::kSmem) != cudaSuccess) return check_launch("conv_kxn attr");
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return YK_EUNSUP;
   if (!g_num_sms[dev]) cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  const int grid = a.ntiles < g_num_sms[dev] ? a.ntiles : g_num_sms[dev];
+  int grid = a.ntiles < g_num_sms[dev] ? a.ntiles : g_num_sms[dev];
+  if (WR) grid -= grid % a.ntn;   // fixed output channels per CTA (ntiles is a multiple of ntn)
   CUtensorMap tmW, tmX, tmY = {}, tmR = {};
   if (!encode_kxn_w(&tmW, a.w, a.Cin, a.Cout, BN, CB)) return YK_EUNSUP;
   if (!encode_patch_x(&tmX, a.x, a.Cin, a.W, a.H, x->batch, x->stride, Cfg::kRows, CB))
