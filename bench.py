@@ -43,7 +43,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) of the tcgen05 conv launches of one 32-frame yolo11m forward, from
 # one ncu capture of the current kernels, and the algorithmic bytes of the same convs (input,
 # weights, output, residual once each).
-CONV_DRAM_BYTES_PER_STEP = 7.506e9
+CONV_DRAM_BYTES_PER_STEP = 7.509e9
 CONV_ALG_BYTES_PER_STEP = 9.469e9
 
 
