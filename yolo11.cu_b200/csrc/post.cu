@@ -18,7 +18,7 @@ namespace yk {
 // One launch letterboxes a batch of equal-size frames: grid (row blocks, frames), `rows`
 // output rows per block (1 for a single frame, up to 4 for a batch, so the grid fills the
 // GPU).  The block first copies the two source rows each of its output rows samples into
-// shared memory with coalesced 16-byte loads (rows outside the image band are skipped), then
+// shared memory with 16-byte cp.async copies (rows outside the image band are skipped), then
 // every thread computes whole output pixels, consecutive lanes on consecutive pixels, so the
 // shared-memory byte reads of a warp fall on neighbouring bytes and its fp16 stores on one
 // contiguous span.  The arithmetic is the reference's formula in explicitly rounded fp32
@@ -30,6 +30,12 @@ __device__ __forceinline__ int lb_src_row(int y, int top, float scale, int sh, i
   const float fy = DM_SUB(DM_DIV(DM_ADD((float)(y - top), 0.5f), scale), 0.5f);
   const int y0 = (int)floorf(fy);
   return which ? min(y0 + 1, sh - 1) : max(y0, 0);
+}
+
+// A byte as a float, exactly: 2^23 + b has b in its low mantissa bits, and the subtraction
+// of 2^23 is exact.
+__device__ __forceinline__ float lb_u8f(uint32_t b) {
+  return __fsub_rn(__uint_as_float(0x4B000000u | b), 8388608.f);
 }
 
 __global__ void __launch_bounds__(256) letterbox_kernel(
@@ -52,62 +58,82 @@ __global__ void __launch_bounds__(256) letterbox_kernel(
     const uintptr_t a0 = (uintptr_t)row & ~(uintptr_t)15, end = (uintptr_t)row + rb;
     uint8_t* s = lb_rows + slot * pitch;
     const int nvec = (int)((end - a0) >> 4);           // whole 16-byte words inside the row
-    for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
-      const uintptr_t p = a0 + ((uintptr_t)i << 4);
-      if (p < (uintptr_t)row) {                          // head word: the row's bytes only
-        for (int k = (int)((uintptr_t)row - p); k < 16; k++) s[i * 16 + k] = __ldg((const uint8_t*)p + k);
-      } else {
-        *(uint4*)(s + i * 16) = __ldg((const uint4*)p);
-      }
-    }
+    // asynchronous copies, all of the block's words in flight at once (the head word may
+    // start before the row: the aligned word holding the row's first byte lies inside the
+    // same allocation, and the bytes before the row are never read from shared memory)
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x)
+      cp_async16(smem_u32(s + i * 16), (const void*)(a0 + ((uintptr_t)i << 4)), 16u);
     // bytes past the last whole word (all of a row shorter than one word), never before it
     const uintptr_t t0 = max(a0 + ((uintptr_t)nvec << 4), (uintptr_t)row);
     for (uintptr_t p = t0 + threadIdx.x; p < end; p += blockDim.x)
       s[p - a0] = __ldg((const uint8_t*)p);
   }
+  cp_async_commit();
+  cp_async_wait<0>();
   __syncthreads();
   const __half pad = __float2half_rn(dm_div255(114.f));
   const int tid = threadIdx.y * blockDim.x + threadIdx.x, nthr = blockDim.x * blockDim.y;
-  for (int r = 0; r < nrow; r++) {
+  // per-row terms (the vertical weight and the staged source rows), computed once
+  float wyr[kLbMaxRows], wy1r[kLbMaxRows];
+  const uint8_t* s0r[kLbMaxRows];
+  const uint8_t* s1r[kLbMaxRows];
+  bool inr[kLbMaxRows];
+#pragma unroll
+  for (int r = 0; r < kLbMaxRows; r++) {
     const int y = y_beg + r;
-    __half* orow = out + (size_t)y * dw * dstride;
-    const bool row_in = y >= top && y < top + nh;
+    inr[r] = r < nrow && y >= top && y < top + nh;
     float wy = 0.f;
     int sh0 = 0, sh1 = 0;
-    if (row_in) {
+    if (inr[r]) {
       const float fy = DM_SUB(DM_DIV(DM_ADD((float)(y - top), 0.5f), scale), 0.5f);
       wy = DM_SUB(fy, floorf(fy));
       sh0 = (int)((uintptr_t)(img + (size_t)lb_src_row(y, top, scale, sh, 0) * rb) & 15);
       sh1 = (int)((uintptr_t)(img + (size_t)lb_src_row(y, top, scale, sh, 1) * rb) & 15);
     }
-    const uint8_t* s0 = lb_rows + (2 * r) * pitch + sh0;
-    const uint8_t* s1 = lb_rows + (2 * r + 1) * pitch + sh1;
-    const float wy1 = DM_SUB(1.f, wy);
-    for (int x = tid; x < dw; x += nthr) {
+    wyr[r] = wy;
+    wy1r[r] = DM_SUB(1.f, wy);
+    s0r[r] = lb_rows + (2 * r) * pitch + sh0;
+    s1r[r] = lb_rows + (2 * r + 1) * pitch + sh1;
+  }
+  // Column-major walk: the horizontal terms of a column (a division, a floor and two
+  // float/int conversions) are computed once and serve every row of the block, and source
+  // bytes become floats by an exact integer-or / subtract on the ALU and FMA pipes instead
+  // of the conversion unit, which bounded the row-major version.
+  for (int x = tid; x < dw; x += nthr) {
+    const bool col_in = x >= left && x < left + nw;
+    float wx = 0.f, wx1 = 1.f;
+    int x0 = 0, x1 = 0;
+    if (col_in) {
+      const float fx = DM_SUB(DM_DIV(DM_ADD((float)(x - left), 0.5f), scale), 0.5f);
+      x0 = (int)floorf(fx);
+      wx = DM_SUB(fx, (float)x0);
+      x1 = min(x0 + 1, sw - 1) * 3;
+      x0 = max(x0, 0) * 3;
+      wx1 = DM_SUB(1.f, wx);
+    }
+#pragma unroll
+    for (int r = 0; r < kLbMaxRows; r++) {
+      if (r >= nrow) break;
       __half o0 = pad, o1 = pad, o2 = pad;
-      if (row_in && x >= left && x < left + nw) {
-        const float fx = DM_SUB(DM_DIV(DM_ADD((float)(x - left), 0.5f), scale), 0.5f);
-        int x0 = (int)floorf(fx);
-        const float wx = DM_SUB(fx, (float)x0);
-        const int x1 = min(x0 + 1, sw - 1) * 3;
-        x0 = max(x0, 0) * 3;
-        const float wx1 = DM_SUB(1.f, wx);
-        const float w00 = DM_MUL(wy1, wx1), w01 = DM_MUL(wy1, wx);
-        const float w10 = DM_MUL(wy, wx1), w11 = DM_MUL(wy, wx);
+      if (inr[r] && col_in) {
+        const float w00 = DM_MUL(wy1r[r], wx1), w01 = DM_MUL(wy1r[r], wx);
+        const float w10 = DM_MUL(wyr[r], wx1), w11 = DM_MUL(wyr[r], wx);
+        const uint8_t* s0 = s0r[r];
+        const uint8_t* s1 = s1r[r];
         float v[3];
 #pragma unroll
         for (int c = 0; c < 3; c++) {
-          float t = DM_MUL((float)s0[x0 + c], w00);
-          t = DM_ADD(t, DM_MUL((float)s0[x1 + c], w01));
-          t = DM_ADD(t, DM_MUL((float)s1[x0 + c], w10));
-          v[c] = DM_ADD(t, DM_MUL((float)s1[x1 + c], w11));
+          float t = DM_MUL(lb_u8f(s0[x0 + c]), w00);
+          t = DM_ADD(t, DM_MUL(lb_u8f(s0[x1 + c]), w01));
+          t = DM_ADD(t, DM_MUL(lb_u8f(s1[x0 + c]), w10));
+          v[c] = DM_ADD(t, DM_MUL(lb_u8f(s1[x1 + c]), w11));
         }
         // BGR in, RGB out
         o0 = __float2half_rn(dm_div255(v[2]));
         o1 = __float2half_rn(dm_div255(v[1]));
         o2 = __float2half_rn(dm_div255(v[0]));
       }
-      __half* o = orow + (size_t)x * dstride;
+      __half* o = out + ((size_t)(y_beg + r) * dw + x) * dstride;
       o[0] = o0;
       o[1] = o1;
       o[2] = o2;
@@ -196,13 +222,31 @@ __global__ void __launch_bounds__(256) decode_kernel(DevLevels lv, int batch, in
   const __half* cp = L0.cls.p + L0.cls.pix(img, p.y, p.x);
   float best = -INFINITY;
   int bcls = 0;
-  for (int c0 = sub * 8; c0 < nc; c0 += 32) {
+  // the first 128 classes: every 16-byte load of the lane is issued before the first
+  // compare, so an anchor costs one memory latency, not one per word
+  constexpr int kPre = 4;
+  uint4 cv[kPre];
+#pragma unroll
+  for (int k = 0; k < kPre; k++)
+    if (sub * 8 + 32 * k < nc) cv[k] = *(const uint4*)(cp + sub * 8 + 32 * k);
+#pragma unroll
+  for (int k = 0; k < kPre; k++) {
+    const int c0 = sub * 8 + 32 * k;
+    if (c0 >= nc) break;
+    const __half* h = (const __half*)&cv[k];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float f = __half2float(h[i]);
+      if (c0 + i < nc && f > best) { best = f; bcls = c0 + i; }   // first max wins
+    }
+  }
+  for (int c0 = sub * 8 + 32 * kPre; c0 < nc; c0 += 32) {
     const uint4 v = *(const uint4*)(cp + c0);
     const __half* h = (const __half*)&v;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
       const float f = __half2float(h[i]);
-      if (c0 + i < nc && f > best) { best = f; bcls = c0 + i; }   // first max wins
+      if (c0 + i < nc && f > best) { best = f; bcls = c0 + i; }
     }
   }
 #pragma unroll
