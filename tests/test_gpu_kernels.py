@@ -343,9 +343,11 @@ def _v(rt, t, coff=0, Cv=None):
 
 
 @pytest.mark.parametrize("shape", [(2, 20, 20, 32), (3, 20, 20, 256), (1, 13, 17, 128),
-                                   (1, 32, 32, 96), (1, 100, 100, 64)])
+                                   (1, 32, 32, 96), (1, 100, 100, 64), (32, 20, 20, 256),
+                                   (148, 20, 80, 32)])
 def test_maxpool_chain(lib, cuda, shape):
-    """SPPF chain: shared-memory planes (small images) or the direct windows (large)."""
+    """SPPF chain: shared-memory planes (small images; a fixed column per thread when a plane
+    row has at most 256 16-byte chunks, else the flat walk) or the direct windows (large)."""
     from yolo11_cu_b200 import runtime as rt
     x = torch.randn(*shape, device=cuda).half()
     ys = [torch.empty_like(x) for _ in range(3)]

@@ -143,7 +143,7 @@ static int launch_attn(const YkView* qkv, const YkView* y, int heads, int N, siz
 
 // ---------------- tensor-core path (kd = 32, hd = 64) ----------------
 // Flash-style: a warp owns 16 queries; keys stream through shared memory in chunks of 192
-// (K rows padded to 40 halves, V rows to 72, so fragment loads are bank-conflict free).
+// (copied by cp.async, zero past the last key; K rows padded to 40 halves, V rows to 72, so fragment loads are bank-conflict free).
 // Per 16-key block: S = Q K^T with four m16n8k16 MMAs (fp32 accumulate), online softmax in
 // registers (row max / sum shared by the 4 lanes of a row through shuffles), then the fp16
 // probabilities are reused in place as the A operand of O += P V (eight MMAs, V fragments by
@@ -182,13 +182,17 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(DView qkv, DView y, int N
     const int cn = min(kAttnChunk, N - c0);
     __syncthreads();
     const int cn16 = (cn + 15) & ~15;   // rows past the last key are zero (P = 0 there)
-    for (int i = threadIdx.x; i < cn16 * 12; i += 128) {   // 4 K + 8 V 16-byte chunks per key
+    // 4 K + 8 V 16-byte chunks per key, all of the block's copies in flight at once
+    for (int i = threadIdx.x; i < cn16 * 12; i += 128) {
       const int j = i / 12, cc = i - j * 12;
-      const uint4 v = j < cn ? *(const uint4*)(base + (size_t)(c0 + j) * qkv.stride + 32 + cc * 8)
-                             : make_uint4(0, 0, 0, 0);
-      if (cc < 4) *(uint4*)(Ks + j * kKs + cc * 8) = v;
-      else *(uint4*)(Vs + j * kVs + (cc - 4) * 8) = v;
+      const bool ok = j < cn;
+      const __half* src = ok ? base + (size_t)(c0 + j) * qkv.stride + 32 + cc * 8 : base;
+      const uint32_t dst = cc < 4 ? smem_u32(Ks + j * kKs + cc * 8)
+                                  : smem_u32(Vs + j * kVs + (cc - 4) * 8);
+      cp_async16(dst, src, ok ? 16u : 0u);
     }
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
     for (int kb = 0; kb < cn; kb += 16) {
       // S = Q K^T for 16 keys: two n-tiles of 8 keys

@@ -688,6 +688,42 @@ __global__ void __launch_bounds__(256) pool5x3_plane_kernel(DView x, DView y1, D
   }
   __syncthreads();
   const DView* outs[3] = {&y1, &y2, &y3};
+  const int wk = W * kG;                 // 16-byte chunks per plane row
+  if (wk <= 256) {
+    // each thread keeps one (column, channel group) and walks rows rstep apart: no
+    // per-element division, and neighbours along a row are chunk offsets of +-kG
+    const int rstep = 256 / wk;
+    const int col = threadIdx.x % wk, r0 = threadIdx.x / wk;
+    const int xx = col / kG;
+    const bool act = r0 < rstep;
+#pragma unroll 1
+    for (int pass = 0; pass < 3; pass++) {
+      if (act)
+        for (int yy = r0; yy < H; yy += rstep) {   // max over 5 columns: A -> B
+          const int i = yy * wk + col;
+          uint4 m = A[i];
+#pragma unroll
+          for (int dx = -2; dx <= 2; dx++)
+            if (dx != 0 && xx + dx >= 0 && xx + dx < W) hmax8(m, A[i + dx * kG]);
+          Bp[i] = m;
+        }
+      __syncthreads();
+      const DView& yo = *outs[pass];
+      __half* orow = yo.p + (size_t)img * H * W * yo.stride + c0 + (col - xx * kG) * 8;
+      if (act)
+        for (int yy = r0; yy < H; yy += rstep) {   // max over 5 rows: B -> A, and out
+          const int i = yy * wk + col;
+          uint4 m = Bp[i];
+#pragma unroll
+          for (int dy = -2; dy <= 2; dy++)
+            if (dy != 0 && yy + dy >= 0 && yy + dy < H) hmax8(m, Bp[i + dy * wk]);
+          A[i] = m;
+          *(uint4*)(orow + (size_t)(yy * W + xx) * yo.stride) = m;
+        }
+      __syncthreads();
+    }
+    return;
+  }
 #pragma unroll 1
   for (int pass = 0; pass < 3; pass++) {
     for (int i = threadIdx.x; i < n; i += 256) {   // max over 5 columns: A -> B
@@ -950,8 +986,8 @@ int yk_maxpool5x3(const YkView* x, const YkView* y1, const YkView* y2, const YkV
   const long long total = (long long)x->batch * x->H * x->W * (x->C / 8);
   // whole planes in shared memory: two of H*W*CB halves within 200 KB
   const size_t plane = (size_t)x->H * x->W * 2;
-  // 64-channel blocks only when 32-channel ones would not fill the GPU twice over
-  const bool many32 = (long long)x->batch * (x->C / 32) >= 2 * 148;
+  // 64-channel blocks only when 32-channel ones would not fill the GPU
+  const bool many32 = (long long)x->batch * (x->C / 32) >= 148;
   const int cbk = (x->C % 32 == 0 && 2 * plane * 32 <= 200 * 1024 && (many32 || x->C % 64))
                       ? 32
                   : (x->C % 64 == 0 && 2 * plane * 64 <= 200 * 1024) ? 64
