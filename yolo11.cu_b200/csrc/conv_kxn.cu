@@ -23,10 +23,10 @@
 
 namespace yk {
 
-// 21 warps: 0 producer, 4-19 epilogue, 20 MMA.  The kx sums make the epilogue the long pole
-// for small Cin, so it has 16 warps: with four TMEM accumulators (when four tiles fit in 512
-// columns) each accumulator has its own four warps and four tiles drain at once; with two,
-// each is drained by eight warps taking alternate 16-channel blocks.  Residual rows are
+// 21 warps: 0 producer, 4-19 epilogue, 20 MMA.  The epilogue has 16 warps (the kx sums):
+// with four TMEM accumulators (when four tiles fit in 512 columns) each accumulator has its
+// own four warps and four tiles drain at once; with two, each is drained by eight warps
+// taking alternate 16-channel blocks.  Residual rows are
 // copied to shared memory (cp.async) before the accumulator wait, hiding their latency
 // behind the MMAs.
 constexpr int kKxMma = 20;
@@ -330,6 +330,10 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
     // ---------------- MMA issuer ----------------
     constexpr uint32_t idesc = idesc_f16_m128(3 * BN);
     uint32_t gw = 0, li = 0;
+    // resident weight stages complete once (with the first tile) and stay valid: their
+    // barriers are not polled again (three polls and fences per tile cost the 32-channel
+    // 160x160 conv 15 %)
+    bool wready = false;
     for (int t = blockIdx.x; t < a.ntiles && !*abort_flag; t += gridDim.x, li++) {
       const int acc = li % Cfg::kNacc;
       const uint32_t use = li / Cfg::kNacc;
@@ -346,8 +350,10 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
 #pragma unroll
         for (int ky = 0; ky < 3; ky++) {
           const int bs = (wres ? cb : ws) * 3 + ky;
-          if (!mbar_wait(bfull(bs), wres ? 0u : par, 0x306)) { ok = false; break; }
-          tc_fence_after();
+          if (!(wres && wready)) {
+            if (!mbar_wait(bfull(bs), wres ? 0u : par, 0x306)) { ok = false; break; }
+            tc_fence_after();
+          }
           const uint32_t sb = bbase + bs * Cfg::kB;
 #pragma unroll
           for (int kk = 0; kk < CB / 16; kk++)
@@ -366,6 +372,7 @@ conv_kxn_kernel(const PatchArgs a, const __grid_constant__ CUtensorMap tmW,
       }
       if (!ok) { *abort_flag = 1; break; }
       tc_commit(tfull(acc));
+      wready = true;
     }
   }
   __syncthreads();
