@@ -116,17 +116,18 @@ __global__ void __launch_bounds__(256) letterbox_kernel(
       if (r >= nrow) break;
       __half o0 = pad, o1 = pad, o2 = pad;
       if (inr[r] && col_in) {
-        const float w00 = DM_MUL(wy1r[r], wx1), w01 = DM_MUL(wy1r[r], wx);
-        const float w10 = DM_MUL(wyr[r], wx1), w11 = DM_MUL(wyr[r], wx);
-        const uint8_t* s0 = s0r[r];
-        const uint8_t* s1 = s1r[r];
+        // tap weights: upper-left, upper-right, lower-left, lower-right
+        const float wul = DM_MUL(wy1r[r], wx1), wur = DM_MUL(wy1r[r], wx);
+        const float wll = DM_MUL(wyr[r], wx1), wlr = DM_MUL(wyr[r], wx);
+        const uint8_t* up = s0r[r];
+        const uint8_t* lo = s1r[r];
         float v[3];
 #pragma unroll
         for (int c = 0; c < 3; c++) {
-          float t = DM_MUL(lb_u8f(s0[x0 + c]), w00);
-          t = DM_ADD(t, DM_MUL(lb_u8f(s0[x1 + c]), w01));
-          t = DM_ADD(t, DM_MUL(lb_u8f(s1[x0 + c]), w10));
-          v[c] = DM_ADD(t, DM_MUL(lb_u8f(s1[x1 + c]), w11));
+          float acc = DM_MUL(lb_u8f(up[x0 + c]), wul);
+          acc = DM_ADD(acc, DM_MUL(lb_u8f(up[x1 + c]), wur));
+          acc = DM_ADD(acc, DM_MUL(lb_u8f(lo[x0 + c]), wll));
+          v[c] = DM_ADD(acc, DM_MUL(lb_u8f(lo[x1 + c]), wlr));
         }
         // BGR in, RGB out
         o0 = __float2half_rn(dm_div255(v[2]));

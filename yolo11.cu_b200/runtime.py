@@ -164,6 +164,11 @@ def tview(t, coff: int = 0, Cv: int | None = None) -> YkView:
     return view(t.data_ptr(), B, H, W, Ct, coff, Ct - coff if Cv is None else Cv)
 
 
+def np_contig(a):
+    import numpy as np
+    return np.ascontiguousarray(a)
+
+
 class Engine:
     """Thin owner of a yolo_* handle (device = current CUDA device unless given)."""
 
@@ -175,6 +180,7 @@ class Engine:
         o.device, o.conf, o.iou, o.max_det = device, conf, iou, max_det
         o.autotune, o.fuse = int(autotune), int(fuse)
         self.max_det = max_det
+        self.device = device
         self.h = self.lib.yolo_create_ex(model_dir.encode(), max_batch, C.byref(o))
         if not self.h:
             raise RuntimeError("yolo_create failed: " + self.lib.yolo_last_error().decode())
@@ -208,6 +214,21 @@ class Engine:
 
     def preprocess_cls(self, dev_bgr_ptr: int, h: int, w: int, slot: int):
         self.lib.yolo_preprocess_cls(self.h, C.c_void_p(dev_bgr_ptr), h, w, slot)
+
+    def preprocess_host(self, bgr, slot: int):
+        """Preprocess a host BGR u8 HWC frame (numpy) into `slot` with the task's own
+        preprocessing: the frame goes to a device buffer of the handle's GPU first, which
+        is held until the engine stream has consumed it."""
+        import torch
+        dev = self.device if self.device >= 0 else torch.cuda.current_device()
+        d = torch.from_numpy(np_contig(bgr)).to(f"cuda:{dev}")
+        h, w = bgr.shape[:2]
+        if self.task() == 2:
+            self.preprocess_cls(d.data_ptr(), h, w, slot)
+        else:
+            self.preprocess(d.data_ptr(), h, w, slot)
+        self.sync()
+        self._check()
 
     def task(self) -> int:
         return self.lib.yolo_task(self.h)
