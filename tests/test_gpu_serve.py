@@ -1,6 +1,6 @@
 """The gRPC batching server on the GPU: real engines behind yolo.Yolo/Detect on 127.0.0.1,
-several concurrent clients sending JPEG (nvJPEG) and PNG (CPU decode) images to a detect and
-a segment model.  Every response must equal what the engine returns for that image alone
+several concurrent clients sending JPEG and PNG images to a detect and a segment model, with
+JPEG decoded by nvJPEG on the handle or on the CPU decoder pool.  Every response must equal what the engine returns for that image alone
 (same handle options, heuristic tiles, so batch composition cannot change a result): boxes
 bit for bit, segment masks as decoded run lengths, letterbox geometry."""
 import importlib.util
@@ -43,10 +43,10 @@ def _images():
     return out
 
 
-def _direct(eng, data):
+def _direct(eng, data, decode):
     """The engine alone on one image: (boxes, masks, geometry)."""
     import cv2
-    if data[:2] == b"\xff\xd8":
+    if decode == "gpu" and data[:2] == b"\xff\xd8":
         assert eng.preprocess_jpeg(data, 0) == 0
     else:
         eng.preprocess_host(cv2.imdecode(np.frombuffer(data, np.uint8), cv2.IMREAD_COLOR), 0)
@@ -56,7 +56,8 @@ def _direct(eng, data):
     return dets, masks, eng.slot_geom(0)
 
 
-def test_serve_matches_engine(lib, cuda, pkg):
+@pytest.mark.parametrize("decode", ["gpu", "cpu"])
+def test_serve_matches_engine(lib, cuda, pkg, decode):
     import grpc
     from yolo11_cu_b200 import export, runtime as rt
     det_dir = export.ensure_model_dir("yolo11n", MODELS, 640)
@@ -64,7 +65,7 @@ def test_serve_matches_engine(lib, cuda, pkg):
     mk = lambda d, b: rt.Engine(d, b, device=0, autotune=False)
     batcher = serve.Batcher([("yolo11n", [mk(det_dir, 4), mk(det_dir, 4)], 4),
                              ("yolo11n-seg", [mk(seg_dir, 2), mk(seg_dir, 2)], 2)],
-                            target_ms=20.0)
+                            target_ms=20.0, decode=decode, decoders=4)
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
@@ -93,7 +94,7 @@ def test_serve_matches_engine(lib, cuda, pkg):
         batcher.close()
     assert len(got) == len(jobs)
     ref_det, ref_seg = mk(det_dir, 4), mk(seg_dir, 2)
-    want = {(m, i): _direct(ref_seg if m else ref_det, imgs[i])
+    want = {(m, i): _direct(ref_seg if m else ref_det, imgs[i], decode)
             for m in ("", "yolo11n-seg") for i in range(len(imgs))}
     assert max(r.batch for r in got.values()) >= 1
     for k, r in got.items():

@@ -113,6 +113,10 @@ class FakeEngine:
     def preprocess_host(self, bgr, slot):
         self._put(slot, 1_000_000 + int(bgr.sum()) % 1000)
 
+    def preprocess_host_batch(self, bgrs, slots):
+        for b, s in zip(bgrs, slots):
+            self.preprocess_host(b, s)
+
     def run_async(self, B):
         time.sleep(0.002)
         self.results = list(self.slots[:B])
@@ -262,3 +266,26 @@ def test_grpc_end_to_end():
     finally:
         server.stop(0)
         b.close()
+
+
+def test_cpu_decode_pool():
+    """decode="cpu": a batch's images decoded on the thread pool (PNG and BMP alike), an
+    undecodable one fails alone while the rest of its batch is served."""
+    import cv2
+    eng = [FakeEngine(), FakeEngine()]
+    b = serve.Batcher([("m", eng, 4)], target_ms=1e6, decode="cpu", decoders=3)
+    imgs = [np.full((6, 9, 3), 10 + i, np.uint8) for i in range(3)]
+    blobs = [cv2.imencode(".png", imgs[0])[1].tobytes(), cv2.imencode(".png", imgs[1])[1].tobytes(),
+             cv2.imencode(".bmp", imgs[2])[1].tobytes(), b"\xff\xd8 broken"]
+    out = {}
+    ths = [threading.Thread(target=lambda i=i: out.__setitem__(i, b.submit("", blobs[i], timeout=10)))
+           for i in range(4)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join(20)
+    b.close()
+    for i in range(3):
+        ok, r = out[i]
+        assert ok and r.batch == 4 and r.boxes[0].score == 1_000_000 + int(imgs[i].sum()) % 1000
+    assert out[3][0] is False

@@ -215,6 +215,21 @@ class Engine:
     def preprocess_cls(self, dev_bgr_ptr: int, h: int, w: int, slot: int):
         self.lib.yolo_preprocess_cls(self.h, C.c_void_p(dev_bgr_ptr), h, w, slot)
 
+    def preprocess_host_batch(self, bgrs, slots):
+        """preprocess_host for several frames: all uploads, then all preprocessing, one sync."""
+        import torch
+        dev = self.device if self.device >= 0 else torch.cuda.current_device()
+        bufs = [torch.from_numpy(np_contig(b)).to(f"cuda:{dev}") for b in bgrs]
+        cls = self.task() == 2
+        for d, b, s in zip(bufs, bgrs, slots):
+            h, w = b.shape[:2]
+            if cls:
+                self.preprocess_cls(d.data_ptr(), h, w, s)
+            else:
+                self.preprocess(d.data_ptr(), h, w, s)
+        self.sync()
+        self._check()
+
     def preprocess_host(self, bgr, slot: int):
         """Preprocess a host BGR u8 HWC frame (numpy) into `slot` with the task's own
         preprocessing: the frame goes to a device buffer of the handle's GPU first, which

@@ -20,8 +20,11 @@ Behaviour (server/serve.cpp):
     the GPU runs the current one.  Here each model holds two engine handles used in turn, so
     batch k+1's decode and letterbox go into one handle's slots while batch k's graph runs
     on the other's; the results of batch k are read before that handle is refilled.
-  * decode: JPEG by nvJPEG through `yolo_preprocess_jpeg`; other formats (PNG, ...) on the
-    CPU (cv2, the reference uses stb_image) and preprocessed from device memory.
+  * decode: JPEG by nvJPEG through `yolo_preprocess_jpeg` one image after another (the
+    handle has one nvJPEG state), other formats (PNG, ...) on the CPU (cv2; the reference
+    uses stb_image); or (--decode cpu) every image of a batch on a pool of CPU threads
+    (OpenCV; the reference's decoder pool runs nvJPEG's CPU Huffman stage on 8 threads,
+    serve.cpp:104-146), then uploaded and preprocessed on the GPU.
   * responses: boxes (detect / segment), rotated boxes (obb), top-5 classes (classify),
     segment masks as row-major 0/1 run lengths starting with a 0-run plus the letterbox
     geometry (serve.cpp:193-259); queue_ms, infer_ms, batch as the reference fills them.
@@ -137,10 +140,17 @@ class Batcher:
 
     `models`: list of (name, [engine, engine], max_batch); an engine is anything with the
     runtime.Engine methods the worker calls (task, mask_dim, exec_ms, preprocess_jpeg,
-    preprocess_host, run_async, sync, get, get_obb, get_cls, get_mask, slot_geom)."""
+    preprocess_host, preprocess_host_batch, run_async, sync, get, get_obb, get_cls,
+    get_mask, slot_geom)."""
 
-    def __init__(self, models, target_ms=50.0, safety_ms=1.0, response_cls=None):
+    def __init__(self, models, target_ms=50.0, safety_ms=1.0, response_cls=None,
+                 decode="gpu", decoders=8):
         self.models = [_Model(n, e, b) for n, e, b in models]
+        # decode="gpu": JPEG by nvJPEG on the handle, one image after another; "cpu": every
+        # image of a batch decoded by OpenCV on a pool of `decoders` threads (the reference's
+        # decoder pool, serve.cpp:104-146), then uploaded and preprocessed on the GPU
+        self.decode = decode
+        self.pool = futures.ThreadPoolExecutor(max_workers=decoders) if decode == "cpu" else None
         self.names = {m.name: i for i, m in enumerate(self.models)}
         self.target_ms, self.safety_ms = target_ms, safety_ms
         self.decode_ema_ms = 2.0
@@ -169,6 +179,8 @@ class Batcher:
             self._stop = True
             self.cv.notify_all()
         self._thread.join(timeout=5)
+        if self.pool is not None:
+            self.pool.shutdown(wait=False)
 
     # -- the firing rule (serve.cpp:163-191) --
     def slack_ms(self, m: _Model, now: float) -> float:
@@ -203,19 +215,38 @@ class Batcher:
             return pick, [m.q.popleft() for _ in range(B)]
 
     # -- the two-stage worker (serve.cpp:264-302) --
-    def _load(self, m: _Model, eng, r: _Req, slot: int) -> bool:
-        data = r.data
-        if len(data) > 3 and data[0] == 0xFF and data[1] == 0xD8:
-            return eng.preprocess_jpeg(data, slot) == 0
+    @staticmethod
+    def _cpu_decode(data: bytes):
         try:
             import cv2
-            img = cv2.imdecode(np.frombuffer(data, np.uint8), cv2.IMREAD_COLOR)
+            return cv2.imdecode(np.frombuffer(data, np.uint8), cv2.IMREAD_COLOR)
         except Exception:
-            img = None
-        if img is None:
-            return False
-        eng.preprocess_host(img, slot)
-        return True
+            return None
+
+    def _load_batch(self, m: _Model, eng, batch) -> list[bool]:
+        """Decode and preprocess the batch's images into slots 0..B-1 of `eng`."""
+        ok = [False] * len(batch)
+        if self.decode == "cpu":
+            imgs = list(self.pool.map(lambda r: self._cpu_decode(r.data), batch))
+            good = [(i, im) for i, im in enumerate(imgs) if im is not None]
+            if good:
+                eng.preprocess_host_batch([im for _, im in good], [i for i, _ in good])
+            for i, _ in good:
+                ok[i] = True
+            return ok
+        for i, r in enumerate(batch):
+            data = r.data
+            try:
+                if len(data) > 3 and data[0] == 0xFF and data[1] == 0xD8:
+                    ok[i] = eng.preprocess_jpeg(data, i) == 0
+                else:
+                    img = self._cpu_decode(data)
+                    if img is not None:
+                        eng.preprocess_host(img, i)
+                        ok[i] = True
+            except Exception:
+                ok[i] = False
+        return ok
 
     def _respond(self, m: _Model, eng, batch, ok, t_launch):
         eng.sync()
@@ -261,12 +292,10 @@ class Batcher:
             eng = m.engines[m.turn]
             m.turn ^= 1
             t0 = time.monotonic()
-            ok = [False] * len(batch)
-            for i, r in enumerate(batch):   # into the idle handle while prev's graph runs
-                try:
-                    ok[i] = self._load(m, eng, r, i)
-                except Exception:
-                    ok[i] = False
+            try:   # into the idle handle while prev's graph runs
+                ok = self._load_batch(m, eng, batch)
+            except Exception:
+                ok = [False] * len(batch)
             self.decode_ema_ms = 0.9 * self.decode_ema_ms + 0.1 * (time.monotonic() - t0) * 1e3
             if prev is not None:
                 self._respond(*prev)
@@ -337,6 +366,9 @@ def main(argv=None):
     ap.add_argument("--max-batch", type=int, default=16)
     ap.add_argument("--target-ms", type=float, default=50.0)
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--decode", choices=("gpu", "cpu"), default="gpu",
+                    help="JPEG decode: nvJPEG per image on the handle, or a CPU thread pool")
+    ap.add_argument("--decoders", type=int, default=8)
     a = ap.parse_args(argv)
     rt = _runtime()
     specs = []
@@ -350,7 +382,7 @@ def main(argv=None):
         print(f"model '{name}': task={TASKS.get(engines[0].task(), 'detect')} max-batch={maxb}",
               flush=True)
         specs.append((name, engines, maxb))
-    batcher = Batcher(specs, a.target_ms)
+    batcher = Batcher(specs, a.target_ms, decode=a.decode, decoders=a.decoders)
     server = make_server(batcher, a.addr)
     server.start()
     print(f"yoloserve listening on {a.addr} ({len(specs)} models, target={a.target_ms:.0f} ms)",
