@@ -164,8 +164,11 @@ __global__ void __launch_bounds__(128) conv_stem_mma_kernel(DView x, DView y,
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       const int k = 16 * ks + 2 * t + (j & 1) + (j >> 1) * 8;
-      const int tap = k / 3, ci = k - tap * 3, ky = tap / 3, kx = tap - ky * 3;
-      koff[ks][j] = k < 27 ? ky * pitch + 8 + (kx - p) * 3 + ci : -1;
+      // taps 27..31 pad K to 32 with zero weights: their A element may be any finite window
+      // value, so they read tap 26 and the gathers need no bounds select
+      const int kc = k < 27 ? k : 26;
+      const int tc = kc / 3, cc = kc - tc * 3, kyc = tc / 3, kxc = tc - kyc * 3;
+      koff[ks][j] = kyc * pitch + 8 + (kxc - p) * 3 + cc;
     }
   uint32_t bf[2][NF][2];
   float bias2[NF][2];
@@ -228,8 +231,8 @@ __global__ void __launch_bounds__(128) conv_stem_mma_kernel(DView x, DView y,
         __half va[4], vb[4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-          va[j] = koff[ks][j] >= 0 ? pa[koff[ks][j]] : __float2half(0.f);
-          vb[j] = koff[ks][j] >= 0 ? pb[koff[ks][j]] : __float2half(0.f);
+          va[j] = pa[koff[ks][j]];
+          vb[j] = pb[koff[ks][j]];
         }
         uint32_t a[4];
         a[0] = (uint32_t)__half_as_ushort(va[0]) | ((uint32_t)__half_as_ushort(va[1]) << 16);
@@ -248,10 +251,11 @@ __global__ void __launch_bounds__(128) conv_stem_mma_kernel(DView x, DView y,
         *(__half2*)(stg + (g + 8) * kStgRow + 8 * f + 2 * t) = h23;
       }
       __syncwarp();
+      __half* yrow = y.p + y.pix(img, oy, ox0);
       for (int q = lane; q < 16 * NF; q += 32) {
-        const int px = q / NF, f = q - px * NF, ox = ox0 + px;
-        if (ox < y.W)
-          *(uint4*)(y.p + y.pix(img, oy, ox) + 8 * f) = *(const uint4*)(stg + px * kStgRow + 8 * f);
+        const int px = q / NF, f = q - px * NF;
+        if (ox0 + px < y.W)
+          *(uint4*)(yrow + px * y.stride + 8 * f) = *(const uint4*)(stg + px * kStgRow + 8 * f);
       }
       __syncwarp();
     }
