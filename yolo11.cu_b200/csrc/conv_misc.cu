@@ -402,18 +402,24 @@ __global__ void __launch_bounds__(kDwThreads, YK_DW_MINB) dwconv3t_kernel(DView 
     wsm[i] = c < cvalid ? w[(size_t)(c0 + c) * 9 + t] : __float2half(0.f);
   }
   const int per_img = tiles_y * tiles_x * tiles_c;
+  // staging: thread tid copies channel chunk tid % 8 of window positions tid / 8 + 16 k (the
+  // chunk is the same for all its copies, as 128 threads are a multiple of 8); addresses are
+  // 32-bit offsets from the tile's image (the host checks an image fits in 2^31 elements)
+  const int sch = tid & 7;
+  const bool sch_ok = sch * 8 < cvalid;
   auto stage = [&](int t, __half* buf) {
     const int img = t / per_img;
     const int q = (t - img * per_img) / tiles_c;
     const int ty = q / tiles_x, tx = q - ty * tiles_x;
-    const int oy0 = ty * kDwTY, ox0 = tx * kDwTX;
-    for (int i = tid; i < kDwIH * kDwIW * 8; i += kDwThreads) {
-      const int ch = i & 7, pos = i >> 3;
+    const int oy0 = ty * kDwTY - 1, ox0 = tx * kDwTX - 1;
+    const __half* ibase = x.p + (size_t)img * x.H * x.W * x.stride + c0 + sch * 8;
+#pragma unroll 4
+    for (int pos = tid >> 3; pos < kDwIH * kDwIW; pos += kDwThreads / 8) {
       const int rr = pos / kDwIW, cc = pos - rr * kDwIW;
-      const int iy = oy0 - 1 + rr, ix = ox0 - 1 + cc;
-      const bool ok = iy >= 0 && iy < x.H && ix >= 0 && ix < x.W && ch * 8 < cvalid;
-      const __half* src = ok ? x.p + x.pix(img, iy, ix) + c0 + ch * 8 : x.p;
-      cp_async16(smem_u32(buf + pos * kDwCh + ch * 8), src, ok ? 16u : 0u);
+      const int iy = oy0 + rr, ix = ox0 + cc;
+      const bool ok = sch_ok && (unsigned)iy < (unsigned)x.H && (unsigned)ix < (unsigned)x.W;
+      const __half* src = ok ? ibase + (iy * x.W + ix) * x.stride : x.p;
+      cp_async16(smem_u32(buf + pos * kDwCh + sch * 8), src, ok ? 16u : 0u);
     }
   };
   const int cg = tid & 7, q16 = tid >> 3;                // q16: 4 row pairs x 4 column quads
@@ -911,7 +917,9 @@ int yk_conv(const YkView* x, const YkView* y, const YkView* res, const YkConv* p
     if (!view_vec8(x)) return YK_EINVAL;
     DView r = res ? dview(*res) : DView{nullptr, 0, 0, 0, 0};
     const long long total = npix * (p->Cout / 8);
-    if (p->k == 3 && p->p == 1 && p->s == 1 && dw_tiled_enabled()) {
+    // tiled path: 32-bit offsets within one image (larger images take the direct kernel)
+    if (p->k == 3 && p->p == 1 && p->s == 1 && dw_tiled_enabled() &&
+        (long long)x->H * x->W * x->stride < (1LL << 31)) {
       const int tcn = (p->Cout + kDwCh - 1) / kDwCh, txn = (y->W + kDwTX - 1) / kDwTX;
       const int tyn = (y->H + kDwTY - 1) / kDwTY;
       const long long nt = (long long)y->batch * tyn * txn * tcn;
